@@ -1,0 +1,191 @@
+/*
+ * projectai_cuda.h — C ABI of libprojectai_cuda.so, the B200 (sm_100a) compute backend that plugs in
+ * behind project-ai's IComputeBackend seam.
+ *
+ * Every entry point here is what a P/Invoke layer for ProjectAI.Core/IComputeBackend.cs would bind:
+ * plain pointers, sizes and a POD tensor descriptor, no C++ or torch types. Each declaration names the
+ * reference member it replaces (file:line, paths relative to the project-ai repository).
+ *
+ * Conventions
+ *  - Every function returns a pai_status; on failure pai_last_error() holds a message for the calling thread.
+ *    The status maps onto the .NET exception the reference throws for the same condition:
+ *      PAI_ERR_ARGUMENT      -> ArgumentException            (shape / rank / broadcast mismatch)
+ *      PAI_ERR_OUT_OF_RANGE  -> ArgumentOutOfRangeException  (axis, id or target out of range)
+ *      PAI_ERR_INVALID_OP    -> InvalidOperationException
+ *      PAI_ERR_OUT_OF_MEMORY -> OutOfMemory; the message always contains "out of memory"
+ *                               (ProjectAI.Trainer/Program.cs:152-157 matches on that text)
+ *  - Ops never modify their inputs. Each op allocates a fresh, contiguous, zero-offset result in the
+ *    context's current scope and describes it in *out (IComputeBackend.cs:9-96: "every op consumes and
+ *    produces Tensor handles allocated by the same backend"). Inputs may be arbitrary views: element
+ *    strides (0 = broadcast), a non-zero element offset, rank <= PAI_MAX_RANK.
+ *  - All work is ordered on the context's compute stream. Only pai_to_host, pai_sync and the ops that
+ *    return a host scalar block the caller.
+ *  - dtype: the hot path computes in F32 (the CPU oracle is F32-only, CpuComputeBackend.cs:41-53).
+ */
+#ifndef PROJECTAI_CUDA_H
+#define PROJECTAI_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PAI_MAX_RANK 8
+
+/* ProjectAI.Core/DType.cs:4-13, same order. */
+enum pai_dtype { PAI_F32 = 0, PAI_F16 = 1, PAI_BF16 = 2, PAI_I64 = 3, PAI_I32 = 4, PAI_U8 = 5, PAI_BOOL = 6 };
+
+typedef enum pai_status {
+  PAI_OK = 0,
+  PAI_ERR_ARGUMENT = 1,
+  PAI_ERR_OUT_OF_RANGE = 2,
+  PAI_ERR_INVALID_OP = 3,
+  PAI_ERR_OUT_OF_MEMORY = 4,
+  PAI_ERR_CUDA = 5,
+  PAI_ERR_NCCL = 6,
+  PAI_ERR_TIMEOUT = 7,
+  PAI_ERR_UNSUPPORTED = 8
+} pai_status;
+
+/* A tensor view (ProjectAI.Core/Tensor.cs:17-48): storage base + element offset + shape + element strides.
+ * `base` is the pointer returned by an allocating call; views share it. */
+typedef struct pai_tensor {
+  void* base;
+  int64_t offset;
+  int32_t rank;
+  int32_t dtype;
+  int32_t dims[PAI_MAX_RANK];
+  int64_t strides[PAI_MAX_RANK];
+} pai_tensor;
+
+/* One backend instance bound to one device and one compute stream (IComputeBackend.cs:9-12). */
+typedef struct pai_ctx pai_ctx;
+
+/* Thread-local message for the last failing call on this thread. Never NULL. */
+const char* pai_last_error(void);
+
+/* ---- Lifetime (IComputeBackend.cs:9 IDisposable; Backends.cs:24-31 factory) ---- */
+pai_status pai_ctx_create(int device_ordinal, pai_ctx** out);
+pai_status pai_ctx_destroy(pai_ctx* ctx);
+pai_status pai_sync(pai_ctx* ctx);
+/* Device name, for IComputeBackend.Name / Device (IComputeBackend.cs:11-12). */
+pai_status pai_device_name(pai_ctx* ctx, char* buf, int32_t buf_len);
+
+/* ---- Allocation & host transfer (IComputeBackend.cs:15-18; CpuComputeBackend.cs:41-81) ---- */
+/* Allocate: zero-filled contiguous tensor (CpuComputeBackend.cs:41-42 returns a zeroed array). */
+pai_status pai_alloc(pai_ctx* ctx, int32_t rank, const int32_t* dims, int32_t dtype, pai_tensor* out);
+/* FromHost: `count` floats, row-major, must equal the shape's element count. */
+pai_status pai_from_host(pai_ctx* ctx, const float* host, int64_t count, int32_t rank, const int32_t* dims,
+                         int32_t dtype, pai_tensor* out);
+/* ToHost: the view's logical elements in row-major order (CpuComputeBackend.cs:55-67). Blocks. */
+pai_status pai_to_host(pai_ctx* ctx, const pai_tensor* src, float* host, int64_t count);
+/* Copy: logical elements of src into a (possibly strided) destination view of equal element count
+ * (CpuComputeBackend.cs:69-81). */
+pai_status pai_copy(pai_ctx* ctx, const pai_tensor* src, const pai_tensor* dst);
+
+/* ---- Scopes (IComputeBackend.cs:69-95; semantics of TorchComputeBackend.cs:208-218) ----
+ * scope_begin pushes a scope; every allocation lands in the innermost open scope (or in no scope).
+ * scope_end frees everything the innermost scope owns except blocks passed to keep_alive, which move to
+ * the enclosing scope (exactly one level) or to no scope.
+ * release frees a block now (a superseded moment or gradient).
+ * finalize is the garbage-collector path: it frees a block only if no open scope owns it. */
+pai_status pai_scope_begin(pai_ctx* ctx);
+pai_status pai_scope_end(pai_ctx* ctx);
+pai_status pai_keep_alive(pai_ctx* ctx, const void* base);
+pai_status pai_release(pai_ctx* ctx, const void* base);
+pai_status pai_finalize(pai_ctx* ctx, const void* base);
+/* Bytes currently allocated to tensors, the peak since the last reset, and bytes held by the caching
+ * allocator (in use + cached). */
+pai_status pai_memory_stats(pai_ctx* ctx, int64_t* in_use, int64_t* peak, int64_t* reserved);
+pai_status pai_reset_peak(pai_ctx* ctx);
+
+/* ---- Elementwise, NumPy broadcasting (IComputeBackend.cs:20-31; CpuComputeBackend.cs:86-156, 304-317) ---- */
+pai_status pai_add(pai_ctx* ctx, const pai_tensor* a, const pai_tensor* b, pai_tensor* out);
+pai_status pai_sub(pai_ctx* ctx, const pai_tensor* a, const pai_tensor* b, pai_tensor* out);
+pai_status pai_mul(pai_ctx* ctx, const pai_tensor* a, const pai_tensor* b, pai_tensor* out);
+pai_status pai_div(pai_ctx* ctx, const pai_tensor* a, const pai_tensor* b, pai_tensor* out);
+pai_status pai_add_scalar(pai_ctx* ctx, const pai_tensor* a, float scalar, pai_tensor* out);
+pai_status pai_mul_scalar(pai_ctx* ctx, const pai_tensor* a, float scalar, pai_tensor* out);
+pai_status pai_sqrt(pai_ctx* ctx, const pai_tensor* x, pai_tensor* out);
+pai_status pai_sigmoid(pai_ctx* ctx, const pai_tensor* x, pai_tensor* out);
+
+/* ---- Linear algebra (IComputeBackend.cs:33-35; CpuComputeBackend.cs:159-219) ----
+ * Batched GEMM over the trailing two axes with NumPy batch broadcasting; transpose_b != 0 treats b's
+ * trailing axes as [n, k]. Computed with a 3xTF32 split on the tcgen05 tensor cores. */
+pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tensor* b, int32_t transpose_b, pai_tensor* out);
+
+/* ---- Reductions along one axis (IComputeBackend.cs:37-43; CpuComputeBackend.cs:248-301) ---- */
+pai_status pai_sum(pai_ctx* ctx, const pai_tensor* x, int32_t axis, int32_t keep_dims, pai_tensor* out);
+pai_status pai_mean(pai_ctx* ctx, const pai_tensor* x, int32_t axis, int32_t keep_dims, pai_tensor* out);
+pai_status pai_max(pai_ctx* ctx, const pai_tensor* x, int32_t axis, int32_t keep_dims, pai_tensor* out);
+
+/* ---- Transformer primitives (IComputeBackend.cs:45-49; CpuComputeBackend.cs:322-420) ---- */
+pai_status pai_softmax(pai_ctx* ctx, const pai_tensor* x, int32_t axis, pai_tensor* out);
+pai_status pai_rmsnorm(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* weight, float eps, pai_tensor* out);
+pai_status pai_silu(pai_ctx* ctx, const pai_tensor* x, pai_tensor* out);
+pai_status pai_rotary(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* cos, const pai_tensor* sin, pai_tensor* out);
+
+/* ---- Indexing & loss (IComputeBackend.cs:51-59; CpuComputeBackend.cs:424-500) ----
+ * ids / targets are host int32 arrays, as the contract's int[] parameters are. */
+pai_status pai_gather(pai_ctx* ctx, const pai_tensor* table, const int32_t* ids, int64_t n_ids, pai_tensor* out);
+pai_status pai_scatter_add_rows(pai_ctx* ctx, const pai_tensor* rows, const int32_t* ids, int64_t n_ids,
+                                int32_t row_count, pai_tensor* out);
+pai_status pai_cross_entropy(pai_ctx* ctx, const pai_tensor* logits, const int32_t* targets, int64_t n_targets,
+                             int32_t ignore_index, pai_tensor* out);
+pai_status pai_cross_entropy_grad(pai_ctx* ctx, const pai_tensor* logits, const int32_t* targets, int64_t n_targets,
+                                  int32_t ignore_index, pai_tensor* out);
+
+/* ---- Structural (IComputeBackend.cs:61-68; CpuComputeBackend.cs:509-540) ---- */
+pai_status pai_cat(pai_ctx* ctx, const pai_tensor* a, const pai_tensor* b, int32_t axis, pai_tensor* out);
+
+/* ==== Fused extensions ====
+ * Optional ops that a backend may offer beyond the reference seam. The reference composes each of them
+ * from the primitives above; a caller that finds them absent composes them the same way. */
+
+/* Causal scaled-dot-product attention with GQA, replacing the composed chain of
+ * ProjectAI.Models/Modules.cs:169-196 (Contiguous q/k/v, scores = (q*scale)·kᵀ, + causal mask, softmax, ·v).
+ * q [B,H,S,D], k/v [B,KVH,L,D] (any strides), H % KVH == 0; query i sits at absolute position
+ * pos_offset + i and attends keys j <= pos_offset + i when causal != 0 (Modules.cs:211-218).
+ * out: [B,S,H,D] contiguous (the merged-heads layout of Modules.cs:199-200);
+ * lse: [B,H,S] row log-sum-exp (natural log) of the scaled, masked scores, kept for the backward. */
+pai_status pai_sdpa_fwd(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v, float scale,
+                        int32_t causal, int32_t pos_offset, pai_tensor* out, pai_tensor* lse);
+/* Gradients of pai_sdpa_fwd (the Autograd.cs:54-73 MatMul and :197-205 Softmax rules fused).
+ * dout is [B,S,H,D] (any strides); dq [B,H,S,D], dk/dv [B,KVH,L,D] contiguous (GQA groups summed). */
+pai_status pai_sdpa_bwd(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v,
+                        const pai_tensor* out, const pai_tensor* lse, const pai_tensor* dout, float scale,
+                        int32_t causal, int32_t pos_offset, pai_tensor* dq, pai_tensor* dk, pai_tensor* dv);
+/* RMSNorm backward (Autograd.cs:223-244): dx and dw = Σ_rows g⊙x·inv in one pass over x and g. */
+pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* weight, const pai_tensor* g,
+                           float eps, pai_tensor* dx, pai_tensor* dw);
+/* SwiGLU gate: silu(gate) ⊙ up (Modules.cs:103-108 with Autograd.cs:208-217 and the Mul rule). */
+pai_status pai_silu_mul_fwd(pai_ctx* ctx, const pai_tensor* gate, const pai_tensor* up, pai_tensor* out);
+pai_status pai_silu_mul_bwd(pai_ctx* ctx, const pai_tensor* gate, const pai_tensor* up, const pai_tensor* g,
+                            pai_tensor* dgate, pai_tensor* dup);
+/* Cross-entropy value and gradient in one read of the logits (CpuComputeBackend.cs:453-500 fused with
+ * Autograd.cs:187-192). loss: scalar tensor. grad = (softmax − onehot)/count · grad_scale. */
+pai_status pai_cross_entropy_fused(pai_ctx* ctx, const pai_tensor* logits, const int32_t* targets, int64_t n_targets,
+                                   int32_t ignore_index, float grad_scale, pai_tensor* loss, pai_tensor* grad);
+/* One AdamW update in place on p, m, v (ProjectAI.Core/Optimizers.cs:81-123 in one pass, same operation
+ * order per element). p, g, m, v: contiguous tensors of equal element count. grad_scale multiplies g
+ * first (1/world for a data-parallel sum). */
+pai_status pai_adamw_step(pai_ctx* ctx, const pai_tensor* p, const pai_tensor* g, const pai_tensor* m,
+                          const pai_tensor* v, float lr, float beta1, float beta2, float eps, float weight_decay,
+                          int32_t t, float grad_scale);
+
+/* ==== Data parallel (one process per GPU; no counterpart in the single-device reference) ==== */
+pai_status pai_nccl_unique_id(uint8_t id_out[128]);
+pai_status pai_nccl_init(pai_ctx* ctx, const uint8_t id[128], int32_t rank, int32_t world_size, int32_t timeout_ms);
+/* Sum-all-reduce a bucket of contiguous F32 tensors in place on the communication stream, ordered after all
+ * work queued so far on the compute stream; later compute-stream work that touches the bucket waits for it. */
+pai_status pai_allreduce_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n_tensors);
+/* Makes the compute stream wait for every all-reduce issued so far. */
+pai_status pai_allreduce_wait(pai_ctx* ctx);
+pai_status pai_nccl_abort(pai_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PROJECTAI_CUDA_H */

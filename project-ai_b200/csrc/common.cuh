@@ -1,0 +1,139 @@
+// Shared internals of libprojectai_cuda.so: the per-device context (streams, caching allocator, scopes),
+// error reporting, and the view descriptors kernels index through.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <unordered_set>
+#include <vector>
+
+#include "projectai_cuda.h"
+
+#define PAI_API extern "C" __attribute__((visibility("default")))
+
+namespace pai {
+
+// ---------------------------------------------------------------- errors
+pai_status set_error(pai_status st, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+pai_status cuda_error(cudaError_t e, const char* what);
+
+#define PAI_TRY(x) do { pai_status _s = (x); if (_s != PAI_OK) return _s; } while (0)
+#define PAI_CUDA(x) do { cudaError_t _e = (x); if (_e != cudaSuccess) return ::pai::cuda_error(_e, #x); } while (0)
+#define PAI_LAUNCH_CHECK(what) do { cudaError_t _e = cudaGetLastError(); if (_e != cudaSuccess) return ::pai::cuda_error(_e, what); } while (0)
+
+// ---------------------------------------------------------------- context
+struct BlockInfo {
+  size_t bytes;      // rounded size held from the cache
+  int scope;         // index of the owning open scope, or -1
+};
+
+struct NcclState;  // defined in dp.cu
+
+}  // namespace pai
+
+struct pai_ctx {
+  int device = 0;
+  int sm_count = 148;
+  cudaStream_t stream = nullptr;       // compute stream: every op is ordered here
+  cudaStream_t comm_stream = nullptr;  // data-parallel all-reduce stream
+  std::recursive_mutex mu;
+  // caching allocator: rounded size -> free device blocks
+  std::unordered_map<size_t, std::vector<void*>> free_blocks;
+  std::unordered_map<void*, pai::BlockInfo> live;
+  std::vector<std::unordered_set<void*>> scopes;
+  int64_t in_use = 0, peak = 0, reserved = 0;
+  // device flag the kernels with bounded waits report into (0 = ok)
+  int* d_error_flag = nullptr;
+  pai::NcclState* nccl = nullptr;
+  char name[128] = {0};
+};
+
+namespace pai {
+
+// Makes ctx's device current on the calling thread (the contract may be driven from any thread).
+pai_status enter(pai_ctx* ctx);
+
+// Stream-ordered caching allocator. Blocks return to the cache on free and are reused by later work on the same
+// compute stream, so reuse never races with a kernel still reading the block.
+pai_status raw_alloc(pai_ctx* ctx, size_t bytes, void** out);
+void raw_free(pai_ctx* ctx, void* p);
+
+// Allocates a contiguous tensor registered in the innermost scope. zero != 0 clears it on the stream.
+pai_status alloc_tensor(pai_ctx* ctx, int rank, const int32_t* dims, int dtype, bool zero, pai_tensor* out);
+// A scratch buffer that is not a tensor: freed by the caller with raw_free (stream-ordered).
+struct Scratch {
+  pai_ctx* ctx = nullptr;
+  void* p = nullptr;
+  ~Scratch() { if (p) raw_free(ctx, p); }
+};
+pai_status scratch(pai_ctx* ctx, size_t bytes, Scratch* s);
+
+// Host -> device copy of a small host array into a stream-ordered scratch block.
+pai_status upload(pai_ctx* ctx, const void* host, size_t bytes, Scratch* s);
+
+// ---------------------------------------------------------------- views
+int64_t numel(const pai_tensor& t);
+std::string shape_str(const pai_tensor& t);
+bool is_dense(const pai_tensor& t);  // contiguous row-major (offset may be non-zero)
+pai_status check_view(pai_ctx* ctx, const pai_tensor* t, const char* what);
+void set_contiguous(pai_tensor* t, void* base, int rank, const int32_t* dims, int dtype);
+pai_tensor broadcast_view(const pai_tensor& t, int rank, const int32_t* dims);
+bool broadcast_shape(const pai_tensor& a, const pai_tensor& b, int* rank, int32_t* dims);
+inline int norm_axis(int axis, int rank) { return axis < 0 ? axis + rank : axis; }
+
+// A view reduced for indexing on the device: size-1 axes dropped, mergeable neighbours merged.
+struct DView {
+  int64_t offset;
+  int32_t rank;
+  int32_t dims[PAI_MAX_RANK];
+  int64_t strides[PAI_MAX_RANK];
+};
+// Collapses n views that share one logical shape (dims) jointly, so one flat index addresses all of them.
+void collapse(int rank, const int32_t* dims, const pai_tensor* const* views, int n, DView* out);
+
+inline float* fptr(const pai_tensor& t) { return static_cast<float*>(t.base) + t.offset; }
+
+// Grid size for a grid-stride loop: at most `waves` resident waves of `threads`-thread blocks.
+inline int grid_for(pai_ctx* ctx, int64_t n, int threads, int per_thread = 1, int waves = 8) {
+  int64_t want = (n + (int64_t)threads * per_thread - 1) / ((int64_t)threads * per_thread);
+  int64_t cap = (int64_t)ctx->sm_count * waves;
+  if (want < 1) want = 1;
+  return (int)(want < cap ? want : cap);
+}
+
+}  // namespace pai
+
+// Logical row-major index -> element offset of a collapsed view.
+__device__ __forceinline__ int64_t dview_offset(const pai::DView& v, int64_t i) {
+  int64_t off = v.offset;
+  for (int d = v.rank - 1; d >= 0; d--) {
+    int64_t dim = v.dims[d];
+    int64_t q = i / dim;
+    off += (i - q * dim) * v.strides[d];
+    i = q;
+  }
+  return off;
+}
+
+__device__ __forceinline__ int64_t dview_offset32(const pai::DView& v, uint32_t i) {
+  int64_t off = v.offset;
+  for (int d = v.rank - 1; d >= 0; d--) {
+    uint32_t dim = (uint32_t)v.dims[d];
+    uint32_t q = i / dim;
+    off += (int64_t)(i - q * dim) * v.strides[d];
+    i = q;
+  }
+  return off;
+}
+
+// Internal launchers shared across translation units.
+namespace pai {
+// dst (dense, element offset dst_off in buffer dst_base) <- logical elements of src view.
+pai_status gather_dense(pai_ctx* ctx, const pai_tensor& src, float* dst);
+// Makes `t` dense: returns t itself if already dense, else a gathered copy held in `holder`.
+pai_status dense_input(pai_ctx* ctx, const pai_tensor& t, const float** out, Scratch* holder);
+}  // namespace pai

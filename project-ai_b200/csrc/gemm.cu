@@ -1,0 +1,594 @@
+// Batched GEMM for IComputeBackend.MatMul (IComputeBackend.cs:33-35; semantics CpuComputeBackend.cs:159-219):
+// C[b] = A[b] · B[b] (or · B[b]ᵀ), NumPy batch broadcasting, arbitrary operand views.
+//
+// fp32 semantics on the tensor cores (3xTF32): every operand element x is split into hi = tf32(x) and
+// lo = tf32(x − hi) (round-to-nearest, both exactly representable in tf32), and each product is accumulated as
+// a_lo·b_hi + a_hi·b_lo + a_hi·b_hi in an fp32 TMEM accumulator. The dropped a_lo·b_lo term and the tf32 rounding
+// of lo leave a relative error near 2^-21 per product, well inside the 1e-4 conformance tolerance.
+//
+// Pipeline:
+//   1. k_pack: reads the operand view once (any strides, batch offsets), splits hi/lo, and writes 128-row x 32-k
+//      tiles already in the tcgen05 K-major SWIZZLE_128B shared-memory layout, so the GEMM moves each tile with
+//      one plain bulk copy (cp.async.bulk) and no tensor map.
+//   2. k_gemm_tc: persistent kernel, one CTA per SM, warp-specialised:
+//        warp 0   bulk-copy producer into a STAGES-deep shared-memory ring (mbarrier complete_tx);
+//        warp 1   allocates TMEM and issues tcgen05.mma.kind::tf32 (M=128, N=BN) from one elected lane;
+//        warps 2-5 epilogue: tcgen05.ld from a double-buffered TMEM accumulator, fp32 stores to C.
+//      Split-K (partials + deterministic reduce) keeps the SMs busy on deep-K, small-MN products (weight grads).
+//   Every mbarrier wait is bounded; a timeout sets the context's device error flag and the kernel drains and exits.
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "common.cuh"
+
+namespace pai {
+
+constexpr int kBM = 128;                        // UMMA M (rows of A per tile)
+constexpr int kBK = 32;                         // fp32 elements per 128-byte swizzle row
+constexpr int kTileFloats = kBM * kBK;          // one packed 128x32 tile (16 KiB)
+constexpr uint32_t kWaitLimit = 1u << 26;       // bounded mbarrier polls before declaring a hang
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Returns false if the phase did not complete within the poll budget.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kWaitLimit; i++) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// tcgen05 shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);           // start address
+  d |= (uint64_t)1 << 16;                            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                            // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::tf32, fp32 accumulate, A and B K-major, M=128, N=bn.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int bn) {
+  return (1u << 4)                    // D format: f32
+         | (2u << 7)                  // A format: tf32
+         | (2u << 10)                 // B format: tf32
+         | ((uint32_t)(bn >> 3) << 17)  // N >> 3
+         | ((uint32_t)(kBM >> 4) << 24);  // M >> 4
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// ---------------------------------------------------------------- pack
+struct PackDesc {
+  const float* src;
+  const int64_t* batch_off;  // element offset of each batch matrix (device array)
+  int64_t sr, sk;            // element strides along rows and along k
+  int rows, k;               // logical extent
+  int kt, rt_pad;            // k tiles, row tiles (padded)
+};
+
+// grid (kt, rt_pad, batches); 256 threads. Writes one 128x32 hi tile and one lo tile.
+__global__ void __launch_bounds__(256) k_pack(PackDesc d, float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[kBM][kBK + 1];
+  int kt = blockIdx.x, rt = blockIdx.y, b = blockIdx.z;
+  int tid = threadIdx.x;
+  const float* src = d.src + d.batch_off[b];
+  int r0 = rt * kBM, k0 = kt * kBK;
+  if (d.sk == 1) {
+    for (int idx = tid; idx < kBM * kBK; idx += 256) {
+      int r = idx >> 5, k = idx & 31;
+      int gr = r0 + r, gk = k0 + k;
+      tile[r][k] = (gr < d.rows && gk < d.k) ? src[(int64_t)gr * d.sr + gk] : 0.0f;
+    }
+  } else {
+    for (int idx = tid; idx < kBM * kBK; idx += 256) {
+      int r = idx & (kBM - 1), k = idx >> 7;
+      int gr = r0 + r, gk = k0 + k;
+      tile[r][k] = (gr < d.rows && gk < d.k) ? src[(int64_t)gr * d.sr + (int64_t)gk * d.sk] : 0.0f;
+    }
+  }
+  __syncthreads();
+  size_t base = ((size_t)(b * d.kt + kt) * d.rt_pad + rt) * kTileFloats;
+  float4* h4 = reinterpret_cast<float4*>(hi + base);
+  float4* l4 = reinterpret_cast<float4*>(lo + base);
+  for (int ch = tid; ch < kBM * 8; ch += 256) {
+    int r = ch >> 3, c = ch & 7;
+    float v[4], vh[4], vl[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      v[j] = tile[r][c * 4 + j];
+      uint32_t h = to_tf32(v[j]);
+      vh[j] = __uint_as_float(h);
+      vl[j] = __uint_as_float(to_tf32(v[j] - vh[j]));
+    }
+    int phys = r * 8 + (c ^ (r & 7));  // SWIZZLE_128B: 16-byte chunk index XOR row within the 8-row group
+    h4[phys] = make_float4(vh[0], vh[1], vh[2], vh[3]);
+    l4[phys] = make_float4(vl[0], vl[1], vl[2], vl[3]);
+  }
+}
+
+// ---------------------------------------------------------------- tcgen05 GEMM
+struct GemmArgs {
+  const float* a_hi; const float* a_lo;  // packed A: [batch_a][kt][mt][tile]
+  const float* b_hi; const float* b_lo;  // packed B: [batch_b][kt][nt_pad][tile]
+  const int32_t* a_index;                // output batch -> A batch
+  const int32_t* b_index;                // output batch -> B batch
+  float* c;                              // [batch][m][n] (or split partials [split][batch][m][n])
+  int m, n, kt;                          // rows, cols, k tiles
+  int mt, nt_pad;                        // A row tiles, B row tiles (padded)
+  int tiles_m, tiles_n, batches, splits;
+  int kt_per_split;
+  int* error_flag;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kA = kBM * kBK * 4;          // 16 KiB
+  static constexpr int kB = BN * kBK * 4;           // BN/128 tiles
+  static constexpr int kStage = 2 * kA + 2 * kB;
+  static constexpr int kBytes = STAGES * kStage + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1) k_gemm_tc(GemmArgs g) {
+  using S = GemmSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStage);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_full = empty_bar + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+    for (int a = 0; a < 2; a++) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], 4); }
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(2 * BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_per_split = g.tiles_m * g.tiles_n * g.batches;
+  const int total = tiles_per_split * g.splits;
+  constexpr uint32_t kStageBytes = (uint32_t)S::kStage;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
+        int split = t / tiles_per_split, rem = t % tiles_per_split;
+        int bt = rem / (g.tiles_m * g.tiles_n);
+        int r2 = rem % (g.tiles_m * g.tiles_n);
+        int nb = r2 / g.tiles_m, mb = r2 % g.tiles_m;  // m fastest: concurrent CTAs share the B tile
+        int ba = g.a_index[bt], bb = g.b_index[bt];
+        int k0 = split * g.kt_per_split;
+        int k1 = min(g.kt, k0 + g.kt_per_split);
+        for (int kb = k0; kb < k1; kb++) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { atomicExch(g.error_flag, 1); s_abort = 1; break; }
+          uint8_t* st = smem + stage * S::kStage;
+          mbar_expect_tx(&full_bar[stage], kStageBytes);
+          size_t aoff = ((size_t)(ba * g.kt + kb) * g.mt + mb) * kTileFloats;
+          size_t boff = ((size_t)(bb * g.kt + kb) * g.nt_pad + (size_t)nb * (BN / kBM)) * kTileFloats;
+          bulk_g2s(st, g.a_hi + aoff, S::kA, &full_bar[stage]);
+          bulk_g2s(st + S::kA, g.a_lo + aoff, S::kA, &full_bar[stage]);
+          bulk_g2s(st + 2 * S::kA, g.b_hi + boff, S::kB, &full_bar[stage]);
+          bulk_g2s(st + 2 * S::kA + S::kB, g.b_lo + boff, S::kB, &full_bar[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: every stage issued must have landed (and been consumed) before the CTA may exit.
+      for (int s = 0; s < STAGES; s++) {
+        mbar_wait(&empty_bar[stage], phase ^ 1);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_tf32(BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x, local++) {
+        int split = t / tiles_per_split;
+        int k0 = split * g.kt_per_split;
+        int k1 = min(g.kt, k0 + g.kt_per_split);
+        int acc = local & 1;
+        uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) { atomicExch(g.error_flag, 2); s_abort = 1; break; }
+        tc_fence_after();
+        uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = k0; kb < k1; kb++) {
+          if (!mbar_wait(&full_bar[stage], phase)) { atomicExch(g.error_flag, 3); s_abort = 1; break; }
+          tc_fence_after();
+          uint8_t* st = smem + stage * S::kStage;
+          uint32_t a_hi = smem_u32(st), a_lo = a_hi + S::kA, b_hi = a_hi + 2 * S::kA, b_lo = b_hi + S::kB;
+#pragma unroll
+          for (int ks = 0; ks < kBK / 8; ks++) {
+            uint32_t koff = ks * 32;  // 8 tf32 = 32 bytes along K inside the 128-byte swizzle row
+            uint32_t accum = (kb > k0 || ks > 0) ? 1u : 0u;
+            umma_tf32(d_tmem, umma_desc_sw128(a_lo + koff), umma_desc_sw128(b_hi + koff), idesc, accum);
+            umma_tf32(d_tmem, umma_desc_sw128(a_hi + koff), umma_desc_sw128(b_lo + koff), idesc, 1u);
+            umma_tf32(d_tmem, umma_desc_sw128(a_hi + koff), umma_desc_sw128(b_hi + koff), idesc, 1u);
+          }
+          umma_commit(&empty_bar[stage]);  // frees the stage once these MMAs have read it
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        umma_commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
+      int split = t / tiles_per_split, rem = t % tiles_per_split;
+      int bt = rem / (g.tiles_m * g.tiles_n);
+      int r2 = rem % (g.tiles_m * g.tiles_n);
+      int nb = r2 / g.tiles_m, mb = r2 % g.tiles_m;
+      int acc = local & 1;
+      uint32_t acc_phase = (local >> 1) & 1;
+      bool ok = mbar_wait(&acc_full[acc], acc_phase);
+      if (!ok) { atomicExch(g.error_flag, 4); s_abort = 1; break; }
+      tc_fence_after();
+      int row = mb * kBM + row_in_tile;
+      float* crow = g.c + ((size_t)split * g.batches + bt) * (size_t)g.m * g.n + (size_t)row * g.n;
+      bool vec_ok = (g.n & 3) == 0;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; cc++) {
+        float v[32];
+        uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + cc * 32);
+        tmem_ld32(taddr, v);
+        int col0 = nb * BN + cc * 32;
+        if (row < g.m) {
+          if (vec_ok && col0 + 32 <= g.n) {
+            float4* dst = reinterpret_cast<float4*>(crow + col0);
+#pragma unroll
+            for (int j = 0; j < 8; j++) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (col0 + j < g.n) crow[col0 + j] = v[j];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
+  }
+}
+
+// Deterministic split-K reduction: c[i] = Σ_s part[s][i] in split order.
+__global__ void k_splitk_reduce(const float* __restrict__ part, float* __restrict__ c, int64_t n, int splits) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = part[i];
+    for (int s = 1; s < splits; s++) acc += part[(int64_t)s * n + i];
+    c[i] = acc;
+  }
+}
+
+// ---------------------------------------------------------------- SIMT reference GEMM (exact fp32 FMA)
+struct SimtArgs {
+  const float* a; const float* b; float* c;
+  const int64_t* a_off; const int64_t* b_off;  // per output batch
+  int64_t sam, sak, sbn, sbk;
+  int m, n, k;
+};
+
+__global__ void __launch_bounds__(256) k_gemm_simt(SimtArgs g) {
+  __shared__ float As[16][64 + 1];
+  __shared__ float Bs[16][64 + 1];
+  int bt = blockIdx.z;
+  const float* a = g.a + g.a_off[bt];
+  const float* b = g.b + g.b_off[bt];
+  int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < g.k; k0 += 16) {
+    for (int idx = threadIdx.x; idx < 16 * 64; idx += 256) {
+      int kk = idx / 64, mm = idx % 64;
+      int gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < g.m && gk < g.k) ? a[gm * g.sam + gk * g.sak] : 0.0f;
+      int gn = n0 + mm;
+      Bs[kk][mm] = (gn < g.n && gk < g.k) ? b[gn * g.sbn + gk * g.sbk] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; kk++) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) { av[i] = As[kk][ty * 4 + i]; bv[i] = Bs[kk][tx * 4 + i]; }
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  float* c = g.c + (size_t)bt * g.m * g.n;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      int gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + j;
+      if (gm < g.m && gn < g.n) c[(size_t)gm * g.n + gn] = acc[i][j];
+    }
+}
+
+// ---------------------------------------------------------------- host side
+static int gemm_mode() {
+  static int mode = [] {
+    const char* e = getenv("PAI_GEMM");
+    return (e && strcmp(e, "simt") == 0) ? 1 : 0;
+  }();
+  return mode;
+}
+
+template <int BN, int STAGES>
+static pai_status launch_tc(pai_ctx* ctx, GemmArgs& g) {
+  using S = GemmSmem<BN, STAGES>;
+  static bool attr_set = false;  // per process; every device gets the same attribute
+  if (!attr_set) {
+    PAI_CUDA(cudaFuncSetAttribute(k_gemm_tc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
+    attr_set = true;
+  }
+  int total = g.tiles_m * g.tiles_n * g.batches * g.splits;
+  int grid = total < ctx->sm_count ? total : ctx->sm_count;
+  k_gemm_tc<BN, STAGES><<<grid, 192, S::kBytes, ctx->stream>>>(g);
+  PAI_LAUNCH_CHECK("tcgen05 gemm");
+  return PAI_OK;
+}
+
+// Packs one operand (batched 2-D view) into hi/lo tiles.
+static pai_status pack_operand(pai_ctx* ctx, const float* base, const std::vector<int64_t>& boffs, int64_t sr, int64_t sk,
+                               int rows, int k, int rt_pad, Scratch* hi, Scratch* lo) {
+  int kt = (k + kBK - 1) / kBK;
+  size_t floats = (size_t)boffs.size() * kt * rt_pad * kTileFloats;
+  PAI_TRY(scratch(ctx, floats * 4, hi));
+  PAI_TRY(scratch(ctx, floats * 4, lo));
+  Scratch doff;
+  PAI_TRY(upload(ctx, boffs.data(), boffs.size() * 8, &doff));
+  PackDesc d{base, static_cast<const int64_t*>(doff.p), sr, sk, rows, k, kt, rt_pad};
+  dim3 grid((unsigned)kt, (unsigned)rt_pad, (unsigned)boffs.size());
+  k_pack<<<grid, 256, 0, ctx->stream>>>(d, static_cast<float*>(hi->p), static_cast<float*>(lo->p));
+  PAI_LAUNCH_CHECK("gemm pack");
+  return PAI_OK;
+}
+
+}  // namespace pai
+
+using namespace pai;
+
+PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tensor* b, int32_t tb, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, a, "a"));
+  PAI_TRY(check_view(ctx, b, "b"));
+  int ra = a->rank, rb = b->rank;
+  if (ra < 2 || rb < 2)
+    return set_error(PAI_ERR_ARGUMENT, "MatMul requires rank >= 2 operands; got %s and %s.", shape_str(*a).c_str(),
+                     shape_str(*b).c_str());
+  int m = a->dims[ra - 2], k = a->dims[ra - 1];
+  int kb = tb ? b->dims[rb - 1] : b->dims[rb - 2];
+  int n = tb ? b->dims[rb - 2] : b->dims[rb - 1];
+  if (k != kb)
+    return set_error(PAI_ERR_ARGUMENT, "MatMul inner dimensions disagree: %s x %s (transposeB=%s).", shape_str(*a).c_str(),
+                     shape_str(*b).c_str(), tb ? "True" : "False");
+  pai_tensor abt{}, bbt{};
+  abt.rank = ra - 2;
+  bbt.rank = rb - 2;
+  for (int i = 0; i < abt.rank; i++) abt.dims[i] = a->dims[i];
+  for (int i = 0; i < bbt.rank; i++) bbt.dims[i] = b->dims[i];
+  int brank;
+  int32_t bdims[PAI_MAX_RANK];
+  if (!broadcast_shape(abt, bbt, &brank, bdims) || brank + 2 > PAI_MAX_RANK)
+    return set_error(PAI_ERR_ARGUMENT, "Shapes %s and %s are not broadcast-compatible.", shape_str(abt).c_str(),
+                     shape_str(bbt).c_str());
+  int32_t od[PAI_MAX_RANK];
+  for (int i = 0; i < brank; i++) od[i] = bdims[i];
+  od[brank] = m;
+  od[brank + 1] = n;
+  pai_tensor r;
+  PAI_TRY(alloc_tensor(ctx, brank + 2, od, a->dtype, false, &r));
+  int64_t batch = 1;
+  for (int i = 0; i < brank; i++) batch *= bdims[i];
+  if (batch == 0 || m == 0 || n == 0) { *out = r; return PAI_OK; }
+  if (k == 0) {
+    PAI_CUDA(cudaMemsetAsync(r.base, 0, (size_t)numel(r) * 4, ctx->stream));
+    *out = r;
+    return PAI_OK;
+  }
+
+  // Per output batch: the element offset of the A and B matrices (size-1 batch dims repeat, CpuComputeBackend.cs:222-233),
+  // and the index of the distinct A / B batch matrices so each is packed once.
+  std::vector<int64_t> a_off((size_t)batch), b_off((size_t)batch);
+  std::vector<int32_t> a_idx((size_t)batch), b_idx((size_t)batch);
+  std::vector<int64_t> a_distinct, b_distinct;
+  {
+    int64_t na = 1, nb = 1;
+    for (int i = 0; i < abt.rank; i++) na *= abt.dims[i];
+    for (int i = 0; i < bbt.rank; i++) nb *= bbt.dims[i];
+    a_distinct.resize((size_t)na);
+    b_distinct.resize((size_t)nb);
+    // offsets of the distinct batch matrices, row-major over each operand's own batch dims
+    for (int64_t i = 0; i < na; i++) {
+      int64_t rem = i, off = a->offset;
+      for (int d = abt.rank - 1; d >= 0; d--) { off += (rem % abt.dims[d]) * a->strides[d]; rem /= abt.dims[d]; }
+      a_distinct[(size_t)i] = off;
+    }
+    for (int64_t i = 0; i < nb; i++) {
+      int64_t rem = i, off = b->offset;
+      for (int d = bbt.rank - 1; d >= 0; d--) { off += (rem % bbt.dims[d]) * b->strides[d]; rem /= bbt.dims[d]; }
+      b_distinct[(size_t)i] = off;
+    }
+    std::vector<int> counter((size_t)brank, 0);
+    for (int64_t bi = 0; bi < batch; bi++) {
+      int64_t ia = 0, ib = 0;
+      int la = brank - abt.rank, lb = brank - bbt.rank;
+      for (int i = 0; i < abt.rank; i++) ia = ia * abt.dims[i] + (abt.dims[i] == 1 ? 0 : counter[(size_t)(la + i)]);
+      for (int i = 0; i < bbt.rank; i++) ib = ib * bbt.dims[i] + (bbt.dims[i] == 1 ? 0 : counter[(size_t)(lb + i)]);
+      a_idx[(size_t)bi] = (int32_t)ia;
+      b_idx[(size_t)bi] = (int32_t)ib;
+      a_off[(size_t)bi] = a_distinct[(size_t)ia];
+      b_off[(size_t)bi] = b_distinct[(size_t)ib];
+      for (int ax = brank - 1; ax >= 0; ax--) {
+        if (++counter[(size_t)ax] < bdims[ax]) break;
+        counter[(size_t)ax] = 0;
+      }
+    }
+  }
+  int64_t sam = a->strides[ra - 2], sak = a->strides[ra - 1];
+  int64_t sbn = tb ? b->strides[rb - 2] : b->strides[rb - 1];
+  int64_t sbk = tb ? b->strides[rb - 1] : b->strides[rb - 2];
+  const float* abase = static_cast<const float*>(a->base);
+  const float* bbase = static_cast<const float*>(b->base);
+
+  if (gemm_mode() == 1) {
+    Scratch dao, dbo;
+    PAI_TRY(upload(ctx, a_off.data(), a_off.size() * 8, &dao));
+    PAI_TRY(upload(ctx, b_off.data(), b_off.size() * 8, &dbo));
+    SimtArgs s{abase, bbase, fptr(r), static_cast<int64_t*>(dao.p), static_cast<int64_t*>(dbo.p), sam, sak, sbn, sbk, m, n, k};
+    dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
+    k_gemm_simt<<<grid, 256, 0, ctx->stream>>>(s);
+    PAI_LAUNCH_CHECK("simt gemm");
+    *out = r;
+    return PAI_OK;
+  }
+
+  constexpr int BN = 256, STAGES = 2;
+  int kt = (k + kBK - 1) / kBK;
+  int mt = (m + kBM - 1) / kBM;
+  int tiles_n = (n + BN - 1) / BN;
+  int nt_pad = tiles_n * (BN / kBM);
+  Scratch ahi, alo, bhi, blo, dai, dbi, part;
+  PAI_TRY(pack_operand(ctx, abase, a_distinct, sam, sak, m, k, mt, &ahi, &alo));
+  PAI_TRY(pack_operand(ctx, bbase, b_distinct, sbn, sbk, n, k, nt_pad, &bhi, &blo));
+  PAI_TRY(upload(ctx, a_idx.data(), a_idx.size() * 4, &dai));
+  PAI_TRY(upload(ctx, b_idx.data(), b_idx.size() * 4, &dbi));
+
+  int tiles = mt * tiles_n * (int)batch;
+  int splits = 1;
+  if (tiles * 2 <= ctx->sm_count && kt >= 16) {
+    splits = ctx->sm_count / tiles;
+    if (splits > kt / 8) splits = kt / 8;
+    if (splits < 1) splits = 1;
+  }
+  int kt_per_split = (kt + splits - 1) / splits;
+  splits = (kt + kt_per_split - 1) / kt_per_split;
+  float* cdst = fptr(r);
+  if (splits > 1) {
+    PAI_TRY(scratch(ctx, (size_t)splits * numel(r) * 4, &part));
+    cdst = static_cast<float*>(part.p);
+  }
+  GemmArgs g{};
+  g.a_hi = static_cast<float*>(ahi.p); g.a_lo = static_cast<float*>(alo.p);
+  g.b_hi = static_cast<float*>(bhi.p); g.b_lo = static_cast<float*>(blo.p);
+  g.a_index = static_cast<int32_t*>(dai.p); g.b_index = static_cast<int32_t*>(dbi.p);
+  g.c = cdst; g.m = m; g.n = n; g.kt = kt; g.mt = mt; g.nt_pad = nt_pad;
+  g.tiles_m = mt; g.tiles_n = tiles_n; g.batches = (int)batch; g.splits = splits; g.kt_per_split = kt_per_split;
+  g.error_flag = ctx->d_error_flag;
+  PAI_TRY((launch_tc<BN, STAGES>(ctx, g)));
+  if (splits > 1) {
+    int64_t nn = numel(r);
+    k_splitk_reduce<<<grid_for(ctx, nn, 256), 256, 0, ctx->stream>>>(cdst, fptr(r), nn, splits);
+    PAI_LAUNCH_CHECK("splitk reduce");
+  }
+  *out = r;
+  return PAI_OK;
+}
+
+// Reads and clears the device error flag that bounded waits in the kernels report into.
+PAI_API pai_status pai_check_device_error(pai_ctx* ctx, int32_t* code) {
+  PAI_TRY(enter(ctx));
+  int v = 0;
+  PAI_CUDA(cudaMemcpyAsync(&v, ctx->d_error_flag, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  PAI_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (v) PAI_CUDA(cudaMemsetAsync(ctx->d_error_flag, 0, 4, ctx->stream));
+  if (code) *code = v;
+  if (v) return set_error(PAI_ERR_TIMEOUT, "a kernel wait timed out (site %d); results of the affected launch are invalid", v);
+  return PAI_OK;
+}

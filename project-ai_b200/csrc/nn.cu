@@ -1,0 +1,277 @@
+// RMSNorm, rotary embedding and the SwiGLU gate: HBM-streaming row kernels.
+// Forward semantics: CpuComputeBackend.cs:361-382 (RmsNorm), :397-420 (RotaryEmbedding), :385-391 (Silu).
+// Fused backward rules restate Autograd.cs:223-244 (RmsNorm) and :208-217 with the Mul rule (:39-47) for SwiGLU.
+#include "common.cuh"
+
+namespace pai {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float sigmoid_dev(float v) {
+  if (v >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+  float t = expf(v);
+  return __fdiv_rn(t, __fadd_rn(1.0f, t));
+}
+
+// ---------------------------------------------------------------- RMSNorm forward: one warp per row.
+__global__ void k_rmsnorm_fwd(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
+                              int64_t rows, int d, float eps) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    const float* p = x + r * d;
+    float ss = 0.0f;
+    for (int j = lane; j < d; j += 32) { float v = p[j]; ss = fmaf(v, v, ss); }
+    ss = warp_sum(ss);
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps)));
+    float* q = y + r * d;
+    for (int j = lane; j < d; j += 32) q[j] = __fmul_rn(__fmul_rn(p[j], inv), w[j]);
+  }
+}
+
+// ---------------------------------------------------------------- RMSNorm backward.
+// dx = inv·(g⊙w) − (inv²/D)·x·Σ(g⊙y);  dw partial per block = Σ_rows g⊙x·inv, reduced by k_colsum.
+__global__ void k_rmsnorm_bwd(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ g,
+                              float* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int d, float eps,
+                              int rows_per_block) {
+  extern __shared__ float s_dw[];  // [warps][d]
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float* my_dw = s_dw + (size_t)wid * d;
+  for (int j = lane; j < d; j += 32) my_dw[j] = 0.0f;
+  int64_t r0 = (int64_t)blockIdx.x * rows_per_block;
+  int64_t r1 = r0 + rows_per_block < rows ? r0 + rows_per_block : rows;
+  for (int64_t r = r0 + wid; r < r1; r += nw) {
+    const float* px = x + r * d;
+    const float* pg = g + r * d;
+    float ss = 0.0f;
+    for (int j = lane; j < d; j += 32) { float v = px[j]; ss = fmaf(v, v, ss); }
+    ss = warp_sum(ss);
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps)));
+    float dot = 0.0f;
+    for (int j = lane; j < d; j += 32) dot = fmaf(pg[j], px[j] * inv * w[j], dot);
+    dot = warp_sum(dot);
+    float coef = inv * inv / (float)d;
+    float* pdx = dx + r * d;
+    for (int j = lane; j < d; j += 32) {
+      float gv = pg[j], xv = px[j];
+      pdx[j] = (gv * w[j]) * inv - (coef * xv) * dot;
+      my_dw[j] += gv * (xv * inv);
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    float acc = 0.0f;
+    for (int k = 0; k < nw; k++) acc += s_dw[(size_t)k * d + j];
+    dw_part[(size_t)blockIdx.x * d + j] = acc;
+  }
+}
+
+// Deterministic column sum of [parts, d] partials.
+__global__ void k_colsum(const float* __restrict__ part, float* __restrict__ out, int parts, int d) {
+  int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= d) return;
+  float acc = 0.0f;
+  for (int p = 0; p < parts; p++) acc += part[(size_t)p * d + j];
+  out[j] = acc;
+}
+
+// ---------------------------------------------------------------- RoPE (rotate-half), generic views.
+__global__ void k_rotary(const float* __restrict__ x, DView xv, const float* __restrict__ cs, DView cv,
+                         const float* __restrict__ sn, DView sv, float* __restrict__ y, int64_t pairs, int d) {
+  int half = d >> 1;
+  for (int64_t id = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; id < pairs; id += (int64_t)gridDim.x * blockDim.x) {
+    int64_t row = id / half;
+    int j = (int)(id - row * half);
+    int64_t i0 = row * d + j, i1 = i0 + half;
+    float x0 = x[dview_offset(xv, i0)], x1 = x[dview_offset(xv, i1)];
+    float c0 = cs[dview_offset(cv, i0)], c1 = cs[dview_offset(cv, i1)];
+    float s0 = sn[dview_offset(sv, i0)], s1 = sn[dview_offset(sv, i1)];
+    // y[i] = x[i]·cos[i] + rot[i]·sin[i], rot = (−x[i+half], x[i−half])
+    y[i0] = __fadd_rn(__fmul_rn(x0, c0), __fmul_rn(-x1, s0));
+    y[i1] = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1));
+  }
+}
+
+// ---------------------------------------------------------------- SwiGLU gate
+__global__ void k_silu_mul_fwd(const float* __restrict__ gate, const float* __restrict__ up, float* __restrict__ o,
+                               int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float gv = gate[i];
+    float y = __fmul_rn(gv, sigmoid_dev(gv));
+    o[i] = __fmul_rn(y, up[i]);
+  }
+}
+
+__global__ void k_silu_mul_bwd(const float* __restrict__ gate, const float* __restrict__ up, const float* __restrict__ g,
+                               float* __restrict__ dgate, float* __restrict__ dup, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float gv = gate[i], u = up[i], go = g[i];
+    float s = sigmoid_dev(gv);
+    float y = __fmul_rn(gv, s);
+    float dsilu = __fmul_rn(go, u);                                   // Mul rule: d(silu) = g·up
+    dup[i] = __fmul_rn(go, y);                                         //           d(up)   = g·silu
+    float deriv = __fsub_rn(__fadd_rn(s, y), __fmul_rn(s, y));          // Silu rule: s + y − s·y
+    dgate[i] = __fmul_rn(dsilu, deriv);
+  }
+}
+
+}  // namespace pai
+
+using namespace pai;
+
+PAI_API pai_status pai_rmsnorm(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* w, float eps, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, x, "x"));
+  PAI_TRY(check_view(ctx, w, "weight"));
+  if (x->rank == 0) return set_error(PAI_ERR_ARGUMENT, "RmsNorm requires rank >= 1.");
+  int d = x->dims[x->rank - 1];
+  if (w->rank != 1 || w->dims[0] != d)
+    return set_error(PAI_ERR_ARGUMENT, "RmsNorm weight must be [%d] to match the last axis of %s.", d, shape_str(*x).c_str());
+  pai_tensor r;
+  PAI_TRY(alloc_tensor(ctx, x->rank, x->dims, x->dtype, false, &r));
+  int64_t rows = d ? numel(*x) / d : 0;
+  if (rows > 0) {
+    const float *xp, *wp;
+    Scratch hx, hw;
+    PAI_TRY(dense_input(ctx, *x, &xp, &hx));
+    PAI_TRY(dense_input(ctx, *w, &wp, &hw));
+    k_rmsnorm_fwd<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(xp, wp, fptr(r), rows, d, eps);
+    PAI_LAUNCH_CHECK("rmsnorm");
+  }
+  *out = r;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* w, const pai_tensor* g, float eps,
+                                   pai_tensor* dx, pai_tensor* dw) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, x, "x"));
+  PAI_TRY(check_view(ctx, w, "weight"));
+  PAI_TRY(check_view(ctx, g, "grad"));
+  if (x->rank == 0) return set_error(PAI_ERR_ARGUMENT, "RmsNorm requires rank >= 1.");
+  int d = x->dims[x->rank - 1];
+  if (w->rank != 1 || w->dims[0] != d || numel(*g) != numel(*x))
+    return set_error(PAI_ERR_ARGUMENT, "RmsNormBackward: shapes disagree (%s, %s, %s)", shape_str(*x).c_str(),
+                     shape_str(*w).c_str(), shape_str(*g).c_str());
+  pai_tensor rdx, rdw;
+  PAI_TRY(alloc_tensor(ctx, x->rank, x->dims, x->dtype, false, &rdx));
+  PAI_TRY(alloc_tensor(ctx, 1, &d, x->dtype, true, &rdw));
+  int64_t rows = d ? numel(*x) / d : 0;
+  if (rows > 0) {
+    const float *xp, *wp, *gp;
+    Scratch hx, hw, hg, part;
+    PAI_TRY(dense_input(ctx, *x, &xp, &hx));
+    PAI_TRY(dense_input(ctx, *w, &wp, &hw));
+    PAI_TRY(dense_input(ctx, *g, &gp, &hg));
+    int threads = 256, nw = threads / 32;
+    size_t smem = (size_t)nw * d * 4;
+    if (smem > 200 * 1024) { threads = 64; nw = 2; smem = (size_t)nw * d * 4; }
+    if (smem > 200 * 1024) return set_error(PAI_ERR_UNSUPPORTED, "RmsNormBackward: row length %d too large", d);
+    int blocks = ctx->sm_count * 2;
+    int rpb = (int)((rows + blocks - 1) / blocks);
+    if (rpb < nw) rpb = nw;
+    blocks = (int)((rows + rpb - 1) / rpb);
+    PAI_TRY(scratch(ctx, (size_t)blocks * d * 4, &part));
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k_rmsnorm_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_rmsnorm_bwd<<<blocks, threads, smem, ctx->stream>>>(xp, wp, gp, fptr(rdx), static_cast<float*>(part.p), rows, d, eps, rpb);
+    PAI_LAUNCH_CHECK("rmsnorm_bwd");
+    k_colsum<<<(d + 255) / 256, 256, 0, ctx->stream>>>(static_cast<float*>(part.p), fptr(rdw), blocks, d);
+    PAI_LAUNCH_CHECK("rmsnorm_bwd colsum");
+  }
+  *dx = rdx;
+  *dw = rdw;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_rotary(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* cs, const pai_tensor* sn, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, x, "x"));
+  PAI_TRY(check_view(ctx, cs, "cos"));
+  PAI_TRY(check_view(ctx, sn, "sin"));
+  int rank = x->rank;
+  if (rank == 0) return set_error(PAI_ERR_ARGUMENT, "RotaryEmbedding requires rank >= 1.");
+  int d = x->dims[rank - 1];
+  if (d % 2) return set_error(PAI_ERR_ARGUMENT, "RoPE head dim must be even; got %d.", d);
+  auto ok = [&](const pai_tensor* t) {
+    if (t->rank > rank) return false;
+    int lead = rank - t->rank;
+    for (int i = 0; i < t->rank; i++)
+      if (t->dims[i] != x->dims[lead + i] && t->dims[i] != 1) return false;
+    return true;
+  };
+  if (!ok(cs) || !ok(sn)) return set_error(PAI_ERR_ARGUMENT, "Cannot broadcast cos/sin to %s.", shape_str(*x).c_str());
+  pai_tensor r;
+  PAI_TRY(alloc_tensor(ctx, rank, x->dims, x->dtype, false, &r));
+  int64_t n = numel(*x);
+  if (n > 0) {
+    pai_tensor cb = broadcast_view(*cs, rank, x->dims), sb = broadcast_view(*sn, rank, x->dims);
+    const pai_tensor* views[3] = {x, &cb, &sb};
+    DView dv[3];
+    collapse(rank, x->dims, views, 3, dv);
+    int64_t pairs = n / 2;
+    k_rotary<<<grid_for(ctx, pairs, 256), 256, 0, ctx->stream>>>(static_cast<const float*>(x->base), dv[0],
+                                                               static_cast<const float*>(cs->base), dv[1],
+                                                               static_cast<const float*>(sn->base), dv[2], fptr(r), pairs, d);
+    PAI_LAUNCH_CHECK("rotary");
+  }
+  *out = r;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_silu_mul_fwd(pai_ctx* ctx, const pai_tensor* gate, const pai_tensor* up, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, gate, "gate"));
+  PAI_TRY(check_view(ctx, up, "up"));
+  if (gate->rank != up->rank || numel(*gate) != numel(*up))
+    return set_error(PAI_ERR_ARGUMENT, "SiluMul: shapes differ (%s vs %s)", shape_str(*gate).c_str(), shape_str(*up).c_str());
+  for (int i = 0; i < gate->rank; i++)
+    if (gate->dims[i] != up->dims[i]) return set_error(PAI_ERR_ARGUMENT, "SiluMul: shapes differ");
+  pai_tensor r;
+  PAI_TRY(alloc_tensor(ctx, gate->rank, gate->dims, gate->dtype, false, &r));
+  int64_t n = numel(r);
+  if (n > 0) {
+    const float *gp, *up_;
+    Scratch h1, h2;
+    PAI_TRY(dense_input(ctx, *gate, &gp, &h1));
+    PAI_TRY(dense_input(ctx, *up, &up_, &h2));
+    k_silu_mul_fwd<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(gp, up_, fptr(r), n);
+    PAI_LAUNCH_CHECK("silu_mul_fwd");
+  }
+  *out = r;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_silu_mul_bwd(pai_ctx* ctx, const pai_tensor* gate, const pai_tensor* up, const pai_tensor* g,
+                                    pai_tensor* dgate, pai_tensor* dup) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, gate, "gate"));
+  PAI_TRY(check_view(ctx, up, "up"));
+  PAI_TRY(check_view(ctx, g, "grad"));
+  int64_t n = numel(*gate);
+  if (numel(*up) != n || numel(*g) != n) return set_error(PAI_ERR_ARGUMENT, "SiluMulBackward: shapes differ");
+  pai_tensor r1, r2;
+  PAI_TRY(alloc_tensor(ctx, gate->rank, gate->dims, gate->dtype, false, &r1));
+  PAI_TRY(alloc_tensor(ctx, gate->rank, gate->dims, gate->dtype, false, &r2));
+  if (n > 0) {
+    const float *gp, *up_, *gg;
+    Scratch h1, h2, h3;
+    PAI_TRY(dense_input(ctx, *gate, &gp, &h1));
+    PAI_TRY(dense_input(ctx, *up, &up_, &h2));
+    PAI_TRY(dense_input(ctx, *g, &gg, &h3));
+    k_silu_mul_bwd<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(gp, up_, gg, fptr(r1), fptr(r2), n);
+    PAI_LAUNCH_CHECK("silu_mul_bwd");
+  }
+  *dgate = r1;
+  *dup = r2;
+  return PAI_OK;
+}
