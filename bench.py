@@ -1,0 +1,349 @@
+"""Training-step benchmark of the B200 backend: train tokens/s (forward + per-block recompute + backward + AdamW).
+
+One step = one pass of the reference trainer's step (ProjectAI.Training/Training.cs:87-113) through the host runtime
+and the C ABI: forward with per-block gradient checkpointing, cross-entropy, backward with recompute, fused AdamW.
+Workload at N=1 (and per GPU at N>1, weak scaling): ~125M Llama-style decoder, fp32 — vocab 32000, d_model 768,
+12 layers, 12 heads (head_dim 64), SwiGLU FFN 2048, RMSNorm, RoPE, tied embeddings, weights N(0, 0.02) from a seed;
+synthetic token ids uniform in [0, 32000) from PcgRng(rank*1000 + step), targets shifted by one; seq 1024 x batch 8.
+
+value  — device-resident batches (uploaded before the timed region), timed with CUDA events on the library's stream.
+e2e    — the same step through the public host-buffer entry (Trainer.step with host arrays: the ids H2D copy and the
+         loss D2H read are inside the timed region).
+roofline — the dominant kernel (the 3xTF32 tcgen05 GEMM): algorithmic 2·M·N·K flops per launch over its average
+         event-timed duration inside the timed region, against the measured TF32 tensor peak / 3.
+cpu_baseline / --impl reference — the CPU oracle (a C++ restatement of the reference CpuComputeBackend) running the
+         same step on a bounded sample of the workload on this machine's host cores.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]; N>1 under torchrun.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+import __graft_entry__  # noqa: E402
+
+pai = __graft_entry__.load_package()
+from projectai_b200 import _paihost as H  # noqa: E402
+
+ORACLE_LIB = ROOT / "oracle" / "build" / "liboracle.so"
+METRIC = "train tokens/s (fwd+recompute+bwd+AdamW)"
+CONFIGS = {
+    "125m": dict(vocab_size=32000, embedding_dim=768, layer_count=12, head_count=12, kv_head_count=12, ffn_hidden=2048,
+                 seq=1024, batch=8),
+    "1b": dict(vocab_size=32000, embedding_dim=2048, layer_count=16, head_count=32, kv_head_count=8, ffn_hidden=5632,
+               seq=2048, batch=4),
+    "tiny": dict(vocab_size=256, embedding_dim=128, layer_count=2, head_count=4, kv_head_count=4, ffn_hidden=344,
+                 seq=64, batch=4),
+}
+
+
+def model_config(c, max_seq):
+    return H.ModelConfig(vocab_size=c["vocab_size"], embedding_dim=c["embedding_dim"], layer_count=c["layer_count"],
+                         head_count=c["head_count"], kv_head_count=c["kv_head_count"], ffn_hidden=c["ffn_hidden"],
+                         max_sequence_length=max_seq)
+
+
+def param_count(c):
+    d, f, v, h, kvh = c["embedding_dim"], c["ffn_hidden"], c["vocab_size"], c["head_count"], c["kv_head_count"]
+    hd = d // h
+    per_block = d * h * hd * 2 + d * kvh * hd * 2 + 3 * d * f + 2 * d
+    return v * d + c["layer_count"] * per_block + d
+
+
+def synthetic_batch(rank, step, batch, seq, vocab):
+    r = H.PcgRng(rank * 1000 + step)
+    ids = np.array([r.next_u32() % vocab for _ in range(batch * (seq + 1))], dtype=np.float32).reshape(batch, seq + 1)
+    return np.ascontiguousarray(ids[:, :seq]), np.ascontiguousarray(ids[:, 1:])
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples taken while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.file:
+            return None
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_tf32_peak(device):
+    """Dense TF32 tensor-core peak measured with cuBLAS on this GPU (8192^3 fp32 GEMM with TF32 allowed, best of 10)."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = True
+    n = 8192
+    a = torch.randn(n, n, device=f"cuda:{device}")
+    b = torch.randn(n, n, device=f"cuda:{device}")
+    for _ in range(3):
+        a @ b
+    best = 1e30
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        a @ b
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    del a, b
+    torch.cuda.empty_cache()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the GEMM kernel from the committed ncu summary, if one exists."""
+    p = ROOT / "profiles" / "gemm_tcgen05_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+def cpu_baseline(cfg_name, sample_tokens, threads):
+    """Times the oracle (CPU restatement of the reference backend) on one step of a bounded sample of the workload."""
+    import ctypes
+    ctypes.CDLL(str(ORACLE_LIB)).oracle_set_threads(threads)
+    c = CONFIGS[cfg_name]
+    seq = min(sample_tokens, c["seq"])
+    be = H.Backend(str(ORACLE_LIB), "oracle_", 0)
+    m = H.LlamaModel(be, model_config(c, seq), seed=0, init="normal0.02")
+    tc = H.TrainingConfig(batch_size=1, sequence_length=seq, learning_rate=3e-4, weight_decay=0.1, max_steps=10,
+                          gradient_checkpointing=True, warmup_steps=0)
+    tr = H.Trainer(be, m, tc, 0.9, 0.95)
+    x, y = synthetic_batch(0, 0, 1, seq, c["vocab_size"])
+    t0 = time.perf_counter()
+    tr.step([x], [y])
+    dt = time.perf_counter() - t0
+    return seq / dt, dt, seq
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # under torchrun only rank 0 times the CPU reference
+    c = CONFIGS[args.config]
+    threads = os.cpu_count() or 1
+    import ctypes
+    ctypes.CDLL(str(ORACLE_LIB)).oracle_set_threads(threads)
+    seq = min(args.cpu_sample_tokens, c["seq"])
+    be = H.Backend(str(ORACLE_LIB), "oracle_", 0)
+    m = H.LlamaModel(be, model_config(c, seq), seed=0, init="normal0.02")
+    tc = H.TrainingConfig(batch_size=1, sequence_length=seq, learning_rate=3e-4, weight_decay=0.1, max_steps=1000,
+                          gradient_checkpointing=True, warmup_steps=0)
+    tr = H.Trainer(be, m, tc, 0.9, 0.95)
+    for w in range(args.warmup):
+        x, y = synthetic_batch(0, w, 1, seq, c["vocab_size"])
+        tr.step([x], [y])
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        x, y = synthetic_batch(0, args.warmup + k, 1, seq, c["vocab_size"])
+        tr.step([x], [y])
+    dt = time.perf_counter() - t0
+    value = seq * args.steps / dt
+    sample = (f"{args.config} model, per-block recompute, batch 1 x seq {seq} per step "
+              f"(the workload is batch {c['batch']} x seq {c['seq']})")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args.config, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(name, n):
+    c = CONFIGS[name]
+    return {"workload": f"llama-{name} train step (fwd + per-block recompute + bwd + AdamW), fp32 semantics",
+            "vocab": c["vocab_size"], "d_model": c["embedding_dim"], "layers": c["layer_count"], "heads": c["head_count"],
+            "kv_heads": c["kv_head_count"], "ffn": c["ffn_hidden"], "seq_len": c["seq"], "batch_per_gpu": c["batch"],
+            "global_batch": c["batch"] * n, "params": param_count(c), "parallelism": f"dp{n}",
+            "l2": "working set above L2 (weights alone 4 B x params), no flush needed"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    ap.add_argument("--config", default="125m", choices=sorted(CONFIGS))
+    ap.add_argument("--no-recompute", action="store_true")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=64)
+    ap.add_argument("--skip-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    c = CONFIGS[args.config]
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", local)
+    if world > 1:
+        uid = [be.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        be.nccl_init(uid[0], rank, world, 120000)
+
+    peak_tf32 = measured_tf32_peak(local) if rank == 0 else None
+    m = H.LlamaModel(be, model_config(c, c["seq"]), seed=0, init="normal0.02")
+    tc = H.TrainingConfig(batch_size=c["batch"], sequence_length=c["seq"], learning_rate=3e-4, weight_decay=0.1,
+                          max_steps=args.warmup + 2 * args.steps + 10, gradient_checkpointing=not args.no_recompute,
+                          warmup_steps=0)
+    tr = H.Trainer(be, m, tc, 0.9, 0.95)
+    tr.set_constant_lr(3e-4)
+
+    def barrier():
+        be.sync()
+        if dist:
+            dist.barrier()
+
+    step = 0
+    for _ in range(args.warmup):
+        x, y = synthetic_batch(rank, step, c["batch"], c["seq"], c["vocab_size"])
+        tr.step([x], [y])
+        step += 1
+
+    # ---- value: device-resident batches
+    batches = []
+    for k in range(args.steps):
+        x, y = synthetic_batch(rank, step + k, c["batch"], c["seq"], c["vocab_size"])
+        batches.append((be.from_host(x), be.from_host(y)))
+    step += args.steps
+    barrier()
+    be.kernel_timing(True)
+    launches0 = be.launch_count()
+    losses = []
+    with ClockSampler(local) as clocks:
+        be.timer_start()
+        for x, y in batches:
+            losses.append(tr.step_tensors([x], [y]))
+        ms = be.timer_stop()
+    launches = be.launch_count() - launches0
+    kstats = {f: be.kernel_stats(f) for f in ("gemm", "attn_fwd", "attn_bwd")}
+    be.kernel_timing(False)
+    be.check_device_error()
+    barrier()
+    del batches
+
+    # ---- e2e: host buffers through the public step
+    host_batches = [synthetic_batch(rank, step + k, c["batch"], c["seq"], c["vocab_size"]) for k in range(args.steps)]
+    barrier()
+    be.timer_start()
+    for x, y in host_batches:
+        losses.append(tr.step([x], [y]))
+    ms_e2e = be.timer_stop()
+    barrier()
+
+    if dist:
+        import torch
+        t = torch.tensor([ms, ms_e2e], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = t.tolist()
+
+    tokens = c["batch"] * c["seq"] * world * args.steps
+    value = tokens / (ms * 1e-3)
+    e2e = tokens / (ms_e2e * 1e-3)
+    if rank == 0:
+        g_launches, g_ms, g_flops = kstats["gemm"]
+        avg_ms = g_ms / max(g_launches, 1)
+        achieved = (g_flops / max(g_launches, 1)) / (avg_ms * 1e-3) / 1e12
+        peak = peak_tf32 / 3.0
+        traffic = ncu_traffic()
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                    "kernel": "k_gemm_tc (3xTF32 tcgen05)",
+                    "peak_source": "measured on this GPU: cuBLAS TF32 GEMM (torch.matmul fp32, allow_tf32, 8192^3, best of 10)"
+                                   f" = {peak_tf32:.1f} TFLOP/s, divided by 3 for 3xTF32",
+                    "launches": g_launches, "avg_launch_ms": avg_ms,
+                    "share_of_step": g_ms / ms}
+        kernels = {f: {"launches": v[0], "ms": v[1], "tflops": (v[2] / (v[1] * 1e-3) / 1e12) if v[1] else None,
+                       "share_of_step": v[1] / ms} for f, v in kstats.items()}
+        step_flops = (kstats["gemm"][2] + kstats["attn_fwd"][2] + kstats["attn_bwd"][2]) / args.steps
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (PcgRng token ids, N(0,0.02) weights)",
+                "config": workload_config(args.config, world), "roofline": roofline,
+                "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * c["batch"] * c["seq"] * 4,
+                        "d2h_bytes_per_step": 4, "ms_per_step": ms_e2e / args.steps},
+                "gpu_launches": launches, "kernels": kernels,
+                "model_tflops_per_s": step_flops * args.steps / (ms * 1e-3) / 1e12,
+                "recompute": not args.no_recompute, "final_loss": losses[-1],
+                "clocks": clocks.summary(), "peak_tf32_tflops": peak_tf32}
+        if world == 1 and not args.skip_cpu_baseline:
+            threads = os.cpu_count() or 1
+            v, dt, seq = cpu_baseline(args.config, args.cpu_sample_tokens, threads)
+            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                    "sample": f"one training step of the {args.config} model at batch 1 x seq {seq} "
+                                              f"({dt:.1f} s) on the CPU oracle"}
+        print(json.dumps(line), flush=True)
+    del tr, m
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -184,6 +184,19 @@ pai_status pai_allreduce_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t
 pai_status pai_allreduce_wait(pai_ctx* ctx);
 pai_status pai_nccl_abort(pai_ctx* ctx);
 
+/* ==== Diagnostics (no counterpart in the reference; used by the benchmark and tests) ==== */
+/* Reads and clears the device flag that bounded waits inside kernels set on a timeout (PAI_ERR_TIMEOUT if set). */
+pai_status pai_check_device_error(pai_ctx* ctx, int32_t* code);
+/* Device time between two points of the compute stream, from CUDA events recorded on that stream. stop blocks. */
+pai_status pai_timer_start(pai_ctx* ctx);
+pai_status pai_timer_stop(pai_ctx* ctx, float* ms);
+/* Number of kernels this context has launched so far. */
+pai_status pai_launch_count(pai_ctx* ctx, int64_t* n);
+/* Per-kernel-family event timing ("gemm" = the tcgen05 GEMM kernel, "attn_fwd", "attn_bwd"). Enabling clears
+ * previous samples. stats returns launches, summed device milliseconds and summed algorithmic work (flops). */
+pai_status pai_kernel_timing(pai_ctx* ctx, int32_t enable);
+pai_status pai_kernel_stats(pai_ctx* ctx, const char* family, int64_t* launches, double* total_ms, double* work);
+
 #ifdef __cplusplus
 }
 #endif

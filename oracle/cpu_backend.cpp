@@ -143,12 +143,40 @@ void for_each_offset(const pai_tensor& t, F&& f) {
   }
 }
 
+bool is_dense(const pai_tensor& t) {
+  int64_t acc = 1;
+  for (int i = t.rank - 1; i >= 0; i--) {
+    if (t.dims[i] == 1) continue;
+    if (t.strides[i] != acc) return false;
+    acc *= t.dims[i];
+  }
+  return true;
+}
+
+// A view's logical elements as a dense row-major array: the storage itself when the view is already dense, else a
+// gathered copy.
+struct Dense {
+  std::vector<float> own;
+  const float* p = nullptr;
+  size_t n = 0;
+  float operator[](size_t i) const { return p[i]; }
+  size_t size() const { return n; }
+  const float* data() const { return p; }
+};
+
 // CpuComputeBackend.Materialize (CpuComputeBackend.cs:27-39): the view's logical elements, dense row-major.
-std::vector<float> materialize(const pai_tensor& t) {
-  std::vector<float> dst((size_t)numel(t));
+Dense materialize(const pai_tensor& t, bool force_copy = false) {
+  Dense d;
+  d.n = (size_t)numel(t);
   const float* b = buf(t);
-  for_each_offset(t, [&](int64_t i, int64_t off) { dst[(size_t)i] = b[off]; });
-  return dst;
+  if (is_dense(t) && !force_copy) {
+    d.p = b + t.offset;
+    return d;
+  }
+  d.own.resize(d.n);
+  for_each_offset(t, [&](int64_t i, int64_t off) { d.own[(size_t)i] = b[off]; });
+  d.p = d.own.data();
+  return d;
 }
 
 // Shape.TryBroadcastWith (Shape.cs:94-113).
@@ -193,17 +221,15 @@ pai_status elementwise(pai_ctx* c, const pai_tensor* a, const pai_tensor* b, pai
   if (!broadcast_shape(*a, *b, &rank, dims) || rank > PAI_MAX_RANK)
     return fail(PAI_ERR_ARGUMENT, "Shapes %s and %s are not broadcast-compatible.", shape_str(*a).c_str(), shape_str(*b).c_str());
   pai_tensor av = broadcast_to(*a, rank, dims), bv = broadcast_to(*b, rank, dims);
-  std::vector<int64_t> oa, ob;
   pai_tensor r;
   TRY(alloc(c, rank, dims, a->dtype, &r));
   int64_t n = numel(r);
-  oa.resize((size_t)n); ob.resize((size_t)n);
-  for_each_offset(av, [&](int64_t i, int64_t off) { oa[(size_t)i] = off; });
-  for_each_offset(bv, [&](int64_t i, int64_t off) { ob[(size_t)i] = off; });
-  const float* pa = buf(*a); const float* pb = buf(*b); float* po = buf(r);
+  // Both operands as dense arrays of the result's shape (a broadcast operand is gathered through its stride-0 view).
+  Dense da = materialize(av), db = materialize(bv);
+  const float* pa = da.data(); const float* pb = db.data(); float* po = buf(r);
 #pragma omp parallel for num_threads(g_threads) schedule(static) if (n > 65536)
   for (int64_t i = 0; i < n; i++) {
-    float x = pa[oa[(size_t)i]], y = pb[ob[(size_t)i]];
+    float x = pa[i], y = pb[i];
     float z;
     switch (op) {
       case kAdd: z = x + y; break;
@@ -345,7 +371,7 @@ ORC_API pai_status oracle_copy(pai_ctx* c, const pai_tensor* src, const pai_tens
   TRY(check_desc(c, src, "source"));
   TRY(check_desc(c, dst, "destination"));
   if (numel(*src) != numel(*dst)) return fail(PAI_ERR_ARGUMENT, "Copy: element counts differ (%s vs %s)", shape_str(*src).c_str(), shape_str(*dst).c_str());
-  auto s = materialize(*src);
+  auto s = materialize(*src, src->base == dst->base);  // a copy within one storage reads a snapshot
   float* d = buf(*dst);
   for_each_offset(*dst, [&](int64_t i, int64_t off) { d[off] = s[(size_t)i]; });
   return PAI_OK;
@@ -483,15 +509,23 @@ ORC_API pai_status oracle_matmul(pai_ctx* c, const pai_tensor* a, const pai_tens
   for (int64_t row = 0; row < rows; row++) {
     int64_t bi = row / m; int i = (int)(row % m);
     int64_t arow = aoff[(size_t)bi] + (int64_t)i * k, bo = boff[(size_t)bi], oo = bi * m * n;
-    for (int j = 0; j < n; j++) {
-      float acc = 0.0f;
-      if (tb) {
+    float* orow = po + oo + (int64_t)i * n;
+    if (tb) {
+      for (int j = 0; j < n; j++) {
+        float acc = 0.0f;
         int64_t brow = bo + (int64_t)j * k;
         for (int p = 0; p < k; p++) acc += A[(size_t)(arow + p)] * B[(size_t)(brow + p)];
-      } else {
-        for (int p = 0; p < k; p++) acc += A[(size_t)(arow + p)] * B[(size_t)(bo + (int64_t)p * n + j)];
+        orow[j] = acc;
       }
-      po[oo + (int64_t)i * n + j] = acc;
+    } else {
+      // Loop order i, p, j: every output element still accumulates its products in p order starting from 0 (the
+      // reference's order, CpuComputeBackend.cs:205-208), while B is read along its contiguous rows.
+      for (int j = 0; j < n; j++) orow[j] = 0.0f;
+      for (int p = 0; p < k; p++) {
+        float av = A[(size_t)(arow + p)];
+        const float* brow = B.data() + bo + (int64_t)p * n;
+        for (int j = 0; j < n; j++) orow[j] += av * brow[j];
+      }
     }
   }
   *out = r;

@@ -340,6 +340,13 @@ static pai_status attn_dims(const pai_tensor* q, const pai_tensor* k, const pai_
   return PAI_OK;
 }
 
+// Algorithmic flops of the forward: 2 (QKᵀ) + 2 (PV) per visible (query, key) pair and head-dim element.
+static double attn_fwd_flops(const AttnDims& a) {
+  double pairs = 0;
+  for (int i = 0; i < a.S; i++) pairs += a.causal ? (double)std::min(a.L, a.pos_offset + i + 1) : (double)a.L;
+  return 4.0 * a.D * (double)a.B * a.H * pairs;
+}
+
 constexpr size_t kFwdSmem = (size_t)(2 * kMaxD * kP + 2 * kT * kP) * 4;
 constexpr size_t kKvSmem = (size_t)(4 * kMaxD * kP + 4 * kT * kP + 2 * kT) * 4;
 constexpr size_t kQSmem = (size_t)(4 * kMaxD * kP + 2 * kT * kP + 2 * kT) * 4;
@@ -365,6 +372,7 @@ PAI_API pai_status pai_sdpa_fwd(pai_ctx* ctx, const pai_tensor* q, const pai_ten
     static bool attr = false;
     if (!attr) { cudaFuncSetAttribute(k_attn_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFwdSmem); attr = true; }
     dim3 grid((unsigned)((a.S + kT - 1) / kT), (unsigned)a.H, (unsigned)a.B);
+    KernelTimerScope timer(ctx, "attn_fwd", attn_fwd_flops(a));
     k_attn_fwd<<<grid, 256, kFwdSmem, ctx->stream>>>(a, v4(*q), v4(*k), v4(*v), fptr(ro), fptr(rl));
     PAI_LAUNCH_CHECK("sdpa_fwd");
   }
@@ -404,6 +412,7 @@ PAI_API pai_status pai_sdpa_bwd(pai_ctx* ctx, const pai_tensor* q, const pai_ten
     Scratch dvec;
     int64_t rows = (int64_t)a.B * a.H * a.S;
     PAI_TRY(scratch(ctx, (size_t)rows * 4, &dvec));
+    KernelTimerScope timer(ctx, "attn_bwd", 2.5 * attn_fwd_flops(a));
     k_attn_dot<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, ctx->stream>>>(a, v4(*dout), fptr(*out), static_cast<float*>(dvec.p));
     PAI_LAUNCH_CHECK("sdpa_bwd dot");
     dim3 gkv((unsigned)((a.L + kT - 1) / kT), (unsigned)a.KVH, (unsigned)a.B);

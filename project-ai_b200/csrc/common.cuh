@@ -23,7 +23,13 @@ pai_status cuda_error(cudaError_t e, const char* what);
 
 #define PAI_TRY(x) do { pai_status _s = (x); if (_s != PAI_OK) return _s; } while (0)
 #define PAI_CUDA(x) do { cudaError_t _e = (x); if (_e != cudaSuccess) return ::pai::cuda_error(_e, #x); } while (0)
-#define PAI_LAUNCH_CHECK(what) do { cudaError_t _e = cudaGetLastError(); if (_e != cudaSuccess) return ::pai::cuda_error(_e, what); } while (0)
+// Every kernel launch site ends with this: it reports launch errors and counts the launch on the context.
+#define PAI_LAUNCH_CHECK(what)                                          \
+  do {                                                                  \
+    cudaError_t _e = cudaGetLastError();                                \
+    if (_e != cudaSuccess) return ::pai::cuda_error(_e, what);          \
+    ctx->launches++;                                                    \
+  } while (0)
 
 // ---------------------------------------------------------------- context
 struct BlockInfo {
@@ -50,7 +56,28 @@ struct pai_ctx {
   int* d_error_flag = nullptr;
   pai::NcclState* nccl = nullptr;
   char name[128] = {0};
+  // instrumentation: kernel launches issued, a stream timer, and per-kernel-family event timing
+  int64_t launches = 0;
+  cudaEvent_t timer_start = nullptr, timer_stop = nullptr;
+  bool kernel_timing = false;
+  struct Timed {
+    std::vector<cudaEvent_t> ev;  // start/stop pairs
+    double work = 0;              // algorithmic flops or bytes of the timed launches
+    int64_t launches = 0;
+  };
+  std::unordered_map<std::string, Timed> timed;
+  std::vector<cudaEvent_t> event_pool;
 };
+
+namespace pai {
+// Brackets one launch with events on the compute stream when kernel timing is on (pai_kernel_timing).
+struct KernelTimerScope {
+  pai_ctx* ctx;
+  pai_ctx::Timed* slot = nullptr;
+  KernelTimerScope(pai_ctx* c, const char* family, double work);
+  ~KernelTimerScope();
+};
+}  // namespace pai
 
 namespace pai {
 

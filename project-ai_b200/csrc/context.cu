@@ -491,3 +491,100 @@ PAI_API pai_status pai_reset_peak(pai_ctx* ctx) {
   ctx->peak = ctx->in_use;
   return PAI_OK;
 }
+
+// ================================================================ instrumentation
+namespace pai {
+
+static cudaEvent_t pooled_event(pai_ctx* ctx) {
+  if (!ctx->event_pool.empty()) {
+    cudaEvent_t e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+KernelTimerScope::KernelTimerScope(pai_ctx* c, const char* family, double work) : ctx(c) {
+  if (!ctx->kernel_timing) return;
+  slot = &ctx->timed[family];
+  cudaEvent_t e = pooled_event(ctx);
+  cudaEventRecord(e, ctx->stream);
+  slot->ev.push_back(e);
+  slot->work += work;
+  slot->launches++;
+}
+
+KernelTimerScope::~KernelTimerScope() {
+  if (!slot) return;
+  cudaEvent_t e = pooled_event(ctx);
+  cudaEventRecord(e, ctx->stream);
+  slot->ev.push_back(e);
+}
+
+}  // namespace pai
+
+// Stream timer: events recorded on the compute stream itself (the stream every op is ordered on).
+PAI_API pai_status pai_timer_start(pai_ctx* ctx) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  if (!ctx->timer_start) {
+    PAI_CUDA(cudaEventCreate(&ctx->timer_start));
+    PAI_CUDA(cudaEventCreate(&ctx->timer_stop));
+  }
+  PAI_CUDA(cudaEventRecord(ctx->timer_start, ctx->stream));
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_timer_stop(pai_ctx* ctx, float* ms) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  if (!ctx->timer_start) return set_error(PAI_ERR_INVALID_OP, "timer_stop without timer_start");
+  PAI_CUDA(cudaEventRecord(ctx->timer_stop, ctx->stream));
+  PAI_CUDA(cudaEventSynchronize(ctx->timer_stop));
+  PAI_CUDA(cudaEventElapsedTime(ms, ctx->timer_start, ctx->timer_stop));
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_launch_count(pai_ctx* ctx, int64_t* n) {
+  if (!ctx || !n) return set_error(PAI_ERR_ARGUMENT, "bad arguments");
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  *n = ctx->launches;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_kernel_timing(pai_ctx* ctx, int32_t enable) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  PAI_CUDA(cudaStreamSynchronize(ctx->stream));
+  for (auto& kv : ctx->timed)
+    for (cudaEvent_t e : kv.second.ev) ctx->event_pool.push_back(e);
+  ctx->timed.clear();
+  ctx->kernel_timing = enable != 0;
+  return PAI_OK;
+}
+
+// Launch count, summed device time (ms) and summed algorithmic work of one timed kernel family since timing was enabled.
+PAI_API pai_status pai_kernel_stats(pai_ctx* ctx, const char* family, int64_t* launches, double* total_ms, double* work) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  PAI_CUDA(cudaStreamSynchronize(ctx->stream));
+  auto it = ctx->timed.find(family ? family : "");
+  double ms = 0;
+  int64_t n = 0;
+  double w = 0;
+  if (it != ctx->timed.end()) {
+    for (size_t i = 0; i + 1 < it->second.ev.size(); i += 2) {
+      float t = 0;
+      PAI_CUDA(cudaEventElapsedTime(&t, it->second.ev[i], it->second.ev[i + 1]));
+      ms += t;
+    }
+    n = it->second.launches;
+    w = it->second.work;
+  }
+  if (launches) *launches = n;
+  if (total_ms) *total_ms = ms;
+  if (work) *work = w;
+  return PAI_OK;
+}

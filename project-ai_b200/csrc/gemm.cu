@@ -186,6 +186,7 @@ struct GemmArgs {
   int tiles_m, tiles_n, batches, splits;
   int kt_per_split;
   int* error_flag;
+  int k_elems;                           // logical K (for the work count only)
 };
 
 template <int BN, int STAGES>
@@ -418,6 +419,7 @@ static pai_status launch_tc(pai_ctx* ctx, GemmArgs& g) {
   }
   int total = g.tiles_m * g.tiles_n * g.batches * g.splits;
   int grid = total < ctx->sm_count ? total : ctx->sm_count;
+  KernelTimerScope timer(ctx, "gemm", 2.0 * g.m * g.n * (double)g.k_elems * g.batches);
   k_gemm_tc<BN, STAGES><<<grid, 192, S::kBytes, ctx->stream>>>(g);
   PAI_LAUNCH_CHECK("tcgen05 gemm");
   return PAI_OK;
@@ -571,6 +573,7 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   g.c = cdst; g.m = m; g.n = n; g.kt = kt; g.mt = mt; g.nt_pad = nt_pad;
   g.tiles_m = mt; g.tiles_n = tiles_n; g.batches = (int)batch; g.splits = splits; g.kt_per_split = kt_per_split;
   g.error_flag = ctx->d_error_flag;
+  g.k_elems = k;
   PAI_TRY((launch_tc<BN, STAGES>(ctx, g)));
   if (splits > 1) {
     int64_t nn = numel(r);

@@ -1,0 +1,469 @@
+// C++ host runtime for the B200 backend: a restatement of the reference's C# host layer that sits above the
+// IComputeBackend seam — Tensor views (ProjectAI.Core/Tensor.cs), the autograd facade and tape (Autograd.cs,
+// GradNode.cs, GradMode.cs), PcgRng / Init (Rng.cs, Init.cs), Module (Module.cs), the Llama modules
+// (ProjectAI.Models/*.cs), AdamW (Optimizers.cs), the trainer (ProjectAI.Training/Training.cs) and KV-cache decode
+// (Inference.cs, Sampling.cs). It drives a backend library through the C ABI of include/projectai_cuda.h, bound at
+// run time by path and symbol prefix (the CUDA library's prefix is "pai_").
+//
+// Where the backend offers the fused extensions (SDPA, RMSNorm backward, SiLU·Mul, fused cross-entropy, AdamW
+// step), the autograd records one node per fused op; otherwise it records the reference's composed op chain.
+#pragma once
+
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <memory>
+#include <optional>
+#include <stdexcept>
+#include <string>
+#include <unordered_set>
+#include <vector>
+
+#include "projectai_cuda.h"
+
+namespace paihost {
+
+// ---------------------------------------------------------------- errors (the .NET exception classes)
+struct BackendError : std::runtime_error { using std::runtime_error::runtime_error; };
+struct ArgumentError : BackendError { using BackendError::BackendError; };
+struct OutOfRangeError : ArgumentError { using ArgumentError::ArgumentError; };
+struct InvalidOperationError : BackendError { using BackendError::BackendError; };
+struct OutOfMemoryError : BackendError { using BackendError::BackendError; };
+struct DeviceTimeoutError : BackendError { using BackendError::BackendError; };
+
+using Dims = std::vector<int>;
+int64_t numel(const Dims& d);
+std::string dims_str(const Dims& d);
+std::vector<int64_t> contiguous_strides(const Dims& d);
+Dims broadcast_dims(const Dims& a, const Dims& b);  // Shape.BroadcastWith (Shape.cs:86-113)
+
+class NativeBackend;
+struct GradNode;
+
+// One backend allocation. Freed when its last view dies (unless a scope already freed it), when its scope ends
+// (unless kept alive), or by Release.
+struct Storage {
+  NativeBackend* backend = nullptr;
+  void* base = nullptr;
+  int64_t count = 0;
+  int scope = -1;       // index of the owning open scope, or -1
+  bool freed = false;
+  // Host copy of data uploaded by FromHost (ids, targets, constants): ToHost of an unmodified upload is served from it.
+  std::shared_ptr<std::vector<float>> shadow;
+  ~Storage();
+};
+
+struct TensorImpl;
+using Tensor = std::shared_ptr<TensorImpl>;
+
+// Tensor.cs:17-265: a view (shape, element strides, element offset) over shared storage, plus autograd metadata.
+struct TensorImpl {
+  Dims shape;
+  std::vector<int64_t> strides;
+  int64_t offset = 0;
+  std::shared_ptr<Storage> storage;
+  bool requires_grad = false;
+  Tensor grad;
+  std::shared_ptr<GradNode> grad_fn;
+  NativeBackend* backend = nullptr;  // set by the autograd facade (Tensor.Backend)
+  std::optional<float> known;        // value of a one-element tensor the host already knows (no read-back needed)
+
+  int rank() const { return (int)shape.size(); }
+  int64_t numel() const { return paihost::numel(shape); }
+  bool is_contiguous() const;
+  pai_tensor desc() const;
+  // views (metadata only; detached: requires_grad = false)
+  Tensor reshape(const Dims& d) const;
+  Tensor transpose(int a0, int a1) const;
+  Tensor permute(const std::vector<int>& p) const;
+  Tensor slice(int axis, int start, int length) const;
+  Tensor broadcast_to(const Dims& target) const;
+  void backward();  // Tensor.Backward (Tensor.cs:213-252)
+};
+
+Tensor make_view(const TensorImpl& t, Dims shape, std::vector<int64_t> strides, int64_t offset);
+
+// ---------------------------------------------------------------- backend (the IComputeBackend seam)
+struct OpTable;
+
+class NativeBackend {
+ public:
+  NativeBackend(const std::string& library_path, const std::string& prefix, int device);
+  ~NativeBackend();
+  NativeBackend(const NativeBackend&) = delete;
+  NativeBackend& operator=(const NativeBackend&) = delete;
+
+  std::string name() const;
+  bool has_fused() const;   // SDPA, RMSNorm backward, SiLU·Mul, fused CE, AdamW step
+  bool use_fused = true;    // callers may turn the extensions off to run the reference's composed chains
+  bool has_dp() const;
+
+  // allocation & transfer (IComputeBackend.cs:14-18)
+  Tensor allocate(const Dims& shape);
+  Tensor from_host(const float* data, int64_t count, const Dims& shape);
+  void to_host(const Tensor& t, float* dst, int64_t count);
+  void copy(const Tensor& src, const Tensor& dst);
+  // elementwise
+  Tensor add(const Tensor& a, const Tensor& b);
+  Tensor sub(const Tensor& a, const Tensor& b);
+  Tensor mul(const Tensor& a, const Tensor& b);
+  Tensor div(const Tensor& a, const Tensor& b);
+  Tensor add_scalar(const Tensor& a, float s);
+  Tensor mul_scalar(const Tensor& a, float s);
+  Tensor sqrt(const Tensor& x);
+  Tensor sigmoid(const Tensor& x);
+  Tensor matmul(const Tensor& a, const Tensor& b, bool transpose_b = false);
+  Tensor sum(const Tensor& x, int axis, bool keep = false);
+  Tensor mean(const Tensor& x, int axis, bool keep = false);
+  Tensor max(const Tensor& x, int axis, bool keep = false);
+  Tensor softmax(const Tensor& x, int axis);
+  Tensor rms_norm(const Tensor& x, const Tensor& w, float eps);
+  Tensor silu(const Tensor& x);
+  Tensor rotary(const Tensor& x, const Tensor& cos, const Tensor& sin);
+  Tensor gather(const Tensor& table, const std::vector<int>& ids);
+  Tensor scatter_add_rows(const Tensor& rows, const std::vector<int>& ids, int row_count);
+  Tensor cross_entropy(const Tensor& logits, const std::vector<int>& targets, int ignore);
+  Tensor cross_entropy_grad(const Tensor& logits, const std::vector<int>& targets, int ignore);
+  Tensor cat(const Tensor& a, const Tensor& b, int axis);
+  // fused extensions
+  std::pair<Tensor, Tensor> sdpa_fwd(const Tensor& q, const Tensor& k, const Tensor& v, float scale, bool causal, int pos);
+  std::vector<Tensor> sdpa_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
+                               const Tensor& dout, float scale, bool causal, int pos);
+  std::pair<Tensor, Tensor> rms_norm_bwd(const Tensor& x, const Tensor& w, const Tensor& g, float eps);
+  Tensor silu_mul(const Tensor& gate, const Tensor& up);
+  std::pair<Tensor, Tensor> silu_mul_bwd(const Tensor& gate, const Tensor& up, const Tensor& g);
+  std::pair<Tensor, Tensor> cross_entropy_fused(const Tensor& logits, const std::vector<int>& targets, int ignore, float scale);
+  void adamw_step(const Tensor& p, const Tensor& g, const Tensor& m, const Tensor& v, float lr, float b1, float b2,
+                  float eps, float wd, int t, float grad_scale);
+  // scopes (IComputeBackend.cs:69-95)
+  void begin_scope();
+  void end_scope();
+  void keep_alive(const Tensor& t);
+  void release(const Tensor& t);
+  void sync();
+  void memory_stats(int64_t* in_use, int64_t* peak, int64_t* reserved);
+  void reset_peak();
+  // data parallel
+  void nccl_unique_id(uint8_t out[128]);
+  void nccl_init(const uint8_t id[128], int rank, int world, int timeout_ms);
+  void allreduce(const std::vector<Tensor>& grads);
+  void allreduce_wait();
+  int dp_world = 1, dp_rank = 0;
+  // diagnostics (CUDA library only)
+  void timer_start();
+  float timer_stop();
+  int64_t launch_count();
+  void kernel_timing(bool on);
+  void kernel_stats(const std::string& family, int64_t* launches, double* ms, double* work);
+  void check_device_error();
+
+  // internals used by Storage
+  void free_storage(Storage* s);
+  pai_ctx* ctx() const { return ctx_; }
+
+ private:
+  friend struct Storage;
+  Tensor wrap(const pai_tensor& d);
+  void check(int status) const;
+  Tensor unary(int which, const Tensor& x, float s = 0.0f);
+  Tensor binary(int which, const Tensor& a, const Tensor& b);
+  Tensor reduce(int which, const Tensor& x, int axis, bool keep);
+  void invalidate_shadow(const Tensor& t);
+
+  void* lib_ = nullptr;
+  std::unique_ptr<OpTable> fn_;
+  pai_ctx* ctx_ = nullptr;
+  std::vector<std::unordered_set<Storage*>> scopes_;
+  std::unordered_set<Storage*> live_;  // every Storage object still referring to this backend
+};
+
+// ---------------------------------------------------------------- autograd (GradMode.cs, GradNode.cs, Autograd.cs)
+struct GradMode {
+  static bool enabled();
+  struct Guard {
+    explicit Guard(bool disabled);
+    ~Guard();
+    bool previous;
+  };
+};
+
+struct GradNode {
+  std::string op;
+  std::vector<Tensor> inputs;
+  std::function<std::vector<Tensor>(const Tensor&)> backward;
+};
+
+class Autograd {
+ public:
+  explicit Autograd(NativeBackend* backend) : be(backend) {}
+  NativeBackend* be;
+
+  Tensor add(const Tensor& a, const Tensor& b);
+  Tensor sub(const Tensor& a, const Tensor& b);
+  Tensor mul(const Tensor& a, const Tensor& b);
+  Tensor matmul(const Tensor& a, const Tensor& b, bool transpose_b = false);
+  Tensor contiguous(const Tensor& x);
+  Tensor sum_all(const Tensor& x);
+  Tensor mean(const Tensor& x);
+  Tensor checkpoint(const std::function<Tensor(const Tensor&)>& segment, const Tensor& input,
+                    const std::vector<Tensor>& parameters, const std::function<void()>& on_grads_ready = nullptr);
+  Tensor embedding(const Tensor& weight, const std::vector<int>& ids);
+  Tensor cross_entropy(const Tensor& logits, const std::vector<int>& targets, int ignore);
+  Tensor softmax(const Tensor& x, int axis);
+  Tensor silu(const Tensor& x);
+  Tensor rms_norm(const Tensor& x, const Tensor& w, float eps);
+  Tensor rotary(const Tensor& x, const Tensor& cos, const Tensor& sin);
+  Tensor transpose(const Tensor& x, int a0, int a1);
+  Tensor permute(const Tensor& x, const std::vector<int>& p);
+  Tensor reshape(const Tensor& x, const Dims& d);
+  Tensor slice(const Tensor& x, int axis, int start, int length);
+  Tensor broadcast_to(const Tensor& x, const Dims& target);
+  // fused extensions: one node each (composed fallbacks when the backend lacks them)
+  Tensor silu_mul(const Tensor& gate, const Tensor& up);
+  Tensor attention(const Tensor& q, const Tensor& k, const Tensor& v, float scale, int pos_offset);  // -> [B,S,H,D]
+
+  float to_scalar(const Tensor& t);
+  Tensor reduce_grad_to_shape(const Tensor& g, const Dims& target);
+
+ private:
+  Tensor record(const Tensor& y, const std::string& op, std::vector<Tensor> inputs,
+                std::function<std::vector<Tensor>(const Tensor&)> backward);
+  Tensor detach_leaf(const Tensor& x);
+};
+
+// ---------------------------------------------------------------- Rng / Init (Rng.cs, Init.cs)
+class PcgRng {
+ public:
+  explicit PcgRng(uint64_t seed, uint64_t stream = 0xDA3E39CB94B95BDBull);
+  uint32_t next_u32();
+  float next_float();
+  float next_gaussian();
+
+ private:
+  uint64_t state_, inc_;
+  bool has_spare_ = false;
+  float spare_ = 0.0f;
+};
+
+enum class InitKind { Zeros, Ones, Normal, Xavier, Kaiming };
+struct Initializer {
+  InitKind kind = InitKind::Normal;
+  float a = 0.0f, b = 0.02f;  // Normal: mean, std; Xavier/Kaiming: gain
+  void fill(const Tensor& target, NativeBackend& be, PcgRng& rng) const;
+};
+
+// ---------------------------------------------------------------- modules (Module.cs, ProjectAI.Models)
+struct ModelConfig {
+  int vocab_size = 256, embedding_dim = 128, layer_count = 2, head_count = 4, kv_head_count = 4, ffn_hidden = 344;
+  int max_sequence_length = 4096;
+  float rope_theta = 10000.0f, norm_eps = 1e-5f;
+  int head_dim() const { return embedding_dim / head_count; }
+  void validate() const;
+};
+
+struct ParameterContext {
+  NativeBackend* backend;
+  Autograd* ag;
+  PcgRng* rng;
+  bool skip_init = false;
+  // Overrides every parameter's initializer (the configs that specify N(0, 0.02) weights for all matrices).
+  std::optional<Initializer> override_init;
+};
+
+class KvCache;
+
+struct ForwardContext {
+  KvCache* cache = nullptr;
+};
+
+class Module {
+ public:
+  explicit Module(ParameterContext ctx) : ctx_(ctx) {}
+  virtual ~Module() = default;
+  std::vector<Tensor> parameters() const;
+  std::vector<std::pair<std::string, Tensor>> named_parameters() const;
+
+ protected:
+  Tensor param(const std::string& name, const Dims& shape, Initializer init);
+  template <class T>
+  T* register_module(const std::string& name, std::unique_ptr<T> m) {
+    T* raw = m.get();
+    children_.emplace_back(name, std::move(m));
+    return raw;
+  }
+  ParameterContext ctx_;
+  Autograd& ag() const { return *ctx_.ag; }
+  NativeBackend& be() const { return *ctx_.backend; }
+
+ private:
+  std::vector<std::pair<std::string, Tensor>> params_;
+  std::vector<std::pair<std::string, std::unique_ptr<Module>>> children_;
+};
+
+class Linear : public Module {
+ public:
+  Linear(ParameterContext ctx, int in_dim, int out_dim, Initializer init);
+  Tensor forward(const Tensor& x);
+  Tensor weight;
+  int in_dim, out_dim;
+};
+
+class RmsNorm : public Module {
+ public:
+  RmsNorm(ParameterContext ctx, int dim, float eps);
+  Tensor forward(const Tensor& x);
+  Tensor weight;
+  float eps;
+};
+
+class RotaryEmbedding : public Module {
+ public:
+  RotaryEmbedding(ParameterContext ctx, int head_dim, float theta, int max_seq);
+  Tensor apply_at_offset(const Tensor& x, int offset);
+  Tensor cos, sin;
+  int max_seq;
+};
+
+class SwiGlu : public Module {
+ public:
+  SwiGlu(ParameterContext ctx, int dim, int hidden);
+  Tensor forward(const Tensor& x);
+  Linear *gate, *up, *down;
+};
+
+class Attention : public Module {
+ public:
+  Attention(ParameterContext ctx, const ModelConfig& cfg, int layer);
+  Tensor forward(const Tensor& x, const ForwardContext& fctx);
+  ModelConfig cfg;
+  int layer;
+  Linear *wq, *wk, *wv, *wo;
+  RotaryEmbedding* rope;
+  Tensor inv_sqrt_hd;
+
+ private:
+  Tensor causal_mask(int q_len, int k_len, int pos_offset);
+};
+
+class TransformerBlock : public Module {
+ public:
+  TransformerBlock(ParameterContext ctx, const ModelConfig& cfg, int layer);
+  Tensor forward(const Tensor& x, const ForwardContext& fctx);
+  RmsNorm *attn_norm, *ffn_norm;
+  Attention* attn;
+  SwiGlu* ffn;
+};
+
+class Embedding : public Module {
+ public:
+  Embedding(ParameterContext ctx, int vocab, int dim);
+  Tensor forward(const Tensor& ids);
+  Tensor weight;
+  int vocab, dim;
+};
+
+class LlamaModel : public Module {
+ public:
+  LlamaModel(ParameterContext ctx, const ModelConfig& cfg);
+  Tensor forward(const Tensor& ids, const ForwardContext& fctx = {});
+  ModelConfig cfg;
+  bool gradient_checkpointing = false;
+  // Called after each checkpointed block's recompute has produced that block's parameter gradients.
+  std::function<void(int block)> on_block_grads_ready;
+  Embedding* embedding;
+  std::vector<TransformerBlock*> blocks;
+  RmsNorm* final_norm;
+};
+
+// Modules.cs:290-370: per-layer K/V grown with Cat (the first append round-trips through the host).
+class KvCache {
+ public:
+  KvCache(NativeBackend* be, const ModelConfig& cfg, int max_batch, int max_seq);
+  int length(int layer) const;
+  std::pair<Tensor, Tensor> append(int layer, const Tensor& k, const Tensor& v);
+  void reset();
+  int max_batch, max_seq;
+
+ private:
+  Tensor concat(const Tensor& existing, const Tensor& incoming);
+  NativeBackend* be_;
+  std::vector<Tensor> keys_, values_;
+  std::vector<int> lengths_;
+};
+
+std::vector<int> ids_from_tensor(NativeBackend& be, const Tensor& t);  // Embedding.ToIds / Loss.ToIds
+Tensor cross_entropy_loss(Autograd& ag, const Tensor& logits, const Tensor& targets, int ignore = -100);  // Loss.cs
+
+// ---------------------------------------------------------------- samplers (Sampling.cs)
+int argmax(const float* logits, int n);
+class TopKTopPSampler {
+ public:
+  TopKTopPSampler(uint64_t seed, float temperature, int top_k, float top_p) : rng(seed), temperature(temperature), top_k(top_k), top_p(top_p) {}
+  int sample(const float* logits, int n);
+  PcgRng rng;
+  float temperature;
+  int top_k;
+  float top_p;
+};
+
+// ---------------------------------------------------------------- optimizer (Optimizers.cs)
+class AdamW {
+ public:
+  AdamW(std::vector<Tensor> params, NativeBackend* be, float lr = 1e-3f, float b1 = 0.9f, float b2 = 0.999f,
+        float eps = 1e-8f, float wd = 0.01f);
+  void step();
+  void zero_grad();
+  std::function<float(int)> schedule;
+  float lr, b1, b2, eps, wd;
+  int step_count = 0;
+  float grad_scale = 1.0f;  // 1/world for a data-parallel sum
+  struct State { Tensor m, v; int t = 0; };
+  std::map<TensorImpl*, State> state;
+
+ private:
+  std::vector<Tensor> params_;
+  NativeBackend* be_;
+};
+
+// ---------------------------------------------------------------- training (Training.cs)
+struct TrainingConfig {
+  int batch_size = 8, sequence_length = 512;
+  float learning_rate = 3e-4f, weight_decay = 0.01f;
+  int max_steps = 1000, grad_accum = 1;
+  bool gradient_checkpointing = false;
+  int warmup_steps = 100;
+  uint64_t seed = 0;
+};
+
+std::function<float(int)> warmup_cosine(const TrainingConfig& cfg);
+
+// One training step in the reference trainer's order (Training.cs:87-113): ZeroGrad, per micro-batch scope
+// {forward, loss, ToHost(loss), backward, KeepAlive(grads)}, optimizer step. Batches come from the caller.
+class Trainer {
+ public:
+  Trainer(NativeBackend* be, LlamaModel* model, const TrainingConfig& cfg, float beta1 = 0.9f, float beta2 = 0.999f);
+  // inputs/targets: micro-batches of [batch, seq] token ids (row-major) as floats, one pair per micro step.
+  float step(const std::vector<std::vector<float>>& inputs, const std::vector<std::vector<float>>& targets);
+  // The same step on batches already uploaded to the device ([batch, seq] id tensors from FromHost).
+  float step_tensors(const std::vector<Tensor>& inputs, const std::vector<Tensor>& targets);
+  LlamaModel* model;
+  TrainingConfig cfg;
+  std::unique_ptr<AdamW> optimizer;
+  Autograd ag;
+
+ private:
+  NativeBackend* be_;
+  std::vector<Tensor> params_;
+  std::vector<std::vector<Tensor>> block_params_;
+  std::vector<Tensor> tail_params_;
+};
+
+// Inference.cs:23-64 with a sampler: prefill, then one token per step through the KV cache.
+struct GenerateResult {
+  std::vector<int> tokens;
+  double prefill_seconds = 0, decode_seconds = 0;
+};
+GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<int>& prompt, int max_tokens,
+                        TopKTopPSampler* sampler, int batch = 1);
+
+}  // namespace paihost

@@ -1,0 +1,217 @@
+// AdamW (ProjectAI.Core/Optimizers.cs:14-133), the training step of Trainer.Train (ProjectAI.Training/Training.cs:59-120)
+// with its warmup+cosine schedule (:165-181), data-parallel gradient buckets, and the decode loop of
+// Inference.GenerateText (Inference.cs:23-74).
+#include <chrono>
+#include <cmath>
+
+#include "runtime.h"
+
+namespace paihost {
+
+AdamW::AdamW(std::vector<Tensor> params, NativeBackend* be, float lr_, float b1_, float b2_, float eps_, float wd_)
+    : lr(lr_), b1(b1_), b2(b2_), eps(eps_), wd(wd_), params_(std::move(params)), be_(be) {}
+
+// AdamW.Step (Optimizers.cs:81-123). The fused path runs the same per-element operations in one kernel, in place.
+void AdamW::step() {
+  step_count++;
+  float cur_lr = schedule ? schedule(step_count) : lr;
+  GradMode::Guard nograd(true);
+  bool fused = be_->use_fused && be_->has_fused();
+  if (fused) {
+    for (const auto& p : params_) {
+      if (!p->grad) continue;
+      State& s = state[p.get()];
+      if (!s.m) {
+        s.m = be_->allocate(p->shape);  // zero-initialised moments, persisting across steps
+        s.v = be_->allocate(p->shape);
+        be_->keep_alive(s.m);
+        be_->keep_alive(s.v);
+      }
+      s.t += 1;
+      be_->adamw_step(p, p->grad, s.m, s.v, cur_lr, b1, b2, eps, wd, s.t, grad_scale);
+    }
+    return;
+  }
+  be_->begin_scope();
+  try {
+    for (const auto& p : params_) {
+      if (!p->grad) continue;
+      Tensor g = p->grad;
+      if (grad_scale != 1.0f) g = be_->mul_scalar(g, grad_scale);
+      State& s = state[p.get()];
+      Tensor prev_m = s.m, prev_v = s.v;
+      if (!s.m) s.m = be_->allocate(p->shape);
+      if (!s.v) s.v = be_->allocate(p->shape);
+      int t = s.t + 1;
+      Tensor m = be_->add(be_->mul_scalar(s.m, b1), be_->mul_scalar(g, 1.0f - b1));
+      Tensor v = be_->add(be_->mul_scalar(s.v, b2), be_->mul_scalar(be_->mul(g, g), 1.0f - b2));
+      s.m = m;
+      s.v = v;
+      s.t = t;
+      be_->keep_alive(m);
+      be_->keep_alive(v);
+      if (prev_m) be_->release(prev_m);
+      if (prev_v) be_->release(prev_v);
+      float bc1 = 1.0f - powf(b1, (float)t);
+      float bc2 = 1.0f - powf(b2, (float)t);
+      Tensor mhat = be_->mul_scalar(m, 1.0f / bc1);
+      Tensor vhat = be_->mul_scalar(v, 1.0f / bc2);
+      Tensor adaptive = be_->div(mhat, be_->add_scalar(be_->sqrt(vhat), eps));
+      Tensor delta = be_->add(be_->mul_scalar(adaptive, cur_lr), be_->mul_scalar(p, cur_lr * wd));
+      be_->copy(be_->sub(p, delta), p);
+    }
+  } catch (...) {
+    be_->end_scope();
+    throw;
+  }
+  be_->end_scope();
+}
+
+void AdamW::zero_grad() {
+  for (const auto& p : params_) {
+    if (p->grad) be_->release(p->grad);
+    p->grad.reset();
+  }
+}
+
+std::function<float(int)> warmup_cosine(const TrainingConfig& cfg) {
+  float base = cfg.learning_rate, min_lr = base * 0.1f;
+  int total = std::max(1, cfg.max_steps);
+  int warmup = std::min(std::max(cfg.warmup_steps, 0), std::max(0, total - 1));
+  return [=](int step) {
+    if (warmup > 0 && step <= warmup) return base * (float)step / (float)warmup;
+    float denom = (float)std::max(1, total - warmup);
+    float progress = std::min(std::max((float)(step - warmup) / denom, 0.0f), 1.0f);
+    float cosine = 0.5f * (1.0f + cosf(3.14159265f * progress));
+    return min_lr + (base - min_lr) * cosine;
+  };
+}
+
+Trainer::Trainer(NativeBackend* be, LlamaModel* m, const TrainingConfig& c, float beta1, float beta2)
+    : model(m), cfg(c), ag(be), be_(be) {
+  model->gradient_checkpointing = cfg.gradient_checkpointing;
+  params_ = model->parameters();
+  optimizer = std::make_unique<AdamW>(params_, be, cfg.learning_rate, beta1, beta2, 1e-8f, cfg.weight_decay);
+  optimizer->schedule = warmup_cosine(cfg);
+  for (auto* b : model->blocks) block_params_.push_back(b->parameters());
+  tail_params_ = model->embedding->parameters();
+  for (const auto& p : model->final_norm->parameters()) tail_params_.push_back(p);
+}
+
+static std::vector<Tensor> grads_of(const std::vector<Tensor>& params) {
+  std::vector<Tensor> g;
+  for (const auto& p : params)
+    if (p->grad) g.push_back(p->grad);
+  return g;
+}
+
+// Host buffers in (NextBatch's FromHost, Training.cs:122-141), host loss out: the end-to-end step.
+float Trainer::step(const std::vector<std::vector<float>>& inputs, const std::vector<std::vector<float>>& targets) {
+  int b = cfg.batch_size, s = cfg.sequence_length;
+  if (inputs.size() != targets.size() || inputs.empty())
+    throw ArgumentError("inputs and targets must hold the same number (>= 1) of micro-batches");
+  std::vector<Tensor> in, tg;
+  for (size_t i = 0; i < inputs.size(); i++) {
+    if ((int64_t)inputs[i].size() != (int64_t)b * s || (int64_t)targets[i].size() != (int64_t)b * s)
+      throw ArgumentError("each micro-batch must hold batch_size x sequence_length ids");
+    in.push_back(be_->from_host(inputs[i].data(), (int64_t)b * s, {b, s}));
+    tg.push_back(be_->from_host(targets[i].data(), (int64_t)b * s, {b, s}));
+  }
+  return step_tensors(in, tg);
+}
+
+float Trainer::step_tensors(const std::vector<Tensor>& inputs, const std::vector<Tensor>& targets) {
+  int micro_steps = std::max(1, (int)inputs.size());
+  if ((int)targets.size() != micro_steps) throw ArgumentError("inputs and targets must hold the same number of micro-batches");
+  bool dp = be_->dp_world > 1;
+  optimizer->grad_scale = dp ? 1.0f / (float)be_->dp_world : 1.0f;
+  optimizer->zero_grad();
+  float inv_micro_v = 1.0f / (float)micro_steps;
+  Tensor inv_micro = be_->from_host(&inv_micro_v, 1, {1});
+  float step_loss = 0.0f;
+  for (int micro = 0; micro < micro_steps; micro++) {
+    bool last = micro == micro_steps - 1;
+    // Data parallel: each checkpointed block's gradients are final once its recompute ran; sum them across ranks
+    // right away so the exchange overlaps the backward of the earlier blocks.
+    if (dp && last && model->gradient_checkpointing) {
+      model->on_block_grads_ready = [this](int i) { be_->allreduce(grads_of(block_params_[(size_t)i])); };
+    } else {
+      model->on_block_grads_ready = nullptr;
+    }
+    be_->begin_scope();
+    try {
+      const Tensor& input = inputs[(size_t)micro];
+      const Tensor& target = targets[(size_t)micro];
+      Tensor logits = model->forward(input);
+      Tensor loss = cross_entropy_loss(ag, logits, target);
+      float lh = 0.0f;
+      be_->to_host(loss, &lh, 1);
+      step_loss += lh / (float)micro_steps;
+      Tensor scaled = micro_steps > 1 ? ag.mul(loss, inv_micro) : loss;
+      scaled->backward();
+      for (const auto& p : params_)
+        if (p->grad) be_->keep_alive(p->grad);
+    } catch (...) {
+      model->on_block_grads_ready = nullptr;
+      be_->end_scope();
+      throw;
+    }
+    be_->end_scope();
+  }
+  model->on_block_grads_ready = nullptr;
+  if (dp) {
+    if (model->gradient_checkpointing) {
+      be_->allreduce(grads_of(tail_params_));
+    } else {
+      be_->allreduce(grads_of(params_));
+    }
+    be_->allreduce_wait();
+  }
+  optimizer->step();
+  return step_loss;
+}
+
+// Inference.GenerateText (Inference.cs:23-64) on token ids, for a lockstep batch (KvCache supports uniform batches).
+// Only each row's last logits row is read back (SampleLast reads exactly that row of the full download).
+GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<int>& prompt, int max_tokens,
+                        TopKTopPSampler* sampler, int batch) {
+  using clock = std::chrono::steady_clock;
+  GenerateResult r;
+  const ModelConfig& cfg = model->cfg;
+  int p_len = (int)prompt.size() / batch;
+  if (p_len * batch != (int)prompt.size() || p_len == 0) throw ArgumentError("prompt must hold batch x length ids");
+  KvCache cache(be, cfg, batch, cfg.max_sequence_length);
+  ForwardContext ctx;
+  ctx.cache = &cache;
+  GradMode::Guard nograd(true);
+  int vocab = cfg.vocab_size;
+  std::vector<float> row((size_t)vocab);
+  auto pick = [&](const Tensor& logits, std::vector<int>& out) {
+    int rows = logits->shape[1];
+    out.clear();
+    for (int bi = 0; bi < batch; bi++) {
+      Tensor last = logits->slice(0, bi, 1)->slice(1, rows - 1, 1);
+      be->to_host(last, row.data(), vocab);
+      out.push_back(sampler ? sampler->sample(row.data(), vocab) : argmax(row.data(), vocab));
+    }
+  };
+  auto t0 = clock::now();
+  std::vector<float> pf(prompt.begin(), prompt.end());
+  Tensor logits = model->forward(be->from_host(pf.data(), (int64_t)pf.size(), {batch, p_len}), ctx);
+  std::vector<int> next;
+  pick(logits, next);
+  auto t1 = clock::now();
+  r.prefill_seconds = std::chrono::duration<double>(t1 - t0).count();
+  for (int produced = 0; produced < max_tokens; produced++) {
+    for (int v : next) r.tokens.push_back(v);
+    if (produced + 1 >= max_tokens || p_len + produced + 1 >= cfg.max_sequence_length) break;
+    std::vector<float> step(next.begin(), next.end());
+    logits = model->forward(be->from_host(step.data(), batch, {batch, 1}), ctx);
+    pick(logits, next);
+  }
+  be->sync();
+  r.decode_seconds = std::chrono::duration<double>(clock::now() - t1).count();
+  return r;
+}
+
+}  // namespace paihost
