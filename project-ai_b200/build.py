@@ -45,6 +45,19 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f"command failed ({r.returncode}): {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
 
 
+def nccl_lib_dir() -> Path | None:
+    """The NCCL that PyTorch ships (the image also has an older system NCCL with the same soname). Linking against
+    PyTorch's copy, with an rpath to it, keeps one NCCL in the process whichever of the two is loaded first."""
+    import importlib.util
+
+    spec = importlib.util.find_spec("nvidia")
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        d = Path(base) / "nccl" / "lib"
+        if (d / "libnccl.so.2").exists():
+            return d
+    return None
+
+
 def build_cuda(verbose: bool = False) -> Path:
     """Compiles every ``csrc/*.cu`` for sm_100a and links ``lib/libprojectai_cuda.so``."""
     BUILD.mkdir(exist_ok=True)
@@ -61,7 +74,9 @@ def build_cuda(verbose: bool = False) -> Path:
             list(ex.map(_run, jobs))
     objs = [BUILD / (s.stem + ".o") for s in sources]
     if _newer(CUDA_LIB, objs):
-        _run([NVCC, *ARCH, "-shared", "-ccbin", CXX, "-o", str(CUDA_LIB), *map(str, objs), "-lnccl",
+        nccl = nccl_lib_dir()
+        link_nccl = ["-L" + str(nccl), "-l:libnccl.so.2", "-Xlinker", "-rpath," + str(nccl)] if nccl else ["-lnccl"]
+        _run([NVCC, *ARCH, "-shared", "-ccbin", CXX, "-o", str(CUDA_LIB), *map(str, objs), *link_nccl,
               "-Xlinker", "--no-undefined"])
     if verbose:
         print(f"built {CUDA_LIB}")
