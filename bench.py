@@ -205,6 +205,88 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def op_sweep(args):
+    """Op-level sweep on one GPU (inputs N(0,1) fp32): each op timed with CUDA events on the library's stream after
+    warm-up, reported against its roofline (tensor: measured TF32 / 3; HBM: measured copy bandwidth)."""
+    from projectai_b200 import cabi
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    tf32 = measured_tf32_peak(0) if args.op != "gemm-only" else 727.8
+    lib = pai.cuda_library()
+    be = cabi.NativeBackend(lib, 0)
+    rng = np.random.RandomState(0)
+
+    def timed(fn, reps):
+        for _ in range(2):
+            fn()
+        be.timer_start()
+        for _ in range(reps):
+            fn()
+        return be.timer_stop() / reps
+
+    rows = []
+
+    def emit(op, shape, ms, work, unit, peak):
+        achieved = work / (ms * 1e-3) / (1e12 if unit == "TFLOP/s" else 1e9)
+        rows.append({"op": op, "shape": shape, "ms": ms, "achieved": achieved, "unit": unit, "peak": peak,
+                     "frac": achieved / peak})
+        print(json.dumps(rows[-1]), flush=True)
+
+    def randt(*shape):
+        return be.from_host(rng.standard_normal(shape).astype(np.float32))
+
+    gemm_shapes = [(m, k, k) for m in (2048, 8192) for k in (768, 2048, 5632)]
+    if args.shape:
+        gemm_shapes = [tuple(int(x) for x in args.shape.split(","))]
+    if args.op in ("all", "gemm", "gemm-only"):
+        for m, k, n in gemm_shapes:
+            a, b = randt(m, k), randt(n, k)
+            be.scope_begin()
+            ms = timed(lambda: be.matmul(a, b, True), args.steps)
+            be.scope_end()
+            emit("matmul(3xTF32, transposeB)", [m, k, n], ms, 2.0 * m * n * k, "TFLOP/s", tf32 / 3)
+            be.release(a)
+            be.release(b)
+    if args.op in ("all", "attention"):
+        for s in (512, 2048, 4096):
+            B, Hh, D = 4, 32, 64
+            q, k, v, do = randt(B, Hh, s, D), randt(B, Hh, s, D), randt(B, Hh, s, D), randt(B, s, Hh, D)
+            fl = 2.0 * B * Hh * s * (s + 1) * D  # causal: 4·D per visible pair, s(s+1)/2 pairs
+            be.scope_begin()
+            ms = timed(lambda: be.sdpa_fwd(q, k, v, 0.125, True, 0), max(2, args.steps // 2))
+            o, lse = be.sdpa_fwd(q, k, v, 0.125, True, 0)
+            emit("attention fwd (causal)", [B, Hh, s, D], ms, fl, "TFLOP/s", tf32 / 3)
+            ms = timed(lambda: be.sdpa_bwd(q, k, v, o, lse, do, 0.125, True, 0), max(2, args.steps // 2))
+            emit("attention bwd (causal)", [B, Hh, s, D], ms, 2.5 * fl, "TFLOP/s", tf32 / 3)
+            be.scope_end()
+            for t in (q, k, v, do):
+                be.release(t)
+    if args.op in ("all", "hbm"):
+        x, w, g = randt(8192, 2048), randt(2048), randt(8192, 2048)
+        cs, sn = randt(2048, 64), randt(2048, 64)
+        xr = cabi.reshape(x, (4, 2048, 32, 64))
+        be.scope_begin()
+        emit("rmsnorm fwd", [8192, 2048], timed(lambda: be.rmsnorm(x, w, 1e-5), args.steps), 2 * 8192 * 2048 * 4, "GB/s", hbm)
+        emit("rmsnorm bwd", [8192, 2048], timed(lambda: be.rmsnorm_bwd(x, w, g, 1e-5), args.steps), 3 * 8192 * 2048 * 4, "GB/s", hbm)
+        xv = cabi.transpose(xr, 1, 2)
+        emit("rope (strided q view)", [4, 32, 2048, 64], timed(lambda: be.rotary(xv, cs, sn), args.steps), 2 * 8192 * 2048 * 4, "GB/s", hbm)
+        emit("swiglu silu(gate)*up", [8192, 2048], timed(lambda: be.silu_mul_fwd(x, g), args.steps), 3 * 8192 * 2048 * 4, "GB/s", hbm)
+        be.scope_end()
+        logits = randt(8192, 32000)
+        targets = rng.randint(0, 32000, size=8192).astype(np.int32)
+        be.scope_begin()
+        emit("cross-entropy loss+grad", [8192, 32000], timed(lambda: be.cross_entropy_fused(logits, targets), args.steps),
+             2 * 8192 * 32000 * 4, "GB/s", hbm)
+        be.scope_end()
+        be.release(logits)
+        n = 1_100_000_000 if args.op == "hbm" or args.op == "all" else 100_000_000
+        p = be.allocate((n,))
+        gg, mm, vv = be.allocate((n,)), be.allocate((n,)), be.allocate((n,))
+        emit("adamw (fused, in place)", [n], timed(lambda: be.adamw_step(p, gg, mm, vv, 3e-4, 0.9, 0.95, 1e-8, 0.1, 1),
+                                                  max(2, args.steps // 2)), 28.0 * n, "GB/s", hbm)
+    be.close()
+
+
 def workload_config(name, n):
     c = CONFIGS[name]
     return {"workload": f"llama-{name} train step (fwd + per-block recompute + bwd + AdamW), fp32 semantics",
@@ -224,9 +306,14 @@ def main():
     ap.add_argument("--no-recompute", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=64)
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm"],
+                    help="op-level sweep instead of the training step")
+    ap.add_argument("--shape", default=None, help="M,K,N for --op gemm")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.op:
+        return op_sweep(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -136,6 +136,9 @@ _SIGS = {
     "allreduce_wait": [c_void_p],
     "nccl_abort": [c_void_p],
     "check_device_error": [c_void_p, _I32P],
+    "timer_start": [c_void_p],
+    "timer_stop": [c_void_p, POINTER(c_float)],
+    "launch_count": [c_void_p, POINTER(c_int64)],
 }
 
 
@@ -340,6 +343,14 @@ class NativeBackend:
     def adamw_step(self, p, g, m, v, lr, beta1, beta2, eps, weight_decay, t, grad_scale=1.0):
         self._c("adamw_step", ctypes.byref(p), ctypes.byref(g), ctypes.byref(m), ctypes.byref(v), c_float(lr),
                 c_float(beta1), c_float(beta2), c_float(eps), c_float(weight_decay), int(t), c_float(grad_scale))
+
+    def timer_start(self) -> None:
+        self._c("timer_start")
+
+    def timer_stop(self) -> float:
+        ms = c_float()
+        self._c("timer_stop", ctypes.byref(ms))
+        return ms.value
 
     def check_device_error(self) -> int:
         code = c_int32()
