@@ -67,6 +67,11 @@ struct pai_ctx {
   };
   std::unordered_map<std::string, Timed> timed;
   std::vector<cudaEvent_t> event_pool;
+  // pinned staging ring for small host->device uploads (ids, targets, batch offsets): copies from pinned memory are
+  // truly asynchronous, so an op's small uploads never stall the stream
+  char* pinned = nullptr;
+  cudaEvent_t pinned_ev[32] = {};
+  int pinned_next = 0;
 };
 
 namespace pai {
@@ -101,6 +106,10 @@ pai_status scratch(pai_ctx* ctx, size_t bytes, Scratch* s);
 
 // Host -> device copy of a small host array into a stream-ordered scratch block.
 pai_status upload(pai_ctx* ctx, const void* host, size_t bytes, Scratch* s);
+// Stream-ordered host -> device copy; buffers up to kPinnedChunk bytes go through the pinned staging ring.
+constexpr size_t kPinnedChunk = 256 * 1024;
+constexpr int kPinnedChunks = 32;
+pai_status h2d(pai_ctx* ctx, void* dst, const void* host, size_t bytes);
 
 // ---------------------------------------------------------------- views
 int64_t numel(const pai_tensor& t);

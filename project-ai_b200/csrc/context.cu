@@ -113,10 +113,29 @@ pai_status scratch(pai_ctx* ctx, size_t bytes, Scratch* s) {
   return raw_alloc(ctx, bytes, &s->p);
 }
 
+pai_status h2d(pai_ctx* ctx, void* dst, const void* host, size_t bytes) {
+  if (bytes == 0) return PAI_OK;
+  if (bytes > kPinnedChunk) {
+    PAI_CUDA(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    return PAI_OK;
+  }
+  if (!ctx->pinned) {
+    PAI_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&ctx->pinned), kPinnedChunk * kPinnedChunks, cudaHostAllocDefault));
+    for (int i = 0; i < kPinnedChunks; i++) PAI_CUDA(cudaEventCreateWithFlags(&ctx->pinned_ev[i], cudaEventDisableTiming));
+  }
+  int c = ctx->pinned_next;
+  ctx->pinned_next = (c + 1) % kPinnedChunks;
+  PAI_CUDA(cudaEventSynchronize(ctx->pinned_ev[c]));  // the copy that last read this chunk has completed
+  char* slot = ctx->pinned + (size_t)c * kPinnedChunk;
+  memcpy(slot, host, bytes);
+  PAI_CUDA(cudaMemcpyAsync(dst, slot, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  PAI_CUDA(cudaEventRecord(ctx->pinned_ev[c], ctx->stream));
+  return PAI_OK;
+}
+
 pai_status upload(pai_ctx* ctx, const void* host, size_t bytes, Scratch* s) {
   PAI_TRY(scratch(ctx, bytes, s));
-  if (bytes) PAI_CUDA(cudaMemcpyAsync(s->p, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
-  return PAI_OK;
+  return h2d(ctx, s->p, host, bytes);
 }
 
 // ---------------------------------------------------------------- views
@@ -334,6 +353,14 @@ PAI_API pai_status pai_ctx_destroy(pai_ctx* ctx) {
   for (auto& kv : ctx->free_blocks)
     for (void* p : kv.second) cudaFree(p);
   cudaFree(ctx->d_error_flag);
+  if (ctx->pinned) {
+    cudaFreeHost(ctx->pinned);
+    for (int i = 0; i < pai::kPinnedChunks; i++) cudaEventDestroy(ctx->pinned_ev[i]);
+  }
+  for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
+  for (auto& kv : ctx->timed)
+    for (cudaEvent_t e : kv.second.ev) cudaEventDestroy(e);
+  if (ctx->timer_start) { cudaEventDestroy(ctx->timer_start); cudaEventDestroy(ctx->timer_stop); }
   cudaStreamDestroy(ctx->stream);
   cudaStreamDestroy(ctx->comm_stream);
   delete ctx;
@@ -371,7 +398,7 @@ PAI_API pai_status pai_from_host(pai_ctx* ctx, const float* host, int64_t count,
     pai_release(ctx, r.base);
     return set_error(PAI_ERR_ARGUMENT, "FromHost: %lld values for a tensor of %lld elements", (long long)count, (long long)n);
   }
-  if (n) PAI_CUDA(cudaMemcpyAsync(r.base, host, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+  PAI_TRY(h2d(ctx, r.base, host, (size_t)n * 4));
   *out = r;
   return PAI_OK;
 }

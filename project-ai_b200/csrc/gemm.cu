@@ -132,6 +132,7 @@ struct PackDesc {
   int64_t sr, sk;            // element strides along rows and along k
   int rows, k;               // logical extent
   int kt, rt_pad;            // k tiles, row tiles (padded)
+  int vec;                   // 1: 16-byte loads along the unit-stride axis are aligned and never straddle an edge
 };
 
 // grid (kt, rt_pad, batches); 256 threads. Writes one 128x32 hi tile and one lo tile.
@@ -141,7 +142,23 @@ __global__ void __launch_bounds__(256) k_pack(PackDesc d, float* __restrict__ hi
   int tid = threadIdx.x;
   const float* src = d.src + d.batch_off[b];
   int r0 = rt * kBM, k0 = kt * kBK;
-  if (d.sk == 1) {
+  if (d.vec && d.sk == 1) {
+    for (int idx = tid; idx < kBM * (kBK / 4); idx += 256) {
+      int r = idx >> 3, k = (idx & 7) * 4;
+      int gr = r0 + r, gk = k0 + k;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gr < d.rows && gk < d.k) v = *reinterpret_cast<const float4*>(src + (int64_t)gr * d.sr + gk);
+      tile[r][k] = v.x; tile[r][k + 1] = v.y; tile[r][k + 2] = v.z; tile[r][k + 3] = v.w;
+    }
+  } else if (d.vec && d.sr == 1) {
+    for (int idx = tid; idx < (kBM / 4) * kBK; idx += 256) {
+      int r = (idx & 31) * 4, k = idx >> 5;
+      int gr = r0 + r, gk = k0 + k;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gr < d.rows && gk < d.k) v = *reinterpret_cast<const float4*>(src + gr + (int64_t)gk * d.sk);
+      tile[r][k] = v.x; tile[r + 1][k] = v.y; tile[r + 2][k] = v.z; tile[r + 3][k] = v.w;
+    }
+  } else if (d.sk == 1) {
     for (int idx = tid; idx < kBM * kBK; idx += 256) {
       int r = idx >> 5, k = idx & 31;
       int gr = r0 + r, gk = k0 + k;
@@ -189,6 +206,26 @@ struct GemmArgs {
   int k_elems;                           // logical K (for the work count only)
 };
 
+// Tile order: split-K slice, then batch, then a grouped raster over (m, n) — kGroupM row tiles walked first inside
+// each column band — so the ~148 tiles in flight at once share a few A row-blocks and B column-blocks in L2 instead
+// of each streaming its own operands from HBM.
+constexpr int kGroupM = 16;
+
+__device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& split, int& bt, int& mb, int& nb) {
+  int per_split = g.tiles_m * g.tiles_n * g.batches;
+  split = t / per_split;
+  int rem = t % per_split;
+  bt = rem / (g.tiles_m * g.tiles_n);
+  int r2 = rem % (g.tiles_m * g.tiles_n);
+  int span = kGroupM * g.tiles_n;
+  int group = r2 / span;
+  int first_m = group * kGroupM;
+  int gsize = min(g.tiles_m - first_m, kGroupM);
+  int within = r2 % span;
+  mb = first_m + within % gsize;
+  nb = within / gsize;
+}
+
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr int kA = kBM * kBK * 4;          // 16 KiB
@@ -234,10 +271,8 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(GemmArgs g) {
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
-        int split = t / tiles_per_split, rem = t % tiles_per_split;
-        int bt = rem / (g.tiles_m * g.tiles_n);
-        int r2 = rem % (g.tiles_m * g.tiles_n);
-        int nb = r2 / g.tiles_m, mb = r2 % g.tiles_m;  // m fastest: concurrent CTAs share the B tile
+        int split, bt, mb, nb;
+        tile_coords(g, t, split, bt, mb, nb);
         int ba = g.a_index[bt], bb = g.b_index[bt];
         int k0 = split * g.kt_per_split;
         int k1 = min(g.kt, k0 + g.kt_per_split);
@@ -300,10 +335,8 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(GemmArgs g) {
     const int row_in_tile = quad * 32 + lane;
     int local = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
-      int split = t / tiles_per_split, rem = t % tiles_per_split;
-      int bt = rem / (g.tiles_m * g.tiles_n);
-      int r2 = rem % (g.tiles_m * g.tiles_n);
-      int nb = r2 / g.tiles_m, mb = r2 % g.tiles_m;
+      int split, bt, mb, nb;
+      tile_coords(g, t, split, bt, mb, nb);
       int acc = local & 1;
       uint32_t acc_phase = (local >> 1) & 1;
       bool ok = mbar_wait(&acc_full[acc], acc_phase);
@@ -434,7 +467,14 @@ static pai_status pack_operand(pai_ctx* ctx, const float* base, const std::vecto
   PAI_TRY(scratch(ctx, floats * 4, lo));
   Scratch doff;
   PAI_TRY(upload(ctx, boffs.data(), boffs.size() * 8, &doff));
-  PackDesc d{base, static_cast<const int64_t*>(doff.p), sr, sk, rows, k, kt, rt_pad};
+  // 16-byte loads along the unit-stride axis: every batch matrix and row start 16-byte aligned, and the unit-stride
+  // extent a multiple of 4 so a vector never crosses the edge.
+  bool aligned = (reinterpret_cast<uintptr_t>(base) & 15) == 0;
+  for (int64_t o : boffs) aligned = aligned && (o % 4 == 0);
+  int vec = 0;
+  if (aligned && sk == 1 && sr % 4 == 0 && k % 4 == 0) vec = 1;
+  else if (aligned && sr == 1 && sk % 4 == 0 && rows % 4 == 0) vec = 1;
+  PackDesc d{base, static_cast<const int64_t*>(doff.p), sr, sk, rows, k, kt, rt_pad, vec};
   dim3 grid((unsigned)kt, (unsigned)rt_pad, (unsigned)boffs.size());
   k_pack<<<grid, 256, 0, ctx->stream>>>(d, static_cast<float*>(hi->p), static_cast<float*>(lo->p));
   PAI_LAUNCH_CHECK("gemm pack");

@@ -97,6 +97,25 @@ __global__ void k_rotary(const float* __restrict__ x, DView xv, const float* __r
   }
 }
 
+// Row-wise RoPE when the head dim is unit-stride in x, cos and sin: one warp per row, the row's offsets computed
+// once from the leading dims, the row itself read and written contiguously.
+__global__ void k_rotary_rows(const float* __restrict__ x, DView xr, const float* __restrict__ cs, DView cr,
+                              const float* __restrict__ sn, DView sr, float* __restrict__ y, int64_t rows, int d) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  int half = d >> 1;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    int64_t xo = dview_offset(xr, r), co = dview_offset(cr, r), so = dview_offset(sr, r);
+    float* yr = y + r * d;
+    for (int j = lane; j < half; j += 32) {
+      float x0 = x[xo + j], x1 = x[xo + j + half];
+      yr[j] = __fadd_rn(__fmul_rn(x0, cs[co + j]), __fmul_rn(-x1, sn[so + j]));
+      yr[j + half] = __fadd_rn(__fmul_rn(x1, cs[co + j + half]), __fmul_rn(x0, sn[so + j + half]));
+    }
+  }
+}
+
 // ---------------------------------------------------------------- SwiGLU gate
 __global__ void k_silu_mul_fwd(const float* __restrict__ gate, const float* __restrict__ up, float* __restrict__ o,
                                int64_t n) {
@@ -215,11 +234,20 @@ PAI_API pai_status pai_rotary(pai_ctx* ctx, const pai_tensor* x, const pai_tenso
     pai_tensor cb = broadcast_view(*cs, rank, x->dims), sb = broadcast_view(*sn, rank, x->dims);
     const pai_tensor* views[3] = {x, &cb, &sb};
     DView dv[3];
-    collapse(rank, x->dims, views, 3, dv);
-    int64_t pairs = n / 2;
-    k_rotary<<<grid_for(ctx, pairs, 256), 256, 0, ctx->stream>>>(static_cast<const float*>(x->base), dv[0],
-                                                               static_cast<const float*>(cs->base), dv[1],
-                                                               static_cast<const float*>(sn->base), dv[2], fptr(r), pairs, d);
+    bool unit_last = d == 1 || (x->strides[rank - 1] == 1 && cb.strides[rank - 1] == 1 && sb.strides[rank - 1] == 1);
+    if (unit_last) {
+      collapse(rank - 1, x->dims, views, 3, dv);  // leading (row) dims only
+      int64_t rows = n / d;
+      k_rotary_rows<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(
+          static_cast<const float*>(x->base), dv[0], static_cast<const float*>(cs->base), dv[1],
+          static_cast<const float*>(sn->base), dv[2], fptr(r), rows, d);
+    } else {
+      collapse(rank, x->dims, views, 3, dv);
+      int64_t pairs = n / 2;
+      k_rotary<<<grid_for(ctx, pairs, 256), 256, 0, ctx->stream>>>(static_cast<const float*>(x->base), dv[0],
+                                                                 static_cast<const float*>(cs->base), dv[1],
+                                                                 static_cast<const float*>(sn->base), dv[2], fptr(r), pairs, d);
+    }
     PAI_LAUNCH_CHECK("rotary");
   }
   *out = r;
