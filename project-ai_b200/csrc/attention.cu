@@ -351,9 +351,21 @@ constexpr size_t kFwdSmem = (size_t)(2 * kMaxD * kP + 2 * kT * kP) * 4;
 constexpr size_t kKvSmem = (size_t)(4 * kMaxD * kP + 4 * kT * kP + 2 * kT) * 4;
 constexpr size_t kQSmem = (size_t)(4 * kMaxD * kP + 2 * kT * kP + 2 * kT) * 4;
 
+// PAI_ATTN=simt selects the CUDA-core kernels (used to cross-check the tensor-core path).
+static bool attn_force_simt() {
+  static int v = [] {
+    const char* e = getenv("PAI_ATTN");
+    return (e && strcmp(e, "simt") == 0) ? 1 : 0;
+  }();
+  return v != 0;
+}
+
 }  // namespace pai
 
 using namespace pai;
+
+pai_status attn_tc_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int B, int H, int KVH,
+                       int S, int L, int D, float scale, int causal, int pos_offset, float* out, float* lse);
 
 PAI_API pai_status pai_sdpa_fwd(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v, float scale,
                                 int32_t causal, int32_t pos_offset, pai_tensor* out, pai_tensor* lse) {
@@ -371,10 +383,14 @@ PAI_API pai_status pai_sdpa_fwd(pai_ctx* ctx, const pai_tensor* q, const pai_ten
   if (numel(ro) > 0 && a.L > 0) {
     static bool attr = false;
     if (!attr) { cudaFuncSetAttribute(k_attn_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFwdSmem); attr = true; }
-    dim3 grid((unsigned)((a.S + kT - 1) / kT), (unsigned)a.H, (unsigned)a.B);
     KernelTimerScope timer(ctx, "attn_fwd", attn_fwd_flops(a));
-    k_attn_fwd<<<grid, 256, kFwdSmem, ctx->stream>>>(a, v4(*q), v4(*k), v4(*v), fptr(ro), fptr(rl));
-    PAI_LAUNCH_CHECK("sdpa_fwd");
+    if (!attn_force_simt()) {
+      PAI_TRY(attn_tc_fwd(ctx, *q, *k, *v, a.B, a.H, a.KVH, a.S, a.L, a.D, scale, causal, pos_offset, fptr(ro), fptr(rl)));
+    } else {
+      dim3 grid((unsigned)((a.S + kT - 1) / kT), (unsigned)a.H, (unsigned)a.B);
+      k_attn_fwd<<<grid, 256, kFwdSmem, ctx->stream>>>(a, v4(*q), v4(*k), v4(*v), fptr(ro), fptr(rl));
+      PAI_LAUNCH_CHECK("sdpa_fwd");
+    }
   }
   *out = ro;
   *lse = rl;

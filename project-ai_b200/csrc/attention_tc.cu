@@ -1,0 +1,336 @@
+// Tensor-core (tcgen05, 3xTF32) fused causal attention forward.
+//
+// Same contract and semantics as the CUDA-core kernel in attention.cu (the composed chain of Modules.cs:169-203):
+// scores = (q·scale)·kᵀ with q rounded to fp32 after scaling, keys j <= pos_offset + i, online softmax, ·v, output in
+// the merged-heads layout [B,S,H,D] plus the row log-sum-exp for the backward.
+//
+// Per CTA: 128 queries of one (batch, head), key blocks of 64, head dim padded to 64.
+//   pre-pass k_attn_pack: q·scale, k and vᵀ split into tf32 hi/lo and written as SWIZZLE_128B K-major tiles;
+//   warp 0      bulk-copies the Q tile once and K/Vᵀ blocks into a 2-stage ring;
+//   warp 1      allocates TMEM and issues S = Q·Kᵀ (3 MMAs per k-step, M=128 N=64) into a double-buffered TMEM S,
+//               then O_j = P_j·V_j with P read from TMEM as the A operand;
+//   warps 2-5   one thread per query row: reads its S row from TMEM, masks, online-softmax update, splits P into
+//               hi/lo and stores it to TMEM; accumulates O_j into registers with the running rescale.
+// Every wait is bounded; a timeout raises the context's device error flag and the CTA drains and exits.
+#include <math.h>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace pai {
+
+using namespace tc;
+
+constexpr int kQT = 128;  // queries per CTA
+constexpr int kKB = 64;   // keys per block
+constexpr int kDP = 64;   // padded head dim
+
+// ---------------------------------------------------------------- pack pre-pass
+struct AttnPackArgs {
+  const float* src;
+  int64_t s_b, s_x, s_r, s_d;  // element strides of the [B, X, R, D] view
+  int X, R, D;
+  int blk;        // sequence positions per packed tile (128 for Q, 64 for K/V)
+  int transpose;  // 0: tile rows = positions, cols = d;  1: tile rows = d, cols = positions
+  float scale;
+  int nblk;
+  float* out;
+};
+
+// grid (nblk, B*X). Output per tile: [hi kb0][hi kb1][lo kb0][lo kb1], kb = 32 columns, rows x 32 floats each.
+__global__ void __launch_bounds__(256) k_attn_pack(AttnPackArgs a) {
+  __shared__ float tile[kQT][kDP + 1];
+  int bi = blockIdx.x, bx = blockIdx.y;
+  int b = bx / a.X, x = bx % a.X;
+  const float* src = a.src + b * a.s_b + x * a.s_x;
+  int rows = a.transpose ? kDP : a.blk;
+  int p0 = bi * a.blk;
+  for (int idx = threadIdx.x; idx < a.blk * kDP; idx += blockDim.x) {
+    int pos = idx / kDP, d = idx % kDP;
+    float v = 0.0f;
+    if (p0 + pos < a.R && d < a.D) {
+      v = src[(int64_t)(p0 + pos) * a.s_r + (int64_t)d * a.s_d];
+      if (a.scale != 1.0f) v = __fmul_rn(v, a.scale);
+    }
+    if (a.transpose) tile[d][pos] = v;
+    else tile[pos][d] = v;
+  }
+  __syncthreads();
+  float* out = a.out + ((size_t)bx * a.nblk + bi) * (size_t)(4 * rows * 32);
+  for (int ch = threadIdx.x; ch < 2 * rows * 8; ch += blockDim.x) {
+    int kb = ch / (rows * 8), rem = ch % (rows * 8);
+    int r = rem >> 3, c = rem & 7;
+    float hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) split_tf32(tile[r][kb * 32 + c * 4 + j], hi[j], lo[j]);
+    int phys = r * 8 + (c ^ (r & 7));
+    reinterpret_cast<float4*>(out + (size_t)kb * rows * 32)[phys] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    reinterpret_cast<float4*>(out + (size_t)(2 + kb) * rows * 32)[phys] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+// ---------------------------------------------------------------- forward kernel
+struct AttnTcArgs {
+  const float* qp;  // [B*H][q_tiles][64 KB]
+  const float* kp;  // [B*KVH][k_blocks][32 KB]
+  const float* vp;  // [B*KVH][k_blocks][32 KB]  (vᵀ tiles)
+  float* out;       // [B,S,H,D]
+  float* lse;       // [B,H,S]
+  int B, H, KVH, S, L, D, pos_offset, causal, q_tiles, k_blocks;
+  int* error_flag;
+};
+
+constexpr uint32_t kQBytes = kQT * kDP * 4 * 2;        // 64 KB (hi + lo)
+constexpr uint32_t kKBytes = kKB * kDP * 4 * 2;        // 32 KB
+constexpr uint32_t kStageBytes = 2 * kKBytes;          // K + Vᵀ
+constexpr int kFwdSmemBytes = kQBytes + 2 * kStageBytes + 1024 + 256;
+// TMEM columns
+constexpr uint32_t kColS0 = 0, kColS1 = 64, kColPhi = 128, kColPlo = 192, kColPV = 256, kTmemCols = 512;
+
+__global__ void __launch_bounds__(192, 1) k_attn_fwd_tc(AttnTcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sStage = smem + kQBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kQBytes + 2 * kStageBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_full = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = a.q_tiles - 1 - (int)blockIdx.x;  // longest causal tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (a.H / a.KVH);
+  const int q0 = qt * kQT;
+  int kend = a.L;
+  if (a.causal) kend = min(a.L, a.pos_offset + q0 + kQT);
+  const int nblk = kend > 0 ? (kend + kKB - 1) / kKB : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_full, 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && nblk > 0) {
+      const float* qsrc = a.qp + ((size_t)(b * a.H + h) * a.q_tiles + qt) * (kQBytes / 4);
+      mbar_expect_tx(q_full, kQBytes);
+      bulk_g2s(sQ, qsrc, kQBytes, q_full);
+      for (int j = 0; j < nblk && !s_abort; j++) {
+        int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) { atomicExch(a.error_flag, 11); s_abort = 1; break; }
+        size_t off = ((size_t)(b * a.KVH + kvh) * a.k_blocks + j) * (kKBytes / 4);
+        uint8_t* dst = sStage + st * kStageBytes;
+        mbar_expect_tx(&kv_full[st], kStageBytes);
+        bulk_g2s(dst, a.kp + off, kKBytes, &kv_full[st]);
+        bulk_g2s(dst + kKBytes, a.vp + off, kKBytes, &kv_full[st]);
+      }
+      // drain: the last issued stages must land before the CTA exits
+      for (int j = nblk; j < nblk + 2; j++) mbar_wait(&kv_empty[j & 1], ((j >> 1) & 1) ^ 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nblk > 0) {
+      constexpr uint32_t idesc = idesc_tf32(128, 64);
+      const uint32_t q_hi = smem_u32(sQ), q_lo = q_hi + kQBytes / 2;
+      auto issue_s = [&](int j) {
+        int st = j & 1;
+        uint32_t k_hi = smem_u32(sStage + st * kStageBytes), k_lo = k_hi + kKBytes / 2;
+        uint32_t d = tmem + (st ? kColS1 : kColS0);
+#pragma unroll
+        for (int ks = 0; ks < kDP / 8; ks++) {
+          uint32_t qo = (ks >> 2) * (kQT * 128) + (ks & 3) * 32;  // Q kb stride 16 KB
+          uint32_t ko = (ks >> 2) * (kKB * 128) + (ks & 3) * 32;  // K kb stride 8 KB
+          mma_ss(d, desc_sw128(q_lo + qo), desc_sw128(k_hi + ko), idesc, ks > 0 ? 1u : 0u);
+          mma_ss(d, desc_sw128(q_hi + qo), desc_sw128(k_lo + ko), idesc, 1u);
+          mma_ss(d, desc_sw128(q_hi + qo), desc_sw128(k_hi + ko), idesc, 1u);
+        }
+        commit(&s_full[st]);
+      };
+      bool ok = mbar_wait(q_full, 0) && mbar_wait(&kv_full[0], 0);
+      if (!ok) { atomicExch(a.error_flag, 12); s_abort = 1; }
+      if (ok) {
+        fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; j < nblk && ok && !s_abort; j++) {
+        if (j + 1 < nblk) {
+          int st = (j + 1) & 1;
+          if (!mbar_wait(&kv_full[st], ((j + 1) >> 1) & 1) || !mbar_wait(&s_free[st], (((j + 1) >> 1) & 1) ^ 1)) {
+            atomicExch(a.error_flag, 13); s_abort = 1; break;
+          }
+          fence_after();
+          issue_s(j + 1);
+        }
+        if (!mbar_wait(p_full, j & 1)) { atomicExch(a.error_flag, 14); s_abort = 1; break; }
+        fence_after();
+        int st = j & 1;
+        uint32_t v_hi = smem_u32(sStage + st * kStageBytes + kKBytes), v_lo = v_hi + kKBytes / 2;
+        uint32_t d = tmem + kColPV;
+#pragma unroll
+        for (int ks = 0; ks < kKB / 8; ks++) {
+          uint32_t vo = (ks >> 2) * (kDP * 128) + (ks & 3) * 32;  // Vᵀ kb (32 keys) stride 8 KB
+          uint32_t pc = (uint32_t)(ks * 8);
+          mma_ts(d, tmem + kColPlo + pc, desc_sw128(v_hi + vo), idesc, ks > 0 ? 1u : 0u);
+          mma_ts(d, tmem + kColPhi + pc, desc_sw128(v_lo + vo), idesc, 1u);
+          mma_ts(d, tmem + kColPhi + pc, desc_sw128(v_hi + vo), idesc, 1u);
+        }
+        commit(pv_full);
+        commit(&kv_empty[st]);
+      }
+    }
+  } else {
+    // softmax / correction warps: thread = query row
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int qi = q0 + row;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    float o[kDP];
+#pragma unroll
+    for (int d = 0; d < kDP; d++) o[d] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = nblk > 0;
+    for (int j = 0; j < nblk && ok; j++) {
+      int st = j & 1;
+      if (!warp_wait(&s_full[st], (j >> 1) & 1)) { ok = false; break; }
+      fence_after();
+      float s[kKB];
+      tmem_ld32(tmem + lane_off + (st ? kColS1 : kColS0), s);
+      tmem_ld32(tmem + lane_off + (st ? kColS1 : kColS0) + 32, s + 32);
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[st]);
+      const int k0 = j * kKB;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kKB; c++) {
+        int kj = k0 + c;
+        bool vis = kj < a.L && (!a.causal || kj <= a.pos_offset + qi);
+        if (!vis) s[c] = -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      float mn = fmaxf(m, mx);
+      float alpha = (m == -INFINITY) ? 0.0f : expf(m - mn);
+      float sum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < kKB; c++) {
+        float p = (s[c] == -INFINITY) ? 0.0f : expf(s[c] - mn);
+        s[c] = p;
+        sum += p;
+      }
+      if (mn == -INFINITY) alpha = 1.0f;
+      l = l * alpha + sum;
+      m = mn;
+      if (j > 0) {
+        if (!warp_wait(pv_full, (j - 1) & 1)) { ok = false; break; }
+        fence_after();
+        float pv[32];
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+          tmem_ld32(tmem + lane_off + kColPV + half * 32, pv);
+#pragma unroll
+          for (int d = 0; d < 32; d++) o[half * 32 + d] += pv[d];
+        }
+      }
+#pragma unroll
+      for (int d = 0; d < kDP; d++) o[d] *= alpha;
+      // P_j -> TMEM as hi/lo (the A operand of P·V)
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+        float hi[32], lo[32];
+#pragma unroll
+        for (int c = 0; c < 32; c++) split_tf32(s[half * 32 + c], hi[c], lo[c]);
+        tmem_st32(tmem + lane_off + kColPhi + half * 32, hi);
+        tmem_st32(tmem + lane_off + kColPlo + half * 32, lo);
+      }
+      tmem_st_wait();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && nblk > 0) {
+      if (warp_wait(pv_full, (nblk - 1) & 1)) {
+        fence_after();
+        float pv[32];
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+          tmem_ld32(tmem + lane_off + kColPV + half * 32, pv);
+#pragma unroll
+          for (int d = 0; d < 32; d++) o[half * 32 + d] += pv[d];
+        }
+        if (qi < a.S) {
+          float inv = 1.0f / l;
+          float* orow = a.out + (((int64_t)b * a.S + qi) * a.H + h) * a.D;
+#pragma unroll
+          for (int d = 0; d < kDP; d++)
+            if (d < a.D) orow[d] = o[d] * inv;
+          a.lse[((int64_t)b * a.H + h) * a.S + qi] = m + logf(l);
+        }
+      } else {
+        ok = false;
+      }
+    }
+    if (!ok && nblk > 0 && lane == 0) { atomicExch(a.error_flag, 15); s_abort = 1; }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace pai
+
+using namespace pai;
+
+// Packs q (scaled), k and vᵀ and runs the tensor-core forward. Called by pai_sdpa_fwd for head dims <= 64.
+pai_status attn_tc_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int B, int H, int KVH,
+                       int S, int L, int D, float scale, int causal, int pos_offset, float* out, float* lse) {
+  int q_tiles = (S + kQT - 1) / kQT, k_blocks = (L + kKB - 1) / kKB;
+  Scratch qp, kp, vp;
+  PAI_TRY(scratch(ctx, (size_t)B * H * q_tiles * kQBytes, &qp));
+  PAI_TRY(scratch(ctx, (size_t)B * KVH * k_blocks * kKBytes, &kp));
+  PAI_TRY(scratch(ctx, (size_t)B * KVH * k_blocks * kKBytes, &vp));
+  auto pack = [&](const pai_tensor& t, int X, int R, int blk, int transpose, float sc, int nblk, void* dst) -> pai_status {
+    AttnPackArgs p{static_cast<const float*>(t.base) + t.offset, t.strides[0], t.strides[1], t.strides[2], t.strides[3],
+                   X, R, D, blk, transpose, sc, nblk, static_cast<float*>(dst)};
+    dim3 grid((unsigned)nblk, (unsigned)(B * X));
+    k_attn_pack<<<grid, 256, 0, ctx->stream>>>(p);
+    PAI_LAUNCH_CHECK("attention pack");
+    return PAI_OK;
+  };
+  PAI_TRY(pack(q, H, S, kQT, 0, scale, q_tiles, qp.p));
+  PAI_TRY(pack(k, KVH, L, kKB, 0, 1.0f, k_blocks, kp.p));
+  PAI_TRY(pack(v, KVH, L, kKB, 1, 1.0f, k_blocks, vp.p));
+  static bool attr = false;
+  if (!attr) {
+    PAI_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmemBytes));
+    attr = true;
+  }
+  AttnTcArgs args{static_cast<float*>(qp.p), static_cast<float*>(kp.p), static_cast<float*>(vp.p), out, lse,
+                  B, H, KVH, S, L, D, pos_offset, causal, q_tiles, k_blocks, ctx->d_error_flag};
+  dim3 grid((unsigned)q_tiles, (unsigned)H, (unsigned)B);
+  k_attn_fwd_tc<<<grid, 192, kFwdSmemBytes, ctx->stream>>>(args);
+  PAI_LAUNCH_CHECK("attention fwd (tcgen05)");
+  return PAI_OK;
+}
