@@ -9,8 +9,10 @@
 //   warp 0      bulk-copies the Q tile once and K/Vᵀ blocks into a 2-stage ring;
 //   warp 1      allocates TMEM and issues S = Q·Kᵀ (3 MMAs per k-step, M=128 N=64) into a double-buffered TMEM S,
 //               then O_j = P_j·V_j with P read from TMEM as the A operand;
-//   warps 2-5   one thread per query row: reads its S row from TMEM, masks, online-softmax update, splits P into
-//               hi/lo and stores it to TMEM; accumulates O_j into registers with the running rescale.
+//   warps 2-9   softmax: two warps per TMEM lane quadrant, so each query row is owned by two threads, each holding
+//               32 of the block's 64 scores (and 32 of the 64 output columns); the pair agrees on the running row
+//               max through shared memory. Each thread masks (diagonal blocks only), exponentiates, splits P into
+//               hi/lo and stores it to TMEM, and accumulates its half of O_j in registers with the running rescale.
 // Every wait is bounded; a timeout raises the context's device error flag and the CTA drains and exits.
 #include <math.h>
 
@@ -24,6 +26,8 @@ using namespace tc;
 constexpr int kQT = 128;  // queries per CTA
 constexpr int kKB = 64;   // keys per block
 constexpr int kDP = 64;   // padded head dim
+constexpr int kSoftmaxWarps = 8;
+constexpr int kFwdThreads = 64 + 32 * kSoftmaxWarps;
 
 // ---------------------------------------------------------------- pack pre-pass
 struct AttnPackArgs {
@@ -87,7 +91,11 @@ constexpr int kFwdSmemBytes = kQBytes + 2 * kStageBytes + 1024 + 256;
 // TMEM columns
 constexpr uint32_t kColS0 = 0, kColS1 = 64, kColPhi = 128, kColPlo = 192, kColPV = 256, kTmemCols = 512;
 
-__global__ void __launch_bounds__(192, 1) k_attn_fwd_tc(AttnTcArgs a) {
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -102,6 +110,8 @@ __global__ void __launch_bounds__(192, 1) k_attn_fwd_tc(AttnTcArgs a) {
   uint64_t* pv_full = bars + 10;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   __shared__ volatile int s_abort;
+  __shared__ float s_max[2][2][kQT];  // [block parity][column half][row]
+  __shared__ float s_l[2][kQT];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = a.q_tiles - 1 - (int)blockIdx.x;  // longest causal tiles first
@@ -118,9 +128,9 @@ __global__ void __launch_bounds__(192, 1) k_attn_fwd_tc(AttnTcArgs a) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
+      mbar_init(&s_free[i], kSoftmaxWarps);
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, kSoftmaxWarps);
     mbar_init(pv_full, 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -199,95 +209,115 @@ __global__ void __launch_bounds__(192, 1) k_attn_fwd_tc(AttnTcArgs a) {
       }
     }
   } else {
-    // softmax / correction warps: thread = query row
+    // softmax warps: (quad, half) -> query row quad*32+lane, columns [32*half, 32*half+32) of S, P and O
+    const int sw = warp - 2;
     const int quad = warp & 3;
+    const int half = sw >> 2;
     const int row = quad * 32 + lane;
     const int qi = q0 + row;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    float o[kDP];
+    const uint32_t col = (uint32_t)(32 * half);
+    const float kLog2e = 1.4426950408889634f;
+    float o[32];
 #pragma unroll
-    for (int d = 0; d < kDP; d++) o[d] = 0.0f;
+    for (int d = 0; d < 32; d++) o[d] = 0.0f;
     float m = -INFINITY, l = 0.0f;
+    // After a timed-out wait `ok` turns false: the warp skips all further TMEM and barrier work but still reaches
+    // every named barrier, so its partner warp never waits on it.
     bool ok = nblk > 0;
-    for (int j = 0; j < nblk && ok; j++) {
+    for (int j = 0; j < nblk; j++) {
       int st = j & 1;
-      if (!warp_wait(&s_full[st], (j >> 1) & 1)) { ok = false; break; }
-      fence_after();
-      float s[kKB];
-      tmem_ld32(tmem + lane_off + (st ? kColS1 : kColS0), s);
-      tmem_ld32(tmem + lane_off + (st ? kColS1 : kColS0) + 32, s + 32);
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[st]);
-      const int k0 = j * kKB;
-      float mx = -INFINITY;
+      float s[32];
 #pragma unroll
-      for (int c = 0; c < kKB; c++) {
-        int kj = k0 + c;
-        bool vis = kj < a.L && (!a.causal || kj <= a.pos_offset + qi);
-        if (!vis) s[c] = -INFINITY;
-        mx = fmaxf(mx, s[c]);
+      for (int c = 0; c < 32; c++) s[c] = 0.0f;
+      if (ok && !warp_wait(&s_full[st], (j >> 1) & 1)) ok = false;
+      if (ok) {
+        fence_after();
+        tmem_ld32(tmem + lane_off + (st ? kColS1 : kColS0) + col, s);
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[st]);
       }
+      const int k0 = j * kKB;
+      // Masking is needed only where the block crosses the causal diagonal or the end of the keys.
+      const bool need_mask = (k0 + kKB > a.L) || (a.causal && k0 + kKB - 1 > a.pos_offset + q0);
+      float mx = -INFINITY;
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < 32; c++) {
+          int kj = k0 + (int)col + c;
+          bool vis = kj < a.L && (!a.causal || kj <= a.pos_offset + qi);
+          if (!vis) s[c] = -INFINITY;
+          mx = fmaxf(mx, s[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; c++) mx = fmaxf(mx, s[c]);
+      }
+      // The row max over both halves: exchange through shared memory with the partner warp of this quadrant.
+      s_max[st][half][row] = mx;
+      named_sync(1 + quad, 64);
+      mx = fmaxf(mx, s_max[st][half ^ 1][row]);
       float mn = fmaxf(m, mx);
-      float alpha = (m == -INFINITY) ? 0.0f : expf(m - mn);
+      float alpha = (m == -INFINITY) ? 0.0f : __expf(m - mn);
+      if (mn == -INFINITY) alpha = 1.0f;
+      const float mn2 = mn * kLog2e;
       float sum = 0.0f;
 #pragma unroll
-      for (int c = 0; c < kKB; c++) {
-        float p = (s[c] == -INFINITY) ? 0.0f : expf(s[c] - mn);
+      for (int c = 0; c < 32; c++) {
+        float p = (s[c] == -INFINITY) ? 0.0f : exp2f(fmaf(s[c], kLog2e, -mn2));
         s[c] = p;
         sum += p;
       }
-      if (mn == -INFINITY) alpha = 1.0f;
       l = l * alpha + sum;
       m = mn;
-      if (j > 0) {
-        if (!warp_wait(pv_full, (j - 1) & 1)) { ok = false; break; }
-        fence_after();
-        float pv[32];
+      if (ok && j > 0) {
+        if (!warp_wait(pv_full, (j - 1) & 1)) {
+          ok = false;
+        } else {
+          fence_after();
+          float pv[32];
+          tmem_ld32(tmem + lane_off + kColPV + col, pv);
 #pragma unroll
-        for (int half = 0; half < 2; half++) {
-          tmem_ld32(tmem + lane_off + kColPV + half * 32, pv);
-#pragma unroll
-          for (int d = 0; d < 32; d++) o[half * 32 + d] += pv[d];
+          for (int d = 0; d < 32; d++) o[d] += pv[d];
         }
       }
 #pragma unroll
-      for (int d = 0; d < kDP; d++) o[d] *= alpha;
-      // P_j -> TMEM as hi/lo (the A operand of P·V)
-#pragma unroll
-      for (int half = 0; half < 2; half++) {
+      for (int d = 0; d < 32; d++) o[d] *= alpha;
+      if (ok) {
+        // P_j -> TMEM as hi/lo (the A operand of P·V)
         float hi[32], lo[32];
 #pragma unroll
-        for (int c = 0; c < 32; c++) split_tf32(s[half * 32 + c], hi[c], lo[c]);
-        tmem_st32(tmem + lane_off + kColPhi + half * 32, hi);
-        tmem_st32(tmem + lane_off + kColPlo + half * 32, lo);
+        for (int c = 0; c < 32; c++) split_tf32(s[c], hi[c], lo[c]);
+        tmem_st32(tmem + lane_off + kColPhi + col, hi);
+        tmem_st32(tmem + lane_off + kColPlo + col, lo);
+        tmem_st_wait();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
       }
-      tmem_st_wait();
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
     }
     if (ok && nblk > 0) {
       if (warp_wait(pv_full, (nblk - 1) & 1)) {
         fence_after();
         float pv[32];
+        tmem_ld32(tmem + lane_off + kColPV + col, pv);
 #pragma unroll
-        for (int half = 0; half < 2; half++) {
-          tmem_ld32(tmem + lane_off + kColPV + half * 32, pv);
-#pragma unroll
-          for (int d = 0; d < 32; d++) o[half * 32 + d] += pv[d];
-        }
-        if (qi < a.S) {
-          float inv = 1.0f / l;
-          float* orow = a.out + (((int64_t)b * a.S + qi) * a.H + h) * a.D;
-#pragma unroll
-          for (int d = 0; d < kDP; d++)
-            if (d < a.D) orow[d] = o[d] * inv;
-          a.lse[((int64_t)b * a.H + h) * a.S + qi] = m + logf(l);
-        }
+        for (int d = 0; d < 32; d++) o[d] += pv[d];
       } else {
         ok = false;
       }
+    }
+    s_l[half][row] = l;
+    named_sync(1 + quad, 64);
+    float lt = s_l[0][row] + s_l[1][row];
+    if (ok && nblk > 0 && qi < a.S) {
+      float inv = 1.0f / lt;
+      float* orow = a.out + (((int64_t)b * a.S + qi) * a.H + h) * a.D;
+#pragma unroll
+      for (int d = 0; d < 32; d++)
+        if ((int)col + d < a.D) orow[col + d] = o[d] * inv;
+      if (half == 0) a.lse[((int64_t)b * a.H + h) * a.S + qi] = m + logf(lt);
     }
     if (!ok && nblk > 0 && lane == 0) { atomicExch(a.error_flag, 15); s_abort = 1; }
   }
@@ -330,7 +360,7 @@ pai_status attn_tc_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   AttnTcArgs args{static_cast<float*>(qp.p), static_cast<float*>(kp.p), static_cast<float*>(vp.p), out, lse,
                   B, H, KVH, S, L, D, pos_offset, causal, q_tiles, k_blocks, ctx->d_error_flag};
   dim3 grid((unsigned)q_tiles, (unsigned)H, (unsigned)B);
-  k_attn_fwd_tc<<<grid, 192, kFwdSmemBytes, ctx->stream>>>(args);
+  k_attn_fwd_tc<<<grid, kFwdThreads, kFwdSmemBytes, ctx->stream>>>(args);
   PAI_LAUNCH_CHECK("attention fwd (tcgen05)");
   return PAI_OK;
 }
