@@ -366,6 +366,9 @@ using namespace pai;
 
 pai_status attn_tc_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int B, int H, int KVH,
                        int S, int L, int D, float scale, int causal, int pos_offset, float* out, float* lse);
+pai_status attn_tc_bwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, const pai_tensor& dout,
+                       const float* lse, const float* dvec, int B, int H, int KVH, int S, int L, int D, float scale,
+                       int causal, int pos_offset, float* dq, float* dk, float* dv);
 
 PAI_API pai_status pai_sdpa_fwd(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v, float scale,
                                 int32_t causal, int32_t pos_offset, pai_tensor* out, pai_tensor* lse) {
@@ -431,14 +434,19 @@ PAI_API pai_status pai_sdpa_bwd(pai_ctx* ctx, const pai_tensor* q, const pai_ten
     KernelTimerScope timer(ctx, "attn_bwd", 2.5 * attn_fwd_flops(a));
     k_attn_dot<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, ctx->stream>>>(a, v4(*dout), fptr(*out), static_cast<float*>(dvec.p));
     PAI_LAUNCH_CHECK("sdpa_bwd dot");
-    dim3 gkv((unsigned)((a.L + kT - 1) / kT), (unsigned)a.KVH, (unsigned)a.B);
-    k_attn_bwd_kv<<<gkv, 256, kKvSmem, ctx->stream>>>(a, v4(*q), v4(*k), v4(*v), v4(*dout), fptr(*lse),
-                                                      static_cast<float*>(dvec.p), fptr(rk), fptr(rv));
-    PAI_LAUNCH_CHECK("sdpa_bwd kv");
-    dim3 gq((unsigned)((a.S + kT - 1) / kT), (unsigned)a.H, (unsigned)a.B);
-    k_attn_bwd_q<<<gq, 256, kQSmem, ctx->stream>>>(a, v4(*q), v4(*k), v4(*v), v4(*dout), fptr(*lse),
-                                                   static_cast<float*>(dvec.p), fptr(rq));
-    PAI_LAUNCH_CHECK("sdpa_bwd q");
+    if (!attn_force_simt()) {
+      PAI_TRY(attn_tc_bwd(ctx, *q, *k, *v, *dout, fptr(*lse), static_cast<float*>(dvec.p), a.B, a.H, a.KVH, a.S, a.L, a.D,
+                          scale, causal, pos_offset, fptr(rq), fptr(rk), fptr(rv)));
+    } else {
+      dim3 gkv((unsigned)((a.L + kT - 1) / kT), (unsigned)a.KVH, (unsigned)a.B);
+      k_attn_bwd_kv<<<gkv, 256, kKvSmem, ctx->stream>>>(a, v4(*q), v4(*k), v4(*v), v4(*dout), fptr(*lse),
+                                                        static_cast<float*>(dvec.p), fptr(rk), fptr(rv));
+      PAI_LAUNCH_CHECK("sdpa_bwd kv");
+      dim3 gq((unsigned)((a.S + kT - 1) / kT), (unsigned)a.H, (unsigned)a.B);
+      k_attn_bwd_q<<<gq, 256, kQSmem, ctx->stream>>>(a, v4(*q), v4(*k), v4(*v), v4(*dout), fptr(*lse),
+                                                     static_cast<float*>(dvec.p), fptr(rq));
+      PAI_LAUNCH_CHECK("sdpa_bwd q");
+    }
   }
   *dq = rq;
   *dk = rk;

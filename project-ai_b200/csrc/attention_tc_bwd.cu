@@ -1,0 +1,525 @@
+// Tensor-core (tcgen05, 3xTF32) fused causal attention backward.
+//
+// The gradients of the composed chain of Modules.cs:169-203 under the Autograd rules (MatMul Autograd.cs:54-73,
+// Softmax :197-205, Mul by the 1/√d scale :39-47, GQA group sum ReduceGradToShape :320-333):
+//   P = exp(S − lse), dP = dO·Vᵀ, dS = P ⊙ (dP − rowsum(dO ⊙ O)),
+//   dV = Σ_group Pᵀ·dO,  dK = Σ_group dSᵀ·(q·scale),  dQ = scale · dS·K.
+//
+// Two kernels, 320 threads each (warp 0 bulk-copy producer, warp 1 MMA issuer, warps 2-9 element-wise — two warps
+// per TMEM lane quadrant, 32 of each 64-wide block's columns per thread):
+//   k_attn_bwd_kv_tc  128 keys of one (batch, kv head) stay resident (K, V as A operands in shared memory); the
+//                     group's heads x 64-query blocks stream through a 3-slot ring (q·scale, dO, dOᵀ, (q·scale)ᵀ);
+//                     Sᵀ and dPᵀ land in TMEM, Pᵀ / dSᵀ go back to TMEM as hi/lo A operands of dV += Pᵀ·dO and
+//                     dK += dSᵀ·(q·scale).
+//   k_attn_bwd_q_tc   128 queries of one (batch, head) stay resident (q·scale, dO); 64-key blocks stream through the
+//                     ring (K, V, Kᵀ); dS goes to TMEM as the A operand of dQ += dS·K.
+// All operands are 64-row SWIZZLE_128B hi/lo tiles from k_attn_pack; 128-row A operands are assembled in shared
+// memory from two 64-row tiles. Every wait is bounded (device error flag on timeout).
+#include <math.h>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace pai {
+
+using namespace tc;
+
+namespace bwd {
+
+constexpr int kRows = 128;               // resident rows per CTA (keys or queries)
+constexpr int kBlk = 64;                 // streamed block (queries or keys)
+constexpr int kDP = 64;                  // padded head dim
+constexpr uint32_t kTile = 64 * 64 * 4 * 2;   // one packed 64x64 hi/lo tile: 32 KB
+constexpr uint32_t kA = 2 * kTile;            // a resident 128-row operand: 64 KB
+constexpr int kSlots = 3;
+constexpr int kThreads = 320;
+constexpr int kSmem = 2 * kA + kSlots * kTile + 1024 + 256;
+constexpr uint32_t kTmemCols = 512;
+
+struct Args {
+  const float* qs;   // q·scale, 64-row tiles   [B*H][nq2][tile]
+  const float* dO;   // dO,      64-row tiles   [B*H][nq2][tile]
+  const float* qsT;  // (q·scale)ᵀ tiles        [B*H][nq][tile]
+  const float* dOT;  // dOᵀ tiles               [B*H][nq][tile]
+  const float* k;    // k, 64-row tiles         [B*KVH][nk2][tile]
+  const float* v;    // v, 64-row tiles         [B*KVH][nk2][tile]
+  const float* kT;   // kᵀ tiles                [B*KVH][nk][tile]
+  const float* lse;  // [B,H,S]
+  const float* dvec; // [B,H,S]  rowsum(dO ⊙ O)
+  float* dq;         // [B,H,S,D]
+  float* dk;         // [B,KVH,L,D]
+  float* dv;         // [B,KVH,L,D]
+  int B, H, KVH, S, L, D, pos_offset, causal;
+  int nq, nq2, nk, nk2;  // 64-blocks along S and L (nq2/nk2 rounded up to even)
+  float scale;
+  int* error_flag;
+};
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Resident 128-row operand from two consecutive 64-row packed tiles: smem (hl, kb) sub-tile = 16 KB, rows 64-127 at +8 KB.
+__device__ __forceinline__ void load_resident(uint8_t* dst, const float* tile0, uint64_t* bar) {
+#pragma unroll
+  for (int half = 0; half < 2; half++)
+#pragma unroll
+    for (int hk = 0; hk < 4; hk++)  // (hl, kb) in the packed order hi kb0, hi kb1, lo kb0, lo kb1
+      bulk_g2s(dst + hk * 16384 + half * 8192, tile0 + (size_t)half * (kTile / 4) + (size_t)hk * 2048, 8192, bar);
+}
+
+// S(+)= A(128-row resident, smem) · B(64-row tile, smem)ᵀ over the padded head dim.
+__device__ __forceinline__ void mma_res_tile(uint32_t d, uint32_t a, uint32_t bt, uint32_t idesc) {
+  const uint32_t a_lo = a + kA / 2, b_lo = bt + kTile / 2;
+#pragma unroll
+  for (int ks = 0; ks < kDP / 8; ks++) {
+    uint32_t ao = (ks >> 2) * 16384 + (ks & 3) * 32, bo = (ks >> 2) * 8192 + (ks & 3) * 32;
+    mma_ss(d, desc_sw128(a_lo + ao), desc_sw128(bt + bo), idesc, ks > 0 ? 1u : 0u);
+    mma_ss(d, desc_sw128(a + ao), desc_sw128(b_lo + bo), idesc, 1u);
+    mma_ss(d, desc_sw128(a + ao), desc_sw128(bt + bo), idesc, 1u);
+  }
+}
+
+// D(+)= A(TMEM hi/lo, 64 columns of K) · B(64-row tile over the same K)ᵀ
+__device__ __forceinline__ void mma_tmem_tile(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t bt, uint32_t idesc,
+                                              bool accumulate) {
+  const uint32_t b_lo = bt + kTile / 2;
+#pragma unroll
+  for (int ks = 0; ks < kBlk / 8; ks++) {
+    uint32_t bo = (ks >> 2) * 8192 + (ks & 3) * 32;
+    uint32_t c = (uint32_t)(ks * 8);
+    mma_ts(d, a_lo + c, desc_sw128(bt + bo), idesc, (accumulate || ks > 0) ? 1u : 0u);
+    mma_ts(d, a_hi + c, desc_sw128(b_lo + bo), idesc, 1u);
+    mma_ts(d, a_hi + c, desc_sw128(bt + bo), idesc, 1u);
+  }
+}
+
+// The dK/dV kernel's ring carries, per streamed block n, four tiles: 0 = q·scale, 1 = dO (read by the Sᵀ/dPᵀ
+// MMAs), 2 = dOᵀ, 3 = (q·scale)ᵀ (read by the dV/dK MMAs). The MMA warp consumes them in the order
+//   (0,Qs) (0,dO) | (1,Qs) (1,dO) (0,dOᵀ) (0,Qsᵀ) | (2,Qs) (2,dO) (1,dOᵀ) (1,Qsᵀ) | ... | (N-1,dOᵀ) (N-1,Qsᵀ)
+// (the next block's scores are issued before this block's gradient products), and the producer loads in exactly
+// that order, so a slot is always released before the load that reuses it is needed.
+__device__ __forceinline__ int kv_ring_pos(int n, int type, int N) {
+  if (type < 2) return (n == 0 ? 0 : 4 * n - 2) + type;
+  return (n < N - 1 ? 4 * n + 4 : 4 * n + 2) + (type - 2);
+}
+__device__ __forceinline__ void kv_ring_item(int i, int N, int& n, int& type) {
+  if (i < 2) { n = 0; type = i; return; }
+  int r = i - 2, it = r >> 2, w = r & 3;
+  if (it + 1 < N) {
+    if (w < 2) { n = it + 1; type = w; } else { n = it; type = w; }
+  } else {
+    n = it; type = 2 + w;
+  }
+}
+
+__device__ __forceinline__ void store_hilo(uint32_t hi_addr, uint32_t lo_addr, const float* x) {
+  float hi[32], lo[32];
+#pragma unroll
+  for (int c = 0; c < 32; c++) split_tf32(x[c], hi[c], lo[c]);
+  tmem_st32(hi_addr, hi);
+  tmem_st32(lo_addr, lo);
+}
+
+// ---------------------------------------------------------------- dK, dV
+__global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + kA;
+  uint8_t* sRing = smem + 2 * kA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * kA + kSlots * kTile);
+  uint64_t* a_full = bars;
+  uint64_t* ring_full = bars + 1;   // [3]
+  uint64_t* ring_empty = bars + 4;  // [3]
+  uint64_t* st_full = bars + 7;
+  uint64_t* st_free = bars + 8;
+  uint64_t* pd_full = bars + 9;
+  uint64_t* pd_free = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int g = a.H / a.KVH;
+  const int j0 = kt * kRows;
+  int qb_start = 0;
+  if (a.causal) {
+    int first = j0 - a.pos_offset;  // the first query that can see key j0
+    qb_start = first > 0 ? first / kBlk : 0;
+  }
+  const int qb_count = a.nq > qb_start ? a.nq - qb_start : 0;
+  const int N = g * qb_count;  // (head, query block) pairs streamed past these keys
+  // TMEM columns
+  const uint32_t cS = 0, cDP = 64, cPhi = 128, cPlo = 192, cDShi = 256, cDSlo = 320, cDV = 384, cDK = 448;
+
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    for (int i = 0; i < kSlots; i++) { mbar_init(&ring_full[i], 1); mbar_init(&ring_empty[i], 1); }
+    mbar_init(st_full, 1);
+    mbar_init(st_free, 8);
+    mbar_init(pd_full, 8);
+    mbar_init(pd_free, 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto head_of = [&](int n) { return kvh * g + n / max(qb_count, 1); };
+  auto qblk_of = [&](int n) { return qb_start + n % max(qb_count, 1); };
+
+  if (warp == 0) {
+    if (lane == 0 && N > 0) {
+      size_t kvbase = ((size_t)(b * a.KVH + kvh) * a.nk2 + 2 * kt) * (kTile / 4);
+      mbar_expect_tx(a_full, 2 * kA);
+      load_resident(sK, a.k + kvbase, a_full);
+      load_resident(sV, a.v + kvbase, a_full);
+      for (int t = 0; t < 4 * N && !s_abort; t++) {
+        int n, type;
+        kv_ring_item(t, N, n, type);
+        int slot = t % kSlots;
+        if (!mbar_wait(&ring_empty[slot], ((t / kSlots) & 1) ^ 1)) { atomicExch(a.error_flag, 21); s_abort = 1; break; }
+        int h = head_of(n), qb = qblk_of(n);
+        const float* src;
+        if (type == 0) src = a.qs + ((size_t)(b * a.H + h) * a.nq2 + qb) * (kTile / 4);
+        else if (type == 1) src = a.dO + ((size_t)(b * a.H + h) * a.nq2 + qb) * (kTile / 4);
+        else if (type == 2) src = a.dOT + ((size_t)(b * a.H + h) * a.nq + qb) * (kTile / 4);
+        else src = a.qsT + ((size_t)(b * a.H + h) * a.nq + qb) * (kTile / 4);
+        mbar_expect_tx(&ring_full[slot], kTile);
+        bulk_g2s(sRing + slot * kTile, src, kTile, &ring_full[slot]);
+      }
+      for (int t = 4 * N; t < 4 * N + kSlots; t++) mbar_wait(&ring_empty[t % kSlots], ((t / kSlots) & 1) ^ 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && N > 0) {
+      constexpr uint32_t idesc = idesc_tf32(128, 64);
+      const uint32_t k_s = smem_u32(sK), v_s = smem_u32(sV), ring = smem_u32(sRing);
+      bool ok = mbar_wait(a_full, 0);
+      auto issue_st = [&](int n) -> bool {
+        int t0 = kv_ring_pos(n, 0, N), t1 = kv_ring_pos(n, 1, N);
+        if (!mbar_wait(&ring_full[t0 % kSlots], (t0 / kSlots) & 1) || !mbar_wait(&ring_full[t1 % kSlots], (t1 / kSlots) & 1))
+          return false;
+        fence_after();
+        mma_res_tile(tmem + cS, k_s, ring + (t0 % kSlots) * kTile, idesc);   // Sᵀ  = K·(q·scale)ᵀ
+        mma_res_tile(tmem + cDP, v_s, ring + (t1 % kSlots) * kTile, idesc);  // dPᵀ = V·dOᵀ
+        commit(st_full);
+        commit(&ring_empty[t0 % kSlots]);
+        commit(&ring_empty[t1 % kSlots]);
+        return true;
+      };
+      if (ok) ok = issue_st(0);
+      for (int n = 0; n < N && ok && !s_abort; n++) {
+        if (n + 1 < N) {
+          if (!mbar_wait(st_free, n & 1)) { ok = false; break; }
+          fence_after();
+          if (!issue_st(n + 1)) { ok = false; break; }
+        }
+        int t2 = kv_ring_pos(n, 2, N), t3 = kv_ring_pos(n, 3, N);
+        if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[t2 % kSlots], (t2 / kSlots) & 1) ||
+            !mbar_wait(&ring_full[t3 % kSlots], (t3 / kSlots) & 1)) { ok = false; break; }
+        fence_after();
+        mma_tmem_tile(tmem + cDV, tmem + cPhi, tmem + cPlo, ring + (t2 % kSlots) * kTile, idesc, n > 0);    // dV += Pᵀ·dO
+        mma_tmem_tile(tmem + cDK, tmem + cDShi, tmem + cDSlo, ring + (t3 % kSlots) * kTile, idesc, n > 0);  // dK += dSᵀ·qs
+        commit(pd_free);
+        commit(&ring_empty[t2 % kSlots]);
+        commit(&ring_empty[t3 % kSlots]);
+      }
+      if (!ok) { atomicExch(a.error_flag, 22); s_abort = 1; }
+    }
+  } else {
+    const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
+    const int row = quad * 32 + lane;
+    const int key = j0 + row;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t col = (uint32_t)(32 * half);
+    const float kLog2e = 1.4426950408889634f;
+    bool ok = N > 0;
+    for (int n = 0; n < N; n++) {
+      const int h = head_of(n), q0 = qblk_of(n) * kBlk + (int)col;
+      float s[32], dp[32];
+#pragma unroll
+      for (int c = 0; c < 32; c++) { s[c] = 0.0f; dp[c] = 0.0f; }
+      if (ok && !warp_wait(st_full, n & 1)) ok = false;
+      if (ok) {
+        fence_after();
+        tmem_ld32(tmem + lane_off + cS + col, s);
+        tmem_ld32(tmem + lane_off + cDP + col, dp);
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(st_free);
+      }
+      const float* lse_row = a.lse + ((int64_t)b * a.H + h) * a.S;
+      const float* dv_row = a.dvec + ((int64_t)b * a.H + h) * a.S;
+#pragma unroll
+      for (int c = 0; c < 32; c++) {
+        int q = q0 + c;
+        bool vis = q < a.S && key < a.L && (!a.causal || key <= a.pos_offset + q);
+        float p = vis ? exp2f(fmaf(s[c], kLog2e, -lse_row[q] * kLog2e)) : 0.0f;
+        float dvq = vis ? dv_row[q] : 0.0f;
+        s[c] = p;
+        dp[c] = p * (dp[c] - dvq);
+      }
+      if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) ok = false;
+      if (ok) {
+        store_hilo(tmem + lane_off + cPhi + col, tmem + lane_off + cPlo + col, s);
+        store_hilo(tmem + lane_off + cDShi + col, tmem + lane_off + cDSlo + col, dp);
+        tmem_st_wait();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pd_full);
+      }
+    }
+    if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) ok = false;
+    if (ok && N > 0) {
+      fence_after();
+      float dvv[32], dkk[32];
+      tmem_ld32(tmem + lane_off + cDV + col, dvv);
+      tmem_ld32(tmem + lane_off + cDK + col, dkk);
+      if (key < a.L) {
+        int64_t base = (((int64_t)b * a.KVH + kvh) * a.L + key) * a.D;
+#pragma unroll
+        for (int d = 0; d < 32; d++)
+          if ((int)col + d < a.D) { a.dv[base + col + d] = dvv[d]; a.dk[base + col + d] = dkk[d]; }
+      }
+    }
+    if (!ok && N > 0 && lane == 0) { atomicExch(a.error_flag, 23); s_abort = 1; }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- dQ
+__global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sDO = smem + kA;
+  uint8_t* sRing = smem + 2 * kA;  // slot 0: K tile, 1: V tile, 2: Kᵀ tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * kA + kSlots * kTile);
+  uint64_t* a_full = bars;
+  uint64_t* ring_full = bars + 1;   // [3]
+  uint64_t* ring_empty = bars + 4;  // [3]
+  uint64_t* st_full = bars + 7;
+  uint64_t* st_free = bars + 8;
+  uint64_t* pd_full = bars + 9;
+  uint64_t* pd_free = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest causal tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (a.H / a.KVH);
+  const int q0 = qt * kRows;
+  int kend = a.L;
+  if (a.causal) kend = min(a.L, a.pos_offset + q0 + kRows);
+  const int N = kend > 0 ? (kend + kBlk - 1) / kBlk : 0;
+  const uint32_t cS = 0, cDP = 64, cDShi = 128, cDSlo = 192, cDQ = 256;
+
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    for (int i = 0; i < kSlots; i++) { mbar_init(&ring_full[i], 1); mbar_init(&ring_empty[i], 1); }
+    mbar_init(st_full, 1);
+    mbar_init(st_free, 8);
+    mbar_init(pd_full, 8);
+    mbar_init(pd_free, 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && N > 0) {
+      size_t qbase = ((size_t)(b * a.H + h) * a.nq2 + 2 * qt) * (kTile / 4);
+      mbar_expect_tx(a_full, 2 * kA);
+      load_resident(sQ, a.qs + qbase, a_full);
+      load_resident(sDO, a.dO + qbase, a_full);
+      for (int n = 0; n < N && !s_abort; n++) {
+        for (int type = 0; type < 3; type++) {
+          if (!mbar_wait(&ring_empty[type], (n & 1) ^ 1)) { atomicExch(a.error_flag, 31); s_abort = 1; break; }
+          const float* src;
+          if (type == 0) src = a.k + ((size_t)(b * a.KVH + kvh) * a.nk2 + n) * (kTile / 4);
+          else if (type == 1) src = a.v + ((size_t)(b * a.KVH + kvh) * a.nk2 + n) * (kTile / 4);
+          else src = a.kT + ((size_t)(b * a.KVH + kvh) * a.nk + n) * (kTile / 4);
+          mbar_expect_tx(&ring_full[type], kTile);
+          bulk_g2s(sRing + type * kTile, src, kTile, &ring_full[type]);
+        }
+      }
+      for (int type = 0; type < 3; type++) mbar_wait(&ring_empty[type], (N & 1) ^ 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && N > 0) {
+      constexpr uint32_t idesc = idesc_tf32(128, 64);
+      const uint32_t q_s = smem_u32(sQ), do_s = smem_u32(sDO), ring = smem_u32(sRing);
+      bool ok = mbar_wait(a_full, 0);
+      auto issue_st = [&](int n) -> bool {
+        if (!mbar_wait(&ring_full[0], n & 1) || !mbar_wait(&ring_full[1], n & 1)) return false;
+        fence_after();
+        mma_res_tile(tmem + cS, q_s, ring, idesc);            // S  = (q·scale)·Kᵀ
+        mma_res_tile(tmem + cDP, do_s, ring + kTile, idesc);  // dP = dO·Vᵀ
+        commit(st_full);
+        commit(&ring_empty[0]);
+        commit(&ring_empty[1]);
+        return true;
+      };
+      if (ok) ok = issue_st(0);
+      for (int n = 0; n < N && ok && !s_abort; n++) {
+        if (n + 1 < N) {
+          if (!mbar_wait(st_free, n & 1)) { ok = false; break; }
+          fence_after();
+          if (!issue_st(n + 1)) { ok = false; break; }
+        }
+        if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[2], n & 1)) { ok = false; break; }
+        fence_after();
+        mma_tmem_tile(tmem + cDQ, tmem + cDShi, tmem + cDSlo, ring + 2 * kTile, idesc, n > 0);  // dQ += dS·K
+        commit(pd_free);
+        commit(&ring_empty[2]);
+      }
+      if (!ok) { atomicExch(a.error_flag, 32); s_abort = 1; }
+    }
+  } else {
+    const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
+    const int row = quad * 32 + lane;
+    const int qi = q0 + row;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t col = (uint32_t)(32 * half);
+    const float kLog2e = 1.4426950408889634f;
+    const float lse2 = qi < a.S ? a.lse[((int64_t)b * a.H + h) * a.S + qi] * kLog2e : 0.0f;
+    const float dvq = qi < a.S ? a.dvec[((int64_t)b * a.H + h) * a.S + qi] : 0.0f;
+    bool ok = N > 0;
+    for (int n = 0; n < N; n++) {
+      float s[32], dp[32];
+#pragma unroll
+      for (int c = 0; c < 32; c++) { s[c] = 0.0f; dp[c] = 0.0f; }
+      if (ok && !warp_wait(st_full, n & 1)) ok = false;
+      if (ok) {
+        fence_after();
+        tmem_ld32(tmem + lane_off + cS + col, s);
+        tmem_ld32(tmem + lane_off + cDP + col, dp);
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(st_free);
+      }
+      const int k0 = n * kBlk + (int)col;
+#pragma unroll
+      for (int c = 0; c < 32; c++) {
+        int kj = k0 + c;
+        bool vis = qi < a.S && kj < a.L && (!a.causal || kj <= a.pos_offset + qi);
+        float p = vis ? exp2f(fmaf(s[c], kLog2e, -lse2)) : 0.0f;
+        dp[c] = p * (dp[c] - dvq);
+      }
+      if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) ok = false;
+      if (ok) {
+        store_hilo(tmem + lane_off + cDShi + col, tmem + lane_off + cDSlo + col, dp);
+        tmem_st_wait();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pd_full);
+      }
+    }
+    if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) ok = false;
+    if (ok && N > 0) {
+      fence_after();
+      float dq[32];
+      tmem_ld32(tmem + lane_off + cDQ + col, dq);
+      if (qi < a.S) {
+        int64_t base = (((int64_t)b * a.H + h) * a.S + qi) * a.D;
+#pragma unroll
+        for (int d = 0; d < 32; d++)
+          if ((int)col + d < a.D) a.dq[base + col + d] = dq[d] * a.scale;
+      }
+    }
+    if (!ok && N > 0 && lane == 0) { atomicExch(a.error_flag, 33); s_abort = 1; }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace bwd
+
+// k_attn_pack lives in attention_tc.cu
+struct AttnPackArgs {
+  const float* src;
+  int64_t s_b, s_x, s_r, s_d;
+  int X, R, D;
+  int blk;
+  int transpose;
+  float scale;
+  int nblk;
+  float* out;
+};
+__global__ void k_attn_pack(AttnPackArgs a);
+
+}  // namespace pai
+
+using namespace pai;
+
+// Backward on the tensor cores for head dims <= 64. dvec = rowsum(dO ⊙ O) [B,H,S] (already computed).
+pai_status attn_tc_bwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, const pai_tensor& dout,
+                       const float* lse, const float* dvec, int B, int H, int KVH, int S, int L, int D, float scale,
+                       int causal, int pos_offset, float* dq, float* dk, float* dv) {
+  using namespace bwd;
+  int nq = (S + kBlk - 1) / kBlk, nk = (L + kBlk - 1) / kBlk;
+  int nq2 = (nq + 1) & ~1, nk2 = (nk + 1) & ~1;
+  size_t tf = kTile;
+  Scratch qs, dO, qsT, dOT, kp, vp, kT;
+  PAI_TRY(scratch(ctx, (size_t)B * H * nq2 * tf, &qs));
+  PAI_TRY(scratch(ctx, (size_t)B * H * nq2 * tf, &dO));
+  PAI_TRY(scratch(ctx, (size_t)B * H * nq * tf, &qsT));
+  PAI_TRY(scratch(ctx, (size_t)B * H * nq * tf, &dOT));
+  PAI_TRY(scratch(ctx, (size_t)B * KVH * nk2 * tf, &kp));
+  PAI_TRY(scratch(ctx, (size_t)B * KVH * nk2 * tf, &vp));
+  PAI_TRY(scratch(ctx, (size_t)B * KVH * nk * tf, &kT));
+  // [B, X, R, D] view strides of each operand (dout is [B,S,H,D]: its head axis is 2, its row axis 1).
+  auto pack = [&](const float* base, int64_t sb, int64_t sx, int64_t sr, int64_t sd, int X, int R, int transpose,
+                  float sc, int nblk, void* dst) -> pai_status {
+    AttnPackArgs p{base, sb, sx, sr, sd, X, R, D, kBlk, transpose, sc, nblk, static_cast<float*>(dst)};
+    dim3 grid((unsigned)nblk, (unsigned)(B * X));
+    k_attn_pack<<<grid, 256, 0, ctx->stream>>>(p);
+    PAI_LAUNCH_CHECK("attention backward pack");
+    return PAI_OK;
+  };
+  const float* qb = static_cast<const float*>(q.base) + q.offset;
+  const float* kb = static_cast<const float*>(k.base) + k.offset;
+  const float* vb = static_cast<const float*>(v.base) + v.offset;
+  const float* ob = static_cast<const float*>(dout.base) + dout.offset;
+  PAI_TRY(pack(qb, q.strides[0], q.strides[1], q.strides[2], q.strides[3], H, S, 0, scale, nq2, qs.p));
+  PAI_TRY(pack(qb, q.strides[0], q.strides[1], q.strides[2], q.strides[3], H, S, 1, scale, nq, qsT.p));
+  PAI_TRY(pack(ob, dout.strides[0], dout.strides[2], dout.strides[1], dout.strides[3], H, S, 0, 1.0f, nq2, dO.p));
+  PAI_TRY(pack(ob, dout.strides[0], dout.strides[2], dout.strides[1], dout.strides[3], H, S, 1, 1.0f, nq, dOT.p));
+  PAI_TRY(pack(kb, k.strides[0], k.strides[1], k.strides[2], k.strides[3], KVH, L, 0, 1.0f, nk2, kp.p));
+  PAI_TRY(pack(kb, k.strides[0], k.strides[1], k.strides[2], k.strides[3], KVH, L, 1, 1.0f, nk, kT.p));
+  PAI_TRY(pack(vb, v.strides[0], v.strides[1], v.strides[2], v.strides[3], KVH, L, 0, 1.0f, nk2, vp.p));
+  static bool attr = false;
+  if (!attr) {
+    PAI_CUDA(cudaFuncSetAttribute(k_attn_bwd_kv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    PAI_CUDA(cudaFuncSetAttribute(k_attn_bwd_q_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    attr = true;
+  }
+  Args args{static_cast<float*>(qs.p), static_cast<float*>(dO.p), static_cast<float*>(qsT.p), static_cast<float*>(dOT.p),
+            static_cast<float*>(kp.p), static_cast<float*>(vp.p), static_cast<float*>(kT.p), lse, dvec, dq, dk, dv,
+            B, H, KVH, S, L, D, pos_offset, causal, nq, nq2, nk, nk2, scale, ctx->d_error_flag};
+  dim3 gkv((unsigned)((L + kRows - 1) / kRows), (unsigned)KVH, (unsigned)B);
+  k_attn_bwd_kv_tc<<<gkv, kThreads, kSmem, ctx->stream>>>(args);
+  PAI_LAUNCH_CHECK("attention bwd dK/dV (tcgen05)");
+  dim3 gq((unsigned)((S + kRows - 1) / kRows), (unsigned)H, (unsigned)B);
+  k_attn_bwd_q_tc<<<gq, kThreads, kSmem, ctx->stream>>>(args);
+  PAI_LAUNCH_CHECK("attention bwd dQ (tcgen05)");
+  return PAI_OK;
+}
