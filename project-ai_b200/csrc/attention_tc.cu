@@ -49,7 +49,27 @@ __global__ void __launch_bounds__(256) k_attn_pack(AttnPackArgs a) {
   const float* src = a.src + b * a.s_b + x * a.s_x;
   int rows = a.transpose ? kDP : a.blk;
   int p0 = bi * a.blk;
-  for (int idx = threadIdx.x; idx < a.blk * kDP; idx += blockDim.x) {
+  // 16-byte loads along the head dim when it is unit-stride, every row start is 16-byte aligned and D % 4 == 0.
+  bool vec = a.s_d == 1 && (a.D & 3) == 0 && (a.s_r & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+  if (vec) {
+    for (int idx = threadIdx.x; idx < a.blk * (kDP / 4); idx += blockDim.x) {
+      int pos = idx / (kDP / 4), d = (idx % (kDP / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (p0 + pos < a.R && d < a.D) {
+        v = *reinterpret_cast<const float4*>(src + (int64_t)(p0 + pos) * a.s_r + d);
+        if (a.scale != 1.0f) {
+          v.x = __fmul_rn(v.x, a.scale); v.y = __fmul_rn(v.y, a.scale);
+          v.z = __fmul_rn(v.z, a.scale); v.w = __fmul_rn(v.w, a.scale);
+        }
+      }
+      if (a.transpose) {
+        tile[d][pos] = v.x; tile[d + 1][pos] = v.y; tile[d + 2][pos] = v.z; tile[d + 3][pos] = v.w;
+      } else {
+        tile[pos][d] = v.x; tile[pos][d + 1] = v.y; tile[pos][d + 2] = v.z; tile[pos][d + 3] = v.w;
+      }
+    }
+  }
+  for (int idx = vec ? a.blk * kDP : threadIdx.x; idx < a.blk * kDP; idx += blockDim.x) {
     int pos = idx / kDP, d = idx % kDP;
     float v = 0.0f;
     if (p0 + pos < a.R && d < a.D) {

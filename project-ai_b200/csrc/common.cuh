@@ -166,6 +166,23 @@ __device__ __forceinline__ int64_t dview_offset32(const pai::DView& v, uint32_t 
   return off;
 }
 
+// Row r of up to three jointly collapsed views (same dims): one 32-bit coordinate decomposition, three offsets.
+__device__ __forceinline__ void row_offsets3(const pai::DView& a, const pai::DView& b, const pai::DView& c, uint32_t r,
+                                             int64_t& oa, int64_t& ob, int64_t& oc) {
+  oa = a.offset;
+  ob = b.offset;
+  oc = c.offset;
+  for (int d = a.rank - 1; d >= 0; d--) {
+    uint32_t dim = (uint32_t)a.dims[d];
+    uint32_t q = r / dim;
+    int64_t i = (int64_t)(r - q * dim);
+    oa += i * a.strides[d];
+    ob += i * b.strides[d];
+    oc += i * c.strides[d];
+    r = q;
+  }
+}
+
 // Internal launchers shared across translation units.
 namespace pai {
 // dst (dense, element offset dst_off in buffer dst_base) <- logical elements of src view.

@@ -280,6 +280,22 @@ __global__ void k_copy_strided(const float* __restrict__ src, pai::DView sv, flo
     dst[dview_offset(dv, i)] = src[dview_offset(sv, i)];
 }
 
+// Unit-stride rows of `len` elements (a permuted view whose last axis stays contiguous, e.g. the [b,s,h,d] view of a
+// [b,h,s,d] tensor): one warp per row, the row's offset from one 32-bit coordinate decomposition.
+__global__ void k_gather_rows_view(const float* __restrict__ src, pai::DView rv, float* __restrict__ dst, int64_t rows,
+                                   int len) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    int64_t off, o2, o3;
+    row_offsets3(rv, rv, rv, (uint32_t)r, off, o2, o3);
+    const float* s = src + off;
+    float* d = dst + r * len;
+    for (int j = lane; j < len; j += 32) d[j] = s[j];
+  }
+}
+
 pai_status gather_dense(pai_ctx* ctx, const pai_tensor& src, float* dst) {
   int64_t n = numel(src);
   if (n == 0) return PAI_OK;
@@ -291,7 +307,15 @@ pai_status gather_dense(pai_ctx* ctx, const pai_tensor& src, float* dst) {
   DView dv;
   collapse(src.rank, src.dims, v, 1, &dv);
   dv.offset = 0;
-  k_gather<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(fptr(src), dv, dst, n);
+  if (dv.rank >= 2 && dv.strides[dv.rank - 1] == 1 && dv.dims[dv.rank - 1] >= 32 && n < (1ll << 31)) {
+    int len = dv.dims[dv.rank - 1];
+    DView rv = dv;
+    rv.rank = dv.rank - 1;
+    int64_t rows = n / len;
+    k_gather_rows_view<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(fptr(src), rv, dst, rows, len);
+  } else {
+    k_gather<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(fptr(src), dv, dst, n);
+  }
   PAI_LAUNCH_CHECK("gather");
   return PAI_OK;
 }

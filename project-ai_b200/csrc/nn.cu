@@ -71,6 +71,66 @@ __global__ void k_rmsnorm_bwd(const float* __restrict__ x, const float* __restri
   }
 }
 
+// The same rule with each row held in registers (d = 128·C): one read of x and g, dx written once, and each lane
+// accumulating its own columns of dw across the rows its warp visits; partials reduced per block in shared memory.
+template <int C>
+__global__ void __launch_bounds__(256) k_rmsnorm_bwd_reg(const float* __restrict__ x, const float* __restrict__ w,
+                                                         const float* __restrict__ g, float* __restrict__ dx,
+                                                         float* __restrict__ dw_part, int64_t rows, float eps) {
+  extern __shared__ float s_dw[];  // [warps][d]
+  constexpr int d = 128 * C;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float4 wv[C], acc[C];
+#pragma unroll
+  for (int c = 0; c < C; c++) {
+    wv[c] = reinterpret_cast<const float4*>(w)[c * 32 + lane];
+    acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int64_t r = (int64_t)blockIdx.x * nw + wid; r < rows; r += (int64_t)gridDim.x * nw) {
+    const float4* px = reinterpret_cast<const float4*>(x + r * d);
+    const float4* pg = reinterpret_cast<const float4*>(g + r * d);
+    float4 xv[C], gv[C];
+    float ss = 0.0f;
+#pragma unroll
+    for (int c = 0; c < C; c++) {
+      xv[c] = px[c * 32 + lane];
+      gv[c] = pg[c * 32 + lane];
+      ss = fmaf(xv[c].x, xv[c].x, ss); ss = fmaf(xv[c].y, xv[c].y, ss);
+      ss = fmaf(xv[c].z, xv[c].z, ss); ss = fmaf(xv[c].w, xv[c].w, ss);
+    }
+    ss = warp_sum(ss);
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps)));
+    float dot = 0.0f;
+#pragma unroll
+    for (int c = 0; c < C; c++) {
+      dot = fmaf(gv[c].x, xv[c].x * inv * wv[c].x, dot); dot = fmaf(gv[c].y, xv[c].y * inv * wv[c].y, dot);
+      dot = fmaf(gv[c].z, xv[c].z * inv * wv[c].z, dot); dot = fmaf(gv[c].w, xv[c].w * inv * wv[c].w, dot);
+    }
+    dot = warp_sum(dot);
+    float coef = inv * inv / (float)d;
+    float4* pdx = reinterpret_cast<float4*>(dx + r * d);
+#pragma unroll
+    for (int c = 0; c < C; c++) {
+      float4 o;
+      o.x = (gv[c].x * wv[c].x) * inv - (coef * xv[c].x) * dot;
+      o.y = (gv[c].y * wv[c].y) * inv - (coef * xv[c].y) * dot;
+      o.z = (gv[c].z * wv[c].z) * inv - (coef * xv[c].z) * dot;
+      o.w = (gv[c].w * wv[c].w) * inv - (coef * xv[c].w) * dot;
+      pdx[c * 32 + lane] = o;
+      acc[c].x += gv[c].x * (xv[c].x * inv); acc[c].y += gv[c].y * (xv[c].y * inv);
+      acc[c].z += gv[c].z * (xv[c].z * inv); acc[c].w += gv[c].w * (xv[c].w * inv);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < C; c++) reinterpret_cast<float4*>(s_dw + (size_t)wid * d)[c * 32 + lane] = acc[c];
+  __syncthreads();
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    float s = 0.0f;
+    for (int k = 0; k < nw; k++) s += s_dw[(size_t)k * d + j];
+    dw_part[(size_t)blockIdx.x * d + j] = s;
+  }
+}
+
 // Deterministic column sum of [parts, d] partials.
 __global__ void k_colsum(const float* __restrict__ part, float* __restrict__ out, int parts, int d) {
   int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -106,7 +166,8 @@ __global__ void k_rotary_rows(const float* __restrict__ x, DView xr, const float
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   int half = d >> 1;
   for (int64_t r = warp; r < rows; r += nwarps) {
-    int64_t xo = dview_offset(xr, r), co = dview_offset(cr, r), so = dview_offset(sr, r);
+    int64_t xo, co, so;
+    row_offsets3(xr, cr, sr, (uint32_t)r, xo, co, so);
     float* yr = y + r * d;
     for (int j = lane; j < half; j += 32) {
       float x0 = x[xo + j], x1 = x[xo + j + half];
@@ -117,27 +178,52 @@ __global__ void k_rotary_rows(const float* __restrict__ x, DView xr, const float
 }
 
 // ---------------------------------------------------------------- SwiGLU gate
+__device__ __forceinline__ float silu_mul_elem(float gv, float u) {
+  float y = __fmul_rn(gv, sigmoid_dev(gv));
+  return __fmul_rn(y, u);
+}
+
+__device__ __forceinline__ void silu_mul_bwd_elem(float gv, float u, float go, float& dg, float& du) {
+  float s = sigmoid_dev(gv);
+  float y = __fmul_rn(gv, s);
+  float dsilu = __fmul_rn(go, u);                               // Mul rule: d(silu) = g·up
+  du = __fmul_rn(go, y);                                         //           d(up)   = g·silu
+  float deriv = __fsub_rn(__fadd_rn(s, y), __fmul_rn(s, y));      // Silu rule: s + y − s·y
+  dg = __fmul_rn(dsilu, deriv);
+}
+
+// n4 = number of float4 groups; the scalar tail [4*n4, n) is handled by the same grid.
 __global__ void k_silu_mul_fwd(const float* __restrict__ gate, const float* __restrict__ up, float* __restrict__ o,
-                               int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    float gv = gate[i];
-    float y = __fmul_rn(gv, sigmoid_dev(gv));
-    o[i] = __fmul_rn(y, up[i]);
+                               int64_t n, bool vec) {
+  int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t n4 = vec ? n >> 2 : 0;
+  for (int64_t i = tid; i < n4; i += stride) {
+    float4 g4 = reinterpret_cast<const float4*>(gate)[i], u4 = reinterpret_cast<const float4*>(up)[i];
+    reinterpret_cast<float4*>(o)[i] =
+        make_float4(silu_mul_elem(g4.x, u4.x), silu_mul_elem(g4.y, u4.y), silu_mul_elem(g4.z, u4.z), silu_mul_elem(g4.w, u4.w));
   }
+  for (int64_t i = (n4 << 2) + tid; i < n; i += stride) o[i] = silu_mul_elem(gate[i], up[i]);
 }
 
 __global__ void k_silu_mul_bwd(const float* __restrict__ gate, const float* __restrict__ up, const float* __restrict__ g,
-                               float* __restrict__ dgate, float* __restrict__ dup, int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    float gv = gate[i], u = up[i], go = g[i];
-    float s = sigmoid_dev(gv);
-    float y = __fmul_rn(gv, s);
-    float dsilu = __fmul_rn(go, u);                                   // Mul rule: d(silu) = g·up
-    dup[i] = __fmul_rn(go, y);                                         //           d(up)   = g·silu
-    float deriv = __fsub_rn(__fadd_rn(s, y), __fmul_rn(s, y));          // Silu rule: s + y − s·y
-    dgate[i] = __fmul_rn(dsilu, deriv);
+                               float* __restrict__ dgate, float* __restrict__ dup, int64_t n, bool vec) {
+  int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t n4 = vec ? n >> 2 : 0;
+  for (int64_t i = tid; i < n4; i += stride) {
+    float4 g4 = reinterpret_cast<const float4*>(gate)[i], u4 = reinterpret_cast<const float4*>(up)[i];
+    float4 o4 = reinterpret_cast<const float4*>(g)[i];
+    float4 dg, du;
+    silu_mul_bwd_elem(g4.x, u4.x, o4.x, dg.x, du.x);
+    silu_mul_bwd_elem(g4.y, u4.y, o4.y, dg.y, du.y);
+    silu_mul_bwd_elem(g4.z, u4.z, o4.z, dg.z, du.z);
+    silu_mul_bwd_elem(g4.w, u4.w, o4.w, dg.w, du.w);
+    reinterpret_cast<float4*>(dgate)[i] = dg;
+    reinterpret_cast<float4*>(dup)[i] = du;
   }
+  for (int64_t i = (n4 << 2) + tid; i < n; i += stride) silu_mul_bwd_elem(gate[i], up[i], g[i], dgate[i], dup[i]);
 }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace pai
 
@@ -189,6 +275,34 @@ PAI_API pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_
     PAI_TRY(dense_input(ctx, *x, &xp, &hx));
     PAI_TRY(dense_input(ctx, *w, &wp, &hw));
     PAI_TRY(dense_input(ctx, *g, &gp, &hg));
+    bool aligned = aligned16(xp) && aligned16(wp) && aligned16(gp) && aligned16(fptr(rdx));
+    int chunks = d % 128 == 0 ? d / 128 : 0;
+    if (aligned && (chunks == 1 || chunks == 2 || chunks == 4 || chunks == 6 || chunks == 8 || chunks == 16)) {
+      int blocks = (int)std::min<int64_t>(ctx->sm_count, (rows + 7) / 8);
+      size_t smem = (size_t)8 * d * 4;
+      PAI_TRY(scratch(ctx, (size_t)blocks * d * 4, &part));
+      float* pp = static_cast<float*>(part.p);
+#define RMS_REG(C)                                                                                              \
+  do {                                                                                                          \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k_rmsnorm_bwd_reg<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    k_rmsnorm_bwd_reg<C><<<blocks, 256, smem, ctx->stream>>>(xp, wp, gp, fptr(rdx), pp, rows, eps);            \
+  } while (0)
+      switch (chunks) {
+        case 1: RMS_REG(1); break;
+        case 2: RMS_REG(2); break;
+        case 4: RMS_REG(4); break;
+        case 6: RMS_REG(6); break;
+        case 8: RMS_REG(8); break;
+        default: RMS_REG(16); break;
+      }
+#undef RMS_REG
+      PAI_LAUNCH_CHECK("rmsnorm_bwd");
+      k_colsum<<<(d + 255) / 256, 256, 0, ctx->stream>>>(pp, fptr(rdw), blocks, d);
+      PAI_LAUNCH_CHECK("rmsnorm_bwd colsum");
+      *dx = rdx;
+      *dw = rdw;
+      return PAI_OK;
+    }
     int threads = 256, nw = threads / 32;
     size_t smem = (size_t)nw * d * 4;
     if (smem > 200 * 1024) { threads = 64; nw = 2; smem = (size_t)nw * d * 4; }
@@ -234,7 +348,8 @@ PAI_API pai_status pai_rotary(pai_ctx* ctx, const pai_tensor* x, const pai_tenso
     pai_tensor cb = broadcast_view(*cs, rank, x->dims), sb = broadcast_view(*sn, rank, x->dims);
     const pai_tensor* views[3] = {x, &cb, &sb};
     DView dv[3];
-    bool unit_last = d == 1 || (x->strides[rank - 1] == 1 && cb.strides[rank - 1] == 1 && sb.strides[rank - 1] == 1);
+    bool unit_last = (x->strides[rank - 1] == 1 && cb.strides[rank - 1] == 1 && sb.strides[rank - 1] == 1) &&
+                     n / d < (1ll << 31);
     if (unit_last) {
       collapse(rank - 1, x->dims, views, 3, dv);  // leading (row) dims only
       int64_t rows = n / d;
@@ -271,7 +386,8 @@ PAI_API pai_status pai_silu_mul_fwd(pai_ctx* ctx, const pai_tensor* gate, const 
     Scratch h1, h2;
     PAI_TRY(dense_input(ctx, *gate, &gp, &h1));
     PAI_TRY(dense_input(ctx, *up, &up_, &h2));
-    k_silu_mul_fwd<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(gp, up_, fptr(r), n);
+    bool vec = aligned16(gp) && aligned16(up_) && aligned16(fptr(r));
+    k_silu_mul_fwd<<<grid_for(ctx, n, 256, vec ? 4 : 1), 256, 0, ctx->stream>>>(gp, up_, fptr(r), n, vec);
     PAI_LAUNCH_CHECK("silu_mul_fwd");
   }
   *out = r;
@@ -296,7 +412,8 @@ PAI_API pai_status pai_silu_mul_bwd(pai_ctx* ctx, const pai_tensor* gate, const 
     PAI_TRY(dense_input(ctx, *gate, &gp, &h1));
     PAI_TRY(dense_input(ctx, *up, &up_, &h2));
     PAI_TRY(dense_input(ctx, *g, &gg, &h3));
-    k_silu_mul_bwd<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(gp, up_, gg, fptr(r1), fptr(r2), n);
+    bool vec = aligned16(gp) && aligned16(up_) && aligned16(gg) && aligned16(fptr(r1)) && aligned16(fptr(r2));
+    k_silu_mul_bwd<<<grid_for(ctx, n, 256, vec ? 4 : 1), 256, 0, ctx->stream>>>(gp, up_, gg, fptr(r1), fptr(r2), n, vec);
     PAI_LAUNCH_CHECK("silu_mul_bwd");
   }
   *dgate = r1;

@@ -68,6 +68,20 @@ __global__ void k_reduce_cols(const float* __restrict__ x, float* __restrict__ o
   }
 }
 
+// Short middle axis (len <= 64, e.g. the batch fold of a broadcast weight gradient): one thread per output column,
+// reading the axis sequentially — every load is coalesced across the warp.
+template <int K>
+__global__ void k_reduce_cols_short(const float* __restrict__ x, float* __restrict__ o, int64_t outer, int len, int64_t inner) {
+  int64_t total = outer * inner;
+  for (int64_t id = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; id < total; id += (int64_t)gridDim.x * blockDim.x) {
+    int64_t ob = id / inner, c = id - ob * inner;
+    const float* p = x + ob * (int64_t)len * inner + c;
+    float acc = K == kRMax ? -INFINITY : 0.0f;
+    for (int t = 0; t < len; t++) acc = red_combine<K>(acc, p[(int64_t)t * inner]);
+    o[id] = K == kRMean ? acc / (float)len : acc;
+  }
+}
+
 template <int K>
 static pai_status reduce(pai_ctx* ctx, const pai_tensor* x, int axis, int keep, pai_tensor* out) {
   PAI_TRY(enter(ctx));
@@ -107,6 +121,8 @@ static pai_status reduce(pai_ctx* ctx, const pai_tensor* x, int axis, int keep, 
         int threads = len >= 1024 ? 512 : (len >= 256 ? 256 : 128);
         int64_t blocks = outer < (int64_t)ctx->sm_count * 16 ? outer : (int64_t)ctx->sm_count * 16;
         k_reduce_rows<K><<<(int)blocks, threads, 0, ctx->stream>>>(src, fptr(r), outer, len);
+      } else if (len <= 64 || outer * inner >= (int64_t)ctx->sm_count * 2048) {
+        k_reduce_cols_short<K><<<grid_for(ctx, outer * inner, 256), 256, 0, ctx->stream>>>(src, fptr(r), outer, len, inner);
       } else {
         dim3 grid((unsigned)((inner + 31) / 32), (unsigned)(outer < 65535 ? outer : 65535));
         k_reduce_cols<K><<<grid, dim3(32, 8), 0, ctx->stream>>>(src, fptr(r), outer, len, inner);
