@@ -291,6 +291,16 @@ PYBIND11_MODULE(_paihost, m) {
                              py::return_value_policy::reference_internal)
       .def("set_constant_lr", [](PyTrainer& t, float lr) {
         t.trainer->optimizer->schedule = [lr](int) { return lr; };
+      })
+      .def_property("world", [](PyTrainer& t) { return t.trainer->world; },
+                    [](PyTrainer& t, int w) { t.trainer->world = w; })
+      // fn(list[Tensor]) must sum each tensor in place across ranks (called with the GIL held).
+      .def("set_allreduce", [](PyTrainer& t, py::function fn) {
+        t.trainer->allreduce = [fn](const std::vector<Tensor>& grads) {
+          py::gil_scoped_acquire gil;
+          fn(grads);
+        };
+        t.trainer->allreduce_wait = [] {};
       });
 
   py::class_<TopKTopPSampler>(m, "TopKTopPSampler")

@@ -450,6 +450,11 @@ class Trainer {
   TrainingConfig cfg;
   std::unique_ptr<AdamW> optimizer;
   Autograd ag;
+  // Data parallel: the number of ranks and the bucket exchange. Default: the backend's NCCL communicator
+  // (world = backend.dp_world); callers may substitute another sum-all-reduce (e.g. a CPU collective in tests).
+  int world = 0;  // 0: take the backend's dp_world
+  std::function<void(const std::vector<Tensor>&)> allreduce;
+  std::function<void()> allreduce_wait;
 
  private:
   NativeBackend* be_;

@@ -123,8 +123,14 @@ float Trainer::step(const std::vector<std::vector<float>>& inputs, const std::ve
 float Trainer::step_tensors(const std::vector<Tensor>& inputs, const std::vector<Tensor>& targets) {
   int micro_steps = std::max(1, (int)inputs.size());
   if ((int)targets.size() != micro_steps) throw ArgumentError("inputs and targets must hold the same number of micro-batches");
-  bool dp = be_->dp_world > 1;
-  optimizer->grad_scale = dp ? 1.0f / (float)be_->dp_world : 1.0f;
+  const int ranks = world > 0 ? world : be_->dp_world;
+  const bool dp = ranks > 1;
+  auto exchange = [this](const std::vector<Tensor>& g) {
+    if (g.empty()) return;
+    if (allreduce) allreduce(g);
+    else be_->allreduce(g);
+  };
+  optimizer->grad_scale = dp ? 1.0f / (float)ranks : 1.0f;
   optimizer->zero_grad();
   float inv_micro_v = 1.0f / (float)micro_steps;
   Tensor inv_micro = be_->from_host(&inv_micro_v, 1, {1});
@@ -134,7 +140,7 @@ float Trainer::step_tensors(const std::vector<Tensor>& inputs, const std::vector
     // Data parallel: each checkpointed block's gradients are final once its recompute ran; sum them across ranks
     // right away so the exchange overlaps the backward of the earlier blocks.
     if (dp && last && model->gradient_checkpointing) {
-      model->on_block_grads_ready = [this](int i) { be_->allreduce(grads_of(block_params_[(size_t)i])); };
+      model->on_block_grads_ready = [this, exchange](int i) { exchange(grads_of(block_params_[(size_t)i])); };
     } else {
       model->on_block_grads_ready = nullptr;
     }
@@ -161,11 +167,12 @@ float Trainer::step_tensors(const std::vector<Tensor>& inputs, const std::vector
   model->on_block_grads_ready = nullptr;
   if (dp) {
     if (model->gradient_checkpointing) {
-      be_->allreduce(grads_of(tail_params_));
+      exchange(grads_of(tail_params_));
     } else {
-      be_->allreduce(grads_of(params_));
+      exchange(grads_of(params_));
     }
-    be_->allreduce_wait();
+    if (allreduce_wait) allreduce_wait();
+    else if (!allreduce) be_->allreduce_wait();
   }
   optimizer->step();
   return step_loss;

@@ -1,0 +1,172 @@
+"""Data-parallel training step: ranks each take a slice of the batch, per-block gradient buckets are summed across
+ranks during the backward (checkpointed blocks) and the tail bucket after it, and AdamW divides by the world size.
+With equal token counts per rank this equals one full-batch step (Training.cs:81-104 semantics on the union batch).
+
+CPU tests run 2 gloo ranks over the oracle (the trainer's bucket logic with a host all-reduce); the GPU test runs
+2 NCCL ranks over the CUDA library when the machine has at least 2 GPUs. A failure test checks that a rank that dies
+before the exchange makes the surviving rank fail with an error instead of hanging.
+"""
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+TINY = dict(vocab_size=256, embedding_dim=128, layer_count=2, head_count=4, kv_head_count=4, ffn_hidden=344,
+            max_sequence_length=64)
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def full_batch():
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    r = H.PcgRng(7)
+    ids = np.array([r.next_u32() % 256 for _ in range(4 * 33)], np.float32).reshape(4, 33)
+    return np.ascontiguousarray(ids[:, :32]), np.ascontiguousarray(ids[:, 1:])
+
+
+def make_trainer(H, be, world):
+    m = H.LlamaModel(be, H.ModelConfig(**TINY), seed=0)
+    tc = H.TrainingConfig(batch_size=4 // world, sequence_length=32, learning_rate=1e-3, weight_decay=0.1, max_steps=10,
+                          gradient_checkpointing=True, warmup_steps=0)
+    tr = H.Trainer(be, m, tc, 0.9, 0.95)
+    tr.set_constant_lr(1e-3)
+    return m, tr
+
+
+def _gloo_rank(rank, world, port, out_dir, fail_rank):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(ROOT / "oracle" / "build" / "liboracle.so"), "oracle_", 0)
+    m, tr = make_trainer(H, be, world)
+    tr.world = world
+
+    def allreduce(grads):
+        for t in grads:
+            host = torch.from_numpy(be.to_host(t).copy())
+            dist.all_reduce(host)
+            be.copy(be.from_host(host.numpy()), t)
+
+    tr.set_allreduce(allreduce)
+    x, y = full_batch()
+    per = 4 // world
+    status = "ok"
+    try:
+        if rank == fail_rank:
+            raise RuntimeError("injected failure before the step")
+        tr.step([x[rank * per:(rank + 1) * per].copy()], [y[rank * per:(rank + 1) * per].copy()])
+    except Exception as e:  # a surviving rank must see its collective fail, not hang
+        status = "error: " + type(e).__name__
+    if status != "ok":
+        np.savez(out_dir / f"rank{rank}.npz", status=status)
+        return
+    np.savez(out_dir / f"rank{rank}.npz", status=status,
+             **{"p_" + n: be.to_host(p) for n, p in m.named_parameters()},
+             **{"g_" + n: be.to_host(p.grad) for n, p in m.named_parameters() if p.grad is not None})
+    if fail_rank < 0:
+        dist.destroy_process_group()
+
+
+def single_process_reference(lib, prefix):
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(lib), prefix, 0)
+    m, tr = make_trainer(H, be, 1)
+    x, y = full_batch()
+    tr.step([x], [y])
+    return ({n: be.to_host(p.grad) for n, p in m.named_parameters()}, {n: be.to_host(p) for n, p in m.named_parameters()})
+
+
+def test_gloo_two_ranks_match_full_batch(tmp_path):
+    port = free_port()
+    mp.spawn(_gloo_rank, args=(2, port, tmp_path, -1), nprocs=2, join=True)
+    ref_g, ref_p = single_process_reference(ROOT / "oracle" / "build" / "liboracle.so", "oracle_")
+    r0 = np.load(tmp_path / "rank0.npz")
+    r1 = np.load(tmp_path / "rank1.npz")
+    assert str(r0["status"]) == "ok" and str(r1["status"]) == "ok"
+    for n in ref_g:
+        # rank grads after the exchange are the sum over ranks; AdamW divides by the world size
+        np.testing.assert_array_equal(r0["g_" + n], r1["g_" + n])
+        np.testing.assert_allclose(r0["g_" + n] / 2, ref_g[n], rtol=1e-4, atol=1e-6 * np.abs(ref_g[n]).max() + 1e-9,
+                                   err_msg=n)
+        np.testing.assert_array_equal(r0["p_" + n], r1["p_" + n])  # replicas stay identical
+        # The first AdamW step moves each weight by lr·g/(|g|+eps); where g is at rounding-noise level its sign is
+        # decided by summation order, so those elements are bounded by 2·lr (as in test_model_parity).
+        noise = np.abs(ref_g[n]) < 1e-4 * np.abs(ref_g[n]).max()
+        err = np.abs(r0["p_" + n].astype(np.float64) - ref_p[n])
+        assert np.all(err[~noise] <= 1e-5 * np.abs(ref_p[n][~noise]) + 2e-6), n
+        assert np.all(err[noise] <= 2e-3 + 1e-6), n
+
+
+def test_dead_rank_fails_the_collective_instead_of_hanging(tmp_path):
+    port = free_port()
+    ctx = mp.start_processes(_gloo_rank, args=(2, port, tmp_path, 1), nprocs=2, join=False, start_method="spawn")
+    for p in ctx.processes:
+        p.join(120)
+        assert not p.is_alive(), "a rank hung"
+    r0 = np.load(tmp_path / "rank0.npz")
+    assert str(r0["status"]).startswith("error"), str(r0["status"])
+
+
+def _nccl_rank(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    pai = __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", rank)
+    uid = [be.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    be.nccl_init(uid[0], rank, world, 60000)
+    m, tr = make_trainer(H, be, world)
+    x, y = full_batch()
+    per = 4 // world
+    tr.step([x[rank * per:(rank + 1) * per].copy()], [y[rank * per:(rank + 1) * per].copy()])
+    np.savez(out_dir / f"rank{rank}.npz", **{"p_" + n: be.to_host(p) for n, p in m.named_parameters()},
+             **{"g_" + n: be.to_host(p.grad) for n, p in m.named_parameters()})
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_nccl_two_gpus_match_full_batch(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    port = free_port()
+    mp.spawn(_nccl_rank, args=(2, port, tmp_path), nprocs=2, join=True)
+    import __graft_entry__
+    pai = __graft_entry__.load_package()
+    ref_g, ref_p = single_process_reference(pai.CUDA_LIB_PATH, "pai_")
+    r0 = np.load(tmp_path / "rank0.npz")
+    r1 = np.load(tmp_path / "rank1.npz")
+    for n in ref_g:
+        np.testing.assert_array_equal(r0["g_" + n], r1["g_" + n])
+        np.testing.assert_allclose(r0["g_" + n] / 2, ref_g[n], rtol=1e-4, atol=1e-4 * np.abs(ref_g[n]).max(), err_msg=n)
+        np.testing.assert_array_equal(r0["p_" + n], r1["p_" + n])
