@@ -174,6 +174,17 @@ pai_status pai_adamw_step(pai_ctx* ctx, const pai_tensor* p, const pai_tensor* g
                           const pai_tensor* v, float lr, float beta1, float beta2, float eps, float weight_decay,
                           int32_t t, float grad_scale);
 
+/* RMSNorm backward that allocates nothing: no counterpart in the reference. It is for callers that cannot call
+ * cudaMalloc, such as a process that reserves all device memory for its own pools, or code that must avoid the
+ * synchronisation an allocation can cause. The caller passes dense F32 inputs and dense F32 outputs: dx shaped
+ * like x, dw shaped [d]. The per-block partial sums live in a fixed 4 MiB file-scope device array that every GPU
+ * loading the library holds until exit. The first call on a device resolves that array's address
+ * (cudaGetSymbolAddress), so make it before any stream capture. Calls share the array: calls that overlap on the
+ * GPU race, while calls ordered on one stream are safe. Rows longer than 8192 elements are rejected with
+ * PAI_ERR_OUT_OF_RANGE. Results match pai_rmsnorm_bwd. */
+pai_status pai_rmsnorm_bwd_noalloc(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* weight, const pai_tensor* g,
+                                   float eps, const pai_tensor* dx, const pai_tensor* dw);
+
 /* ==== Data parallel (one process per GPU; no counterpart in the single-device reference) ==== */
 pai_status pai_nccl_unique_id(uint8_t id_out[128]);
 pai_status pai_nccl_init(pai_ctx* ctx, const uint8_t id[128], int32_t rank, int32_t world_size, int32_t timeout_ms);

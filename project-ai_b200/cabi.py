@@ -136,6 +136,7 @@ _SIGS = {
     "allreduce_wait": [c_void_p],
     "nccl_abort": [c_void_p],
     "check_device_error": [c_void_p, _I32P],
+    "rmsnorm_bwd_noalloc": [c_void_p, T, T, T, c_float, T, T],
     "timer_start": [c_void_p],
     "timer_stop": [c_void_p, POINTER(c_float)],
     "launch_count": [c_void_p, POINTER(c_int64)],
