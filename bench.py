@@ -171,6 +171,61 @@ def cpu_baseline(cfg_name, sample_tokens, threads):
     return seq / dt, dt, seq
 
 
+def decode_bench(local, cfg_name="1b", prompt_len=512, gen=256, batches=(1, 32)):
+    """KV-cache decode on one GPU: the ~1B model with seeded N(0,0.02) weights, a prompt of `prompt_len` uniform
+    random ids per sequence, `gen` new tokens per sequence, greedy and top-k 40 / temperature 0.8 sampling.
+
+    tok/s follows the reference's bench (ProjectAI.Bench/BenchRunner.cs:110-122): generated tokens over the whole
+    generate call (prefill + decode steps + host sampling), after one untimed warm-up call; the call is timed with CUDA
+    events on the library's stream. decode_tok_s counts only the per-token steps after the prefill."""
+    c = CONFIGS[cfg_name]
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", local)
+    t0 = time.perf_counter()
+    m = H.LlamaModel(be, model_config(c, prompt_len + gen), seed=0, init="normal0.02")
+    init_s = time.perf_counter() - t0
+    out = {"metric": "decode tok/s", "unit": "tokens/s",
+           "config": {"workload": f"llama-{cfg_name} KV-cache decode", "prompt_len": prompt_len, "new_tokens": gen,
+                      "params": param_count(c), "weights": "N(0,0.02) seeded", "prompt": "uniform random ids (PcgRng 7)"},
+           "model_init_s": init_s}
+    for b in batches:
+        r = H.PcgRng(7)
+        prompt = [int(r.next_u32() % c["vocab_size"]) for _ in range(b * prompt_len)]
+        row = {}
+        for mode in ("greedy", "topk40_t0.8"):
+            sampler = None if mode == "greedy" else H.TopKTopPSampler(11, 0.8, 40, 1.0)
+            H.generate(be, m, prompt, 4, sampler, b)  # warm-up (the reference's r == 0 run)
+            be.timer_start()
+            res = H.generate(be, m, prompt, gen, sampler, b)
+            ms = be.timer_stop()
+            n = len(res["tokens"])
+            row[mode] = {"tok_s": n / (ms * 1e-3), "ms": ms, "generated": n, "prefill_ms": res["prefill_seconds"] * 1e3,
+                         "decode_tok_s": b * (n // b - 1) / max(res["decode_seconds"], 1e-9)}
+        out[f"batch{b}"] = row
+    # per-kernel device time of one greedy batch-1 generation: the weight-streaming GEMV is the dominant kernel
+    r = H.PcgRng(7)
+    prompt = [int(r.next_u32() % c["vocab_size"]) for _ in range(prompt_len)]
+    be.kernel_timing(True)
+    be.timer_start()
+    H.generate(be, m, prompt, 64, None, 1)
+    ms_timed = be.timer_stop()
+    stats = {f: be.kernel_stats(f) for f in ("gemv", "attn_decode", "gemm", "attn_fwd")}
+    be.kernel_timing(False)
+    g_launches, g_ms, g_bytes = stats["gemv"]
+    achieved = (g_bytes / max(g_launches, 1)) / ((g_ms / max(g_launches, 1)) * 1e-3) / 1e9 if g_ms else 0.0
+    out["roofline"] = {"bound": "hbm", "kernel": "k_gemv_tn (weight-streaming x·Wᵀ)", "achieved": achieved, "peak": hbm,
+                       "unit": "GB/s", "frac": achieved / hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
+                       "launches": g_launches, "avg_launch_ms": g_ms / max(g_launches, 1),
+                       "sample": "greedy batch 1, prompt 512 + 64 new tokens (prefill GEMMs excluded: family gemm)"}
+    out["kernels"] = {f: {"launches": v[0], "ms": v[1], "share": v[1] / ms_timed} for f, v in stats.items()}
+    out["weights_gb_per_token"] = 4.0 * param_count(c) / 1e9
+    out["hbm_ceiling_tok_s_batch1"] = hbm / (4.0 * param_count(c) / 1e9)
+    del m
+    be.sync()
+    return out
+
+
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -266,6 +321,34 @@ def op_sweep(args):
             be.scope_end()
             for t in (q, k, v, do):
                 be.release(t)
+    if args.op in ("all", "decode"):
+        # 1B decode: every weight shape of a layer plus the LM head, x·Wᵀ for 1 and 32 rows; enough weight copies are
+        # cycled that each timed call reads its W from HBM, not L2
+        for n, k in ((2048, 2048), (512, 2048), (5632, 2048), (2048, 5632), (32000, 2048)):
+            copies = max(1, -(-300_000_000 // (n * k * 4)))
+            ws = [randt(n, k) for _ in range(copies)]
+            for rows_ in (1, 32):
+                x = randt(rows_, k)
+                it = [0]
+
+                def call():
+                    it[0] = (it[0] + 1) % copies
+                    be.matmul(x, ws[it[0]], True)
+                reps = max(args.steps, 2 * copies)
+                emit("gemv x·Wᵀ", [rows_, k, n], timed(call, reps), 4.0 * (n * k + rows_ * (n + k)), "GB/s", hbm)
+                be.release(x)
+            for t in ws:
+                be.release(t)
+        for B in (1, 32):
+            Hh, KV, D, L = 32, 8, 64, 768
+            q = randt(B, Hh, 1, D)
+            kc, vc = randt(B, KV, L, D), randt(B, KV, L, D)
+            be.scope_begin()
+            ms = timed(lambda: be.sdpa_fwd(q, kc, vc, 0.125, True, L - 1), max(4, args.steps))
+            be.scope_end()
+            emit("decode attention (1 query, GQA 32/8)", [B, Hh, L, D], ms, 8.0 * B * KV * L * D, "GB/s", hbm)
+            for t in (q, kc, vc):
+                be.release(t)
     if args.op in ("all", "hbm"):
         x, w, g = randt(8192, 2048), randt(2048), randt(8192, 2048)
         cs, sn = randt(2048, 64), randt(2048, 64)
@@ -311,14 +394,20 @@ def main():
     ap.add_argument("--no-recompute", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=64)
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm"],
+    ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm", "decode"],
                     help="op-level sweep instead of the training step")
     ap.add_argument("--shape", default=None, help="M,K,N for --op gemm")
+    ap.add_argument("--skip-decode", action="store_true", help="leave the ~1B decode measurement out of the N=1 line")
+    ap.add_argument("--decode-only", action="store_true", help="print only the decode measurement")
+    ap.add_argument("--decode-tokens", type=int, default=256)
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
     if args.op:
         return op_sweep(args)
+    if args.decode_only:
+        print(json.dumps(decode_bench(0, gen=args.decode_tokens)), flush=True)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -437,8 +526,14 @@ def main():
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
                                     "sample": f"one training step of the {args.config} model at batch 1 x seq {seq} "
                                               f"({dt:.1f} s) on the CPU oracle"}
-        print(json.dumps(line), flush=True)
     del tr, m
+    if rank == 0:
+        if world == 1 and not args.skip_decode:
+            try:
+                line["decode"] = decode_bench(local, gen=args.decode_tokens)
+            except Exception as e:  # the training line still prints; the failure is reported in its place
+                line["decode"] = {"error": f"{type(e).__name__}: {e}"}
+        print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()

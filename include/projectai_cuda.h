@@ -185,6 +185,49 @@ pai_status pai_adamw_step(pai_ctx* ctx, const pai_tensor* p, const pai_tensor* g
 pai_status pai_rmsnorm_bwd_noalloc(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* weight, const pai_tensor* g,
                                    float eps, const pai_tensor* dx, const pai_tensor* dw);
 
+/* ==== KV-cache decode as a replayed CUDA graph (no counterpart in the reference) ====
+ * Consecutive decode steps (ProjectAI.Training/Inference.cs:46-56 feeding Modules.cs:142-204 and the cache of
+ * Modules.cs:290-370) differ only in their token ids and their position. These entry points are the decode-step ops
+ * with both read from device tensors, so one captured step replays for every later token: `ids` holds token ids
+ * and `pos` (one element) the position of the first new query row, both as integral F32 values written with
+ * pai_write before each replay. A value out of range cannot raise on the device: the kernel sets the device
+ * error flag (pai_check_device_error) and skips the work, and callers validate ids and positions on the host. */
+typedef struct pai_graph pai_graph;
+/* Host -> device copy into an existing dense tensor (stream-ordered; the host buffer may be reused on return). */
+pai_status pai_write(pai_ctx* ctx, const float* host, int64_t count, const pai_tensor* dst);
+/* Gather (IComputeBackend.cs:51-53) with ids from a device tensor: out = table rows ids, shape ids.shape + [d]. */
+pai_status pai_gather_dev(pai_ctx* ctx, const pai_tensor* table, const pai_tensor* ids, pai_tensor* out);
+/* RotaryEmbedding (IComputeBackend.cs:49) of x [..., S, d] at positions pos .. pos+S-1 of full [T, d] tables. */
+pai_status pai_rotary_at(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* cos_table, const pai_tensor* sin_table,
+                         const pai_tensor* pos, pai_tensor* out);
+/* Writes k, v [B, KVH, S, D] into positions pos .. pos+S-1 of the caches [B, KVH, T, D] (the KvCache append). */
+pai_status pai_kv_append(pai_ctx* ctx, const pai_tensor* k, const pai_tensor* v, const pai_tensor* k_cache,
+                         const pai_tensor* v_cache, const pai_tensor* pos);
+/* pai_rotary_at of q into q_out and of k into cache positions pos .. pos+S-1, with v copied there: the rotations and
+ * the cache append of one decode step in one launch (values identical to pai_rotary_at + pai_kv_append). */
+pai_status pai_rope_append(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v,
+                           const pai_tensor* cos_table, const pai_tensor* sin_table, const pai_tensor* k_cache,
+                           const pai_tensor* v_cache, const pai_tensor* pos, pai_tensor* q_out);
+/* Causal attention of q [B, H, S, D] (S * H / KVH <= 16, D <= 64) over cache positions 0 .. pos+S-1: out
+ * [B, S, H, D], the values of pai_sdpa_fwd with causal = 1, pos_offset = pos and the filled cache prefix. */
+pai_status pai_sdpa_decode(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k_cache, const pai_tensor* v_cache,
+                           const pai_tensor* pos, float scale, pai_tensor* out);
+/* Decode-step products of one activation x [..., k] (at most 32 rows, contiguous rows) with up to four weights
+ * W_i [n_i, k] (Linear.cs:10-43: y = x·Wᵀ), in one pass over the weights:
+ *   mode 0: out [..., Σ n_i] = the products side by side (the attention's q, k and v projections);
+ *   mode 1: out [..., n_0] = residual + x·W_0ᵀ (a Linear followed by TransformerBlock's residual Add, Modules.cs:222-246);
+ *   mode 2: out [..., n_0] = SiLU(x·W_0ᵀ) ⊙ (x·W_1ᵀ) (SwiGluFeedForward's gate and up, Modules.cs:84-109).
+ * The values are those of the separate MatMul / Add / SiluMul calls up to the summation order of the dot products. */
+pai_status pai_linear_fused(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* weights, int32_t n_weights, int32_t mode,
+                            const pai_tensor* residual, pai_tensor* out);
+/* Captures every op issued on the context between begin and end into one CUDA graph; no host upload or
+ * synchronising call may come in between. The device memory the captured ops use stays reserved for the graph
+ * until pai_graph_destroy, so tensors created during the capture hold each replay's results. */
+pai_status pai_graph_begin(pai_ctx* ctx);
+pai_status pai_graph_end(pai_ctx* ctx, pai_graph** graph);
+pai_status pai_graph_launch(pai_ctx* ctx, pai_graph* graph);
+pai_status pai_graph_destroy(pai_ctx* ctx, pai_graph* graph);
+
 /* ==== Data parallel (one process per GPU; no counterpart in the single-device reference) ==== */
 pai_status pai_nccl_unique_id(uint8_t id_out[128]);
 pai_status pai_nccl_init(pai_ctx* ctx, const uint8_t id[128], int32_t rank, int32_t world_size, int32_t timeout_ms);

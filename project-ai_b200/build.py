@@ -99,7 +99,7 @@ def build_host(verbose: bool = False) -> Path:
         return out
     BUILD.mkdir(exist_ok=True)
     py_inc = sysconfig.get_paths()["include"]
-    flags = ["-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-Wall", f"-I{INCLUDE}", f"-I{HOST}",
+    flags = ["-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-Wall", "-pthread", f"-I{INCLUDE}", f"-I{HOST}",
              f"-I{pybind11.get_include()}", f"-I{py_inc}"]
     jobs = []
     objs = []

@@ -360,6 +360,12 @@ static bool attn_force_simt() {
   return v != 0;
 }
 
+// attention_decode.cu
+bool attn_decode_fits(const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int H, int KVH, int S, int D);
+pai_status attn_decode_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int B, int H,
+                           int KVH, int S, int L, int D, float scale, int causal, int pos_offset, float* out, float* lse,
+                           const float* pos_dev = nullptr);
+
 }  // namespace pai
 
 using namespace pai;
@@ -383,7 +389,12 @@ PAI_API pai_status pai_sdpa_fwd(pai_ctx* ctx, const pai_tensor* q, const pai_ten
   pai_tensor ro, rl;
   PAI_TRY(alloc_tensor(ctx, 4, od, q->dtype, false, &ro));
   PAI_TRY(alloc_tensor(ctx, 3, ld, q->dtype, false, &rl));
-  if (numel(ro) > 0 && a.L > 0) {
+  if (numel(ro) > 0 && a.L > 0 && !attn_force_simt() && attn_decode_fits(*q, *k, *v, a.H, a.KVH, a.S, a.D)) {
+    // decode step: HBM-bound split-KV kernel (attention_decode.cu); work = K and V bytes read
+    int kend = causal ? std::min(a.L, pos_offset + a.S) : a.L;
+    KernelTimerScope timer(ctx, "attn_decode", 8.0 * a.B * a.KVH * (double)kend * a.D);
+    PAI_TRY(attn_decode_fwd(ctx, *q, *k, *v, a.B, a.H, a.KVH, a.S, a.L, a.D, scale, causal, pos_offset, fptr(ro), fptr(rl)));
+  } else if (numel(ro) > 0 && a.L > 0) {
     static bool attr = false;
     if (!attr) { cudaFuncSetAttribute(k_attn_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFwdSmem); attr = true; }
     KernelTimerScope timer(ctx, "attn_fwd", attn_fwd_flops(a));

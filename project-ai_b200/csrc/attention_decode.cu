@@ -1,0 +1,507 @@
+// Attention for decode steps: a few query positions (S x g query rows per kv head, at most 16) against a long KV
+// cache. Same result as the causal attention forward (Modules.cs:169-203: softmax(q·kᵀ·scale) · v, keys j visible
+// to query row s when j <= pos_offset + s), computed in exact fp32 arithmetic.
+//
+// Decode attention reads every cached key and value once per step and does ~2 flops per byte, so it is bound by
+// HBM, not by the tensor cores: one CTA per (batch, kv head, key split) holds all query rows of that kv head's
+// group, so each K/V row is read from HBM once for all g heads that share it.
+//   QKᵀ: lane j of a warp owns key j of the warp's 32-key tile and dots it (128-bit loads) with every query row
+//        (query rows broadcast from shared memory).
+//   softmax: online per query row with warp max / sum.
+//   PV:  lanes own two head-dim elements each; each key's probability is broadcast with a shuffle.
+// The 4 warps of a CTA and then the key splits are merged in a fixed order (log-sum-exp rescaling), so results are
+// deterministic.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace pai {
+
+namespace dec {
+
+constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxD = 64;
+constexpr int kMaxRows = 16;
+constexpr int kTile = 32;  // keys per warp step
+
+struct View {
+  const float* p;
+  int64_t s0, s1, s2;  // batch, head, position strides (head-dim stride is 1)
+};
+
+struct Args {
+  View q, k, v;          // q [B,H,S,D]; k, v [B,KVH,L,D]
+  int B, H, KVH, S, L, D, g, rows;
+  int pos_offset, causal;
+  float scale;
+  int splits, keys_per_split;
+  const float* pos_dev;  // when set: pos_offset = pos_dev[0] and the keys are cache positions 0 .. pos+S-1 (L = capacity)
+  int* error_flag;
+  int* counters;         // splits > 1: one arrival counter per (batch, kv head); the last CTA merges the splits
+  float* part;           // splits > 1: [B, KVH, splits, rows, D + 2] (acc..., m, l)
+  float* out;            // [B, S, H, D]
+  float* lse;            // [B, H, S]
+};
+
+__device__ __forceinline__ float wmax(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float wsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Writes one finished query row: out[b, s, h, :] and lse[b, h, s].
+__device__ __forceinline__ void store_row(const Args& a, int b, int kvh, int r, int d, float acc, float m, float l) {
+  int hg = r / a.S, s = r - hg * a.S, h = kvh * a.g + hg;
+  bool any = l > 0.0f;  // false only for a call whose position was rejected (device error flag set)
+  if (d < a.D) a.out[(((int64_t)b * a.S + s) * a.H + h) * a.D + d] = any ? acc / l : 0.0f;
+  if (d == 0) a.lse[((int64_t)b * a.H + h) * a.S + s] = any ? m + logf(l) : -INFINITY;
+}
+
+// Merges the key splits of query row r of (b, kvh) in split order (log-sum-exp rescaling) and stores it.
+__device__ __forceinline__ void combine_row(const Args& a, int b, int kvh, int r, int d) {
+  const float* base = a.part + (((int64_t)b * a.KVH + kvh) * a.splits * a.rows + r) * (a.D + 2);
+  const int64_t stride = (int64_t)a.rows * (a.D + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < a.splits; s++) M = fmaxf(M, __ldcg(base + s * stride + a.D));
+  float L = 0.0f, A = 0.0f;
+  for (int s = 0; s < a.splits; s++) {
+    const float* pr = base + s * stride;
+    float ms = __ldcg(pr + a.D);
+    if (ms == -INFINITY) continue;
+    float e = expf(ms - M);
+    L += __ldcg(pr + a.D + 1) * e;
+    if (d < a.D) A += __ldcg(pr + d) * e;
+  }
+  store_row(a, b, kvh, r, d, A, M, L);
+}
+
+// DC: the head dim when known at compile time (64), else 0 (read from the arguments).
+template <int R, int DC>
+__global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
+  const int D = DC ? DC : a.D;
+  __shared__ __align__(16) float qs[R][kMaxD];
+  __shared__ float wm[kWarps][R], wl[kWarps][R];
+  __shared__ float wacc[kWarps][R][kMaxD];
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = a.rows;
+
+  // query rows of this kv head's group, pre-scaled: row r = (head hg of the group, position s)
+  for (int t = threadIdx.x; t < R * kMaxD; t += kThreads) {
+    int r = t / kMaxD, d = t - r * kMaxD;
+    float val = 0.0f;
+    if (r < rows && d < a.D) {
+      int hg = r / a.S, s = r - hg * a.S, h = kvh * a.g + hg;
+      val = a.q.p[(int64_t)b * a.q.s0 + (int64_t)h * a.q.s1 + (int64_t)s * a.q.s2 + d] * a.scale;
+    }
+    qs[r][d] = val;
+  }
+  __syncthreads();
+
+  int pos_offset = a.pos_offset, kend = a.L;
+  if (a.pos_dev) {
+    float pf = a.pos_dev[0];
+    pos_offset = (int)pf;
+    if (!(pf >= 0.0f) || pos_offset + a.S > a.L) {  // outside the cache: flag it and attend to nothing
+      if (split == 0 && threadIdx.x == 0) atomicExch(a.error_flag, 63);
+      pos_offset = 0;
+      kend = 0;
+    }
+  }
+  if (a.causal) kend = min(kend, pos_offset + a.S);
+  const int j0 = split * a.keys_per_split;
+  const int j1 = min(kend, j0 + a.keys_per_split);
+  const float* kbase = a.k.p + (int64_t)b * a.k.s0 + (int64_t)kvh * a.k.s1;
+  const float* vbase = a.v.p + (int64_t)b * a.v.s0 + (int64_t)kvh * a.v.s1;
+  const int d0 = 2 * lane;  // this lane's head-dim pair in PV
+
+  float m[R], l[R], acc0[R], acc1[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) { m[r] = -INFINITY; l[r] = 0.0f; acc0[r] = 0.0f; acc1[r] = 0.0f; }
+
+  for (int t0 = j0 + warp * kTile; t0 < j1; t0 += kWarps * kTile) {
+    const int j = t0 + lane;
+    const bool in = j < j1;
+    const int nk = min(kTile, j1 - t0);
+    // this lane's head-dim pair of every V row of the tile, issued first so the loads overlap the QK step
+    float2 vv[kTile];
+#pragma unroll
+    for (int jj = 0; jj < kTile; jj++)
+      vv[jj] = (jj < nk && d0 < D) ? *reinterpret_cast<const float2*>(vbase + (int64_t)(t0 + jj) * a.v.s2 + d0)
+                                   : make_float2(0.f, 0.f);
+    float s[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) s[r] = 0.0f;
+    if (in) {
+      const float4* kr = reinterpret_cast<const float4*>(kbase + (int64_t)j * a.k.s2);
+#pragma unroll
+      for (int d4 = 0; d4 < (DC ? DC / 4 : kMaxD / 4); d4++) {
+        if (!DC && d4 >= (D >> 2)) break;
+        float4 kv = kr[d4];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          float4 qv = *reinterpret_cast<const float4*>(&qs[r][4 * d4]);
+          s[r] = fmaf(qv.x, kv.x, s[r]);
+          s[r] = fmaf(qv.y, kv.y, s[r]);
+          s[r] = fmaf(qv.z, kv.z, s[r]);
+          s[r] = fmaf(qv.w, kv.w, s[r]);
+        }
+      }
+    }
+    float p[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      bool vis = in && r < rows && (!a.causal || j <= pos_offset + (r % a.S));
+      float sv = vis ? s[r] : -INFINITY;
+      float mx = wmax(sv);
+      float mn = fmaxf(m[r], mx);
+      // mn stays -inf only for a row with no visible key so far; it then keeps its zero state
+      float alpha = (m[r] == -INFINITY) ? 0.0f : expf(m[r] - mn);
+      p[r] = vis ? expf(sv - mn) : 0.0f;
+      float rs = wsum(p[r]);
+      l[r] = l[r] * alpha + rs;
+      acc0[r] *= alpha;
+      acc1[r] *= alpha;
+      m[r] = mn;
+    }
+    // keys past the tile's end have p = 0 and zero V rows
+#pragma unroll
+    for (int jj = 0; jj < kTile; jj++) {
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        float pj = __shfl_sync(0xffffffffu, p[r], jj);
+        acc0[r] = fmaf(pj, vv[jj].x, acc0[r]);
+        acc1[r] = fmaf(pj, vv[jj].y, acc1[r]);
+      }
+    }
+  }
+
+  // merge the warps (fixed order)
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    if (lane == 0) { wm[warp][r] = m[r]; wl[warp][r] = l[r]; }
+    wacc[warp][r][d0] = acc0[r];
+    wacc[warp][r][d0 + 1] = acc1[r];
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < rows * kMaxD; t += kThreads) {
+    int r = t / kMaxD, d = t - r * kMaxD;
+    float M = -INFINITY;
+    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wm[w][r]);
+    float L = 0.0f, A = 0.0f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < kWarps; w++) {
+        float e = wm[w][r] == -INFINITY ? 0.0f : expf(wm[w][r] - M);
+        L += wl[w][r] * e;
+        A += wacc[w][r][d] * e;
+      }
+    }
+    if (a.splits == 1) {
+      store_row(a, b, kvh, r, d, A, M, L);
+    } else {
+      float* pr = a.part + ((((int64_t)b * a.KVH + kvh) * a.splits + split) * rows + r) * (a.D + 2);
+      if (d < a.D) pr[d] = A;
+      if (d == 0) { pr[a.D] = M; pr[a.D + 1] = L; }
+    }
+  }
+  if (a.splits == 1 || !a.counters) return;
+  // the last CTA of this (batch, kv head) to finish merges every split, then re-arms the counter
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[b * a.KVH + kvh], 1) == a.splits - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int t = threadIdx.x; t < rows * kMaxD; t += kThreads) combine_row(a, b, kvh, t / kMaxD, t % kMaxD);
+  if (threadIdx.x == 0) a.counters[b * a.KVH + kvh] = 0;
+}
+
+// Merges the key splits of one query row (fixed split order), for grids too large for the arrival counters.
+__global__ void __launch_bounds__(kMaxD) k_attn_decode_combine(const Args a) {
+  combine_row(a, blockIdx.z, blockIdx.y, blockIdx.x, threadIdx.x);
+}
+
+}  // namespace dec
+
+template <int DC>
+static void launch_decode(pai_ctx* ctx, const dec::Args& a, dim3 grid) {
+  int R = a.rows;
+  if (R <= 1) dec::k_attn_decode<1, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
+  else if (R <= 2) dec::k_attn_decode<2, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
+  else if (R <= 4) dec::k_attn_decode<4, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
+  else if (R <= 8) dec::k_attn_decode<8, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
+  else dec::k_attn_decode<16, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
+}
+
+static bool aligned_view(const pai_tensor& t, int vec) {
+  if (t.strides[3] != 1) return false;
+  if ((uintptr_t)t.base % 16) return false;
+  if (t.offset % vec) return false;
+  for (int i = 0; i < 3; i++)
+    if (t.dims[i] > 1 && t.strides[i] % vec) return false;
+  return true;
+}
+
+// True when the decode kernel handles this call: at most 16 query rows per kv head, head dim <= 64 (a multiple of
+// 4), and K/V views whose positions are 16-byte aligned rows.
+bool attn_decode_fits(const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int H, int KVH, int S, int D) {
+  int g = H / KVH;
+  if (g * S > dec::kMaxRows || D > dec::kMaxD || D % 4) return false;
+  return q.strides[3] == 1 && aligned_view(k, 4) && aligned_view(v, 2);
+}
+
+// pos_dev: when set, the query position is read on the device and k, v are the whole caches (L = capacity); the
+// key splits are then sized for the capacity and splits past the filled prefix contribute nothing.
+pai_status attn_decode_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int B, int H,
+                           int KVH, int S, int L, int D, float scale, int causal, int pos_offset, float* out, float* lse,
+                           const float* pos_dev) {
+  dec::Args a{};
+  a.pos_dev = pos_dev;
+  a.error_flag = ctx->d_error_flag;
+  auto view = [](const pai_tensor& t) {
+    return dec::View{static_cast<const float*>(t.base) + t.offset, t.strides[0], t.strides[1], t.strides[2]};
+  };
+  a.q = view(q); a.k = view(k); a.v = view(v);
+  a.B = B; a.H = H; a.KVH = KVH; a.S = S; a.L = L; a.D = D; a.g = H / KVH; a.rows = a.g * S;
+  a.pos_offset = pos_offset; a.causal = causal; a.scale = scale;
+  a.out = out; a.lse = lse;
+  int kend = (causal && !pos_dev) ? std::min(L, pos_offset + S) : L;
+  if (kend < 1) kend = 1;
+  // enough CTAs for two per SM, each split at least one 128-key sweep of the CTA's four warps
+  int64_t heads = (int64_t)B * KVH;
+  int max_splits = (kend + dec::kWarps * dec::kTile - 1) / (dec::kWarps * dec::kTile);
+  int splits = (int)std::min<int64_t>(max_splits, std::max<int64_t>(1, (2LL * ctx->sm_count + heads - 1) / heads));
+  int kps = (kend + splits - 1) / splits;
+  kps = (kps + dec::kTile - 1) / dec::kTile * dec::kTile;
+  splits = (kend + kps - 1) / kps;
+  a.splits = splits;
+  a.keys_per_split = kps;
+  Scratch part;
+  if (splits > 1) {
+    PAI_TRY(scratch(ctx, (size_t)heads * splits * a.rows * (D + 2) * 4, &part));
+    a.part = static_cast<float*>(part.p);
+    if (heads <= kCounters) a.counters = ctx->d_counters;  // merged by the last CTA, no second launch
+  }
+  dim3 grid((unsigned)splits, (unsigned)KVH, (unsigned)B);
+  if (D == 64) launch_decode<64>(ctx, a, grid);
+  else launch_decode<0>(ctx, a, grid);
+  PAI_LAUNCH_CHECK("attn decode");
+  if (splits > 1 && !a.counters) {
+    dec::k_attn_decode_combine<<<dim3((unsigned)a.rows, (unsigned)KVH, (unsigned)B), dec::kMaxD, 0, ctx->stream>>>(a);
+    PAI_LAUNCH_CHECK("attn decode combine");
+  }
+  return PAI_OK;
+}
+
+}  // namespace pai
+
+// ---------------------------------------------------------------- decode-step entry points (position on the device)
+namespace pai {
+
+// k [B, KVH, S, D] (any view) -> cache rows pos .. pos+S-1 of [B, KVH, T, D] (unit head-dim stride).
+__global__ void k_kv_append(const float* __restrict__ src, DView sv, float* __restrict__ dst, int64_t d0, int64_t d1,
+                            int64_t d2, int KVH, int S, int D, int T, const float* __restrict__ pos, int64_t n,
+                            int* error_flag) {
+  float pf = pos[0];
+  int p = (int)pf;
+  if (!(pf >= 0.0f) || p + S > T) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(error_flag, 64);
+    return;
+  }
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i;
+    int dd = (int)(r % D); r /= D;
+    int s = (int)(r % S); r /= S;
+    int h = (int)(r % KVH);
+    int b = (int)(r / KVH);
+    dst[(int64_t)b * d0 + (int64_t)h * d1 + (int64_t)(p + s) * d2 + dd] = src[dview_offset(sv, i)];
+  }
+}
+
+// One warp per row of q, k or v [B, heads, S, D] (unit head-dim stride): q rows are rotated into q_out [B, H, S, D],
+// k rows rotated into cache positions pos + s, v rows copied there. Rotation as k_rotary_rows (RotaryEmbedding,
+// CpuComputeBackend.cs:397-420): y[j] = x[j]·cos[j] − x[j+h]·sin[j], y[j+h] = x[j+h]·cos[j+h] + x[j]·sin[j+h].
+struct RopeAppendArgs {
+  const float* q; int64_t qs[3];
+  const float* k; int64_t ks[3];
+  const float* v; int64_t vs[3];
+  const float* cos; const float* sin; int64_t tab_stride; int tab_rows;
+  float* kc; float* vc; int64_t cs[3];  // caches [B, KVH, T, D]
+  float* q_out;
+  const float* pos;
+  int B, H, KVH, S, D, T;
+  int* error_flag;
+};
+
+__global__ void k_rope_append(const RopeAppendArgs a) {
+  float pf = a.pos[0];
+  int p = (int)pf;
+  if (!(pf >= 0.0f) || p + a.S > a.T || p + a.S > a.tab_rows) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(a.error_flag, 65);
+    return;
+  }
+  const int lane = threadIdx.x & 31, half = a.D >> 1;
+  const int64_t nq = (int64_t)a.B * a.H * a.S, nk = (int64_t)a.B * a.KVH * a.S;
+  int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t w = warp; w < nq + 2 * nk; w += nwarps) {
+    int which = w < nq ? 0 : (w < nq + nk ? 1 : 2);
+    int64_t i = which == 0 ? w : (which == 1 ? w - nq : w - nq - nk);
+    int heads = which == 0 ? a.H : a.KVH;
+    int s = (int)(i % a.S), h = (int)((i / a.S) % heads), b = (int)(i / ((int64_t)a.S * heads));
+    const float* src;
+    float* dst;
+    if (which == 0) {
+      src = a.q + b * a.qs[0] + h * a.qs[1] + s * a.qs[2];
+      dst = a.q_out + i * a.D;
+    } else if (which == 1) {
+      src = a.k + b * a.ks[0] + h * a.ks[1] + s * a.ks[2];
+      dst = a.kc + b * a.cs[0] + h * a.cs[1] + (int64_t)(p + s) * a.cs[2];
+    } else {
+      src = a.v + b * a.vs[0] + h * a.vs[1] + s * a.vs[2];
+      dst = a.vc + b * a.cs[0] + h * a.cs[1] + (int64_t)(p + s) * a.cs[2];
+    }
+    if (which == 2) {
+      for (int j = lane; j < a.D; j += 32) dst[j] = src[j];
+      continue;
+    }
+    const float* cr = a.cos + (int64_t)(p + s) * a.tab_stride;
+    const float* sr = a.sin + (int64_t)(p + s) * a.tab_stride;
+    for (int j = lane; j < half; j += 32) {
+      float x0 = src[j], x1 = src[j + half];
+      dst[j] = __fadd_rn(__fmul_rn(x0, cr[j]), __fmul_rn(-x1, sr[j]));
+      dst[j + half] = __fadd_rn(__fmul_rn(x1, cr[j + half]), __fmul_rn(x0, sr[j + half]));
+    }
+  }
+}
+
+static pai_status check_cache(pai_ctx* ctx, const pai_tensor* c, const pai_tensor* x, const char* what) {
+  PAI_TRY(check_view(ctx, c, what));
+  if (c->rank != 4 || c->dims[0] != x->dims[0] || c->dims[1] != x->dims[1] || c->dims[3] != x->dims[3] ||
+      c->strides[3] != 1)
+    return set_error(PAI_ERR_ARGUMENT, "%s: cache %s does not fit %s (unit head-dim stride required)", what,
+                     shape_str(*c).c_str(), shape_str(*x).c_str());
+  return PAI_OK;
+}
+
+}  // namespace pai
+
+using namespace pai;
+
+PAI_API pai_status pai_kv_append(pai_ctx* ctx, const pai_tensor* k, const pai_tensor* v, const pai_tensor* k_cache,
+                                 const pai_tensor* v_cache, const pai_tensor* pos) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, k, "k"));
+  PAI_TRY(check_view(ctx, v, "v"));
+  PAI_TRY(check_view(ctx, pos, "pos"));
+  if (k->rank != 4 || v->rank != 4 || numel(*pos) != 1)
+    return set_error(PAI_ERR_ARGUMENT, "KvAppend: k, v [B, KVH, S, D] and a one-element position expected");
+  for (int i = 0; i < 4; i++)
+    if (k->dims[i] != v->dims[i]) return set_error(PAI_ERR_ARGUMENT, "KvAppend: k and v shapes differ");
+  PAI_TRY(check_cache(ctx, k_cache, k, "k_cache"));
+  PAI_TRY(check_cache(ctx, v_cache, v, "v_cache"));
+  if (k_cache->dims[2] != v_cache->dims[2] || k->dims[2] > k_cache->dims[2])
+    return set_error(PAI_ERR_ARGUMENT, "KvAppend: caches of %d / %d positions for %d new ones", k_cache->dims[2],
+                     v_cache->dims[2], k->dims[2]);
+  int64_t n = numel(*k);
+  if (n == 0) return PAI_OK;
+  const pai_tensor* pair[2][2] = {{k, k_cache}, {v, v_cache}};
+  for (auto& pr : pair) {
+    const pai_tensor* src = pr[0];
+    const pai_tensor* dst = pr[1];
+    const pai_tensor* sv1[1] = {src};
+    DView sv;
+    collapse(src->rank, src->dims, sv1, 1, &sv);
+    sv.offset = 0;
+    k_kv_append<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(fptr(*src), sv, fptr(*dst), dst->strides[0], dst->strides[1],
+                                                               dst->strides[2], src->dims[1], src->dims[2], src->dims[3],
+                                                               dst->dims[2], fptr(*pos), n, ctx->d_error_flag);
+    PAI_LAUNCH_CHECK("kv append");
+  }
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_sdpa_decode(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k_cache, const pai_tensor* v_cache,
+                                   const pai_tensor* pos, float scale, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, q, "q"));
+  PAI_TRY(check_view(ctx, k_cache, "k_cache"));
+  PAI_TRY(check_view(ctx, v_cache, "v_cache"));
+  PAI_TRY(check_view(ctx, pos, "pos"));
+  if (q->rank != 4 || k_cache->rank != 4 || v_cache->rank != 4 || numel(*pos) != 1)
+    return set_error(PAI_ERR_ARGUMENT, "SdpaDecode: q [B,H,S,D], caches [B,KVH,T,D] and a one-element position expected");
+  int B = q->dims[0], H = q->dims[1], S = q->dims[2], D = q->dims[3];
+  int KVH = k_cache->dims[1], T = k_cache->dims[2];
+  for (int i = 0; i < 4; i++)
+    if (k_cache->dims[i] != v_cache->dims[i]) return set_error(PAI_ERR_ARGUMENT, "SdpaDecode: k and v caches differ");
+  if (k_cache->dims[0] != B || k_cache->dims[3] != D || KVH < 1 || H % KVH)
+    return set_error(PAI_ERR_ARGUMENT, "SdpaDecode: q %s does not fit the cache %s", shape_str(*q).c_str(),
+                     shape_str(*k_cache).c_str());
+  if (!attn_decode_fits(*q, *k_cache, *v_cache, H, KVH, S, D))
+    return set_error(PAI_ERR_UNSUPPORTED, "SdpaDecode: needs S*H/KVH <= 16, head dim <= 64 (multiple of 4) and aligned caches");
+  int32_t od[4] = {B, S, H, D};
+  pai_tensor ro;
+  PAI_TRY(alloc_tensor(ctx, 4, od, q->dtype, false, &ro));
+  Scratch lse;
+  PAI_TRY(scratch(ctx, (size_t)B * H * S * 4, &lse));
+  if (numel(ro) > 0) {
+    KernelTimerScope timer(ctx, "attn_decode", 8.0 * B * KVH * (double)T * D);
+    PAI_TRY(attn_decode_fwd(ctx, *q, *k_cache, *v_cache, B, H, KVH, S, T, D, scale, 1, 0, fptr(ro),
+                            static_cast<float*>(lse.p), fptr(*pos)));
+  }
+  *out = ro;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_rope_append(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v,
+                                   const pai_tensor* cos_table, const pai_tensor* sin_table, const pai_tensor* k_cache,
+                                   const pai_tensor* v_cache, const pai_tensor* pos, pai_tensor* q_out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  const pai_tensor* ins[6] = {q, k, v, cos_table, sin_table, pos};
+  const char* names[6] = {"q", "k", "v", "cos", "sin", "pos"};
+  for (int i = 0; i < 6; i++) PAI_TRY(check_view(ctx, ins[i], names[i]));
+  if (q->rank != 4 || k->rank != 4 || v->rank != 4 || numel(*pos) != 1 || cos_table->rank != 2 || sin_table->rank != 2)
+    return set_error(PAI_ERR_ARGUMENT, "RopeAppend: q [B,H,S,D], k and v [B,KVH,S,D], [T,D] tables and a position expected");
+  for (int i = 0; i < 4; i++)
+    if (k->dims[i] != v->dims[i]) return set_error(PAI_ERR_ARGUMENT, "RopeAppend: k and v shapes differ");
+  int B = q->dims[0], H = q->dims[1], S = q->dims[2], D = q->dims[3];
+  if (k->dims[0] != B || k->dims[2] != S || k->dims[3] != D || D % 2)
+    return set_error(PAI_ERR_ARGUMENT, "RopeAppend: q %s and k %s disagree (or odd head dim)", shape_str(*q).c_str(),
+                     shape_str(*k).c_str());
+  if (q->strides[3] != 1 || k->strides[3] != 1 || v->strides[3] != 1 || cos_table->strides[1] != 1 ||
+      sin_table->strides[1] != 1 || cos_table->strides[0] != sin_table->strides[0])
+    return set_error(PAI_ERR_UNSUPPORTED, "RopeAppend: rows must be contiguous and the tables share one layout");
+  if (cos_table->dims[1] != D || sin_table->dims[1] != D || sin_table->dims[0] != cos_table->dims[0])
+    return set_error(PAI_ERR_ARGUMENT, "RopeAppend: tables must be [T, %d]", D);
+  PAI_TRY(check_cache(ctx, k_cache, k, "k_cache"));
+  PAI_TRY(check_cache(ctx, v_cache, v, "v_cache"));
+  for (int i = 0; i < 3; i++)
+    if (k_cache->strides[i] != v_cache->strides[i] || k_cache->dims[i] != v_cache->dims[i])
+      return set_error(PAI_ERR_ARGUMENT, "RopeAppend: k and v caches must share one layout");
+  pai_tensor r;
+  PAI_TRY(alloc_tensor(ctx, 4, q->dims, q->dtype, false, &r));
+  RopeAppendArgs a{};
+  a.q = fptr(*q); a.k = fptr(*k); a.v = fptr(*v);
+  for (int i = 0; i < 3; i++) { a.qs[i] = q->strides[i]; a.ks[i] = k->strides[i]; a.vs[i] = v->strides[i]; a.cs[i] = k_cache->strides[i]; }
+  a.cos = fptr(*cos_table); a.sin = fptr(*sin_table); a.tab_stride = cos_table->strides[0]; a.tab_rows = cos_table->dims[0];
+  a.kc = fptr(*k_cache); a.vc = fptr(*v_cache); a.q_out = fptr(r); a.pos = fptr(*pos);
+  a.B = B; a.H = H; a.KVH = k->dims[1]; a.S = S; a.D = D; a.T = k_cache->dims[2];
+  a.error_flag = ctx->d_error_flag;
+  int64_t rows = (int64_t)B * S * (H + 2 * a.KVH);
+  if (rows > 0) {
+    k_rope_append<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(a);
+    PAI_LAUNCH_CHECK("rope append");
+  }
+  *q_out = r;
+  return PAI_OK;
+}

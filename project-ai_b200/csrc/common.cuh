@@ -39,7 +39,20 @@ struct BlockInfo {
 
 struct NcclState;  // defined in dp.cu
 
+// Device blocks a captured CUDA graph reads or writes. They stay reserved while the graph exists: blocks freed during
+// or after the capture are parked here instead of returning to the allocator's cache.
+struct GraphPool {
+  std::unordered_set<void*> owned;
+  std::unordered_map<size_t, std::vector<void*>> parked;  // rounded size -> owned blocks not currently live
+};
+
 }  // namespace pai
+
+struct pai_graph {
+  cudaGraphExec_t exec = nullptr;
+  pai::GraphPool pool;
+  int64_t launches = 0;  // kernel launches captured (counted again on every replay)
+};
 
 struct pai_ctx {
   int device = 0;
@@ -54,6 +67,8 @@ struct pai_ctx {
   int64_t in_use = 0, peak = 0, reserved = 0;
   // device flag the kernels with bounded waits report into (0 = ok)
   int* d_error_flag = nullptr;
+  // zeroed arrival counters for kernels whose last CTA finishes the work of the others (each user resets its own)
+  int* d_counters = nullptr;
   pai::NcclState* nccl = nullptr;
   char name[128] = {0};
   // instrumentation: kernel launches issued, a stream timer, and per-kernel-family event timing
@@ -72,6 +87,10 @@ struct pai_ctx {
   char* pinned = nullptr;
   cudaEvent_t pinned_ev[32] = {};
   int pinned_next = 0;
+  // CUDA graph capture: the graph being captured, and which live graph owns each reserved block
+  pai_graph* capture = nullptr;
+  int64_t capture_launches0 = 0;
+  std::unordered_map<void*, pai_graph*> graph_owner;
 };
 
 namespace pai {
@@ -133,6 +152,8 @@ void collapse(int rank, const int32_t* dims, const pai_tensor* const* views, int
 
 inline float* fptr(const pai_tensor& t) { return static_cast<float*>(t.base) + t.offset; }
 
+constexpr int kCounters = 1 << 16;  // entries of pai_ctx::d_counters
+
 // Grid size for a grid-stride loop: at most `waves` resident waves of `threads`-thread blocks.
 inline int grid_for(pai_ctx* ctx, int64_t n, int threads, int per_thread = 1, int waves = 8) {
   int64_t want = (n + (int64_t)threads * per_thread - 1) / ((int64_t)threads * per_thread);
@@ -181,6 +202,19 @@ __device__ __forceinline__ void row_offsets3(const pai::DView& a, const pai::DVi
     oc += i * c.strides[d];
     r = q;
   }
+}
+
+// SiLU(g)·u with the element operations of the reference's Sigmoid (sign-split, CpuComputeBackend.cs:304-317), SiLU
+// (x·sigmoid(x), :385-391) and Mul, each rounded once: shared by the SwiGLU kernel and the fused decode epilogue.
+__device__ __forceinline__ float silu_mul_value(float g, float u) {
+  float s;
+  if (g >= 0.0f) {
+    s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+  } else {
+    float t = expf(g);
+    s = __fdiv_rn(t, __fadd_rn(1.0f, t));
+  }
+  return __fmul_rn(__fmul_rn(g, s), u);
 }
 
 // Internal launchers shared across translation units.

@@ -54,6 +54,18 @@ static void release_cache(pai_ctx* ctx) {
 
 pai_status raw_alloc(pai_ctx* ctx, size_t bytes, void** out) {
   size_t sz = round_size(bytes);
+  if (ctx->capture) {
+    // inside a capture: reuse a block this graph already owns, else take one and make the graph its owner
+    auto pit = ctx->capture->pool.parked.find(sz);
+    if (pit != ctx->capture->pool.parked.end() && !pit->second.empty()) {
+      *out = pit->second.back();
+      pit->second.pop_back();
+      ctx->live[*out] = BlockInfo{sz, -1};
+      ctx->in_use += (int64_t)sz;
+      if (ctx->in_use > ctx->peak) ctx->peak = ctx->in_use;
+      return PAI_OK;
+    }
+  }
   auto it = ctx->free_blocks.find(sz);
   if (it != ctx->free_blocks.end() && !it->second.empty()) {
     *out = it->second.back();
@@ -78,6 +90,10 @@ pai_status raw_alloc(pai_ctx* ctx, size_t bytes, void** out) {
   ctx->live[*out] = BlockInfo{sz, -1};
   ctx->in_use += (int64_t)sz;
   if (ctx->in_use > ctx->peak) ctx->peak = ctx->in_use;
+  if (ctx->capture) {
+    ctx->capture->pool.owned.insert(*out);
+    ctx->graph_owner[*out] = ctx->capture;
+  }
   return PAI_OK;
 }
 
@@ -87,6 +103,11 @@ void raw_free(pai_ctx* ctx, void* p) {
   size_t sz = it->second.bytes;
   ctx->in_use -= (int64_t)sz;
   ctx->live.erase(it);
+  auto own = ctx->graph_owner.find(p);
+  if (own != ctx->graph_owner.end()) {
+    own->second->pool.parked[sz].push_back(p);  // a graph still reads or writes it: keep it out of the cache
+    return;
+  }
   ctx->free_blocks[sz].push_back(p);
 }
 
@@ -115,6 +136,8 @@ pai_status scratch(pai_ctx* ctx, size_t bytes, Scratch* s) {
 
 pai_status h2d(pai_ctx* ctx, void* dst, const void* host, size_t bytes) {
   if (bytes == 0) return PAI_OK;
+  if (ctx->capture)
+    return set_error(PAI_ERR_INVALID_OP, "a host upload cannot be part of a captured graph; pass device tensors instead");
   if (bytes > kPinnedChunk) {
     PAI_CUDA(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
     return PAI_OK;
@@ -356,11 +379,13 @@ PAI_API pai_status pai_ctx_create(int device, pai_ctx** out) {
   cudaError_t e1 = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
   cudaError_t e2 = cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking);
   cudaError_t e3 = cudaMalloc(&c->d_error_flag, 64);
-  if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
+  cudaError_t e4 = cudaMalloc(&c->d_counters, pai::kCounters * sizeof(int));
+  if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess || e4 != cudaSuccess) {
     delete c;
     return set_error(PAI_ERR_CUDA, "failed to create streams for device %d", device);
   }
   cudaMemset(c->d_error_flag, 0, 64);
+  cudaMemset(c->d_counters, 0, pai::kCounters * sizeof(int));
   *out = c;
   return PAI_OK;
 }
@@ -376,7 +401,10 @@ PAI_API pai_status pai_ctx_destroy(pai_ctx* ctx) {
   for (auto& kv : ctx->live) cudaFree(kv.first);
   for (auto& kv : ctx->free_blocks)
     for (void* p : kv.second) cudaFree(p);
+  for (auto& kv : ctx->graph_owner)  // blocks parked by graphs the caller did not destroy
+    if (!ctx->live.count(kv.first)) cudaFree(kv.first);
   cudaFree(ctx->d_error_flag);
+  cudaFree(ctx->d_counters);
   if (ctx->pinned) {
     cudaFreeHost(ctx->pinned);
     for (int i = 0; i < pai::kPinnedChunks; i++) cudaEventDestroy(ctx->pinned_ev[i]);
@@ -558,7 +586,7 @@ static cudaEvent_t pooled_event(pai_ctx* ctx) {
 }
 
 KernelTimerScope::KernelTimerScope(pai_ctx* c, const char* family, double work) : ctx(c) {
-  if (!ctx->kernel_timing) return;
+  if (!ctx->kernel_timing || ctx->capture) return;  // replays of a captured graph are timed as a whole
   slot = &ctx->timed[family];
   cudaEvent_t e = pooled_event(ctx);
   cudaEventRecord(e, ctx->stream);
@@ -638,4 +666,79 @@ PAI_API pai_status pai_kernel_stats(pai_ctx* ctx, const char* family, int64_t* l
   if (total_ms) *total_ms = ms;
   if (work) *work = w;
   return PAI_OK;
+}
+
+// ---------------------------------------------------------------- CUDA graphs
+// Captures every op issued on the context between pai_graph_begin and pai_graph_end into one CUDA graph (no host
+// uploads or synchronising calls in between). The device blocks the captured ops use stay reserved for the graph until
+// pai_graph_destroy, so replays read and write the same memory the capture did.
+PAI_API pai_status pai_graph_begin(pai_ctx* ctx) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  if (ctx->capture) return set_error(PAI_ERR_INVALID_OP, "a graph capture is already in progress");
+  PAI_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeRelaxed));
+  ctx->capture = new pai_graph();
+  ctx->capture_launches0 = ctx->launches;
+  return PAI_OK;
+}
+
+static void release_graph_blocks(pai_ctx* ctx, pai_graph* gr) {
+  for (void* p : gr->pool.owned) ctx->graph_owner.erase(p);
+  for (auto& kv : gr->pool.parked)
+    for (void* p : kv.second) ctx->free_blocks[kv.first].push_back(p);
+  gr->pool.owned.clear();
+  gr->pool.parked.clear();
+}
+
+PAI_API pai_status pai_graph_end(pai_ctx* ctx, pai_graph** out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  if (!ctx->capture) return set_error(PAI_ERR_INVALID_OP, "no graph capture is in progress");
+  pai_graph* gr = ctx->capture;
+  ctx->capture = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&gr->exec, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    release_graph_blocks(ctx, gr);
+    delete gr;
+    return cuda_error(e, "graph capture");
+  }
+  gr->launches = ctx->launches - ctx->capture_launches0;
+  ctx->launches = ctx->capture_launches0;  // nothing ran yet: launches count when the graph is replayed
+  *out = gr;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_graph_launch(pai_ctx* ctx, pai_graph* gr) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  if (!gr || !gr->exec) return set_error(PAI_ERR_ARGUMENT, "not an instantiated graph");
+  PAI_CUDA(cudaGraphLaunch(gr->exec, ctx->stream));
+  ctx->launches += gr->launches;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_graph_destroy(pai_ctx* ctx, pai_graph* gr) {
+  if (!gr) return PAI_OK;
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  PAI_CUDA(cudaStreamSynchronize(ctx->stream));  // the last replay has finished with the reserved blocks
+  if (gr->exec) cudaGraphExecDestroy(gr->exec);
+  release_graph_blocks(ctx, gr);
+  delete gr;
+  return PAI_OK;
+}
+
+// Host -> device copy into an existing dense tensor (stream-ordered; the host buffer may be reused on return).
+PAI_API pai_status pai_write(pai_ctx* ctx, const float* host, int64_t count, const pai_tensor* dst) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  PAI_TRY(check_view(ctx, dst, "destination"));
+  if (!is_dense(*dst)) return set_error(PAI_ERR_ARGUMENT, "Write: the destination must be a dense tensor");
+  if (count != numel(*dst))
+    return set_error(PAI_ERR_ARGUMENT, "Write: %lld values for a tensor of %lld", (long long)count, (long long)numel(*dst));
+  return h2d(ctx, fptr(*dst), host, (size_t)count * 4);
 }

@@ -20,6 +20,21 @@ __global__ void k_gather_rows(const float* __restrict__ table, const int32_t* __
   }
 }
 
+// Gather with ids read from a device tensor (integral F32 values). An id outside [0, vocab) sets the device error flag
+// and yields a zero row.
+__global__ void k_gather_rows_dev(const float* __restrict__ table, const float* __restrict__ ids, float* __restrict__ out,
+                                  int64_t n, int dim, int vocab, int* error_flag) {
+  for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
+    float f = ids[r];
+    int id = (int)f;
+    bool ok = f >= 0.0f && id < vocab && (float)id == f;
+    if (!ok && threadIdx.x == 0) atomicExch(error_flag, 62);
+    const float* src = table + (int64_t)(ok ? id : 0) * dim;
+    float* dst = out + r * dim;
+    for (int j = threadIdx.x; j < dim; j += blockDim.x) dst[j] = ok ? src[j] : 0.0f;
+  }
+}
+
 // One block per distinct id: rows of that id summed in their original order, starting from zero.
 __global__ void k_scatter_rows(const float* __restrict__ rows, const int32_t* __restrict__ uniq, const int32_t* __restrict__ start,
                                const int32_t* __restrict__ pos, float* __restrict__ out, int n_uniq, int dim) {
@@ -240,6 +255,33 @@ PAI_API pai_status pai_gather(pai_ctx* ctx, const pai_tensor* table, const int32
     int blocks = n < ctx->sm_count * 16 ? (int)n : ctx->sm_count * 16;
     k_gather_rows<<<blocks, 256, 0, ctx->stream>>>(tp, static_cast<int32_t*>(hid.p), fptr(r), n, dim);
     PAI_LAUNCH_CHECK("gather");
+  }
+  *out = r;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_gather_dev(pai_ctx* ctx, const pai_tensor* table, const pai_tensor* ids, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, table, "table"));
+  PAI_TRY(check_view(ctx, ids, "ids"));
+  if (table->rank != 2) return set_error(PAI_ERR_ARGUMENT, "Gather: table must be [vocab, dim], got %s", shape_str(*table).c_str());
+  if (ids->rank + 1 > PAI_MAX_RANK) return set_error(PAI_ERR_ARGUMENT, "Gather: ids rank too large");
+  if (!is_dense(*ids)) return set_error(PAI_ERR_ARGUMENT, "Gather: ids must be a dense tensor");
+  int vocab = table->dims[0], dim = table->dims[1];
+  int32_t od[PAI_MAX_RANK];
+  for (int i = 0; i < ids->rank; i++) od[i] = ids->dims[i];
+  od[ids->rank] = dim;
+  pai_tensor r;
+  PAI_TRY(alloc_tensor(ctx, ids->rank + 1, od, table->dtype, false, &r));
+  int64_t n = numel(*ids);
+  if (n > 0 && dim > 0) {
+    const float* tp;
+    Scratch ht;
+    PAI_TRY(dense_input(ctx, *table, &tp, &ht));
+    int blocks = n < ctx->sm_count * 16 ? (int)n : ctx->sm_count * 16;
+    k_gather_rows_dev<<<blocks, 256, 0, ctx->stream>>>(tp, fptr(*ids), fptr(r), n, dim, vocab, ctx->d_error_flag);
+    PAI_LAUNCH_CHECK("gather_dev");
   }
   *out = r;
   return PAI_OK;

@@ -434,6 +434,11 @@ __global__ void __launch_bounds__(256) k_gemm_simt(SimtArgs g) {
 }
 
 // ---------------------------------------------------------------- host side
+// gemv.cu: the small-M weight-streaming path (PAI_GEMV=0 turns it off)
+bool gemv_enabled();
+pai_status gemv_tn(pai_ctx* ctx, const float* x, const int64_t* xoff, int rows, const float* w, int64_t sw, int n, int k,
+                   float* y);
+
 static int gemm_mode() {
   static int mode = [] {
     const char* e = getenv("PAI_GEMM");
@@ -568,6 +573,18 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   int64_t sbk = tb ? b->strides[rb - 1] : b->strides[rb - 2];
   const float* abase = static_cast<const float*>(a->base);
   const float* bbase = static_cast<const float*>(b->base);
+
+  // Decode-sized x · Wᵀ (at most 32 rows against one weight matrix): weight-streaming kernel (gemv.cu).
+  const int64_t rows_total = batch * (int64_t)m;
+  if (tb && gemm_mode() != 1 && gemv_enabled() && b_distinct.size() == 1 && rows_total <= 32 && sak == 1 && sbk == 1) {
+    int64_t xo[32];
+    int idx = 0;
+    for (int64_t bi = 0; bi < batch; bi++)
+      for (int i = 0; i < m; i++) xo[idx++] = a_off[(size_t)bi] + (int64_t)i * sam;
+    PAI_TRY(gemv_tn(ctx, abase, xo, (int)rows_total, bbase + b_distinct[0], sbn, n, k, fptr(r)));
+    *out = r;
+    return PAI_OK;
+  }
 
   if (gemm_mode() == 1) {
     Scratch dao, dbo;

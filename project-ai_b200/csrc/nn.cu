@@ -34,6 +34,42 @@ __global__ void k_rmsnorm_fwd(const float* __restrict__ x, const float* __restri
   }
 }
 
+// Rows of d = 128·C elements: each lane holds C float4 of the row, all loads issued before the reduction, so a warp
+// needs one memory round trip per row instead of d/32 dependent loads (the decode case is a single row).
+template <int C>
+__global__ void __launch_bounds__(256) k_rmsnorm_fwd_reg(const float* __restrict__ x, const float* __restrict__ w,
+                                                         float* __restrict__ y, int64_t rows, float eps) {
+  constexpr int d = 128 * C;
+  const int lane = threadIdx.x & 31;
+  int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    const float4* px = reinterpret_cast<const float4*>(x + r * d);
+    float4 xv[C];
+    float ss = 0.0f;
+#pragma unroll
+    for (int c = 0; c < C; c++) xv[c] = px[c * 32 + lane];
+#pragma unroll
+    for (int c = 0; c < C; c++) {
+      ss = fmaf(xv[c].x, xv[c].x, ss); ss = fmaf(xv[c].y, xv[c].y, ss);
+      ss = fmaf(xv[c].z, xv[c].z, ss); ss = fmaf(xv[c].w, xv[c].w, ss);
+    }
+    ss = warp_sum(ss);
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps)));
+    float4* py = reinterpret_cast<float4*>(y + r * d);
+#pragma unroll
+    for (int c = 0; c < C; c++) {
+      float4 wv = reinterpret_cast<const float4*>(w)[c * 32 + lane];
+      float4 o;
+      o.x = __fmul_rn(__fmul_rn(xv[c].x, inv), wv.x);
+      o.y = __fmul_rn(__fmul_rn(xv[c].y, inv), wv.y);
+      o.z = __fmul_rn(__fmul_rn(xv[c].z, inv), wv.z);
+      o.w = __fmul_rn(__fmul_rn(xv[c].w, inv), wv.w);
+      py[c * 32 + lane] = o;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- RMSNorm backward.
 // dx = inv·(g⊙w) − (inv²/D)·x·Σ(g⊙y);  dw partial per block = Σ_rows g⊙x·inv, reduced by k_colsum.
 __global__ void k_rmsnorm_bwd(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ g,
@@ -159,15 +195,38 @@ __global__ void k_rotary(const float* __restrict__ x, DView xv, const float* __r
 
 // Row-wise RoPE when the head dim is unit-stride in x, cos and sin: one warp per row, the row's offsets computed
 // once from the leading dims, the row itself read and written contiguously.
+// RopeShift: optional position read on the device (pai_rotary_at). The cos/sin views address table rows 0..S-1;
+// the kernel moves them down by pos rows, after checking pos + S <= table_rows.
+struct RopeShift {
+  const float* pos = nullptr;
+  int64_t stride_c = 0, stride_s = 0;  // element stride of one table row
+  int seq = 0, table_rows = 0;
+  int* error_flag = nullptr;
+};
+
 __global__ void k_rotary_rows(const float* __restrict__ x, DView xr, const float* __restrict__ cs, DView cr,
-                              const float* __restrict__ sn, DView sr, float* __restrict__ y, int64_t rows, int d) {
+                              const float* __restrict__ sn, DView sr, float* __restrict__ y, int64_t rows, int d,
+                              RopeShift shift) {
   int lane = threadIdx.x & 31;
   int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   int half = d >> 1;
+  int64_t dc = 0, ds = 0;
+  if (shift.pos) {
+    float pf = shift.pos[0];
+    int p = (int)pf;
+    if (!(pf >= 0.0f) || p + shift.seq > shift.table_rows) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(shift.error_flag, 61);
+      return;
+    }
+    dc = (int64_t)p * shift.stride_c;
+    ds = (int64_t)p * shift.stride_s;
+  }
   for (int64_t r = warp; r < rows; r += nwarps) {
     int64_t xo, co, so;
     row_offsets3(xr, cr, sr, (uint32_t)r, xo, co, so);
+    co += dc;
+    so += ds;
     float* yr = y + r * d;
     for (int j = lane; j < half; j += 32) {
       float x0 = x[xo + j], x1 = x[xo + j + half];
@@ -178,10 +237,7 @@ __global__ void k_rotary_rows(const float* __restrict__ x, DView xr, const float
 }
 
 // ---------------------------------------------------------------- SwiGLU gate
-__device__ __forceinline__ float silu_mul_elem(float gv, float u) {
-  float y = __fmul_rn(gv, sigmoid_dev(gv));
-  return __fmul_rn(y, u);
-}
+__device__ __forceinline__ float silu_mul_elem(float gv, float u) { return silu_mul_value(gv, u); }
 
 __device__ __forceinline__ void silu_mul_bwd_elem(float gv, float u, float go, float& dg, float& du) {
   float s = sigmoid_dev(gv);
@@ -246,7 +302,21 @@ PAI_API pai_status pai_rmsnorm(pai_ctx* ctx, const pai_tensor* x, const pai_tens
     Scratch hx, hw;
     PAI_TRY(dense_input(ctx, *x, &xp, &hx));
     PAI_TRY(dense_input(ctx, *w, &wp, &hw));
-    k_rmsnorm_fwd<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(xp, wp, fptr(r), rows, d, eps);
+    int chunks = d % 128 == 0 ? d / 128 : 0;
+    bool aligned = aligned16(xp) && aligned16(wp) && aligned16(fptr(r));
+    int grid = grid_for(ctx, rows * 32, 256);
+    float* yp = fptr(r);
+    switch (aligned ? chunks : 0) {
+      case 1: k_rmsnorm_fwd_reg<1><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
+      case 2: k_rmsnorm_fwd_reg<2><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
+      case 4: k_rmsnorm_fwd_reg<4><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
+      case 6: k_rmsnorm_fwd_reg<6><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
+      case 8: k_rmsnorm_fwd_reg<8><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
+      case 12: k_rmsnorm_fwd_reg<12><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
+      case 16: k_rmsnorm_fwd_reg<16><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
+      case 32: k_rmsnorm_fwd_reg<32><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
+      default: k_rmsnorm_fwd<<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, d, eps); break;
+    }
     PAI_LAUNCH_CHECK("rmsnorm");
   }
   *out = r;
@@ -323,7 +393,46 @@ PAI_API pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_
   return PAI_OK;
 }
 
+static pai_status rotary_impl(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* cs, const pai_tensor* sn,
+                              const RopeShift& shift, pai_tensor* out);
+
 PAI_API pai_status pai_rotary(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* cs, const pai_tensor* sn, pai_tensor* out) {
+  return rotary_impl(ctx, x, cs, sn, RopeShift{}, out);
+}
+
+PAI_API pai_status pai_rotary_at(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* cos_table, const pai_tensor* sin_table,
+                                 const pai_tensor* pos, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  PAI_TRY(check_view(ctx, x, "x"));
+  PAI_TRY(check_view(ctx, cos_table, "cos"));
+  PAI_TRY(check_view(ctx, sin_table, "sin"));
+  PAI_TRY(check_view(ctx, pos, "pos"));
+  if (x->rank < 2 || cos_table->rank != 2 || sin_table->rank != 2 || numel(*pos) != 1)
+    return set_error(PAI_ERR_ARGUMENT, "RotaryAt: x [..., S, d], tables [T, d] and a one-element position expected");
+  int seq = x->dims[x->rank - 2], d = x->dims[x->rank - 1];
+  int rows = cos_table->dims[0];
+  if (cos_table->dims[1] != d || sin_table->dims[1] != d || sin_table->dims[0] != rows || seq > rows)
+    return set_error(PAI_ERR_ARGUMENT, "RotaryAt: tables %s / %s do not fit x %s", shape_str(*cos_table).c_str(),
+                     shape_str(*sin_table).c_str(), shape_str(*x).c_str());
+  if (x->strides[x->rank - 1] != 1 || cos_table->strides[1] != 1 || sin_table->strides[1] != 1)
+    return set_error(PAI_ERR_UNSUPPORTED, "RotaryAt: rows must be contiguous");
+  // table rows 0..S-1; the kernel adds pos rows
+  pai_tensor c = *cos_table, sv = *sin_table;
+  c.dims[0] = seq;
+  sv.dims[0] = seq;
+  RopeShift shift;
+  shift.pos = fptr(*pos);
+  shift.stride_c = cos_table->strides[0];
+  shift.stride_s = sin_table->strides[0];
+  shift.seq = seq;
+  shift.table_rows = rows;
+  shift.error_flag = ctx->d_error_flag;
+  return rotary_impl(ctx, x, &c, &sv, shift, out);
+}
+
+static pai_status rotary_impl(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* cs, const pai_tensor* sn,
+                              const RopeShift& shift, pai_tensor* out) {
   PAI_TRY(enter(ctx));
   std::lock_guard<std::recursive_mutex> lk(ctx->mu);
   PAI_TRY(check_view(ctx, x, "x"));
@@ -355,7 +464,10 @@ PAI_API pai_status pai_rotary(pai_ctx* ctx, const pai_tensor* x, const pai_tenso
       int64_t rows = n / d;
       k_rotary_rows<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(
           static_cast<const float*>(x->base), dv[0], static_cast<const float*>(cs->base), dv[1],
-          static_cast<const float*>(sn->base), dv[2], fptr(r), rows, d);
+          static_cast<const float*>(sn->base), dv[2], fptr(r), rows, d, shift);
+    } else if (shift.pos) {
+      raw_free(ctx, r.base);
+      return set_error(PAI_ERR_UNSUPPORTED, "RotaryAt: rows must be contiguous");
     } else {
       collapse(rank, x->dims, views, 3, dv);
       int64_t pairs = n / 2;

@@ -131,6 +131,18 @@ PYBIND11_MODULE(_paihost, m) {
         return py::make_tuple(n, ms, work);
       })
       .def("check_device_error", &NativeBackend::check_device_error)
+      .def_property_readonly("has_graphs", &NativeBackend::has_graphs)
+      .def_property_readonly("has_decode_fusions", &NativeBackend::has_decode_fusions)
+      .def("write", [](NativeBackend& be, const Tensor& dst, py::array_t<float, py::array::c_style | py::array::forcecast> a) {
+        be.write(dst, a.data(), (int64_t)a.size());
+      })
+      .def("gather_dev", &NativeBackend::gather_dev)
+      .def("rotary_at", &NativeBackend::rotary_at)
+      .def("kv_append", &NativeBackend::kv_append)
+      .def("sdpa_decode", &NativeBackend::sdpa_decode)
+      .def("linear_fused", &NativeBackend::linear_fused, py::arg("x"), py::arg("weights"), py::arg("mode"),
+           py::arg("residual") = nullptr)
+      .def("rope_append", &NativeBackend::rope_append)
       .def("nccl_unique_id", [](NativeBackend& be) {
         uint8_t id[128];
         be.nccl_unique_id(id);
@@ -236,6 +248,20 @@ PYBIND11_MODULE(_paihost, m) {
       .def("length", &KvCache::length)
       .def("reset", &KvCache::reset);
 
+  py::class_<GraphDecoder>(m, "GraphDecoder")
+      .def(py::init([](std::shared_ptr<NativeBackend> be, std::shared_ptr<PyModel> pm, KvCache& cache, int batch) {
+             return new GraphDecoder(be.get(), pm->model.get(), &cache, batch);
+           }),
+           py::arg("backend"), py::arg("model"), py::arg("cache"), py::arg("batch") = 1, py::keep_alive<1, 2>(),
+           py::keep_alive<1, 3>(), py::keep_alive<1, 4>())
+      .def("step", [](GraphDecoder& g, std::vector<int> ids) {
+        GradMode::Guard nograd(true);
+        return g.step(ids);
+      })
+      .def_property_readonly("captured", &GraphDecoder::captured)
+      .def_readwrite("fused", &GraphDecoder::fused);
+  m.def("has_graphs", [](std::shared_ptr<NativeBackend> be) { return be->has_graphs(); });
+
   m.def("cross_entropy_loss", [](Autograd& ag, const Tensor& logits, const Tensor& targets, int ignore) {
     return cross_entropy_loss(ag, logits, targets, ignore);
   }, py::arg("ag"), py::arg("logits"), py::arg("targets"), py::arg("ignore_index") = -100);
@@ -308,6 +334,12 @@ PYBIND11_MODULE(_paihost, m) {
            py::arg("top_p") = 1.0f)
       .def("sample", [](TopKTopPSampler& s, py::array_t<float, py::array::c_style | py::array::forcecast> a) {
         return s.sample(a.data(), (int)a.size());
+      })
+      .def("sample_rows", [](TopKTopPSampler& s, py::array_t<float, py::array::c_style | py::array::forcecast> a) {
+        if (a.ndim() != 2) throw ArgumentError("sample_rows expects [rows, vocab] logits");
+        std::vector<int> out((size_t)a.shape(0));
+        s.sample_rows(a.data(), (int)a.shape(0), (int)a.shape(1), out.data());
+        return out;
       });
   m.def("argmax", [](py::array_t<float, py::array::c_style | py::array::forcecast> a) { return argmax(a.data(), (int)a.size()); });
 
@@ -322,6 +354,7 @@ PYBIND11_MODULE(_paihost, m) {
     d["tokens"] = r.tokens;
     d["prefill_seconds"] = r.prefill_seconds;
     d["decode_seconds"] = r.decode_seconds;
+    d["graph"] = r.graph;
     return d;
   }, py::arg("backend"), py::arg("model"), py::arg("prompt"), py::arg("max_tokens"), py::arg("sampler") = nullptr,
      py::arg("batch") = 1);

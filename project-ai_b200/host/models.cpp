@@ -2,7 +2,9 @@
 // Linear.cs, Embedding.cs, Loss.cs), the KV cache (Modules.cs:290-370) and the samplers (Sampling.cs).
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 #include <numeric>
+#include <thread>
 
 #include "runtime.h"
 
@@ -299,7 +301,7 @@ Tensor LlamaModel::forward(const Tensor& ids, const ForwardContext& fctx) {
 
 // ---------------------------------------------------------------- KvCache (Modules.cs:301-370)
 KvCache::KvCache(NativeBackend* be, const ModelConfig& cfg, int mb, int ms)
-    : max_batch(mb), max_seq(ms), be_(be), keys_((size_t)cfg.layer_count), values_((size_t)cfg.layer_count),
+    : max_batch(mb), max_seq(ms), be_(be), key_store_((size_t)cfg.layer_count), value_store_((size_t)cfg.layer_count),
       lengths_((size_t)cfg.layer_count, 0) {}
 
 int KvCache::length(int layer) const {
@@ -307,31 +309,43 @@ int KvCache::length(int layer) const {
   return lengths_[(size_t)layer];
 }
 
-Tensor KvCache::concat(const Tensor& existing, const Tensor& incoming) {
-  if (!existing) {
-    std::vector<float> copy((size_t)incoming->numel());
-    be_->to_host(incoming, copy.data(), (int64_t)copy.size());
-    return be_->from_host(copy.data(), (int64_t)copy.size(), incoming->shape);
-  }
-  return be_->cat(existing, incoming, 2);
-}
-
 std::pair<Tensor, Tensor> KvCache::append(int layer, const Tensor& k, const Tensor& v) {
-  if (layer < 0 || layer >= (int)keys_.size()) throw OutOfRangeError("layer out of range for the cache (model/cache config mismatch?)");
+  if (layer < 0 || layer >= (int)key_store_.size()) throw OutOfRangeError("layer out of range for the cache (model/cache config mismatch?)");
   int batch = k->shape[0], new_len = k->shape[2];
   if (batch > max_batch) throw InvalidOperationError("batch exceeds the cache's MaxBatch");
-  if (lengths_[(size_t)layer] + new_len > max_seq)
-    throw InvalidOperationError("KV cache overflow: " + std::to_string(lengths_[(size_t)layer] + new_len) +
-                                " positions exceeds the maximum " + std::to_string(max_seq) + ".");
-  keys_[(size_t)layer] = concat(keys_[(size_t)layer], k);
-  values_[(size_t)layer] = concat(values_[(size_t)layer], v);
-  lengths_[(size_t)layer] = keys_[(size_t)layer]->shape[2];
-  return {keys_[(size_t)layer], values_[(size_t)layer]};
+  int len = lengths_[(size_t)layer];
+  if (len + new_len > max_seq)
+    throw InvalidOperationError("KV cache overflow: " + std::to_string(len + new_len) + " positions exceeds the maximum " +
+                                std::to_string(max_seq) + ".");
+  Tensor& ks = key_store_[(size_t)layer];
+  Tensor& vs = value_store_[(size_t)layer];
+  if (!ks) {
+    ks = be_->allocate({batch, k->shape[1], max_seq, k->shape[3]});
+    vs = be_->allocate({batch, v->shape[1], max_seq, v->shape[3]});
+  } else if (ks->shape[0] != batch || ks->shape[1] != k->shape[1] || ks->shape[3] != k->shape[3]) {
+    // the reference's Cat along the position axis rejects the same mismatch
+    throw ArgumentError("KV cache append: shape [" + std::to_string(batch) + ", " + std::to_string(k->shape[1]) + ", *, " +
+                        std::to_string(k->shape[3]) + "] does not match the cached layer");
+  }
+  be_->copy(k, ks->slice(2, len, new_len));
+  be_->copy(v, vs->slice(2, len, new_len));
+  lengths_[(size_t)layer] = len + new_len;
+  return {ks->slice(2, 0, len + new_len), vs->slice(2, 0, len + new_len)};
+}
+
+void KvCache::advance(int positions) {
+  for (size_t l = 0; l < lengths_.size(); l++) {
+    if (!key_store_[l]) throw InvalidOperationError("KV cache layer " + std::to_string(l) + " has no storage yet (prefill first)");
+    if (lengths_[l] + positions > max_seq)
+      throw InvalidOperationError("KV cache overflow: " + std::to_string(lengths_[l] + positions) +
+                                  " positions exceeds the maximum " + std::to_string(max_seq) + ".");
+  }
+  for (int& n : lengths_) n += positions;
 }
 
 void KvCache::reset() {
-  for (auto& t : keys_) t.reset();
-  for (auto& t : values_) t.reset();
+  for (auto& t : key_store_) t.reset();
+  for (auto& t : value_store_) t.reset();
   std::fill(lengths_.begin(), lengths_.end(), 0);
 }
 
@@ -358,29 +372,39 @@ int argmax(const float* logits, int n) {
   return best < 0 ? 0 : best;
 }
 
-int TopKTopPSampler::sample(const float* logits, int vocab) {
+// Sampling.cs:60-84: temperature softmax, then the indices by descending probability (ties by index) cut to top-k and
+// top-p. The order is a strict total order, so when top-k bounds the kept set only that prefix is sorted
+// (std::partial_sort yields exactly the full sort's first k entries).
+void TopKTopPSampler::prepare(const float* logits, int vocab, Prepared& p) const {
   if (vocab <= 0) throw ArgumentError("logits must be non-empty.");
-  if (temperature <= 0.0f) return argmax(logits, vocab);
+  p.direct = -1;
+  if (temperature <= 0.0f) { p.direct = argmax(logits, vocab); return; }
   float mx = -INFINITY;
   for (int i = 0; i < vocab; i++)
     if (logits[i] > mx) mx = logits[i];
-  std::vector<float> probs((size_t)vocab);
+  std::vector<float>& probs = p.probs;
+  probs.resize((size_t)vocab);
   float sum = 0.0f;
   for (int i = 0; i < vocab; i++) {
     float e = expf((logits[i] - mx) / temperature);
     probs[(size_t)i] = e;
     sum += e;
   }
-  if (!std::isfinite(sum) || sum <= 0.0f) return argmax(logits, vocab);
+  if (!std::isfinite(sum) || sum <= 0.0f) { p.direct = argmax(logits, vocab); return; }
   for (int i = 0; i < vocab; i++) probs[(size_t)i] /= sum;
-  std::vector<int> order((size_t)vocab);
+  std::vector<int>& order = p.order;
+  order.resize((size_t)vocab);
   std::iota(order.begin(), order.end(), 0);
-  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+  auto before = [&](int a, int b) {
     if (probs[(size_t)a] != probs[(size_t)b]) return probs[(size_t)a] > probs[(size_t)b];
     return a < b;
-  });
+  };
   int keep = vocab;
   if (top_k > 0 && top_k < keep) keep = top_k;
+  if (keep < vocab)
+    std::partial_sort(order.begin(), order.begin() + keep, order.end(), before);
+  else
+    std::sort(order.begin(), order.end(), before);
   if (top_p < 1.0f) {
     float cumulative = 0.0f;
     int kept = 0;
@@ -391,15 +415,51 @@ int TopKTopPSampler::sample(const float* logits, int vocab) {
     }
     keep = std::max(1, kept);
   }
+  p.keep = keep;
+}
+
+// Sampling.cs:86-111: one RNG draw over the renormalised kept set.
+int TopKTopPSampler::draw(const Prepared& p) {
+  if (p.direct >= 0) return p.direct;
   float total = 0.0f;
-  for (int i = 0; i < keep; i++) total += probs[(size_t)order[(size_t)i]];
+  for (int i = 0; i < p.keep; i++) total += p.probs[(size_t)p.order[(size_t)i]];
   float r = rng.next_float() * total;
   float acc = 0.0f;
-  for (int i = 0; i < keep; i++) {
-    acc += probs[(size_t)order[(size_t)i]];
-    if (r < acc) return order[(size_t)i];
+  for (int i = 0; i < p.keep; i++) {
+    acc += p.probs[(size_t)p.order[(size_t)i]];
+    if (r < acc) return p.order[(size_t)i];
   }
-  return order[(size_t)keep - 1];
+  return p.order[(size_t)p.keep - 1];
+}
+
+int TopKTopPSampler::sample(const float* logits, int vocab) {
+  Prepared p;
+  prepare(logits, vocab, p);
+  return draw(p);
+}
+
+void TopKTopPSampler::sample_rows(const float* rows, int batch, int vocab, int* out) {
+  std::vector<Prepared> prep((size_t)batch);
+  int threads = (int)std::min<unsigned>((unsigned)batch, std::max(1u, std::thread::hardware_concurrency()));
+  if (threads <= 1) {
+    for (int b = 0; b < batch; b++) prepare(rows + (size_t)b * vocab, vocab, prep[(size_t)b]);
+  } else {
+    std::vector<std::thread> pool;
+    std::exception_ptr err;
+    std::mutex err_mu;
+    for (int t = 0; t < threads; t++)
+      pool.emplace_back([&, t] {
+        try {
+          for (int b = t; b < batch; b += threads) prepare(rows + (size_t)b * vocab, vocab, prep[(size_t)b]);
+        } catch (...) {
+          std::lock_guard<std::mutex> g(err_mu);
+          err = std::current_exception();
+        }
+      });
+    for (auto& th : pool) th.join();
+    if (err) std::rethrow_exception(err);
+  }
+  for (int b = 0; b < batch; b++) out[b] = draw(prep[(size_t)b]);
 }
 
 }  // namespace paihost

@@ -149,6 +149,22 @@ class NativeBackend {
   void allreduce(const std::vector<Tensor>& grads);
   void allreduce_wait();
   int dp_world = 1, dp_rank = 0;
+  // decode steps with device-side ids and position, replayed as CUDA graphs (CUDA library only)
+  bool has_graphs() const;
+  void write(const Tensor& dst, const float* data, int64_t count);
+  Tensor gather_dev(const Tensor& table, const Tensor& ids);
+  Tensor rotary_at(const Tensor& x, const Tensor& cos_table, const Tensor& sin_table, const Tensor& pos);
+  void kv_append(const Tensor& k, const Tensor& v, const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos);
+  Tensor sdpa_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos, float scale);
+  // fused decode-step ops: x·Wᵀ over several weights with a store / residual / SiLU·mul epilogue, and RoPE + KV append
+  bool has_decode_fusions() const;
+  Tensor linear_fused(const Tensor& x, const std::vector<Tensor>& weights, int mode, const Tensor& residual = nullptr);
+  Tensor rope_append(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos_table, const Tensor& sin_table,
+                     const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos);
+  void graph_begin();
+  pai_graph* graph_end();
+  void graph_launch(pai_graph* g);
+  void graph_destroy(pai_graph* g);
   // diagnostics (CUDA library only)
   void timer_start();
   float timer_stop();
@@ -375,7 +391,10 @@ class LlamaModel : public Module {
   RmsNorm* final_norm;
 };
 
-// Modules.cs:290-370: per-layer K/V grown with Cat (the first append round-trips through the host).
+// Modules.cs:290-370: per-layer K/V of the positions seen so far. The reference grows each layer with Cat (the
+// first append round-trips through the host); here each layer's storage [batch, kv_heads, max_seq, head_dim] is
+// allocated on the device at the first append and later appends copy into it in place, so a decode step moves
+// only the new positions. Append returns views of the filled prefix with the same values Cat would produce.
 class KvCache {
  public:
   KvCache(NativeBackend* be, const ModelConfig& cfg, int max_batch, int max_seq);
@@ -383,11 +402,15 @@ class KvCache {
   std::pair<Tensor, Tensor> append(int layer, const Tensor& k, const Tensor& v);
   void reset();
   int max_batch, max_seq;
+  // the whole per-layer storage (null before the first append) and, for appends written on the device
+  // (NativeBackend::kv_append), the host-side length bookkeeping
+  Tensor key_store(int layer) const { return key_store_.at((size_t)layer); }
+  Tensor value_store(int layer) const { return value_store_.at((size_t)layer); }
+  void advance(int positions);
 
  private:
-  Tensor concat(const Tensor& existing, const Tensor& incoming);
   NativeBackend* be_;
-  std::vector<Tensor> keys_, values_;
+  std::vector<Tensor> key_store_, value_store_;
   std::vector<int> lengths_;
 };
 
@@ -400,6 +423,19 @@ class TopKTopPSampler {
  public:
   TopKTopPSampler(uint64_t seed, float temperature, int top_k, float top_p) : rng(seed), temperature(temperature), top_k(top_k), top_p(top_p) {}
   int sample(const float* logits, int n);
+  // Samples `batch` rows of `n` logits in row order (the RNG advances row by row exactly as repeated sample() calls);
+  // each row's distribution is prepared on its own thread.
+  void sample_rows(const float* rows, int batch, int n, int* out);
+  // One row's distribution: `direct` >= 0 when the row falls back to argmax (no RNG draw), else the kept prefix of
+  // the descending-probability order.
+  struct Prepared {
+    int direct = -1;
+    int keep = 0;
+    std::vector<int> order;
+    std::vector<float> probs;
+  };
+  void prepare(const float* logits, int n, Prepared& p) const;
+  int draw(const Prepared& p);
   PcgRng rng;
   float temperature;
   int top_k;
@@ -464,9 +500,37 @@ class Trainer {
 };
 
 // Inference.cs:23-64 with a sampler: prefill, then one token per step through the KV cache.
+// Decode steps of one lockstep batch (one new position per sequence) replayed as a CUDA graph: the ops of
+// LlamaModel::forward with the KV cache for that shape (Modules.cs:142-204, 222-288), with the token ids and the position
+// read from device tensors so the step captured once serves every later position. The first step runs eagerly (it warms
+// the allocator), the second is captured and launched, later ones only launch. The cache must already hold the
+// prompt (a prefill through LlamaModel::forward).
+class GraphDecoder {
+ public:
+  GraphDecoder(NativeBackend* be, LlamaModel* model, KvCache* cache, int batch);
+  ~GraphDecoder();
+  // Runs one step for `ids` (one per sequence) at the cache's current length; returns logits [batch, 1, vocab], a
+  // device tensor the next step overwrites.
+  Tensor step(const std::vector<int>& ids);
+  bool captured() const { return graph_ != nullptr; }
+  bool fused = true;  // use the fused decode ops when the backend has them (false: one backend op per model op)
+
+ private:
+  Tensor body();
+  Tensor body_fused();
+  NativeBackend* be_;
+  LlamaModel* model_;
+  KvCache* cache_;
+  int batch_;
+  Tensor ids_, pos_, logits_;
+  pai_graph* graph_ = nullptr;
+  int steps_ = 0;
+};
+
 struct GenerateResult {
   std::vector<int> tokens;
   double prefill_seconds = 0, decode_seconds = 0;
+  bool graph = false;  // the decode steps ran as a replayed CUDA graph
 };
 GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<int>& prompt, int max_tokens,
                         TopKTopPSampler* sampler, int batch = 1);

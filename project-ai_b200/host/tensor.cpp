@@ -263,7 +263,22 @@ void TensorImpl::backward() {
   X(launch_count, int (*)(pai_ctx*, int64_t*))                                                                           \
   X(kernel_timing, int (*)(pai_ctx*, int32_t))                                                                           \
   X(kernel_stats, int (*)(pai_ctx*, const char*, int64_t*, double*, double*))                                            \
-  X(check_device_error, int (*)(pai_ctx*, int32_t*))
+  X(check_device_error, int (*)(pai_ctx*, int32_t*))                                                                    \
+  X(write, int (*)(pai_ctx*, const float*, int64_t, const pai_tensor*))                                                  \
+  X(gather_dev, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, pai_tensor*))                                    \
+  X(rotary_at, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*, pai_tensor*)) \
+  X(kv_append, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*,             \
+                       const pai_tensor*))                                                                               \
+  X(sdpa_decode, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*, float,    \
+                         pai_tensor*))                                                                                   \
+  X(linear_fused, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, int32_t, int32_t, const pai_tensor*,          \
+                          pai_tensor*))                                                                                  \
+  X(rope_append, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*,           \
+                         const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*, pai_tensor*))       \
+  X(graph_begin, int (*)(pai_ctx*))                                                                                      \
+  X(graph_end, int (*)(pai_ctx*, pai_graph**))                                                                           \
+  X(graph_launch, int (*)(pai_ctx*, pai_graph*))                                                                         \
+  X(graph_destroy, int (*)(pai_ctx*, pai_graph*))
 
 template <class T>
 using Fn = T;
@@ -323,6 +338,13 @@ bool NativeBackend::has_fused() const {
 }
 
 bool NativeBackend::has_dp() const { return fn_->nccl_init && fn_->allreduce_bucket && fn_->allreduce_wait; }
+
+bool NativeBackend::has_graphs() const {
+  return fn_->write && fn_->gather_dev && fn_->rotary_at && fn_->kv_append && fn_->sdpa_decode && fn_->graph_begin &&
+         fn_->graph_end && fn_->graph_launch && fn_->graph_destroy;
+}
+
+bool NativeBackend::has_decode_fusions() const { return fn_->linear_fused && fn_->rope_append; }
 
 Tensor NativeBackend::wrap(const pai_tensor& d) {
   auto st = std::make_shared<Storage>();
@@ -643,6 +665,80 @@ namespace paihost {
 
 static void need(const void* fn, const char* what) {
   if (!fn) throw BackendError(std::string("backend library does not provide ") + what);
+}
+
+void NativeBackend::write(const Tensor& dst, const float* data, int64_t count) {
+  need((void*)fn_->write, "write");
+  pai_tensor d = dst->desc();
+  check(fn_->write(ctx_, data, count, &d));
+  invalidate_shadow(dst);
+  if (count == 1) dst->known = data[0];
+}
+
+Tensor NativeBackend::gather_dev(const Tensor& table, const Tensor& ids) {
+  need((void*)fn_->gather_dev, "gather_dev");
+  pai_tensor dt = table->desc(), di = ids->desc(), o;
+  check(fn_->gather_dev(ctx_, &dt, &di, &o));
+  return wrap(o);
+}
+
+Tensor NativeBackend::rotary_at(const Tensor& x, const Tensor& cos_table, const Tensor& sin_table, const Tensor& pos) {
+  need((void*)fn_->rotary_at, "rotary_at");
+  pai_tensor dx = x->desc(), dc = cos_table->desc(), ds = sin_table->desc(), dp = pos->desc(), o;
+  check(fn_->rotary_at(ctx_, &dx, &dc, &ds, &dp, &o));
+  return wrap(o);
+}
+
+void NativeBackend::kv_append(const Tensor& k, const Tensor& v, const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos) {
+  need((void*)fn_->kv_append, "kv_append");
+  pai_tensor dk = k->desc(), dv = v->desc(), dkc = k_cache->desc(), dvc = v_cache->desc(), dp = pos->desc();
+  check(fn_->kv_append(ctx_, &dk, &dv, &dkc, &dvc, &dp));
+  invalidate_shadow(k_cache);
+  invalidate_shadow(v_cache);
+}
+
+Tensor NativeBackend::sdpa_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos, float scale) {
+  need((void*)fn_->sdpa_decode, "sdpa_decode");
+  pai_tensor dq = q->desc(), dk = k_cache->desc(), dv = v_cache->desc(), dp = pos->desc(), o;
+  check(fn_->sdpa_decode(ctx_, &dq, &dk, &dv, &dp, scale, &o));
+  return wrap(o);
+}
+
+Tensor NativeBackend::linear_fused(const Tensor& x, const std::vector<Tensor>& weights, int mode, const Tensor& residual) {
+  need((void*)fn_->linear_fused, "linear_fused");
+  pai_tensor dx = x->desc(), dr{};
+  std::vector<pai_tensor> dw;
+  for (const auto& w : weights) dw.push_back(w->desc());
+  if (residual) dr = residual->desc();
+  pai_tensor o;
+  check(fn_->linear_fused(ctx_, &dx, dw.data(), (int32_t)dw.size(), mode, residual ? &dr : nullptr, &o));
+  return wrap(o);
+}
+
+Tensor NativeBackend::rope_append(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos_table,
+                                  const Tensor& sin_table, const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos) {
+  need((void*)fn_->rope_append, "rope_append");
+  pai_tensor dq = q->desc(), dk = k->desc(), dv = v->desc(), dc = cos_table->desc(), ds = sin_table->desc(),
+             dkc = k_cache->desc(), dvc = v_cache->desc(), dp = pos->desc(), o;
+  check(fn_->rope_append(ctx_, &dq, &dk, &dv, &dc, &ds, &dkc, &dvc, &dp, &o));
+  invalidate_shadow(k_cache);
+  invalidate_shadow(v_cache);
+  return wrap(o);
+}
+
+void NativeBackend::graph_begin() { need((void*)fn_->graph_begin, "graph_begin"); check(fn_->graph_begin(ctx_)); }
+
+pai_graph* NativeBackend::graph_end() {
+  need((void*)fn_->graph_end, "graph_end");
+  pai_graph* g = nullptr;
+  check(fn_->graph_end(ctx_, &g));
+  return g;
+}
+
+void NativeBackend::graph_launch(pai_graph* g) { need((void*)fn_->graph_launch, "graph_launch"); check(fn_->graph_launch(ctx_, g)); }
+
+void NativeBackend::graph_destroy(pai_graph* g) {
+  if (g && fn_->graph_destroy) check(fn_->graph_destroy(ctx_, g));
 }
 
 void NativeBackend::timer_start() { need((void*)fn_->timer_start, "timer_start"); check(fn_->timer_start(ctx_)); }

@@ -3,6 +3,8 @@
 // Inference.GenerateText (Inference.cs:23-74).
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
+#include <memory>
 
 #include "runtime.h"
 
@@ -178,6 +180,133 @@ float Trainer::step_tensors(const std::vector<Tensor>& inputs, const std::vector
   return step_loss;
 }
 
+// ---------------------------------------------------------------- GraphDecoder
+GraphDecoder::GraphDecoder(NativeBackend* be, LlamaModel* model, KvCache* cache, int batch)
+    : be_(be), model_(model), cache_(cache), batch_(batch) {
+  if (!be->has_graphs()) throw InvalidOperationError("the backend has no graph decode entry points");
+  ids_ = be->allocate({batch});
+  pos_ = be->allocate({1});
+}
+
+GraphDecoder::~GraphDecoder() {
+  if (graph_) {
+    try {
+      be_->graph_destroy(graph_);
+    } catch (...) {
+    }
+  }
+}
+
+// The decode step of LlamaModel::forward for [batch, 1] ids with the cache (TransformerBlock::forward, Attention::forward
+// with the fused attention, SwiGlu::forward), each op on the same backend kernels; only the position-dependent ops read
+// the position from pos_.
+Tensor GraphDecoder::body() {
+  NativeBackend& be = *be_;
+  const ModelConfig& c = model_->cfg;
+  const int b = batch_, h = c.head_count, kvh = c.kv_head_count, dh = c.head_dim(), d = c.embedding_dim;
+  const float scale = 1.0f / sqrtf((float)dh);
+  Tensor x = be.gather_dev(model_->embedding->weight, ids_);  // [b, d]
+  for (size_t l = 0; l < model_->blocks.size(); l++) {
+    TransformerBlock* blk = model_->blocks[l];
+    Attention* at = blk->attn;
+    Tensor hn = be.rms_norm(x, blk->attn_norm->weight, blk->attn_norm->eps);
+    Tensor q = be.matmul(hn, at->wq->weight, true)->reshape({b, 1, h, dh})->transpose(1, 2);
+    Tensor k = be.matmul(hn, at->wk->weight, true)->reshape({b, 1, kvh, dh})->transpose(1, 2);
+    Tensor v = be.matmul(hn, at->wv->weight, true)->reshape({b, 1, kvh, dh})->transpose(1, 2);
+    q = be.rotary_at(q, at->rope->cos, at->rope->sin, pos_);
+    k = be.rotary_at(k, at->rope->cos, at->rope->sin, pos_);
+    Tensor kc = cache_->key_store((int)l), vc = cache_->value_store((int)l);
+    be.kv_append(k, v, kc, vc, pos_);
+    Tensor o = be.sdpa_decode(q, kc, vc, pos_, scale);  // [b, 1, h, dh]
+    x = be.add(x, be.matmul(o->reshape({b, h * dh}), at->wo->weight, true));
+    Tensor hf = be.rms_norm(x, blk->ffn_norm->weight, blk->ffn_norm->eps);
+    SwiGlu* f = blk->ffn;
+    Tensor a = be.silu_mul(be.matmul(hf, f->gate->weight, true), be.matmul(hf, f->up->weight, true));
+    x = be.add(x, be.matmul(a, f->down->weight, true));
+  }
+  x = be.rms_norm(x, model_->final_norm->weight, model_->final_norm->eps);
+  return be.matmul(x, model_->embedding->weight, true)->reshape({b, 1, c.vocab_size});
+}
+
+// The same step with the fused decode ops, 8 launches per block: RMSNorm, q/k/v products in one pass, RoPE + cache
+// append, attention, o-projection + residual, RMSNorm, gate/up products with SiLU·mul, down-projection + residual.
+Tensor GraphDecoder::body_fused() {
+  NativeBackend& be = *be_;
+  const ModelConfig& c = model_->cfg;
+  const int b = batch_, h = c.head_count, kvh = c.kv_head_count, dh = c.head_dim();
+  const float scale = 1.0f / sqrtf((float)dh);
+  const int64_t width = (int64_t)(h + 2 * kvh) * dh;  // columns of the fused q|k|v product
+  Tensor x = be.gather_dev(model_->embedding->weight, ids_);  // [b, d]
+  for (size_t l = 0; l < model_->blocks.size(); l++) {
+    TransformerBlock* blk = model_->blocks[l];
+    Attention* at = blk->attn;
+    Tensor hn = be.rms_norm(x, blk->attn_norm->weight, blk->attn_norm->eps);
+    Tensor qkv = be.linear_fused(hn, {at->wq->weight, at->wk->weight, at->wv->weight}, 0);  // [b, width]
+    // views of one position per sequence: [b, heads, 1, dh] inside each row of qkv
+    Tensor q = make_view(*qkv, {b, h, 1, dh}, {width, dh, width, 1}, 0);
+    Tensor k = make_view(*qkv, {b, kvh, 1, dh}, {width, dh, width, 1}, (int64_t)h * dh);
+    Tensor v = make_view(*qkv, {b, kvh, 1, dh}, {width, dh, width, 1}, (int64_t)(h + kvh) * dh);
+    Tensor kc = cache_->key_store((int)l), vc = cache_->value_store((int)l);
+    Tensor qr = be.rope_append(q, k, v, at->rope->cos, at->rope->sin, kc, vc, pos_);
+    Tensor o = be.sdpa_decode(qr, kc, vc, pos_, scale);  // [b, 1, h, dh]
+    x = be.linear_fused(o->reshape({b, h * dh}), {at->wo->weight}, 1, x);
+    Tensor hf = be.rms_norm(x, blk->ffn_norm->weight, blk->ffn_norm->eps);
+    SwiGlu* f = blk->ffn;
+    Tensor a = be.linear_fused(hf, {f->gate->weight, f->up->weight}, 2);
+    x = be.linear_fused(a, {f->down->weight}, 1, x);
+  }
+  x = be.rms_norm(x, model_->final_norm->weight, model_->final_norm->eps);
+  return be.matmul(x, model_->embedding->weight, true)->reshape({b, 1, c.vocab_size});
+}
+
+Tensor GraphDecoder::step(const std::vector<int>& ids) {
+  const ModelConfig& c = model_->cfg;
+  if ((int)ids.size() != batch_) throw ArgumentError("GraphDecoder: one id per sequence expected");
+  for (int id : ids)
+    if (id < 0 || id >= c.vocab_size)
+      throw OutOfRangeError("id out of range [0," + std::to_string(c.vocab_size) + "). (Parameter 'ids') Actual value was " +
+                            std::to_string(id) + ".");
+  int pos = cache_->length(0);
+  if (pos + 1 > cache_->max_seq)
+    throw InvalidOperationError("KV cache overflow: " + std::to_string(pos + 1) + " positions exceeds the maximum " +
+                                std::to_string(cache_->max_seq) + ".");
+  if (!cache_->key_store(0) || cache_->key_store(0)->shape[0] != batch_)
+    throw InvalidOperationError("GraphDecoder: the cache must hold a prefill of the same batch");
+  std::vector<float> fid(ids.begin(), ids.end());
+  float fpos = (float)pos;
+  be_->write(ids_, fid.data(), batch_);
+  be_->write(pos_, &fpos, 1);
+  const bool use_fused = fused && be_->has_decode_fusions();
+  auto run = [&]() { return use_fused ? body_fused() : body(); };
+  if (steps_ == 0) {
+    logits_ = run();  // eager: every block size the step needs is now in the allocator's cache
+  } else if (!graph_) {
+    logits_.reset();
+    be_->graph_begin();
+    try {
+      logits_ = run();
+    } catch (...) {
+      try {
+        be_->graph_destroy(be_->graph_end());
+      } catch (...) {
+      }
+      throw;
+    }
+    graph_ = be_->graph_end();
+    be_->graph_launch(graph_);
+  } else {
+    be_->graph_launch(graph_);
+  }
+  cache_->advance(1);
+  steps_++;
+  return logits_;
+}
+
+static bool decode_graphs_enabled() {
+  const char* e = getenv("PAI_DECODE_GRAPH");
+  return !(e && e[0] == '0');
+}
+
 // Inference.GenerateText (Inference.cs:23-64) on token ids, for a lockstep batch (KvCache supports uniform batches).
 // Only each row's last logits row is read back (SampleLast reads exactly that row of the full download).
 GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<int>& prompt, int max_tokens,
@@ -192,14 +321,17 @@ GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<
   ctx.cache = &cache;
   GradMode::Guard nograd(true);
   int vocab = cfg.vocab_size;
-  std::vector<float> row((size_t)vocab);
+  std::vector<float> last_rows((size_t)batch * vocab);
   auto pick = [&](const Tensor& logits, std::vector<int>& out) {
     int rows = logits->shape[1];
     out.clear();
-    for (int bi = 0; bi < batch; bi++) {
-      Tensor last = logits->slice(0, bi, 1)->slice(1, rows - 1, 1);
-      be->to_host(last, row.data(), vocab);
-      out.push_back(sampler ? sampler->sample(row.data(), vocab) : argmax(row.data(), vocab));
+    // one download of every sequence's last row [batch, vocab]; rows are then sampled in batch order
+    be->to_host(logits->slice(1, rows - 1, 1), last_rows.data(), (int64_t)last_rows.size());
+    out.resize((size_t)batch);
+    if (sampler) {
+      sampler->sample_rows(last_rows.data(), batch, vocab, out.data());
+    } else {
+      for (int bi = 0; bi < batch; bi++) out[(size_t)bi] = argmax(last_rows.data() + (size_t)bi * vocab, vocab);
     }
   };
   auto t0 = clock::now();
@@ -209,13 +341,24 @@ GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<
   pick(logits, next);
   auto t1 = clock::now();
   r.prefill_seconds = std::chrono::duration<double>(t1 - t0).count();
+  // the per-token steps replay one captured CUDA graph when the backend supports it (dense head dim <= 64 and at most
+  // 16 query rows per kv head, the decode attention kernel's range)
+  std::unique_ptr<GraphDecoder> graph;
+  if (be->has_graphs() && decode_graphs_enabled() && cfg.head_dim() <= 64 && cfg.head_dim() % 4 == 0 &&
+      cfg.head_count / cfg.kv_head_count <= 16)
+    graph = std::make_unique<GraphDecoder>(be, model, &cache, batch);
   for (int produced = 0; produced < max_tokens; produced++) {
     for (int v : next) r.tokens.push_back(v);
     if (produced + 1 >= max_tokens || p_len + produced + 1 >= cfg.max_sequence_length) break;
-    std::vector<float> step(next.begin(), next.end());
-    logits = model->forward(be->from_host(step.data(), batch, {batch, 1}), ctx);
+    if (graph) {
+      logits = graph->step(next);
+    } else {
+      std::vector<float> step(next.begin(), next.end());
+      logits = model->forward(be->from_host(step.data(), batch, {batch, 1}), ctx);
+    }
     pick(logits, next);
   }
+  r.graph = graph && graph->captured();
   be->sync();
   r.decode_seconds = std::chrono::duration<double>(clock::now() - t1).count();
   return r;

@@ -246,6 +246,50 @@ def test_samplers():
     assert [a.sample(logits) for _ in range(50)] == [b.sample(logits) for _ in range(50)]
 
 
+def reference_topk_topp(logits, rng, temperature, top_k, top_p):
+    """Sampling.cs:60-111 in float32 with the full descending sort (distinct logits, so the order is the argsort)."""
+    x = logits.astype(np.float32)
+    e = np.exp((x - x.max()) / np.float32(temperature)).astype(np.float32)
+    s = np.float32(0)
+    for v in e:
+        s = np.float32(s + v)
+    p = (e / s).astype(np.float32)
+    order = sorted(range(len(p)), key=lambda i: (-p[i], i))
+    keep = len(p) if top_k <= 0 else min(top_k, len(p))
+    if top_p < 1:
+        cum, kept = np.float32(0), 0
+        for i in range(keep):
+            cum = np.float32(cum + p[order[i]])
+            kept += 1
+            if cum >= np.float32(top_p):
+                break
+        keep = max(1, kept)
+    total = np.float32(0)
+    for i in range(keep):
+        total = np.float32(total + p[order[i]])
+    r = np.float32(np.float32(rng.next_u32() >> 8) * np.float32(1.0 / (1 << 24))) * total
+    acc = np.float32(0)
+    for i in range(keep):
+        acc = np.float32(acc + p[order[i]])
+        if r < acc:
+            return order[i]
+    return order[keep - 1]
+
+
+def test_topk_partial_sort_and_batched_rows_match_the_reference_sampler():
+    rs = np.random.RandomState(1)
+    rows = np.stack([rs.permutation(2000).astype(np.float32) * 0.01 for _ in range(6)])  # distinct logits per row
+    for k, p in [(40, 1.0), (5, 0.9), (0, 0.5)]:
+        s = H.TopKTopPSampler(9, 0.8, k, p)
+        ref_rng = H.PcgRng(9)
+        got = [s.sample(r) for r in rows]
+        exp = [reference_topk_topp(r, ref_rng, 0.8, k, p) for r in rows]
+        assert got == exp, (k, p)
+        # the batched entry draws in row order: identical to row-by-row sample() calls
+        a, b = H.TopKTopPSampler(21, 0.8, k, p), H.TopKTopPSampler(21, 0.8, k, p)
+        assert a.sample_rows(rows) == [b.sample(r) for r in rows]
+
+
 def test_scopes_release_intermediates(be):
     before = be.memory_stats()[0]
     be.begin_scope()
