@@ -375,9 +375,10 @@ def op_sweep(args):
     be.close()
 
 
-def workload_config(name, n):
+def workload_config(name, n, recompute=True):
     c = CONFIGS[name]
-    return {"workload": f"llama-{name} train step (fwd + per-block recompute + bwd + AdamW), fp32 semantics",
+    mode = "per-block recompute" if recompute else "stored activations, no recompute"
+    return {"workload": f"llama-{name} train step (fwd + {mode} + bwd + AdamW), fp32 semantics",
             "vocab": c["vocab_size"], "d_model": c["embedding_dim"], "layers": c["layer_count"], "heads": c["head_count"],
             "kv_heads": c["kv_head_count"], "ffn": c["ffn_hidden"], "seq_len": c["seq"], "batch_per_gpu": c["batch"],
             "global_batch": c["batch"] * n, "params": param_count(c), "parallelism": f"dp{n}",
@@ -454,6 +455,7 @@ def main():
         batches.append((be.from_host(x), be.from_host(y)))
     step += args.steps
     barrier()
+    be.reset_peak()
     launches0 = be.launch_count()
     losses = []
     with ClockSampler(local) as clocks:
@@ -462,6 +464,7 @@ def main():
             losses.append(tr.step_tensors([x], [y]))
         ms = be.timer_stop()
     launches = be.launch_count() - launches0
+    mem_in_use, mem_peak, mem_reserved = be.memory_stats()
     be.check_device_error()
     barrier()
 
@@ -513,7 +516,10 @@ def main():
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (PcgRng token ids, N(0,0.02) weights)",
-                "config": workload_config(args.config, world), "roofline": roofline,
+                "config": workload_config(args.config, world, not args.no_recompute), "roofline": roofline,
+                "memory": {"peak_allocated_gb": mem_peak / 1e9, "reserved_gb": mem_reserved / 1e9,
+                           "note": "device bytes held by tensors at the peak of the timed steps (weights, AdamW "
+                                   "moments, gradients and activations), from the library's allocator"},
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * c["batch"] * c["seq"] * 4,
                         "d2h_bytes_per_step": 4, "ms_per_step": ms_e2e / args.steps},
                 "gpu_launches": launches, "kernels": kernels,

@@ -208,18 +208,26 @@ pai_status pai_kv_append(pai_ctx* ctx, const pai_tensor* k, const pai_tensor* v,
 pai_status pai_rope_append(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v,
                            const pai_tensor* cos_table, const pai_tensor* sin_table, const pai_tensor* k_cache,
                            const pai_tensor* v_cache, const pai_tensor* pos, pai_tensor* q_out);
+/* pai_rope_append followed by pai_sdpa_decode on its results, in one launch: q, k and v [B, heads, S, D] arrive
+ * unrotated (e.g. views of the fused q|k|v product); the rotated keys and the values are written into the caches at
+ * positions pos .. pos+S-1 and out [B, S, H, D] holds the causal attention over positions 0 .. pos+S-1. */
+pai_status pai_attn_decode_step(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v,
+                                const pai_tensor* cos_table, const pai_tensor* sin_table, const pai_tensor* k_cache,
+                                const pai_tensor* v_cache, const pai_tensor* pos, float scale, pai_tensor* out);
 /* Causal attention of q [B, H, S, D] (S * H / KVH <= 16, D <= 64) over cache positions 0 .. pos+S-1: out
  * [B, S, H, D], the values of pai_sdpa_fwd with causal = 1, pos_offset = pos and the filled cache prefix. */
 pai_status pai_sdpa_decode(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k_cache, const pai_tensor* v_cache,
                            const pai_tensor* pos, float scale, pai_tensor* out);
 /* Decode-step products of one activation x [..., k] (at most 32 rows, contiguous rows) with up to four weights
- * W_i [n_i, k] (Linear.cs:10-43: y = x·Wᵀ), in one pass over the weights:
+ * W_i [n_i, k] (Linear.cs:10-43: y = x·Wᵀ), in one pass over the weights. With norm_weight (a [k] tensor, else NULL)
+ * x is first normalised as pai_rmsnorm(x, norm_weight, eps) would (same values, bit for bit):
  *   mode 0: out [..., Σ n_i] = the products side by side (the attention's q, k and v projections);
  *   mode 1: out [..., n_0] = residual + x·W_0ᵀ (a Linear followed by TransformerBlock's residual Add, Modules.cs:222-246);
  *   mode 2: out [..., n_0] = SiLU(x·W_0ᵀ) ⊙ (x·W_1ᵀ) (SwiGluFeedForward's gate and up, Modules.cs:84-109).
  * The values are those of the separate MatMul / Add / SiluMul calls up to the summation order of the dot products. */
-pai_status pai_linear_fused(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* weights, int32_t n_weights, int32_t mode,
-                            const pai_tensor* residual, pai_tensor* out);
+pai_status pai_linear_fused(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* norm_weight, float eps,
+                            const pai_tensor* weights, int32_t n_weights, int32_t mode, const pai_tensor* residual,
+                            pai_tensor* out);
 /* Captures every op issued on the context between begin and end into one CUDA graph; no host upload or
  * synchronising call may come in between. The device memory the captured ops use stays reserved for the graph
  * until pai_graph_destroy, so tensors created during the capture hold each replay's results. */

@@ -11,6 +11,7 @@
 //   PV:  lanes own two head-dim elements each; each key's probability is broadcast with a shuffle.
 // The 4 warps of a CTA and then the key splits are merged in a fixed order (log-sum-exp rescaling), so results are
 // deterministic.
+#include <cooperative_groups.h>
 #include <math.h>
 
 #include "common.cuh"
@@ -19,11 +20,14 @@ namespace pai {
 
 namespace dec {
 
+namespace cg = cooperative_groups;
+
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxD = 64;
 constexpr int kMaxRows = 16;
-constexpr int kTile = 32;  // keys per warp step
+constexpr int kTile = 32;        // keys per warp step
+constexpr int kMaxCluster = 8;   // key splits of one (batch, kv head): the CTAs of one portable cluster
 
 struct View {
   const float* p;
@@ -35,11 +39,16 @@ struct Args {
   int B, H, KVH, S, L, D, g, rows;
   int pos_offset, causal;
   float scale;
-  int splits, keys_per_split;
+  int splits, keys_per_split;  // splits = the cluster size along x
   const float* pos_dev;  // when set: pos_offset = pos_dev[0] and the keys are cache positions 0 .. pos+S-1 (L = capacity)
   int* error_flag;
-  int* counters;         // splits > 1: one arrival counter per (batch, kv head); the last CTA merges the splits
-  float* part;           // splits > 1: [B, KVH, splits, rows, D + 2] (acc..., m, l)
+  // fused RoPE + cache append: q and the new key/value rows [B, KVH, S, D] arrive unrotated; keys are rotated with the
+  // table rows pos + s and written with the values into the caches (k.p / v.p) before they are attended to
+  View kn, vn;
+  const float* cos;
+  const float* sin;
+  int64_t tab_stride;
+  int tab_rows;
   float* out;            // [B, S, H, D]
   float* lse;            // [B, H, S]
 };
@@ -63,52 +72,38 @@ __device__ __forceinline__ void store_row(const Args& a, int b, int kvh, int r, 
   if (d == 0) a.lse[((int64_t)b * a.H + h) * a.S + s] = any ? m + logf(l) : -INFINITY;
 }
 
-// Merges the key splits of query row r of (b, kvh) in split order (log-sum-exp rescaling) and stores it.
-__device__ __forceinline__ void combine_row(const Args& a, int b, int kvh, int r, int d) {
-  const float* base = a.part + (((int64_t)b * a.KVH + kvh) * a.splits * a.rows + r) * (a.D + 2);
-  const int64_t stride = (int64_t)a.rows * (a.D + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < a.splits; s++) M = fmaxf(M, __ldcg(base + s * stride + a.D));
-  float L = 0.0f, A = 0.0f;
-  for (int s = 0; s < a.splits; s++) {
-    const float* pr = base + s * stride;
-    float ms = __ldcg(pr + a.D);
-    if (ms == -INFINITY) continue;
-    float e = expf(ms - M);
-    L += __ldcg(pr + a.D + 1) * e;
-    if (d < a.D) A += __ldcg(pr + d) * e;
-  }
-  store_row(a, b, kvh, r, d, A, M, L);
+// RotaryEmbedding of element pair (j, j + D/2) of one row (CpuComputeBackend.cs:397-420), as k_rotary_rows rounds it.
+__device__ __forceinline__ void rope_pair(float x0, float x1, const float* cr, const float* sr, int j, int half, float& y0,
+                                          float& y1) {
+  y0 = __fadd_rn(__fmul_rn(x0, cr[j]), __fmul_rn(-x1, sr[j]));
+  y1 = __fadd_rn(__fmul_rn(x1, cr[j + half]), __fmul_rn(x0, sr[j + half]));
 }
 
-// DC: the head dim when known at compile time (64), else 0 (read from the arguments).
-template <int R, int DC>
+// One CTA per (key split, kv head, batch); the splits of one (batch, kv head) form a cluster. Each of the 4 warps
+// takes 32-key tiles of the CTA's key range; the warps merge in shared memory and cluster rank 0 merges the CTAs'
+// partials through distributed shared memory, in rank order.
+// DC: the head dim when known at compile time (64), else 0 (read from the arguments). ROPE: fused RoPE + append.
+template <int R, int DC, bool ROPE>
 __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
   const int D = DC ? DC : a.D;
   __shared__ __align__(16) float qs[R][kMaxD];
   __shared__ float wm[kWarps][R], wl[kWarps][R];
   __shared__ float wacc[kWarps][R][kMaxD];
+  __shared__ float cm[R], cl[R];            // this CTA's merged partial, read by rank 0
+  __shared__ float ca[R][kMaxD];
+  cg::cluster_group cluster = cg::this_cluster();
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows = a.rows;
-
-  // query rows of this kv head's group, pre-scaled: row r = (head hg of the group, position s)
-  for (int t = threadIdx.x; t < R * kMaxD; t += kThreads) {
-    int r = t / kMaxD, d = t - r * kMaxD;
-    float val = 0.0f;
-    if (r < rows && d < a.D) {
-      int hg = r / a.S, s = r - hg * a.S, h = kvh * a.g + hg;
-      val = a.q.p[(int64_t)b * a.q.s0 + (int64_t)h * a.q.s1 + (int64_t)s * a.q.s2 + d] * a.scale;
-    }
-    qs[r][d] = val;
-  }
-  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
 
   int pos_offset = a.pos_offset, kend = a.L;
   if (a.pos_dev) {
     float pf = a.pos_dev[0];
     pos_offset = (int)pf;
-    if (!(pf >= 0.0f) || pos_offset + a.S > a.L) {  // outside the cache: flag it and attend to nothing
+    if (!(pf >= 0.0f) || pos_offset + a.S > a.L || (ROPE && pos_offset + a.S > a.tab_rows)) {
+      // outside the cache or the tables: flag it and attend to nothing
       if (split == 0 && threadIdx.x == 0) atomicExch(a.error_flag, 63);
       pos_offset = 0;
       kend = 0;
@@ -119,8 +114,47 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
   const int j1 = min(kend, j0 + a.keys_per_split);
   const float* kbase = a.k.p + (int64_t)b * a.k.s0 + (int64_t)kvh * a.k.s1;
   const float* vbase = a.v.p + (int64_t)b * a.v.s0 + (int64_t)kvh * a.v.s1;
-  const int d0 = 2 * lane;  // this lane's head-dim pair in PV
+  const int half = D >> 1;
 
+  if (ROPE && kend > 0) {
+    // the new key/value rows in this CTA's key range go into the caches first (rotated keys)
+    for (int t = threadIdx.x; t < a.S * half; t += kThreads) {
+      int s = t / half, j = t - s * half, pos = pos_offset + s;
+      if (pos < j0 || pos >= j1) continue;
+      const float* kr = a.kn.p + (int64_t)b * a.kn.s0 + (int64_t)kvh * a.kn.s1 + (int64_t)s * a.kn.s2;
+      const float* vr = a.vn.p + (int64_t)b * a.vn.s0 + (int64_t)kvh * a.vn.s1 + (int64_t)s * a.vn.s2;
+      float* kd = const_cast<float*>(kbase) + (int64_t)pos * a.k.s2;
+      float* vd = const_cast<float*>(vbase) + (int64_t)pos * a.v.s2;
+      float y0, y1;
+      rope_pair(kr[j], kr[j + half], a.cos + (int64_t)pos * a.tab_stride, a.sin + (int64_t)pos * a.tab_stride, j, half, y0, y1);
+      kd[j] = y0;
+      kd[j + half] = y1;
+      vd[j] = vr[j];
+      vd[j + half] = vr[j + half];
+    }
+  }
+  // query rows of this kv head's group, pre-scaled: row r = (head hg of the group, position s)
+  for (int t = threadIdx.x; t < R * kMaxD; t += kThreads) {
+    int r = t / kMaxD, d = t - r * kMaxD;
+    float val = 0.0f;
+    if (r < rows && d < a.D) {
+      int hg = r / a.S, s = r - hg * a.S, h = kvh * a.g + hg;
+      const float* qr = a.q.p + (int64_t)b * a.q.s0 + (int64_t)h * a.q.s1 + (int64_t)s * a.q.s2;
+      if (ROPE) {
+        int pos = pos_offset + s, j = d < half ? d : d - half;
+        float y0, y1;
+        rope_pair(qr[j], qr[j + half], a.cos + (int64_t)pos * a.tab_stride, a.sin + (int64_t)pos * a.tab_stride, j, half, y0, y1);
+        val = d < half ? y0 : y1;
+      } else {
+        val = qr[d];
+      }
+      val = val * a.scale;
+    }
+    qs[r][d] = val;
+  }
+  __syncthreads();
+
+  const int d0 = 2 * lane;  // this lane's head-dim pair in PV
   float m[R], l[R], acc0[R], acc1[R];
 #pragma unroll
   for (int r = 0; r < R; r++) { m[r] = -INFINITY; l[r] = 0.0f; acc0[r] = 0.0f; acc1[r] = 0.0f; }
@@ -182,7 +216,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
     }
   }
 
-  // merge the warps (fixed order)
+  // merge the warps (fixed order) into this CTA's partial
 #pragma unroll
   for (int r = 0; r < R; r++) {
     if (lane == 0) { wm[warp][r] = m[r]; wl[warp][r] = l[r]; }
@@ -202,42 +236,46 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
         A += wacc[w][r][d] * e;
       }
     }
-    if (a.splits == 1) {
+    ca[r][d] = A;
+    if (d == 0) { cm[r] = M; cl[r] = L; }
+  }
+  // rank 0 merges the cluster's partials in rank order; the second barrier keeps every CTA's shared memory alive
+  // until rank 0 has read it
+  cluster.sync();
+  if (cluster.block_rank() == 0) {
+    const int n = (int)cluster.num_blocks();
+    for (int t = threadIdx.x; t < rows * kMaxD; t += kThreads) {
+      int r = t / kMaxD, d = t - r * kMaxD;
+      float M = -INFINITY;
+      for (int c = 0; c < n; c++) M = fmaxf(M, *cluster.map_shared_rank(&cm[r], c));
+      float L = 0.0f, A = 0.0f;
+      if (M != -INFINITY) {
+        for (int c = 0; c < n; c++) {
+          float mc = *cluster.map_shared_rank(&cm[r], c);
+          if (mc == -INFINITY) continue;
+          float e = expf(mc - M);
+          L += *cluster.map_shared_rank(&cl[r], c) * e;
+          A += *cluster.map_shared_rank(&ca[r][d], c) * e;
+        }
+      }
       store_row(a, b, kvh, r, d, A, M, L);
-    } else {
-      float* pr = a.part + ((((int64_t)b * a.KVH + kvh) * a.splits + split) * rows + r) * (a.D + 2);
-      if (d < a.D) pr[d] = A;
-      if (d == 0) { pr[a.D] = M; pr[a.D + 1] = L; }
     }
   }
-  if (a.splits == 1 || !a.counters) return;
-  // the last CTA of this (batch, kv head) to finish merges every split, then re-arms the counter
-  __shared__ int s_last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[b * a.KVH + kvh], 1) == a.splits - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int t = threadIdx.x; t < rows * kMaxD; t += kThreads) combine_row(a, b, kvh, t / kMaxD, t % kMaxD);
-  if (threadIdx.x == 0) a.counters[b * a.KVH + kvh] = 0;
-}
-
-// Merges the key splits of one query row (fixed split order), for grids too large for the arrival counters.
-__global__ void __launch_bounds__(kMaxD) k_attn_decode_combine(const Args a) {
-  combine_row(a, blockIdx.z, blockIdx.y, blockIdx.x, threadIdx.x);
+  cluster.sync();
 }
 
 }  // namespace dec
 
-template <int DC>
-static void launch_decode(pai_ctx* ctx, const dec::Args& a, dim3 grid) {
+template <int DC, bool ROPE>
+static cudaError_t launch_decode(pai_ctx* ctx, const dec::Args& a, dim3 grid) {
   int R = a.rows;
-  if (R <= 1) dec::k_attn_decode<1, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
-  else if (R <= 2) dec::k_attn_decode<2, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
-  else if (R <= 4) dec::k_attn_decode<4, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
-  else if (R <= 8) dec::k_attn_decode<8, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
-  else dec::k_attn_decode<16, DC><<<grid, dec::kThreads, 0, ctx->stream>>>(a);
+  dim3 blk(dec::kThreads);
+  unsigned cl = (unsigned)a.splits;
+  if (R <= 1) return launch_pdl_cluster(dec::k_attn_decode<1, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
+  if (R <= 2) return launch_pdl_cluster(dec::k_attn_decode<2, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
+  if (R <= 4) return launch_pdl_cluster(dec::k_attn_decode<4, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
+  if (R <= 8) return launch_pdl_cluster(dec::k_attn_decode<8, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
+  return launch_pdl_cluster(dec::k_attn_decode<16, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
 }
 
 static bool aligned_view(const pai_tensor& t, int vec) {
@@ -259,45 +297,39 @@ bool attn_decode_fits(const pai_tensor& q, const pai_tensor& k, const pai_tensor
 
 // pos_dev: when set, the query position is read on the device and k, v are the whole caches (L = capacity); the
 // key splits are then sized for the capacity and splits past the filled prefix contribute nothing.
+// rope: fused RoPE + cache append (q, kn, vn unrotated; a.k / a.v are the caches the new rows are written into).
+pai_status attn_decode_run(pai_ctx* ctx, dec::Args& a, bool rope) {
+  int kend = (a.causal && !a.pos_dev) ? std::min(a.L, a.pos_offset + a.S) : a.L;
+  if (kend < 1) kend = 1;
+  // one 32-key tile per warp (128 keys per CTA) while a cluster of at most 8 CTAs covers the keys, else longer splits
+  int kps = dec::kWarps * dec::kTile;
+  int need = (kend + dec::kMaxCluster - 1) / dec::kMaxCluster;
+  if (need > kps) kps = (need + kps - 1) / kps * kps;
+  a.keys_per_split = kps;
+  a.splits = (kend + kps - 1) / kps;
+  a.error_flag = ctx->d_error_flag;
+  dim3 grid((unsigned)a.splits, (unsigned)a.KVH, (unsigned)a.B);
+  cudaError_t e;
+  if (a.D == 64) e = rope ? launch_decode<64, true>(ctx, a, grid) : launch_decode<64, false>(ctx, a, grid);
+  else e = rope ? launch_decode<0, true>(ctx, a, grid) : launch_decode<0, false>(ctx, a, grid);
+  PAI_PDL_LAUNCH(e, "attn decode");
+  return PAI_OK;
+}
+
+static dec::View dview(const pai_tensor& t) {
+  return dec::View{static_cast<const float*>(t.base) + t.offset, t.strides[0], t.strides[1], t.strides[2]};
+}
+
 pai_status attn_decode_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int B, int H,
                            int KVH, int S, int L, int D, float scale, int causal, int pos_offset, float* out, float* lse,
                            const float* pos_dev) {
   dec::Args a{};
   a.pos_dev = pos_dev;
-  a.error_flag = ctx->d_error_flag;
-  auto view = [](const pai_tensor& t) {
-    return dec::View{static_cast<const float*>(t.base) + t.offset, t.strides[0], t.strides[1], t.strides[2]};
-  };
-  a.q = view(q); a.k = view(k); a.v = view(v);
+  a.q = dview(q); a.k = dview(k); a.v = dview(v);
   a.B = B; a.H = H; a.KVH = KVH; a.S = S; a.L = L; a.D = D; a.g = H / KVH; a.rows = a.g * S;
   a.pos_offset = pos_offset; a.causal = causal; a.scale = scale;
   a.out = out; a.lse = lse;
-  int kend = (causal && !pos_dev) ? std::min(L, pos_offset + S) : L;
-  if (kend < 1) kend = 1;
-  // enough CTAs for two per SM, each split at least one 128-key sweep of the CTA's four warps
-  int64_t heads = (int64_t)B * KVH;
-  int max_splits = (kend + dec::kWarps * dec::kTile - 1) / (dec::kWarps * dec::kTile);
-  int splits = (int)std::min<int64_t>(max_splits, std::max<int64_t>(1, (2LL * ctx->sm_count + heads - 1) / heads));
-  int kps = (kend + splits - 1) / splits;
-  kps = (kps + dec::kTile - 1) / dec::kTile * dec::kTile;
-  splits = (kend + kps - 1) / kps;
-  a.splits = splits;
-  a.keys_per_split = kps;
-  Scratch part;
-  if (splits > 1) {
-    PAI_TRY(scratch(ctx, (size_t)heads * splits * a.rows * (D + 2) * 4, &part));
-    a.part = static_cast<float*>(part.p);
-    if (heads <= kCounters) a.counters = ctx->d_counters;  // merged by the last CTA, no second launch
-  }
-  dim3 grid((unsigned)splits, (unsigned)KVH, (unsigned)B);
-  if (D == 64) launch_decode<64>(ctx, a, grid);
-  else launch_decode<0>(ctx, a, grid);
-  PAI_LAUNCH_CHECK("attn decode");
-  if (splits > 1 && !a.counters) {
-    dec::k_attn_decode_combine<<<dim3((unsigned)a.rows, (unsigned)KVH, (unsigned)B), dec::kMaxD, 0, ctx->stream>>>(a);
-    PAI_LAUNCH_CHECK("attn decode combine");
-  }
-  return PAI_OK;
+  return attn_decode_run(ctx, a, false);
 }
 
 }  // namespace pai
@@ -341,6 +373,8 @@ struct RopeAppendArgs {
 };
 
 __global__ void k_rope_append(const RopeAppendArgs a) {
+  pdl_trigger();
+  pdl_wait();
   float pf = a.pos[0];
   int p = (int)pf;
   if (!(pf >= 0.0f) || p + a.S > a.T || p + a.S > a.tab_rows) {
@@ -499,9 +533,55 @@ PAI_API pai_status pai_rope_append(pai_ctx* ctx, const pai_tensor* q, const pai_
   a.error_flag = ctx->d_error_flag;
   int64_t rows = (int64_t)B * S * (H + 2 * a.KVH);
   if (rows > 0) {
-    k_rope_append<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(a);
-    PAI_LAUNCH_CHECK("rope append");
+    PAI_PDL_LAUNCH(launch_pdl(k_rope_append, dim3(grid_for(ctx, rows * 32, 256)), dim3(256), 0, ctx->stream, a),
+                   "rope append");
   }
   *q_out = r;
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_attn_decode_step(pai_ctx* ctx, const pai_tensor* q, const pai_tensor* k, const pai_tensor* v,
+                                        const pai_tensor* cos_table, const pai_tensor* sin_table, const pai_tensor* k_cache,
+                                        const pai_tensor* v_cache, const pai_tensor* pos, float scale, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  const pai_tensor* ins[6] = {q, k, v, cos_table, sin_table, pos};
+  const char* names[6] = {"q", "k", "v", "cos", "sin", "pos"};
+  for (int i = 0; i < 6; i++) PAI_TRY(check_view(ctx, ins[i], names[i]));
+  if (q->rank != 4 || k->rank != 4 || v->rank != 4 || numel(*pos) != 1 || cos_table->rank != 2 || sin_table->rank != 2)
+    return set_error(PAI_ERR_ARGUMENT, "AttnDecodeStep: q [B,H,S,D], k and v [B,KVH,S,D], [T,D] tables and a position expected");
+  for (int i = 0; i < 4; i++)
+    if (k->dims[i] != v->dims[i]) return set_error(PAI_ERR_ARGUMENT, "AttnDecodeStep: k and v shapes differ");
+  int B = q->dims[0], H = q->dims[1], S = q->dims[2], D = q->dims[3], KVH = k->dims[1];
+  if (k->dims[0] != B || k->dims[2] != S || k->dims[3] != D || D % 2 || KVH < 1 || H % KVH)
+    return set_error(PAI_ERR_ARGUMENT, "AttnDecodeStep: q %s and k %s disagree", shape_str(*q).c_str(), shape_str(*k).c_str());
+  if (q->strides[3] != 1 || k->strides[3] != 1 || v->strides[3] != 1 || cos_table->strides[1] != 1 ||
+      sin_table->strides[1] != 1 || cos_table->strides[0] != sin_table->strides[0] || cos_table->dims[1] != D ||
+      sin_table->dims[1] != D || sin_table->dims[0] != cos_table->dims[0])
+    return set_error(PAI_ERR_ARGUMENT, "AttnDecodeStep: rows must be contiguous and the tables [T, %d] of one layout", D);
+  PAI_TRY(check_cache(ctx, k_cache, k, "k_cache"));
+  PAI_TRY(check_cache(ctx, v_cache, v, "v_cache"));
+  for (int i = 0; i < 4; i++)
+    if (k_cache->dims[i] != v_cache->dims[i]) return set_error(PAI_ERR_ARGUMENT, "AttnDecodeStep: k and v caches differ");
+  if (!attn_decode_fits(*q, *k_cache, *v_cache, H, KVH, S, D))
+    return set_error(PAI_ERR_UNSUPPORTED, "AttnDecodeStep: needs S*H/KVH <= 16, head dim <= 64 (multiple of 4) and aligned caches");
+  int32_t od[4] = {B, S, H, D};
+  pai_tensor ro;
+  PAI_TRY(alloc_tensor(ctx, 4, od, q->dtype, false, &ro));
+  Scratch lse;
+  PAI_TRY(scratch(ctx, (size_t)B * H * S * 4, &lse));
+  int T = k_cache->dims[2];
+  dec::Args a{};
+  a.q = dview(*q); a.k = dview(*k_cache); a.v = dview(*v_cache);
+  a.kn = dview(*k); a.vn = dview(*v);
+  a.cos = fptr(*cos_table); a.sin = fptr(*sin_table); a.tab_stride = cos_table->strides[0]; a.tab_rows = cos_table->dims[0];
+  a.B = B; a.H = H; a.KVH = KVH; a.S = S; a.L = T; a.D = D; a.g = H / KVH; a.rows = a.g * S;
+  a.pos_dev = fptr(*pos); a.causal = 1; a.scale = scale;
+  a.out = fptr(ro); a.lse = static_cast<float*>(lse.p);
+  if (numel(ro) > 0) {
+    KernelTimerScope timer(ctx, "attn_decode", 8.0 * B * KVH * (double)T * D);
+    PAI_TRY(attn_decode_run(ctx, a, true));
+  }
+  *out = ro;
   return PAI_OK;
 }

@@ -7,6 +7,7 @@
 
 #include <mutex>
 #include <string>
+#include <utility>
 #include <unordered_map>
 #include <unordered_set>
 #include <vector>
@@ -23,6 +24,13 @@ pai_status cuda_error(cudaError_t e, const char* what);
 
 #define PAI_TRY(x) do { pai_status _s = (x); if (_s != PAI_OK) return _s; } while (0)
 #define PAI_CUDA(x) do { cudaError_t _e = (x); if (_e != cudaSuccess) return ::pai::cuda_error(_e, #x); } while (0)
+// A launch through launch_pdl: reports its error and counts the launch on the context.
+#define PAI_PDL_LAUNCH(call, what)                                      \
+  do {                                                                  \
+    cudaError_t _e = (call);                                            \
+    if (_e != cudaSuccess) return ::pai::cuda_error(_e, what);          \
+    ctx->launches++;                                                    \
+  } while (0)
 // Every kernel launch site ends with this: it reports launch errors and counts the launch on the context.
 #define PAI_LAUNCH_CHECK(what)                                          \
   do {                                                                  \
@@ -67,8 +75,6 @@ struct pai_ctx {
   int64_t in_use = 0, peak = 0, reserved = 0;
   // device flag the kernels with bounded waits report into (0 = ok)
   int* d_error_flag = nullptr;
-  // zeroed arrival counters for kernels whose last CTA finishes the work of the others (each user resets its own)
-  int* d_counters = nullptr;
   pai::NcclState* nccl = nullptr;
   char name[128] = {0};
   // instrumentation: kernel launches issued, a stream timer, and per-kernel-family event timing
@@ -152,7 +158,47 @@ void collapse(int rank, const int32_t* dims, const pai_tensor* const* views, int
 
 inline float* fptr(const pai_tensor& t) { return static_cast<float*>(t.base) + t.offset; }
 
-constexpr int kCounters = 1 << 16;  // entries of pai_ctx::d_counters
+// Programmatic dependent launch for the decode-step kernels: a kernel launched with launch_pdl may start while the
+// previous kernel on the stream is still running. It must call pdl_wait() before it reads anything an earlier
+// kernel wrote (and before it exits); work that only reads data written before (weights, caches of earlier steps)
+// may be issued first. pdl_trigger() lets the next such kernel launch early.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// launch_pdl with thread-block clusters of cluster_x CTAs along x (grid.x must be a multiple of cluster_x).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                               unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Grid size for a grid-stride loop: at most `waves` resident waves of `threads`-thread blocks.
 inline int grid_for(pai_ctx* ctx, int64_t n, int threads, int per_thread = 1, int waves = 8) {
@@ -203,6 +249,11 @@ __device__ __forceinline__ void row_offsets3(const pai::DView& a, const pai::DVi
     r = q;
   }
 }
+
+// Device side of launch_pdl: wait for the previous kernel's completion (and its memory), and allow the next kernel
+// to launch. Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // SiLU(g)·u with the element operations of the reference's Sigmoid (sign-split, CpuComputeBackend.cs:304-317), SiLU
 // (x·sigmoid(x), :385-391) and Mul, each rounded once: shared by the SwiGLU kernel and the fused decode epilogue.

@@ -2,6 +2,7 @@
 // Contract: ProjectAI.Core/IComputeBackend.cs:14-18 (Allocate/FromHost/ToHost/Copy) and :69-95 (scopes), with
 // the lifetime semantics of ProjectAI.Backends.Torch/TorchComputeBackend.cs:208-218.
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -27,6 +28,14 @@ pai_status cuda_error(cudaError_t e, const char* what) {
   if (e == cudaErrorMemoryAllocation)
     return set_error(PAI_ERR_OUT_OF_MEMORY, "CUDA out of memory (%s): %s", what, cudaGetErrorString(e));
   return set_error(PAI_ERR_CUDA, "CUDA error in %s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("PAI_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 pai_status enter(pai_ctx* ctx) {
@@ -379,13 +388,11 @@ PAI_API pai_status pai_ctx_create(int device, pai_ctx** out) {
   cudaError_t e1 = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
   cudaError_t e2 = cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking);
   cudaError_t e3 = cudaMalloc(&c->d_error_flag, 64);
-  cudaError_t e4 = cudaMalloc(&c->d_counters, pai::kCounters * sizeof(int));
-  if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess || e4 != cudaSuccess) {
+  if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
     delete c;
     return set_error(PAI_ERR_CUDA, "failed to create streams for device %d", device);
   }
   cudaMemset(c->d_error_flag, 0, 64);
-  cudaMemset(c->d_counters, 0, pai::kCounters * sizeof(int));
   *out = c;
   return PAI_OK;
 }
@@ -404,7 +411,6 @@ PAI_API pai_status pai_ctx_destroy(pai_ctx* ctx) {
   for (auto& kv : ctx->graph_owner)  // blocks parked by graphs the caller did not destroy
     if (!ctx->live.count(kv.first)) cudaFree(kv.first);
   cudaFree(ctx->d_error_flag);
-  cudaFree(ctx->d_counters);
   if (ctx->pinned) {
     cudaFreeHost(ctx->pinned);
     for (int i = 0; i < pai::kPinnedChunks; i++) cudaEventDestroy(ctx->pinned_ev[i]);

@@ -24,6 +24,8 @@ __global__ void k_gather_rows(const float* __restrict__ table, const int32_t* __
 // and yields a zero row.
 __global__ void k_gather_rows_dev(const float* __restrict__ table, const float* __restrict__ ids, float* __restrict__ out,
                                   int64_t n, int dim, int vocab, int* error_flag) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
     float f = ids[r];
     int id = (int)f;
@@ -280,8 +282,9 @@ PAI_API pai_status pai_gather_dev(pai_ctx* ctx, const pai_tensor* table, const p
     Scratch ht;
     PAI_TRY(dense_input(ctx, *table, &tp, &ht));
     int blocks = n < ctx->sm_count * 16 ? (int)n : ctx->sm_count * 16;
-    k_gather_rows_dev<<<blocks, 256, 0, ctx->stream>>>(tp, fptr(*ids), fptr(r), n, dim, vocab, ctx->d_error_flag);
-    PAI_LAUNCH_CHECK("gather_dev");
+    PAI_PDL_LAUNCH(launch_pdl(k_gather_rows_dev, dim3(blocks), dim3(256), 0, ctx->stream, tp,
+                              static_cast<const float*>(fptr(*ids)), fptr(r), n, dim, vocab, ctx->d_error_flag),
+                   "gather_dev");
   }
   *out = r;
   return PAI_OK;

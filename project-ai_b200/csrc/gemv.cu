@@ -48,7 +48,28 @@ struct GemvArgs {
   int rows, n, k;                // n = logical output columns
   int ksplit;                    // warps that share one group of 4 W rows (1, 2, 4 or 8)
   int mode;
+  const float* norm_w;           // when set, x rows are RMS-normalised with this weight before the product
+  float eps;
 };
+
+// 1 / sqrt(mean(x²) + eps) of one row of k elements, summed as k_rmsnorm_fwd_reg does for k = 128·C (lane-interleaved
+// float4 chunks, then a warp sum) and as k_rmsnorm_fwd does otherwise, so the normalised row is bit-identical to the
+// separate RmsNorm kernel's output.
+__device__ __forceinline__ float row_inv_rms(const float* x, int k, float eps, bool vec) {
+  const int lane = threadIdx.x & 31;
+  float ss = 0.0f;
+  if (vec && k % 128 == 0) {
+    for (int c = 0; c < k / 128; c++) {
+      float4 v = reinterpret_cast<const float4*>(x)[c * 32 + lane];
+      ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+    }
+  } else {
+    for (int j = lane; j < k; j += 32) { float v = x[j]; ss = fmaf(v, v, ss); }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)k), eps)));
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -69,10 +90,14 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_tn(const GemvArgs a) {
   constexpr int R = kGemvRowsPerWarp;
   constexpr int kWarps = kGemvThreads / 32;
   __shared__ float part[kWarps][MR][P][R];
+  __shared__ float s_inv[MR];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups_per_cta = kWarps / a.ksplit;
   const int group = warp / a.ksplit, kpart = warp - group * a.ksplit;
   const int n0 = (blockIdx.x * groups_per_cta + group) * R;
+  const bool active = n0 < a.n;
+  const bool norm = a.norm_w != nullptr;
+  pdl_trigger();
   float acc[MR][P][R];
 #pragma unroll
   for (int m = 0; m < MR; m++)
@@ -81,73 +106,93 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_tn(const GemvArgs a) {
 #pragma unroll
       for (int r = 0; r < R; r++) acc[m][p][r] = 0.0f;
 
-  if (n0 < a.n) {
-    const float* wr[P][R];
+  const float* wr[P][R];
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-      int col = n0 + r < a.n ? n0 + r : a.n - 1;  // tail columns re-read the last row; their sums are discarded
-      if (P == 2) {
-        wr[0][r] = a.w[0] + (int64_t)col * a.sw[0];
-        wr[P - 1][r] = a.w[1] + (int64_t)col * a.sw[1];
-      } else {
-        int s = 0;
-        while (s + 1 < a.nseg && col >= a.seg_start[s + 1]) s++;
-        wr[0][r] = a.w[s] + (int64_t)(col - a.seg_start[s]) * a.sw[s];
-      }
-    }
-    if (VEC) {
-      const int k4 = a.k >> 2;
-      const int per = (k4 + a.ksplit - 1) / a.ksplit;
-      const int kb = kpart * per, ke = min(k4, kb + per);
-      for (int i = kb + lane; i < ke; i += 32 * U) {
-        float4 wv[U][P][R];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          int j = i + 32 * u;
-#pragma unroll
-          for (int p = 0; p < P; p++)
-#pragma unroll
-            for (int r = 0; r < R; r++)
-              wv[u][p][r] = j < ke ? __ldcs(reinterpret_cast<const float4*>(wr[p][r]) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          int j = i + 32 * u;
-          if (j >= ke) break;
-#pragma unroll
-          for (int m = 0; m < MR; m++) {
-            if (m >= a.rows) break;
-            float4 xv = __ldg(reinterpret_cast<const float4*>(a.x + a.xoff[m]) + j);
-#pragma unroll
-            for (int p = 0; p < P; p++)
-#pragma unroll
-              for (int r = 0; r < R; r++) {
-                acc[m][p][r] = fmaf(xv.x, wv[u][p][r].x, acc[m][p][r]);
-                acc[m][p][r] = fmaf(xv.y, wv[u][p][r].y, acc[m][p][r]);
-                acc[m][p][r] = fmaf(xv.z, wv[u][p][r].z, acc[m][p][r]);
-                acc[m][p][r] = fmaf(xv.w, wv[u][p][r].w, acc[m][p][r]);
-              }
-          }
-        }
-      }
+  for (int r = 0; r < R; r++) {
+    int col = n0 + r < a.n ? n0 + r : a.n - 1;  // tail columns re-read the last row; their sums are discarded
+    if (col < 0) col = 0;
+    if (P == 2) {
+      wr[0][r] = a.w[0] + (int64_t)col * a.sw[0];
+      wr[P - 1][r] = a.w[1] + (int64_t)col * a.sw[1];
     } else {
-      const int per = (a.k + a.ksplit - 1) / a.ksplit;
-      const int kb = kpart * per, ke = min(a.k, kb + per);
-      for (int i = kb + lane; i < ke; i += 32) {
-        float wv[P][R];
+      int s = 0;
+      while (s + 1 < a.nseg && col >= a.seg_start[s + 1]) s++;
+      wr[0][r] = a.w[s] + (int64_t)(col - a.seg_start[s]) * a.sw[s];
+    }
+  }
+  const int k_units = VEC ? (a.k >> 2) : a.k;
+  const int per = (k_units + a.ksplit - 1) / a.ksplit;
+  const int kb = kpart * per, ke = min(k_units, kb + per);
+  float4 wv[U][P][R];
+  auto load_w = [&](int i) {
 #pragma unroll
-        for (int p = 0; p < P; p++)
+    for (int u = 0; u < U; u++) {
+      int j = i + 32 * u;
 #pragma unroll
-          for (int r = 0; r < R; r++) wv[p][r] = __ldcs(wr[p][r] + i);
+      for (int p = 0; p < P; p++)
+#pragma unroll
+        for (int r = 0; r < R; r++)
+          wv[u][p][r] = j < ke ? __ldcs(reinterpret_cast<const float4*>(wr[p][r]) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  // the first trip's weights are requested before waiting on the previous kernel (it never writes the weights)
+  if (VEC && active) load_w(kb + lane);
+  pdl_wait();
+  if (norm) {  // the RmsNorm of each x row, shared by the CTA's warps
+    for (int m = warp; m < a.rows && m < MR; m += kWarps) {
+      float inv = row_inv_rms(a.x + a.xoff[m], a.k, a.eps, VEC);
+      if (lane == 0) s_inv[m] = inv;
+    }
+    __syncthreads();
+  }
+
+  if (active && VEC) {
+    for (int i = kb + lane; i < ke; i += 32 * U) {
+      if (i != kb + lane) load_w(i);
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        int j = i + 32 * u;
+        if (j >= ke) break;
 #pragma unroll
         for (int m = 0; m < MR; m++) {
           if (m >= a.rows) break;
-          float xv = __ldg(a.x + a.xoff[m] + i);
+          float4 xv = __ldg(reinterpret_cast<const float4*>(a.x + a.xoff[m]) + j);
+          if (norm) {  // RmsNorm's (x · inv) · w, each product rounded once
+            float inv = s_inv[m];
+            float4 nw = __ldg(reinterpret_cast<const float4*>(a.norm_w) + j);
+            xv.x = __fmul_rn(__fmul_rn(xv.x, inv), nw.x);
+            xv.y = __fmul_rn(__fmul_rn(xv.y, inv), nw.y);
+            xv.z = __fmul_rn(__fmul_rn(xv.z, inv), nw.z);
+            xv.w = __fmul_rn(__fmul_rn(xv.w, inv), nw.w);
+          }
 #pragma unroll
           for (int p = 0; p < P; p++)
 #pragma unroll
-            for (int r = 0; r < R; r++) acc[m][p][r] = fmaf(xv, wv[p][r], acc[m][p][r]);
+            for (int r = 0; r < R; r++) {
+              acc[m][p][r] = fmaf(xv.x, wv[u][p][r].x, acc[m][p][r]);
+              acc[m][p][r] = fmaf(xv.y, wv[u][p][r].y, acc[m][p][r]);
+              acc[m][p][r] = fmaf(xv.z, wv[u][p][r].z, acc[m][p][r]);
+              acc[m][p][r] = fmaf(xv.w, wv[u][p][r].w, acc[m][p][r]);
+            }
         }
+      }
+    }
+  } else if (active) {
+    for (int i = kb + lane; i < ke; i += 32) {
+      float w1[P][R];
+#pragma unroll
+      for (int p = 0; p < P; p++)
+#pragma unroll
+        for (int r = 0; r < R; r++) w1[p][r] = __ldcs(wr[p][r] + i);
+#pragma unroll
+      for (int m = 0; m < MR; m++) {
+        if (m >= a.rows) break;
+        float xv = __ldg(a.x + a.xoff[m] + i);
+        if (norm) xv = __fmul_rn(__fmul_rn(xv, s_inv[m]), __ldg(a.norm_w + i));
+#pragma unroll
+        for (int p = 0; p < P; p++)
+#pragma unroll
+          for (int r = 0; r < R; r++) acc[m][p][r] = fmaf(xv, w1[p][r], acc[m][p][r]);
       }
     }
   }
@@ -205,8 +250,7 @@ constexpr int kStages = 4;       // shared-memory ring depth
 constexpr int kSlots = 2;        // tensor-memory A slots (hi + lo, 64 columns each)
 constexpr int kWBytes = kRowsW * kK * 4;
 constexpr int kThreads = 192;    // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 converters / epilogue
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColAcc = 0, kColA = 64;
+constexpr uint32_t kColAcc = 0;
 
 struct Args {
   const float* xhi;              // [kt][rows_pad x 32] pre-split, swizzled x tiles
@@ -225,8 +269,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-template <int NP>  // x rows padded to the MMA's N (16 or 32)
+// x = hi + lo for the MMA: hi keeps the sign, exponent and top 10 mantissa bits (exactly representable in tf32) and
+// lo = x - hi is exact in fp32; the MMA then reads lo to tf32 precision. Per product the error stays near 2^-20
+// relative, far inside the 1e-4 tolerance, and the split costs one AND and one subtraction per element.
+__device__ __forceinline__ void split_w(float x, float& hi, float& lo) {
+  hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  lo = x - hi;
+}
+
+template <int NP>  // NP: x rows padded to the MMA's N (16 or 32)
 __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CUtensorMap wmap, const Args a) {
+  constexpr uint32_t kColA = 64;
+  constexpr uint32_t kTmemCols = 256;
   constexpr int kXBytes = NP * 128;
   constexpr int kStage = kWBytes + 2 * kXBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -256,25 +310,37 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+      // the first stages' weight tiles are requested before waiting on the previous kernel (which wrote x's tiles)
+      const int pre = nk < kStages ? nk : kStages;
+      for (int i = 0; i < pre; i++) {
+        mbar_expect_tx(&full[i], kWBytes + 2 * kXBytes);
+        tma_load_2d(smem + i * kStage, &wmap, (k0 + i) * kK, n0, &full[i]);
+      }
+      pdl_wait();
       int issued = 0;
       for (int i = 0; i < nk && !s_abort; i++, issued++) {
         int s = i % kStages;
-        if (!mbar_wait(&stage_free[s], ((i / kStages) & 1) ^ 1)) { atomicExch(a.error_flag, 41); s_abort = 1; break; }
         uint8_t* st = smem + s * kStage;
-        mbar_expect_tx(&full[s], kWBytes + 2 * kXBytes);
-        tma_load_2d(st, &wmap, (k0 + i) * kK, n0, &full[s]);
+        if (i >= pre) {
+          if (!mbar_wait(&stage_free[s], ((i / kStages) & 1) ^ 1)) { atomicExch(a.error_flag, 41); s_abort = 1; break; }
+          mbar_expect_tx(&full[s], kWBytes + 2 * kXBytes);
+          tma_load_2d(st, &wmap, (k0 + i) * kK, n0, &full[s]);
+        }
         size_t xoff = (size_t)(k0 + i) * (kXBytes / 4);
         bulk_g2s(st + kWBytes, a.xhi + xoff, kXBytes, &full[s]);
         bulk_g2s(st + kWBytes + kXBytes, a.xlo + xoff, kXBytes, &full[s]);
       }
-      // every copy issued must land before the CTA may exit
+      // every copy issued (the pre-issued weight tiles included) must land before the CTA may exit
+      if (issued < pre) issued = pre;
       for (int i = (issued > kStages ? issued - kStages : 0); i < issued; i++) mbar_wait(&full[i % kStages], (i / kStages) & 1);
     }
   } else if (warp == 1) {
+    pdl_wait();
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(128, NP);
       for (int i = 0; i < nk && !s_abort; i++) {
@@ -288,9 +354,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
 #pragma unroll
         for (int kk = 0; kk < kK / 8; kk++) {
           uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          mma_ts(tmem + kColAcc, alo + kk * 8, desc_sw128(xhi + kk * 32), idesc, acc);
-          mma_ts(tmem + kColAcc, ahi + kk * 8, desc_sw128(xlo + kk * 32), idesc, 1u);
-          mma_ts(tmem + kColAcc, ahi + kk * 8, desc_sw128(xhi + kk * 32), idesc, 1u);
+          uint32_t d = tmem + kColAcc;
+          mma_ts(d, alo + kk * 8, desc_sw128(xhi + kk * 32), idesc, acc);
+          mma_ts(d, ahi + kk * 8, desc_sw128(xlo + kk * 32), idesc, 1u);
+          mma_ts(d, ahi + kk * 8, desc_sw128(xhi + kk * 32), idesc, 1u);
         }
         commit(&stage_free[s]);
         commit(&slot_free[t]);
@@ -298,6 +365,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
       commit(acc_full);
     }
   } else {
+    pdl_wait();
     // converters: warp quadrant q owns W rows 32q..32q+31 of the tile (its TMEM lanes)
     const int q = warp & 3;
     const int r = q * 32 + lane;
@@ -314,10 +382,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
 #pragma unroll
       for (int c = 0; c < 8; c++) {
         float4 v = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
-        split_tf32(v.x, hi[4 * c], lo[4 * c]);
-        split_tf32(v.y, hi[4 * c + 1], lo[4 * c + 1]);
-        split_tf32(v.z, hi[4 * c + 2], lo[4 * c + 2]);
-        split_tf32(v.w, hi[4 * c + 3], lo[4 * c + 3]);
+        split_w(v.x, hi[4 * c], lo[4 * c]);
+        split_w(v.y, hi[4 * c + 1], lo[4 * c + 1]);
+        split_w(v.z, hi[4 * c + 2], lo[4 * c + 2]);
+        split_w(v.w, hi[4 * c + 3], lo[4 * c + 3]);
       }
       tmem_st32(tmem + lane_base + kColA + t * 64, hi);
       tmem_st32(tmem + lane_base + kColA + t * 64 + 32, lo);
@@ -357,19 +425,39 @@ struct XPack {
   const float* x;
   int64_t xoff[kGemvMaxRows];
   int rows, np, k, kt;
+  const float* norm_w;  // when set, each row is RMS-normalised first (RmsNorm's values, bit for bit)
+  float eps;
+  int vec;              // rows are 16-byte aligned with k a multiple of 4
 };
 
+// One CTA per (padded) x row: optional RmsNorm, then the tf32 hi/lo split into the swizzled tiles.
 __global__ void __launch_bounds__(256) k_pack_x(const XPack p, float* __restrict__ hi, float* __restrict__ lo) {
-  const int chunks = p.kt * p.np * 8;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += gridDim.x * blockDim.x) {
-    int c = i & 7, rr = (i >> 3) % p.np, kb = (i >> 3) / p.np;
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float s_inv;
+  const int rr = blockIdx.x;
+  const bool real = rr < p.rows;
+  const float* src = real ? p.x + p.xoff[rr] : nullptr;
+  if (p.norm_w && real) {
+    if (threadIdx.x < 32) {
+      float inv = row_inv_rms(src, p.k, p.eps, p.vec != 0);
+      if (threadIdx.x == 0) s_inv = inv;
+    }
+    __syncthreads();
+  }
+  const int chunks = p.kt * 8;  // 16-byte chunks of the row across all k tiles
+  for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
+    int c = i & 7, kb = i >> 3;
     int k = kb * kK + 4 * c;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (rr < p.rows) {
-      const float* src = p.x + p.xoff[rr] + k;
+    if (real) {
 #pragma unroll
       for (int e = 0; e < 4; e++)
-        if (k + e < p.k) v[e] = src[e];
+        if (k + e < p.k) {
+          float xv = src[k + e];
+          if (p.norm_w) xv = __fmul_rn(__fmul_rn(xv, s_inv), p.norm_w[k + e]);
+          v[e] = xv;
+        }
     }
     float h[4], l[4];
 #pragma unroll
@@ -389,6 +477,8 @@ constexpr size_t smem_bytes() {
 // y[m, c] = a (store), res[m, c] + a (residual), SiLU(a)·b (SiLU·mul).
 __global__ void k_gemv_finish(const float* __restrict__ pa, int sa, const float* __restrict__ pb, int sb, int rows, int n,
                               float* __restrict__ y, int64_t ldy, int mode, const float* __restrict__ res, int64_t ldr) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t total = (int64_t)rows * n, plane = total;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     int m = (int)(i / n), c = (int)(i - (int64_t)m * n);
@@ -448,7 +538,12 @@ static pai_status gemv_tc_segment(pai_ctx* ctx, const float* xh, const float* xl
   if (cr != CUDA_SUCCESS) return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for W [%d, %d]", (int)cr, n, k);
 
   const int n_tiles = (n + kRowsW - 1) / kRowsW;
+  static const int forced_splits = [] {
+    const char* e = getenv("PAI_GEMV_TC_SPLITS");
+    return e ? atoi(e) : 0;
+  }();
   int splits = std::max(1, std::min(2 * ctx->sm_count / n_tiles, kt / 4));
+  if (forced_splits > 0) splits = std::min(forced_splits, kt);
   int ktp = (kt + splits - 1) / splits;
   splits = (kt + ktp - 1) / ktp;
   Args a{};
@@ -467,24 +562,28 @@ static pai_status gemv_tc_segment(pai_ctx* ctx, const float* xh, const float* xl
   dim3 grid((unsigned)n_tiles, (unsigned)splits);
   if (np == 16) {
     static bool attr = false;
-    if (!attr) { PAI_CUDA(cudaFuncSetAttribute(k_gemv_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<16>())); attr = true; }
-    k_gemv_tc<16><<<grid, kThreads, smem_bytes<16>(), ctx->stream>>>(map, a);
+    if (!attr) {
+      PAI_CUDA(cudaFuncSetAttribute(k_gemv_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<16>()));
+      attr = true;
+    }
+    PAI_PDL_LAUNCH(launch_pdl(k_gemv_tc<16>, grid, dim3(kThreads), smem_bytes<16>(), ctx->stream, map, a), "gemv tc");
   } else {
     static bool attr = false;
-    if (!attr) { PAI_CUDA(cudaFuncSetAttribute(k_gemv_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<32>())); attr = true; }
-    k_gemv_tc<32><<<grid, kThreads, smem_bytes<32>(), ctx->stream>>>(map, a);
+    if (!attr) {
+      PAI_CUDA(cudaFuncSetAttribute(k_gemv_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<32>()));
+      attr = true;
+    }
+    PAI_PDL_LAUNCH(launch_pdl(k_gemv_tc<32>, grid, dim3(kThreads), smem_bytes<32>(), ctx->stream, map, a), "gemv tc");
   }
-  PAI_LAUNCH_CHECK("gemv tc");
   return PAI_OK;
 }
 
 template <int MR, int U, int P>
 static pai_status launch_gemv_mr(pai_ctx* ctx, const GemvArgs& g, bool vec, int grid) {
-  if (vec)
-    k_gemv_tn<MR, U, true, P><<<grid, kGemvThreads, 0, ctx->stream>>>(g);
-  else
-    k_gemv_tn<MR, U, false, P><<<grid, kGemvThreads, 0, ctx->stream>>>(g);
-  PAI_LAUNCH_CHECK("gemv");
+  cudaError_t e = vec ? launch_pdl(k_gemv_tn<MR, U, true, P>, dim3(grid), dim3(kGemvThreads), 0, ctx->stream, g)
+                      : launch_pdl(k_gemv_tn<MR, U, false, P>, dim3(grid), dim3(kGemvThreads), 0, ctx->stream, g);
+  if (e != cudaSuccess) return cuda_error(e, "gemv");
+  ctx->launches++;
   return PAI_OK;
 }
 
@@ -514,7 +613,7 @@ bool gemv_enabled() {
 //   SiLU·mul: y = SiLU(x · W_0ᵀ) · (x · W_1ᵀ)   (W_0, W_1 of one shape)
 // Output row m at y + m * ldy; residual row m at res + m * ldr.
 pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int rows, int k, const LinearSeg* segs, int nseg,
-                       int mode, float* y, int64_t ldy, const float* res, int64_t ldr) {
+                       int mode, float* y, int64_t ldy, const float* res, int64_t ldr, const float* norm_w, float eps) {
   if (rows < 1 || rows > kGemvMaxRows) return set_error(PAI_ERR_ARGUMENT, "gemv supports 1..%d rows", kGemvMaxRows);
   if (nseg < 1 || nseg > kGemvMaxSegs) return set_error(PAI_ERR_ARGUMENT, "gemv supports 1..%d weight segments", kGemvMaxSegs);
   if (mode == kGemvSiluMul && (nseg != 2 || segs[0].n != segs[1].n))
@@ -530,6 +629,7 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
   }
   for (int i = 0; i < rows; i++)
     if (xoff[i] % 4) vec = false;
+  if (norm_w && (uintptr_t)norm_w % 16) vec = false;
   const int n_out = mode == kGemvStore ? n_total : segs[0].n;
   KernelTimerScope timer(ctx, "gemv", wbytes + 4.0 * rows * (k + n_out));
   static const int tc_min_rows = [] {
@@ -548,10 +648,10 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
     PAI_TRY(scratch(ctx, xbytes, &xl));
     XPack xp{};
     xp.x = x; xp.rows = rows; xp.np = np; xp.k = k; xp.kt = kt;
+    xp.norm_w = norm_w; xp.eps = eps; xp.vec = vec ? 1 : 0;
     for (int i = 0; i < rows; i++) xp.xoff[i] = xoff[i];
-    int chunks = kt * np * 8;
-    k_pack_x<<<(chunks + 255) / 256, 256, 0, ctx->stream>>>(xp, static_cast<float*>(xh.p), static_cast<float*>(xl.p));
-    PAI_LAUNCH_CHECK("gemv x pack");
+    PAI_PDL_LAUNCH(launch_pdl(k_pack_x, dim3(np), dim3(256), 0, ctx->stream, xp, static_cast<float*>(xh.p),
+                              static_cast<float*>(xl.p)), "gemv x pack");
     const float* xhp = static_cast<const float*>(xh.p);
     const float* xlp = static_cast<const float*>(xl.p);
     if (mode == kGemvStore) {
@@ -562,9 +662,10 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
         PAI_TRY(gemv_tc_segment(ctx, xhp, xlp, rows, np, k, segs[s], y + col, ldy, false, &part, &sp));
         if (sp) {
           int64_t nn = (int64_t)rows * segs[s].n;
-          k_gemv_finish<<<grid_for(ctx, nn, 256), 256, 0, ctx->stream>>>(static_cast<float*>(part.p), sp, nullptr, 0, rows,
-                                                                         segs[s].n, y + col, ldy, kGemvStore, nullptr, 0);
-          PAI_LAUNCH_CHECK("gemv finish");
+          PAI_PDL_LAUNCH(launch_pdl(k_gemv_finish, dim3(grid_for(ctx, nn, 256)), dim3(256), 0, ctx->stream,
+                                    static_cast<const float*>(part.p), sp, static_cast<const float*>(nullptr), 0, rows,
+                                    segs[s].n, y + col, ldy, (int)kGemvStore, static_cast<const float*>(nullptr), (int64_t)0),
+                         "gemv finish");
         }
         col += segs[s].n;
       }
@@ -575,17 +676,18 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
     PAI_TRY(gemv_tc_segment(ctx, xhp, xlp, rows, np, k, segs[0], nullptr, 0, true, &pa, &sa));
     if (mode == kGemvSiluMul) PAI_TRY(gemv_tc_segment(ctx, xhp, xlp, rows, np, k, segs[1], nullptr, 0, true, &pb, &sb));
     int64_t nn = (int64_t)rows * segs[0].n;
-    k_gemv_finish<<<grid_for(ctx, nn, 256), 256, 0, ctx->stream>>>(static_cast<float*>(pa.p), sa,
-                                                                   static_cast<float*>(pb.p), sb, rows, segs[0].n, y, ldy,
-                                                                   mode, res, ldr);
-    PAI_LAUNCH_CHECK("gemv finish");
+    PAI_PDL_LAUNCH(launch_pdl(k_gemv_finish, dim3(grid_for(ctx, nn, 256)), dim3(256), 0, ctx->stream,
+                              static_cast<const float*>(pa.p), sa, static_cast<const float*>(pb.p), sb, rows, segs[0].n, y,
+                              ldy, mode, res, ldr),
+                   "gemv finish");
     return PAI_OK;
   }
 
   if (mode == kGemvSiluMul && rows > 16) {
     // the paired kernel holds 16 rows of accumulators: two launches of up to 16 rows each
-    PAI_TRY(linear_rows(ctx, x, xoff, 16, k, segs, nseg, mode, y, ldy, res, ldr));
-    return linear_rows(ctx, x, xoff + 16, rows - 16, k, segs, nseg, mode, y + 16 * ldy, ldy, res, ldr);
+    PAI_TRY(linear_rows(ctx, x, xoff, 16, k, segs, nseg, mode, y, ldy, res, ldr, norm_w, eps));
+    return linear_rows(ctx, x, xoff + 16, rows - 16, k, segs, nseg, mode, y + 16 * ldy, ldy, res ? res + 16 * ldr : nullptr,
+                       ldr, norm_w, eps);
   }
   GemvArgs g{};
   g.nseg = nseg;
@@ -599,12 +701,14 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
   g.seg_start[nseg] = start;
   g.x = x; g.y = y; g.ldy = ldy; g.res = res; g.ldr = ldr;
   g.rows = rows; g.n = n_out; g.k = k; g.mode = mode;
+  g.norm_w = norm_w; g.eps = eps;
   for (int i = 0; i < rows; i++) g.xoff[i] = xoff[i];
   const int groups = (n_out + kGemvRowsPerWarp - 1) / kGemvRowsPerWarp;
   const int k_units = vec ? k / 4 : k;
   int ksplit = 1;
-  // more warps per row group while the grid is below two waves of 16 warps per SM and each lane keeps >= 2 loads per row
-  while (ksplit < 8 && (int64_t)groups * ksplit < 2LL * ctx->sm_count * 16 && k_units / (ksplit * 2) >= 64) ksplit *= 2;
+  // more warps per row group while the grid still fits one resident wave (two 8-warp CTAs per SM) and each lane keeps
+  // >= 2 loads per row: every warp then issues its loads at once and no CTA waits for a second wave
+  while (ksplit < 8 && (int64_t)groups * ksplit * 2 <= (int64_t)ctx->sm_count * 16 && k_units / (ksplit * 2) >= 64) ksplit *= 2;
   g.ksplit = ksplit;
   const int groups_per_cta = (kGemvThreads / 32) / ksplit;
   const int grid = (groups + groups_per_cta - 1) / groups_per_cta;
@@ -615,15 +719,16 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
 pai_status gemv_tn(pai_ctx* ctx, const float* x, const int64_t* xoff, int rows, const float* w, int64_t sw, int n, int k,
                    float* y) {
   LinearSeg sg{w, sw, n};
-  return linear_rows(ctx, x, xoff, rows, k, &sg, 1, kGemvStore, y, n, nullptr, 0);
+  return linear_rows(ctx, x, xoff, rows, k, &sg, 1, kGemvStore, y, n, nullptr, 0, nullptr, 0.0f);
 }
 
 }  // namespace pai
 
 using namespace pai;
 
-PAI_API pai_status pai_linear_fused(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* weights, int32_t n_weights,
-                                    int32_t mode, const pai_tensor* residual, pai_tensor* out) {
+PAI_API pai_status pai_linear_fused(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* norm_weight, float eps,
+                                    const pai_tensor* weights, int32_t n_weights, int32_t mode, const pai_tensor* residual,
+                                    pai_tensor* out) {
   PAI_TRY(enter(ctx));
   std::lock_guard<std::recursive_mutex> lk(ctx->mu);
   PAI_TRY(check_view(ctx, x, "x"));
@@ -669,12 +774,20 @@ PAI_API pai_status pai_linear_fused(pai_ctx* ctx, const pai_tensor* x, const pai
     }
     xoff[r] = off;
   }
+  const float* nw = nullptr;
+  if (norm_weight) {
+    PAI_TRY(check_view(ctx, norm_weight, "norm weight"));
+    if (norm_weight->rank != 1 || norm_weight->dims[0] != k || norm_weight->strides[0] != 1)
+      return set_error(PAI_ERR_ARGUMENT, "LinearFused: the norm weight must be a contiguous [%d]", k);
+    nw = fptr(*norm_weight);
+  }
   int32_t od[PAI_MAX_RANK];
   for (int i = 0; i < x->rank - 1; i++) od[i] = x->dims[i];
   od[x->rank - 1] = n_out;
   pai_tensor r;
   PAI_TRY(alloc_tensor(ctx, x->rank, od, x->dtype, false, &r));
-  PAI_TRY(linear_rows(ctx, static_cast<const float*>(x->base), xoff, rows, k, segs, n_weights, mode, fptr(r), n_out, res, ldr));
+  PAI_TRY(linear_rows(ctx, static_cast<const float*>(x->base), xoff, rows, k, segs, n_weights, mode, fptr(r), n_out, res, ldr,
+                      nw, eps));
   *out = r;
   return PAI_OK;
 }

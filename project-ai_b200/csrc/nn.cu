@@ -20,6 +20,8 @@ __device__ __forceinline__ float sigmoid_dev(float v) {
 // ---------------------------------------------------------------- RMSNorm forward: one warp per row.
 __global__ void k_rmsnorm_fwd(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
                               int64_t rows, int d, float eps) {
+  pdl_trigger();
+  pdl_wait();
   int lane = threadIdx.x & 31;
   int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -43,6 +45,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm_fwd_reg(const float* __restrict
   const int lane = threadIdx.x & 31;
   int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  pdl_trigger();
+  pdl_wait();
   for (int64_t r = warp; r < rows; r += nwarps) {
     const float4* px = reinterpret_cast<const float4*>(x + r * d);
     float4 xv[C];
@@ -306,18 +310,21 @@ PAI_API pai_status pai_rmsnorm(pai_ctx* ctx, const pai_tensor* x, const pai_tens
     bool aligned = aligned16(xp) && aligned16(wp) && aligned16(fptr(r));
     int grid = grid_for(ctx, rows * 32, 256);
     float* yp = fptr(r);
+    cudaError_t e;
+    dim3 g(grid), blk(256);
     switch (aligned ? chunks : 0) {
-      case 1: k_rmsnorm_fwd_reg<1><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
-      case 2: k_rmsnorm_fwd_reg<2><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
-      case 4: k_rmsnorm_fwd_reg<4><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
-      case 6: k_rmsnorm_fwd_reg<6><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
-      case 8: k_rmsnorm_fwd_reg<8><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
-      case 12: k_rmsnorm_fwd_reg<12><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
-      case 16: k_rmsnorm_fwd_reg<16><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
-      case 32: k_rmsnorm_fwd_reg<32><<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, eps); break;
-      default: k_rmsnorm_fwd<<<grid, 256, 0, ctx->stream>>>(xp, wp, yp, rows, d, eps); break;
+      case 1: e = launch_pdl(k_rmsnorm_fwd_reg<1>, g, blk, 0, ctx->stream, xp, wp, yp, rows, eps); break;
+      case 2: e = launch_pdl(k_rmsnorm_fwd_reg<2>, g, blk, 0, ctx->stream, xp, wp, yp, rows, eps); break;
+      case 4: e = launch_pdl(k_rmsnorm_fwd_reg<4>, g, blk, 0, ctx->stream, xp, wp, yp, rows, eps); break;
+      case 6: e = launch_pdl(k_rmsnorm_fwd_reg<6>, g, blk, 0, ctx->stream, xp, wp, yp, rows, eps); break;
+      case 8: e = launch_pdl(k_rmsnorm_fwd_reg<8>, g, blk, 0, ctx->stream, xp, wp, yp, rows, eps); break;
+      case 12: e = launch_pdl(k_rmsnorm_fwd_reg<12>, g, blk, 0, ctx->stream, xp, wp, yp, rows, eps); break;
+      case 16: e = launch_pdl(k_rmsnorm_fwd_reg<16>, g, blk, 0, ctx->stream, xp, wp, yp, rows, eps); break;
+      case 32: e = launch_pdl(k_rmsnorm_fwd_reg<32>, g, blk, 0, ctx->stream, xp, wp, yp, rows, eps); break;
+      default: e = launch_pdl(k_rmsnorm_fwd, g, blk, 0, ctx->stream, xp, wp, yp, rows, d, eps); break;
     }
-    PAI_LAUNCH_CHECK("rmsnorm");
+    if (e != cudaSuccess) return cuda_error(e, "rmsnorm");
+    ctx->launches++;
   }
   *out = r;
   return PAI_OK;

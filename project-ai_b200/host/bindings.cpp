@@ -141,8 +141,14 @@ PYBIND11_MODULE(_paihost, m) {
       .def("kv_append", &NativeBackend::kv_append)
       .def("sdpa_decode", &NativeBackend::sdpa_decode)
       .def("linear_fused", &NativeBackend::linear_fused, py::arg("x"), py::arg("weights"), py::arg("mode"),
-           py::arg("residual") = nullptr)
+           py::arg("residual") = nullptr, py::arg("norm_weight") = nullptr, py::arg("eps") = 0.0f)
       .def("rope_append", &NativeBackend::rope_append)
+      .def("attn_decode_step", &NativeBackend::attn_decode_step)
+      // CUDA graph capture of the ops issued between begin and end; the handle is an opaque integer
+      .def("graph_begin", &NativeBackend::graph_begin)
+      .def("graph_end", [](NativeBackend& be) { return reinterpret_cast<uintptr_t>(be.graph_end()); })
+      .def("graph_launch", [](NativeBackend& be, uintptr_t g) { be.graph_launch(reinterpret_cast<pai_graph*>(g)); })
+      .def("graph_destroy", [](NativeBackend& be, uintptr_t g) { be.graph_destroy(reinterpret_cast<pai_graph*>(g)); })
       .def("nccl_unique_id", [](NativeBackend& be) {
         uint8_t id[128];
         be.nccl_unique_id(id);

@@ -158,9 +158,12 @@ class NativeBackend {
   Tensor sdpa_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos, float scale);
   // fused decode-step ops: x·Wᵀ over several weights with a store / residual / SiLU·mul epilogue, and RoPE + KV append
   bool has_decode_fusions() const;
-  Tensor linear_fused(const Tensor& x, const std::vector<Tensor>& weights, int mode, const Tensor& residual = nullptr);
+  Tensor linear_fused(const Tensor& x, const std::vector<Tensor>& weights, int mode, const Tensor& residual = nullptr,
+                      const Tensor& norm_weight = nullptr, float eps = 0.0f);
   Tensor rope_append(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos_table, const Tensor& sin_table,
                      const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos);
+  Tensor attn_decode_step(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos_table, const Tensor& sin_table,
+                          const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos, float scale);
   void graph_begin();
   pai_graph* graph_end();
   void graph_launch(pai_graph* g);

@@ -271,10 +271,13 @@ void TensorImpl::backward() {
                        const pai_tensor*))                                                                               \
   X(sdpa_decode, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*, float,    \
                          pai_tensor*))                                                                                   \
-  X(linear_fused, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, int32_t, int32_t, const pai_tensor*,          \
-                          pai_tensor*))                                                                                  \
+  X(linear_fused, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, float, const pai_tensor*, int32_t, int32_t,   \
+                          const pai_tensor*, pai_tensor*))                                                               \
   X(rope_append, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*,           \
                          const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*, pai_tensor*))       \
+  X(attn_decode_step, int (*)(pai_ctx*, const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*,      \
+                              const pai_tensor*, const pai_tensor*, const pai_tensor*, const pai_tensor*, float,         \
+                              pai_tensor*))                                                                              \
   X(graph_begin, int (*)(pai_ctx*))                                                                                      \
   X(graph_end, int (*)(pai_ctx*, pai_graph**))                                                                           \
   X(graph_launch, int (*)(pai_ctx*, pai_graph*))                                                                         \
@@ -344,7 +347,7 @@ bool NativeBackend::has_graphs() const {
          fn_->graph_end && fn_->graph_launch && fn_->graph_destroy;
 }
 
-bool NativeBackend::has_decode_fusions() const { return fn_->linear_fused && fn_->rope_append; }
+bool NativeBackend::has_decode_fusions() const { return fn_->linear_fused && fn_->rope_append && fn_->attn_decode_step; }
 
 Tensor NativeBackend::wrap(const pai_tensor& d) {
   auto st = std::make_shared<Storage>();
@@ -704,14 +707,17 @@ Tensor NativeBackend::sdpa_decode(const Tensor& q, const Tensor& k_cache, const 
   return wrap(o);
 }
 
-Tensor NativeBackend::linear_fused(const Tensor& x, const std::vector<Tensor>& weights, int mode, const Tensor& residual) {
+Tensor NativeBackend::linear_fused(const Tensor& x, const std::vector<Tensor>& weights, int mode, const Tensor& residual,
+                                   const Tensor& norm_weight, float eps) {
   need((void*)fn_->linear_fused, "linear_fused");
-  pai_tensor dx = x->desc(), dr{};
+  pai_tensor dx = x->desc(), dr{}, dn{};
   std::vector<pai_tensor> dw;
   for (const auto& w : weights) dw.push_back(w->desc());
   if (residual) dr = residual->desc();
+  if (norm_weight) dn = norm_weight->desc();
   pai_tensor o;
-  check(fn_->linear_fused(ctx_, &dx, dw.data(), (int32_t)dw.size(), mode, residual ? &dr : nullptr, &o));
+  check(fn_->linear_fused(ctx_, &dx, norm_weight ? &dn : nullptr, eps, dw.data(), (int32_t)dw.size(), mode,
+                          residual ? &dr : nullptr, &o));
   return wrap(o);
 }
 
@@ -721,6 +727,18 @@ Tensor NativeBackend::rope_append(const Tensor& q, const Tensor& k, const Tensor
   pai_tensor dq = q->desc(), dk = k->desc(), dv = v->desc(), dc = cos_table->desc(), ds = sin_table->desc(),
              dkc = k_cache->desc(), dvc = v_cache->desc(), dp = pos->desc(), o;
   check(fn_->rope_append(ctx_, &dq, &dk, &dv, &dc, &ds, &dkc, &dvc, &dp, &o));
+  invalidate_shadow(k_cache);
+  invalidate_shadow(v_cache);
+  return wrap(o);
+}
+
+Tensor NativeBackend::attn_decode_step(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos_table,
+                                       const Tensor& sin_table, const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos,
+                                       float scale) {
+  need((void*)fn_->attn_decode_step, "attn_decode_step");
+  pai_tensor dq = q->desc(), dk = k->desc(), dv = v->desc(), dc = cos_table->desc(), ds = sin_table->desc(),
+             dkc = k_cache->desc(), dvc = v_cache->desc(), dp = pos->desc(), o;
+  check(fn_->attn_decode_step(ctx_, &dq, &dk, &dv, &dc, &ds, &dkc, &dvc, &dp, scale, &o));
   invalidate_shadow(k_cache);
   invalidate_shadow(v_cache);
   return wrap(o);

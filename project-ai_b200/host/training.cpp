@@ -228,8 +228,8 @@ Tensor GraphDecoder::body() {
   return be.matmul(x, model_->embedding->weight, true)->reshape({b, 1, c.vocab_size});
 }
 
-// The same step with the fused decode ops, 8 launches per block: RMSNorm, q/k/v products in one pass, RoPE + cache
-// append, attention, o-projection + residual, RMSNorm, gate/up products with SiLU·mul, down-projection + residual.
+// The same step with the fused decode ops, 5 launches per block: RMSNorm + q/k/v products in one pass, RoPE + cache
+// append + attention, o-projection + residual, RMSNorm + gate/up products with SiLU·mul, down-projection + residual.
 Tensor GraphDecoder::body_fused() {
   NativeBackend& be = *be_;
   const ModelConfig& c = model_->cfg;
@@ -240,23 +240,22 @@ Tensor GraphDecoder::body_fused() {
   for (size_t l = 0; l < model_->blocks.size(); l++) {
     TransformerBlock* blk = model_->blocks[l];
     Attention* at = blk->attn;
-    Tensor hn = be.rms_norm(x, blk->attn_norm->weight, blk->attn_norm->eps);
-    Tensor qkv = be.linear_fused(hn, {at->wq->weight, at->wk->weight, at->wv->weight}, 0);  // [b, width]
+    Tensor qkv = be.linear_fused(x, {at->wq->weight, at->wk->weight, at->wv->weight}, 0, nullptr, blk->attn_norm->weight,
+                                 blk->attn_norm->eps);  // RmsNorm(x) · [wq; wk; wv]ᵀ: [b, width]
     // views of one position per sequence: [b, heads, 1, dh] inside each row of qkv
     Tensor q = make_view(*qkv, {b, h, 1, dh}, {width, dh, width, 1}, 0);
     Tensor k = make_view(*qkv, {b, kvh, 1, dh}, {width, dh, width, 1}, (int64_t)h * dh);
     Tensor v = make_view(*qkv, {b, kvh, 1, dh}, {width, dh, width, 1}, (int64_t)(h + kvh) * dh);
     Tensor kc = cache_->key_store((int)l), vc = cache_->value_store((int)l);
-    Tensor qr = be.rope_append(q, k, v, at->rope->cos, at->rope->sin, kc, vc, pos_);
-    Tensor o = be.sdpa_decode(qr, kc, vc, pos_, scale);  // [b, 1, h, dh]
+    Tensor o = be.attn_decode_step(q, k, v, at->rope->cos, at->rope->sin, kc, vc, pos_, scale);  // [b, 1, h, dh]
     x = be.linear_fused(o->reshape({b, h * dh}), {at->wo->weight}, 1, x);
-    Tensor hf = be.rms_norm(x, blk->ffn_norm->weight, blk->ffn_norm->eps);
     SwiGlu* f = blk->ffn;
-    Tensor a = be.linear_fused(hf, {f->gate->weight, f->up->weight}, 2);
+    Tensor a = be.linear_fused(x, {f->gate->weight, f->up->weight}, 2, nullptr, blk->ffn_norm->weight, blk->ffn_norm->eps);
     x = be.linear_fused(a, {f->down->weight}, 1, x);
   }
-  x = be.rms_norm(x, model_->final_norm->weight, model_->final_norm->eps);
-  return be.matmul(x, model_->embedding->weight, true)->reshape({b, 1, c.vocab_size});
+  Tensor logits = be.linear_fused(x, {model_->embedding->weight}, 0, nullptr, model_->final_norm->weight,
+                                  model_->final_norm->eps);
+  return logits->reshape({b, 1, c.vocab_size});
 }
 
 Tensor GraphDecoder::step(const std::vector<int>& ids) {

@@ -176,6 +176,14 @@ def test_linear_fused_modes_match_float64(rows):
     assert np.abs(got - exp).max() <= 1e-4 * max(np.abs(exp).max(), 1e-3)
     with pytest.raises(H.ArgumentError):
         be.linear_fused(tx, [tw[0], tw[1]], 2)  # SiLU·mul needs two weights of one shape
+    # with a norm weight: the same values as RmsNorm followed by the product (the normalised rows are bit-identical)
+    nw = be.from_host((1 + 0.1 * rs.standard_normal(k)).astype(np.float32))
+    fused = be.to_host(be.linear_fused(tx, tw, 0, None, nw, 1e-5))
+    unfused = be.to_host(be.linear_fused(be.rms_norm(tx, nw, 1e-5), tw, 0))
+    assert np.array_equal(fused, unfused) if rows < 5 else np.abs(fused - unfused).max() <= 1e-6 * np.abs(unfused).max()
+    fused = be.to_host(be.linear_fused(tx, [tw[1], tw[2]], 2, None, nw, 1e-5))
+    unfused = be.to_host(be.linear_fused(be.rms_norm(tx, nw, 1e-5), [tw[1], tw[2]], 2))
+    assert np.array_equal(fused, unfused) if rows < 5 else np.abs(fused - unfused).max() <= 1e-6 * np.abs(unfused).max()
     be.check_device_error()
 
 
@@ -209,4 +217,34 @@ def test_rope_append_equals_rotary_at_and_kv_append():
     np.testing.assert_allclose(be.to_host(qa)[:, :, 0], rot, rtol=1e-6, atol=1e-6)
     assert np.all(be.to_host(kc1)[:, :, :pos] == 0) and np.all(be.to_host(kc1)[:, :, pos + 1:] == 0)
     assert np.array_equal(be.to_host(vc1)[:, :, pos], be.to_host(v)[:, :, 0])
+    be.check_device_error()
+
+
+@pytest.mark.parametrize("B,NH,KV,D,T,pos", [(1, 32, 8, 64, 768, 517), (3, 8, 2, 16, 200, 130), (2, 16, 4, 64, 2048, 1500),
+                                          (4, 8, 8, 32, 64, 0)])
+def test_attn_decode_step_equals_rope_append_then_sdpa_decode(B, NH, KV, D, T, pos):
+    """The fused decode-step attention (RoPE + cache append + attention, cluster-merged key splits) against the two
+    separate ops: bit-identical outputs and caches; and against float64 attention over the filled cache prefix."""
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", 0)
+    rs = np.random.RandomState(pos)
+    cos = be.from_host(rs.standard_normal((T, D)).astype(np.float32))
+    sin = be.from_host(rs.standard_normal((T, D)).astype(np.float32))
+    p = be.allocate([1])
+    be.write(p, np.array([pos], np.float32))
+    q = be.from_host(rs.standard_normal((B, NH, 1, D)).astype(np.float32))
+    k = be.from_host(rs.standard_normal((B, KV, 1, D)).astype(np.float32))
+    v = be.from_host(rs.standard_normal((B, KV, 1, D)).astype(np.float32))
+    prefix_k = rs.standard_normal((B, KV, T, D)).astype(np.float32)
+    prefix_v = rs.standard_normal((B, KV, T, D)).astype(np.float32)
+    kc1, vc1 = be.from_host(prefix_k), be.from_host(prefix_v)
+    kc2, vc2 = be.from_host(prefix_k), be.from_host(prefix_v)
+    scale = 1.0 / np.sqrt(D)
+    fused = be.to_host(be.attn_decode_step(q, k, v, cos, sin, kc1, vc1, p, scale))
+    qr = be.rope_append(q, k, v, cos, sin, kc2, vc2, p)
+    two = be.to_host(be.sdpa_decode(qr, kc2, vc2, p, scale))
+    assert np.array_equal(fused, two)
+    assert np.array_equal(be.to_host(kc1), be.to_host(kc2)) and np.array_equal(be.to_host(vc1), be.to_host(vc2))
+    kk, vv = be.to_host(kc1)[:, :, :pos + 1], be.to_host(vc1)[:, :, :pos + 1]
+    o_ref = attention_ref(be.to_host(qr), kk, vv, scale, pos)[0]
+    assert_close(np.swapaxes(o_ref, 1, 2), fused, 1e-4, 1e-4, "decode step attention")
     be.check_device_error()
