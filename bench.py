@@ -219,6 +219,17 @@ def decode_bench(local, cfg_name="1b", prompt_len=512, gen=256, batches=(1, 32))
                        "launches": g_launches, "avg_launch_ms": g_ms / max(g_launches, 1),
                        "sample": "greedy batch 1, prompt 512 + 64 new tokens (prefill GEMMs excluded: family gemm)"}
     out["kernels"] = {f: {"launches": v[0], "ms": v[1], "share": v[1] / ms_timed} for f, v in stats.items()}
+    # whole decode steps against the HBM line: every weight and the cached K/V of every sequence are read once per
+    # step (mean cache length over the run: prompt + half the new tokens)
+    kv_row = 2 * c["kv_head_count"] * (c["embedding_dim"] // c["head_count"]) * 4 * c["layer_count"]
+    out["step_roofline"] = {}
+    for b in batches:
+        tok_s = out[f"batch{b}"]["greedy"]["decode_tok_s"]
+        step_s = b / tok_s
+        bytes_step = 4.0 * param_count(c) + b * kv_row * (prompt_len + gen / 2)
+        out["step_roofline"][f"batch{b}"] = {"bytes_per_step": bytes_step, "ms_per_step": step_s * 1e3,
+                                             "achieved_GBps": bytes_step / step_s / 1e9,
+                                             "frac": bytes_step / step_s / 1e9 / hbm}
     out["weights_gb_per_token"] = 4.0 * param_count(c) / 1e9
     out["hbm_ceiling_tok_s_batch1"] = hbm / (4.0 * param_count(c) / 1e9)
     del m
@@ -323,11 +334,15 @@ def op_sweep(args):
                 be.release(t)
     if args.op in ("all", "decode"):
         # 1B decode: every weight shape of a layer plus the LM head, x·Wᵀ for 1 and 32 rows; enough weight copies are
-        # cycled that each timed call reads its W from HBM, not L2
-        for n, k in ((2048, 2048), (512, 2048), (5632, 2048), (2048, 5632), (32000, 2048)):
+        # cycled that each timed call reads its W from HBM, not L2 (--shape rows,k,n: that product only)
+        gemv_shapes = [((n, k), (1, 32)) for n, k in ((2048, 2048), (512, 2048), (5632, 2048), (2048, 5632), (32000, 2048))]
+        if args.op == "decode" and args.shape:
+            r0, k0, n0 = (int(v) for v in args.shape.split(","))
+            gemv_shapes = [((n0, k0), (r0,))]
+        for (n, k), row_counts in gemv_shapes:
             copies = max(1, -(-300_000_000 // (n * k * 4)))
             ws = [randt(n, k) for _ in range(copies)]
-            for rows_ in (1, 32):
+            for rows_ in row_counts:
                 x = randt(rows_, k)
                 it = [0]
 
@@ -339,7 +354,7 @@ def op_sweep(args):
                 be.release(x)
             for t in ws:
                 be.release(t)
-        for B in (1, 32):
+        for B in (() if (args.op == "decode" and args.shape) else (1, 32)):
             Hh, KV, D, L = 32, 8, 64, 768
             q = randt(B, Hh, 1, D)
             kc, vc = randt(B, KV, L, D), randt(B, KV, L, D)
@@ -397,7 +412,7 @@ def main():
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm", "decode"],
                     help="op-level sweep instead of the training step")
-    ap.add_argument("--shape", default=None, help="M,K,N for --op gemm")
+    ap.add_argument("--shape", default=None, help="M,K,N for --op gemm; rows,K,N for --op decode")
     ap.add_argument("--skip-decode", action="store_true", help="leave the ~1B decode measurement out of the N=1 line")
     ap.add_argument("--decode-only", action="store_true", help="print only the decode measurement")
     ap.add_argument("--decode-tokens", type=int, default=256)
@@ -503,8 +518,15 @@ def main():
         achieved = (g_flops / max(g_launches, 1)) / (avg_ms * 1e-3) / 1e12
         peak = peak_tf32 / 3.0
         traffic = ncu_traffic()
+        # DRAM bytes of the captured GEMM launch, scaled to this step's average GEMM launch by algorithmic flops
+        traffic_bytes = None
+        if traffic and traffic.get("flops_per_launch"):
+            traffic_bytes = traffic["bytes_per_launch"] * (g_flops / max(g_launches, 1)) / traffic["flops_per_launch"]
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                    "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                    "traffic": traffic_bytes,
+                    "traffic_source": ("profiles/gemm_tcgen05_traffic.json: ncu dram__bytes_read+write of one "
+                                       f"{traffic.get('shape')} launch, scaled by flops to the average launch")
+                    if traffic else None,
                     "kernel": "k_gemm_tc (3xTF32 tcgen05)",
                     "peak_source": "measured on this GPU: cuBLAS TF32 GEMM (torch.matmul fp32, allow_tf32, 8192^3, best of 10)"
                                    f" = {peak_tf32:.1f} TFLOP/s, divided by 3 for 3xTF32",
