@@ -134,8 +134,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
   __shared__ float s_l[2][kQT];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = a.q_tiles - 1 - (int)blockIdx.x;  // longest causal tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // the query tile is the slowest grid index, in reverse: CTAs start in launch order, so every head's longest causal
+  // tile runs in the first wave and the short tiles fill in behind them
+  const int qt = a.q_tiles - 1 - (int)blockIdx.z;
+  const int h = blockIdx.x, b = blockIdx.y;
   const int kvh = h / (a.H / a.KVH);
   const int q0 = qt * kQT;
   int kend = a.L;
@@ -379,7 +381,7 @@ pai_status attn_tc_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   }
   AttnTcArgs args{static_cast<float*>(qp.p), static_cast<float*>(kp.p), static_cast<float*>(vp.p), out, lse,
                   B, H, KVH, S, L, D, pos_offset, causal, q_tiles, k_blocks, ctx->d_error_flag};
-  dim3 grid((unsigned)q_tiles, (unsigned)H, (unsigned)B);
+  dim3 grid((unsigned)H, (unsigned)B, (unsigned)q_tiles);
   k_attn_fwd_tc<<<grid, kFwdThreads, kFwdSmemBytes, ctx->stream>>>(args);
   PAI_LAUNCH_CHECK("attention fwd (tcgen05)");
   return PAI_OK;

@@ -140,7 +140,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  // key tiles in the slowest grid index: under a causal mask tile 0 is attended by every query, so the longest
+  // tiles start first
+  const int kt = blockIdx.z, kvh = blockIdx.x, b = blockIdx.y;
   const int g = a.H / a.KVH;
   const int j0 = kt * kRows;
   int qb_start = 0;
@@ -315,8 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest causal tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int qt = (int)gridDim.z - 1 - (int)blockIdx.z;  // query tiles slowest and reversed: longest causal tiles first
+  const int h = blockIdx.x, b = blockIdx.y;
   const int kvh = h / (a.H / a.KVH);
   const int q0 = qt * kRows;
   int kend = a.L;
@@ -515,10 +517,10 @@ pai_status attn_tc_bwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   Args args{static_cast<float*>(qs.p), static_cast<float*>(dO.p), static_cast<float*>(qsT.p), static_cast<float*>(dOT.p),
             static_cast<float*>(kp.p), static_cast<float*>(vp.p), static_cast<float*>(kT.p), lse, dvec, dq, dk, dv,
             B, H, KVH, S, L, D, pos_offset, causal, nq, nq2, nk, nk2, scale, ctx->d_error_flag};
-  dim3 gkv((unsigned)((L + kRows - 1) / kRows), (unsigned)KVH, (unsigned)B);
+  dim3 gkv((unsigned)KVH, (unsigned)B, (unsigned)((L + kRows - 1) / kRows));
   k_attn_bwd_kv_tc<<<gkv, kThreads, kSmem, ctx->stream>>>(args);
   PAI_LAUNCH_CHECK("attention bwd dK/dV (tcgen05)");
-  dim3 gq((unsigned)((S + kRows - 1) / kRows), (unsigned)H, (unsigned)B);
+  dim3 gq((unsigned)H, (unsigned)B, (unsigned)((S + kRows - 1) / kRows));
   k_attn_bwd_q_tc<<<gq, kThreads, kSmem, ctx->stream>>>(args);
   PAI_LAUNCH_CHECK("attention bwd dQ (tcgen05)");
   return PAI_OK;

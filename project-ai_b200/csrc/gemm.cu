@@ -598,9 +598,18 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
     return PAI_OK;
   }
 
-  constexpr int BN = 256, STAGES = 2;
   int kt = (k + kBK - 1) / kBK;
   int mt = (m + kBM - 1) / kBM;
+  // N tile: 256 columns (2-stage ring) by default; 128 columns (3-stage ring, same shared memory) when the persistent
+  // CTAs then share the tiles more evenly. A product's time is set by the CTA with the most tiles, so the figure of
+  // merit is tiles / (SMs x the largest per-CTA tile count); 128-column tiles reuse each A tile half as often, which the
+  // 0.92 factor charges for.
+  auto balance = [&](int bn) {
+    int64_t t = (int64_t)mt * ((n + bn - 1) / bn) * batch;
+    int64_t per = (t + ctx->sm_count - 1) / ctx->sm_count;
+    return (double)t / ((double)ctx->sm_count * (double)per);
+  };
+  const int BN = (0.92 * balance(128) > balance(256)) ? 128 : 256;
   int tiles_n = (n + BN - 1) / BN;
   int nt_pad = tiles_n * (BN / kBM);
   Scratch ahi, alo, bhi, blo, dai, dbi, part;
@@ -631,7 +640,8 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   g.tiles_m = mt; g.tiles_n = tiles_n; g.batches = (int)batch; g.splits = splits; g.kt_per_split = kt_per_split;
   g.error_flag = ctx->d_error_flag;
   g.k_elems = k;
-  PAI_TRY((launch_tc<BN, STAGES>(ctx, g)));
+  if (BN == 128) PAI_TRY((launch_tc<128, 3>(ctx, g)));
+  else PAI_TRY((launch_tc<256, 2>(ctx, g)));
   if (splits > 1) {
     int64_t nn = numel(r);
     k_splitk_reduce<<<grid_for(ctx, nn, 256), 256, 0, ctx->stream>>>(cdst, fptr(r), nn, splits);
