@@ -319,8 +319,10 @@ def op_sweep(args):
             be.release(a)
             be.release(b)
     if args.op in ("all", "attention"):
-        for s in (512, 2048, 4096):
-            B, Hh, D = 4, 32, 64
+        attn_shapes = [(4, 32, s_, 64) for s_ in (512, 2048, 4096)]
+        if args.op == "attention" and args.shape:
+            attn_shapes = [tuple(int(v) for v in args.shape.split(","))]
+        for B, Hh, s, D in attn_shapes:
             q, k, v, do = randt(B, Hh, s, D), randt(B, Hh, s, D), randt(B, Hh, s, D), randt(B, s, Hh, D)
             fl = 2.0 * B * Hh * s * (s + 1) * D  # causal: 4·D per visible pair, s(s+1)/2 pairs
             be.scope_begin()
@@ -412,7 +414,7 @@ def main():
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm", "decode"],
                     help="op-level sweep instead of the training step")
-    ap.add_argument("--shape", default=None, help="M,K,N for --op gemm; rows,K,N for --op decode")
+    ap.add_argument("--shape", default=None, help="M,K,N for --op gemm; rows,K,N for --op decode; B,H,S,D for --op attention")
     ap.add_argument("--skip-decode", action="store_true", help="leave the ~1B decode measurement out of the N=1 line")
     ap.add_argument("--decode-only", action="store_true", help="print only the decode measurement")
     ap.add_argument("--decode-tokens", type=int, default=256)

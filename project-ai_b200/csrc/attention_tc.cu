@@ -106,10 +106,17 @@ struct AttnTcArgs {
 
 constexpr uint32_t kQBytes = kQT * kDP * 4 * 2;        // 64 KB (hi + lo)
 constexpr uint32_t kKBytes = kKB * kDP * 4 * 2;        // 32 KB
-constexpr uint32_t kStageBytes = 2 * kKBytes;          // K + Vᵀ
-constexpr int kFwdSmemBytes = kQBytes + 2 * kStageBytes + 1024 + 256;
+// K and Vᵀ blocks travel in separate rings: a K slot frees as soon as S = Q·Kᵀ of its block is done, a Vᵀ slot after
+// P·V, so the next blocks' loads start a block earlier than with one ring of (K, Vᵀ) stages.
+constexpr int kKStages = 2, kVStages = 2;
+constexpr int kFwdSmemBytes = kQBytes + (kKStages + kVStages) * kKBytes + 1024 + 256;
 // TMEM columns
-constexpr uint32_t kColS0 = 0, kColS1 = 64, kColPhi = 128, kColPlo = 192, kColPV = 256, kTmemCols = 512;
+// TMEM columns: S double buffer, then two slots of (P hi, P lo, P·V): P of block j and the product P_j·V_j use slot
+// j & 1, so the softmax warps write P_{j+1} while P_j·V_j is still being computed.
+constexpr uint32_t kColS0 = 0, kColS1 = 64, kTmemCols = 512;
+__host__ __device__ constexpr uint32_t col_phi(int slot) { return 128u + 192u * (uint32_t)slot; }
+__host__ __device__ constexpr uint32_t col_plo(int slot) { return 192u + 192u * (uint32_t)slot; }
+__host__ __device__ constexpr uint32_t col_pv(int slot) { return 256u + 192u * (uint32_t)slot; }
 
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -119,16 +126,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sStage = smem + kQBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kQBytes + 2 * kStageBytes);
+  uint8_t* sK = smem + kQBytes;                 // [kKStages] K hi/lo blocks
+  uint8_t* sV = sK + kKStages * kKBytes;        // [kVStages] Vᵀ hi/lo blocks
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVStages * kKBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_full = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* k_full = bars + 1;                     // [kKStages]
+  uint64_t* k_empty = k_full + kKStages;           // [kKStages]
+  uint64_t* v_full = k_empty + kKStages;           // [kVStages]
+  uint64_t* v_empty = v_full + kVStages;           // [kVStages]
+  uint64_t* s_full = v_empty + kVStages;           // [2]
+  uint64_t* s_free = s_full + 2;                   // [2]
+  uint64_t* p_full = s_free + 2;                   // [2]
+  uint64_t* pv_full = p_full + 2;                  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_full + 2);
   __shared__ volatile int s_abort;
   __shared__ float s_max[2][2][kQT];  // [block parity][column half][row]
   __shared__ float s_l[2][kQT];
@@ -146,14 +156,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    for (int i = 0; i < kKStages; i++) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kVStages; i++) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
     for (int i = 0; i < 2; i++) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kSoftmaxWarps);
     }
-    mbar_init(p_full, kSoftmaxWarps);
-    mbar_init(pv_full, 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&p_full[i], kSoftmaxWarps);
+      mbar_init(&pv_full[i], 1);
+    }
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -168,17 +186,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
       const float* qsrc = a.qp + ((size_t)(b * a.H + h) * a.q_tiles + qt) * (kQBytes / 4);
       mbar_expect_tx(q_full, kQBytes);
       bulk_g2s(sQ, qsrc, kQBytes, q_full);
+      const size_t head_off = (size_t)(b * a.KVH + kvh) * a.k_blocks;
+      // loads in the order the MMA warp consumes them: K0, then per block K_{j+1} before Vᵀ_j
+      auto load_k = [&](int j) {
+        int st = j % kKStages;
+        if (!mbar_wait(&k_empty[st], ((j / kKStages) & 1) ^ 1)) return false;
+        mbar_expect_tx(&k_full[st], kKBytes);
+        bulk_g2s(sK + st * kKBytes, a.kp + (head_off + j) * (kKBytes / 4), kKBytes, &k_full[st]);
+        return true;
+      };
+      auto load_v = [&](int j) {
+        int st = j % kVStages;
+        if (!mbar_wait(&v_empty[st], ((j / kVStages) & 1) ^ 1)) return false;
+        mbar_expect_tx(&v_full[st], kKBytes);
+        bulk_g2s(sV + st * kKBytes, a.vp + (head_off + j) * (kKBytes / 4), kKBytes, &v_full[st]);
+        return true;
+      };
+      if (!load_k(0)) { atomicExch(a.error_flag, 11); s_abort = 1; }
       for (int j = 0; j < nblk && !s_abort; j++) {
-        int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) { atomicExch(a.error_flag, 11); s_abort = 1; break; }
-        size_t off = ((size_t)(b * a.KVH + kvh) * a.k_blocks + j) * (kKBytes / 4);
-        uint8_t* dst = sStage + st * kStageBytes;
-        mbar_expect_tx(&kv_full[st], kStageBytes);
-        bulk_g2s(dst, a.kp + off, kKBytes, &kv_full[st]);
-        bulk_g2s(dst + kKBytes, a.vp + off, kKBytes, &kv_full[st]);
+        if ((j + 1 < nblk && !load_k(j + 1)) || !load_v(j)) { atomicExch(a.error_flag, 11); s_abort = 1; break; }
       }
-      // drain: the last issued stages must land before the CTA exits
-      for (int j = nblk; j < nblk + 2; j++) mbar_wait(&kv_empty[j & 1], ((j >> 1) & 1) ^ 1);
+      // drain: every issued load must land (and be consumed) before the CTA exits
+      for (int j = nblk; j < nblk + kKStages; j++) mbar_wait(&k_empty[j % kKStages], ((j / kKStages) & 1) ^ 1);
+      for (int j = nblk; j < nblk + kVStages; j++) mbar_wait(&v_empty[j % kVStages], ((j / kVStages) & 1) ^ 1);
     }
   } else if (warp == 1) {
     if (lane == 0 && nblk > 0) {
@@ -186,7 +216,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
       const uint32_t q_hi = smem_u32(sQ), q_lo = q_hi + kQBytes / 2;
       auto issue_s = [&](int j) {
         int st = j & 1;
-        uint32_t k_hi = smem_u32(sStage + st * kStageBytes), k_lo = k_hi + kKBytes / 2;
+        uint32_t k_hi = smem_u32(sK + (j % kKStages) * kKBytes), k_lo = k_hi + kKBytes / 2;
         uint32_t d = tmem + (st ? kColS1 : kColS0);
 #pragma unroll
         for (int ks = 0; ks < kDP / 8; ks++) {
@@ -197,8 +227,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
           mma_ss(d, desc_sw128(q_hi + qo), desc_sw128(k_hi + ko), idesc, 1u);
         }
         commit(&s_full[st]);
+        commit(&k_empty[j % kKStages]);  // the K block is free once these MMAs have read it
       };
-      bool ok = mbar_wait(q_full, 0) && mbar_wait(&kv_full[0], 0);
+      bool ok = mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
       if (!ok) { atomicExch(a.error_flag, 12); s_abort = 1; }
       if (ok) {
         fence_after();
@@ -207,27 +238,31 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
       for (int j = 0; j < nblk && ok && !s_abort; j++) {
         if (j + 1 < nblk) {
           int st = (j + 1) & 1;
-          if (!mbar_wait(&kv_full[st], ((j + 1) >> 1) & 1) || !mbar_wait(&s_free[st], (((j + 1) >> 1) & 1) ^ 1)) {
+          if (!mbar_wait(&k_full[(j + 1) % kKStages], ((j + 1) / kKStages) & 1) ||
+              !mbar_wait(&s_free[st], (((j + 1) >> 1) & 1) ^ 1)) {
             atomicExch(a.error_flag, 13); s_abort = 1; break;
           }
           fence_after();
           issue_s(j + 1);
         }
-        if (!mbar_wait(p_full, j & 1)) { atomicExch(a.error_flag, 14); s_abort = 1; break; }
+        const int ps = j & 1;  // P / P·V slot of this block
+        const int vs = j % kVStages;
+        if (!mbar_wait(&p_full[ps], (j >> 1) & 1) || !mbar_wait(&v_full[vs], (j / kVStages) & 1)) {
+          atomicExch(a.error_flag, 14); s_abort = 1; break;
+        }
         fence_after();
-        int st = j & 1;
-        uint32_t v_hi = smem_u32(sStage + st * kStageBytes + kKBytes), v_lo = v_hi + kKBytes / 2;
-        uint32_t d = tmem + kColPV;
+        uint32_t v_hi = smem_u32(sV + vs * kKBytes), v_lo = v_hi + kKBytes / 2;
+        uint32_t d = tmem + col_pv(ps);
 #pragma unroll
         for (int ks = 0; ks < kKB / 8; ks++) {
           uint32_t vo = (ks >> 2) * (kDP * 128) + (ks & 3) * 32;  // Vᵀ kb (32 keys) stride 8 KB
           uint32_t pc = (uint32_t)(ks * 8);
-          mma_ts(d, tmem + kColPlo + pc, desc_sw128(v_hi + vo), idesc, ks > 0 ? 1u : 0u);
-          mma_ts(d, tmem + kColPhi + pc, desc_sw128(v_lo + vo), idesc, 1u);
-          mma_ts(d, tmem + kColPhi + pc, desc_sw128(v_hi + vo), idesc, 1u);
+          mma_ts(d, tmem + col_plo(ps) + pc, desc_sw128(v_hi + vo), idesc, ks > 0 ? 1u : 0u);
+          mma_ts(d, tmem + col_phi(ps) + pc, desc_sw128(v_lo + vo), idesc, 1u);
+          mma_ts(d, tmem + col_phi(ps) + pc, desc_sw128(v_hi + vo), idesc, 1u);
         }
-        commit(pv_full);
-        commit(&kv_empty[st]);
+        commit(&pv_full[ps]);
+        commit(&v_empty[vs]);
       }
     }
   } else {
@@ -243,7 +278,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
     float o[32];
 #pragma unroll
     for (int d = 0; d < 32; d++) o[d] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
+    float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
     // After a timed-out wait `ok` turns false: the warp skips all further TMEM and barrier work but still reaches
     // every named barrier, so its partner warp never waits on it.
     bool ok = nblk > 0;
@@ -293,42 +328,50 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
       }
       l = l * alpha + sum;
       m = mn;
-      if (ok && j > 0) {
-        if (!warp_wait(pv_full, (j - 1) & 1)) {
+      // o holds the blocks up to j-3 in units of the running max. P_{j-2}·V_{j-2} (units of m_{j-2}) sits in this
+      // block's slot: fold it in (factor exp(m_{j-2} - m_j) = alpha_{j-1}·alpha_j) before P_j takes the slot.
+      const int ps = j & 1;
+#pragma unroll
+      for (int d = 0; d < 32; d++) o[d] *= alpha;
+      if (ok && j >= 2) {
+        if (!warp_wait(&pv_full[ps], ((j - 2) >> 1) & 1)) {
           ok = false;
         } else {
           fence_after();
           float pv[32];
-          tmem_ld32(tmem + lane_off + kColPV + col, pv);
+          tmem_ld32(tmem + lane_off + col_pv(ps) + col, pv);
+          const float f = alpha_prev * alpha;
 #pragma unroll
-          for (int d = 0; d < 32; d++) o[d] += pv[d];
+          for (int d = 0; d < 32; d++) o[d] = fmaf(pv[d], f, o[d]);
         }
       }
-#pragma unroll
-      for (int d = 0; d < 32; d++) o[d] *= alpha;
+      alpha_prev = alpha;
       if (ok) {
         // P_j -> TMEM as hi/lo (the A operand of P·V)
         float hi[32], lo[32];
 #pragma unroll
-        for (int c = 0; c < 32; c++) split_tf32(s[c], hi[c], lo[c]);
-        tmem_st32(tmem + lane_off + kColPhi + col, hi);
-        tmem_st32(tmem + lane_off + kColPlo + col, lo);
+        for (int c = 0; c < 32; c++) split_tf32_fast(s[c], hi[c], lo[c]);
+        tmem_st32(tmem + lane_off + col_phi(ps) + col, hi);
+        tmem_st32(tmem + lane_off + col_plo(ps) + col, lo);
         tmem_st_wait();
         fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full);
+        if (lane == 0) mbar_arrive(&p_full[ps]);
       }
     }
-    if (ok && nblk > 0) {
-      if (warp_wait(pv_full, (nblk - 1) & 1)) {
-        fence_after();
-        float pv[32];
-        tmem_ld32(tmem + lane_off + kColPV + col, pv);
-#pragma unroll
-        for (int d = 0; d < 32; d++) o[d] += pv[d];
-      } else {
+    // the last two blocks' P·V products: P_{J-1}·V_{J-1} (units of m_{J-1}: factor alpha_J) and P_J·V_J (units of m_J)
+    for (int jj = (nblk >= 2 ? nblk - 2 : 0); ok && jj < nblk; jj++) {
+      const int ps = jj & 1;
+      if (!warp_wait(&pv_full[ps], (jj >> 1) & 1)) {
         ok = false;
+        break;
       }
+      fence_after();
+      float pv[32];
+      tmem_ld32(tmem + lane_off + col_pv(ps) + col, pv);
+      const float f = (jj == nblk - 1) ? 1.0f : alpha_prev;
+#pragma unroll
+      for (int d = 0; d < 32; d++) o[d] = fmaf(pv[d], f, o[d]);
     }
     s_l[half][row] = l;
     named_sync(1 + quad, 64);

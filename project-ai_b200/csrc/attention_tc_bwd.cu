@@ -116,7 +116,7 @@ __device__ __forceinline__ void kv_ring_item(int i, int N, int& n, int& type) {
 __device__ __forceinline__ void store_hilo(uint32_t hi_addr, uint32_t lo_addr, const float* x) {
   float hi[32], lo[32];
 #pragma unroll
-  for (int c = 0; c < 32; c++) split_tf32(x[c], hi[c], lo[c]);
+  for (int c = 0; c < 32; c++) split_tf32_fast(x[c], hi[c], lo[c]);
   tmem_st32(hi_addr, hi);
   tmem_st32(lo_addr, lo);
 }

@@ -269,14 +269,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-// x = hi + lo for the MMA: hi keeps the sign, exponent and top 10 mantissa bits (exactly representable in tf32) and
-// lo = x - hi is exact in fp32; the MMA then reads lo to tf32 precision. Per product the error stays near 2^-20
-// relative, far inside the 1e-4 tolerance, and the split costs one AND and one subtraction per element.
-__device__ __forceinline__ void split_w(float x, float& hi, float& lo) {
-  hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-  lo = x - hi;
-}
-
 template <int NP>  // NP: x rows padded to the MMA's N (16 or 32)
 __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CUtensorMap wmap, const Args a) {
   constexpr uint32_t kColA = 64;
@@ -382,10 +374,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
 #pragma unroll
       for (int c = 0; c < 8; c++) {
         float4 v = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
-        split_w(v.x, hi[4 * c], lo[4 * c]);
-        split_w(v.y, hi[4 * c + 1], lo[4 * c + 1]);
-        split_w(v.z, hi[4 * c + 2], lo[4 * c + 2]);
-        split_w(v.w, hi[4 * c + 3], lo[4 * c + 3]);
+        split_tf32_fast(v.x, hi[4 * c], lo[4 * c]);
+        split_tf32_fast(v.y, hi[4 * c + 1], lo[4 * c + 1]);
+        split_tf32_fast(v.z, hi[4 * c + 2], lo[4 * c + 2]);
+        split_tf32_fast(v.w, hi[4 * c + 3], lo[4 * c + 3]);
       }
       tmem_st32(tmem + lane_base + kColA + t * 64, hi);
       tmem_st32(tmem + lane_base + kColA + t * 64 + 32, lo);

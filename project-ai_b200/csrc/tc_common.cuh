@@ -22,6 +22,15 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   lo = __uint_as_float(to_tf32(x - hi));
 }
 
+// x = hi + lo exactly, with hi = x truncated to tf32 (low 13 mantissa bits cleared) and lo = x - hi (exact in fp32);
+// the MMA reads lo to tf32 precision, so a product keeps a relative error near 2^-20. Two integer/FP ALU operations
+// instead of two conversions: used where the split sits on a kernel's critical path (tensor-memory operands written
+// by CUDA-core warps).
+__device__ __forceinline__ void split_tf32_fast(float x, float& hi, float& lo) {
+  hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  lo = x - hi;
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }

@@ -144,6 +144,9 @@ PYBIND11_MODULE(_paihost, m) {
            py::arg("residual") = nullptr, py::arg("norm_weight") = nullptr, py::arg("eps") = 0.0f)
       .def("rope_append", &NativeBackend::rope_append)
       .def("attn_decode_step", &NativeBackend::attn_decode_step)
+      .def("sdpa_fwd", [](NativeBackend& be, const Tensor& q, const Tensor& k, const Tensor& v, float scale, bool causal,
+                          int pos) { return be.sdpa_fwd(q, k, v, scale, causal, pos); })
+      .def("sdpa_bwd", &NativeBackend::sdpa_bwd)
       // CUDA graph capture of the ops issued between begin and end; the handle is an opaque integer
       .def("graph_begin", &NativeBackend::graph_begin)
       .def("graph_end", [](NativeBackend& be) { return reinterpret_cast<uintptr_t>(be.graph_end()); })
