@@ -3,31 +3,58 @@
 // to query row s when j <= pos_offset + s), computed in exact fp32 arithmetic.
 //
 // Decode attention reads every cached key and value once per step and does ~2 flops per byte, so it is bound by
-// HBM, not by the tensor cores: one CTA per (batch, kv head, key split) holds all query rows of that kv head's
-// group, so each K/V row is read from HBM once for all g heads that share it.
-//   QKᵀ: lane j of a warp owns key j of the warp's 32-key tile and dots it (128-bit loads) with every query row
-//        (query rows broadcast from shared memory).
-//   softmax: online per query row with warp max / sum.
-//   PV:  lanes own two head-dim elements each; each key's probability is broadcast with a shuffle.
-// The 4 warps of a CTA and then the key splits are merged in a fixed order (log-sum-exp rescaling), so results are
-// deterministic.
+// HBM, not by the tensor cores. One CTA per (key split, kv head, batch) holds all query rows of that kv head's group,
+// so each K/V row is read from HBM once for all g heads that share it:
+//   producer warp: one thread streams 16-key K and V tiles (contiguous rows: one bulk copy each) into an 8-stage
+//                  shared-memory ring, so the CTA keeps up to 64 KB of loads in flight;
+//   4 consumer warps: tile t goes to warp t % 4. QKᵀ: lanes l and l+16 split key l%16's head dims and read them
+//                  in a lane-rotated order (no bank conflicts); online softmax per query row over the tile's 16
+//                  lanes; PV: lanes own two head-dim elements, the tile's probabilities are read back as float4
+//                  broadcasts from shared memory.
+// The key splits of one (batch, kv head) form a thread-block cluster; they divide the visible keys [0, kend) evenly on
+// the device (kend comes from the device-side position in a decode step), and cluster rank 0 merges the CTAs'
+// partials through distributed shared memory. The 4 warps and then the splits are merged in a fixed order
+// (log-sum-exp rescaling), so results are deterministic.
+//
+// Small batches (fewer than 64 (batch, kv head) pairs) leave each warp about one tile, too little for the ring to pay
+// for itself: they take k_attn_decode_direct, in which every warp loads its own 32-key tile straight from global
+// memory and which launches early behind the previous kernel. Both variants compute the same attention; they may
+// round differently, and one shape always takes the same variant.
 #include <cooperative_groups.h>
 #include <math.h>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace pai {
 
 namespace dec {
 
 namespace cg = cooperative_groups;
+using ::pai::tc::bulk_g2s;
+using ::pai::tc::mbar_arrive;
+using ::pai::tc::mbar_expect_tx;
+using ::pai::tc::mbar_init;
+using ::pai::tc::mbar_wait;
+using ::pai::tc::warp_wait;
 
-constexpr int kThreads = 128;
-constexpr int kWarps = kThreads / 32;
+constexpr int kConsumers = 4;                      // consumer warps
+constexpr int kThreads = 32 * (kConsumers + 1);    // + the producer warp
 constexpr int kMaxD = 64;
 constexpr int kMaxRows = 16;
-constexpr int kTile = 32;        // keys per warp step
-constexpr int kMaxCluster = 8;   // key splits of one (batch, kv head): the CTAs of one portable cluster
+constexpr int kTile = 16;                          // keys per tile
+constexpr int kStages = 8;                         // ring depth: two tiles per consumer warp
+static_assert(kStages % kConsumers == 0, "a stage must always belong to the same consumer warp");
+constexpr int kHalfStage = kTile * kMaxD * 4;      // the K tile; the V tile follows it
+constexpr int kStageBytes = 2 * kHalfStage;
+constexpr size_t smem_bytes(int stages) { return (size_t)stages * kStageBytes + 2 * kStages * sizeof(uint64_t); }
+constexpr int kMaxCluster = 8;                     // key splits of one (batch, kv head): a portable cluster
+constexpr int kBarRope = 1;                        // named barrier: new cache rows written (consumers -> producer)
+constexpr int kBarConsumers = 2;                   // named barrier among the consumer warps
+constexpr int kDirectThreads = 128;                // latency variant (k_attn_decode_direct): 4 warps
+constexpr int kDirectWarps = kDirectThreads / 32;
+constexpr int kDirectTile = 32;                    // keys per warp step
+constexpr int kDirectMinPairs = 64;                // the streaming kernel from this many (batch, kv head) pairs on
 
 struct View {
   const float* p;
@@ -39,7 +66,9 @@ struct Args {
   int B, H, KVH, S, L, D, g, rows;
   int pos_offset, causal;
   float scale;
-  int splits, keys_per_split;  // splits = the cluster size along x
+  int splits;            // CTAs per (batch, kv head): the cluster size along x
+  int keys_per_split;    // latency variant: keys of each split (a multiple of 128)
+  int stages;            // shared-memory ring depth (<= kStages): no deeper than the most tiles one CTA can get
   const float* pos_dev;  // when set: pos_offset = pos_dev[0] and the keys are cache positions 0 .. pos+S-1 (L = capacity)
   int* error_flag;
   // fused RoPE + cache append: q and the new key/value rows [B, KVH, S, D] arrive unrotated; keys are rotated with the
@@ -53,14 +82,18 @@ struct Args {
   float* lse;            // [B, H, S]
 };
 
-__device__ __forceinline__ float wmax(float v) {
+__device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void bar_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+// max / sum over the 16 lanes of each half-warp (both halves hold the same values in the tile loop)
+__device__ __forceinline__ float hmax(float v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
-__device__ __forceinline__ float wsum(float v) {
+__device__ __forceinline__ float hsum(float v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 
@@ -79,16 +112,305 @@ __device__ __forceinline__ void rope_pair(float x0, float x1, const float* cr, c
   y1 = __fadd_rn(__fmul_rn(x1, cr[j + half]), __fmul_rn(x0, sr[j + half]));
 }
 
-// One CTA per (key split, kv head, batch); the splits of one (batch, kv head) form a cluster. Each of the 4 warps
-// takes 32-key tiles of the CTA's key range; the warps merge in shared memory and cluster rank 0 merges the CTAs'
-// partials through distributed shared memory, in rank order.
 // DC: the head dim when known at compile time (64), else 0 (read from the arguments). ROPE: fused RoPE + append.
 template <int R, int DC, bool ROPE>
 __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
   const int D = DC ? DC : a.D;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int stages = a.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * kStageBytes);
+  uint64_t* empty = full + kStages;
   __shared__ __align__(16) float qs[R][kMaxD];
-  __shared__ float wm[kWarps][R], wl[kWarps][R];
-  __shared__ float wacc[kWarps][R][kMaxD];
+  __shared__ __align__(16) float ps[kConsumers][R][kTile];
+  __shared__ float wm[kConsumers][R], wl[kConsumers][R];
+  __shared__ float wacc[kConsumers][R][kMaxD];
+  __shared__ float cm[R], cl[R];  // this CTA's merged partial, read by cluster rank 0
+  __shared__ float ca[R][kMaxD];
+  __shared__ volatile int s_abort;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = a.rows;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+
+  int pos_offset = a.pos_offset, kend = a.L;
+  if (a.pos_dev) {
+    float pf = a.pos_dev[0];
+    pos_offset = (int)pf;
+    if (!(pf >= 0.0f) || pos_offset + a.S > a.L || (ROPE && pos_offset + a.S > a.tab_rows)) {
+      // outside the cache or the tables: flag it and attend to nothing
+      if (split == 0 && threadIdx.x == 0) atomicExch(a.error_flag, 63);
+      pos_offset = 0;
+      kend = 0;
+    }
+  }
+  if (a.causal) kend = min(kend, pos_offset + a.S);
+  // the cluster's CTAs divide the visible keys evenly, in whole tiles
+  const int per = ((kend + (int)gridDim.x - 1) / (int)gridDim.x + kTile - 1) / kTile * kTile;
+  const int j0 = min(kend, split * per);
+  const int j1 = min(kend, j0 + per);
+  const int ntiles = (j1 - j0 + kTile - 1) / kTile;
+  // new rows sit at positions pos_offset .. pos_offset+S-1, the end of the visible keys: tiles from first_new on hold
+  // rows this CTA writes (fused RoPE + append) and are copied only after those writes
+  const int first_new = ROPE ? max(0, (pos_offset - j0) / kTile) : ntiles;
+  const float* kbase = a.k.p + (int64_t)b * a.k.s0 + (int64_t)kvh * a.k.s1;
+  const float* vbase = a.v.p + (int64_t)b * a.v.s0 + (int64_t)kvh * a.v.s1;
+  const int half = D >> 1;
+
+  if (warp == kConsumers) {
+    // ---------------- producer: tile t -> stage t % stages
+    const uint32_t row_bytes = (uint32_t)D * 4;
+    int issued = 0;
+    for (int t = 0; t < ntiles; t++) {
+      if (ROPE && t == first_new) bar_sync(kBarRope, kThreads);
+      if (lane == 0 && !s_abort) {
+        const int s = t % stages;
+        if (t >= stages && !mbar_wait(&empty[s], ((t / stages) & 1) ^ 1)) {
+          atomicExch(a.error_flag, 66);
+          s_abort = 1;
+        } else {
+          const int k0 = j0 + t * kTile, nk = min(kTile, j1 - k0);
+          uint8_t* st = smem + s * kStageBytes;
+          mbar_expect_tx(&full[s], 2u * nk * row_bytes);
+          if (a.k.s2 == D) {
+            bulk_g2s(st, kbase + (int64_t)k0 * D, nk * row_bytes, &full[s]);
+          } else {
+            for (int r = 0; r < nk; r++) bulk_g2s(st + r * row_bytes, kbase + (int64_t)(k0 + r) * a.k.s2, row_bytes, &full[s]);
+          }
+          if (a.v.s2 == D) {
+            bulk_g2s(st + kHalfStage, vbase + (int64_t)k0 * D, nk * row_bytes, &full[s]);
+          } else {
+            for (int r = 0; r < nk; r++)
+              bulk_g2s(st + kHalfStage + r * row_bytes, vbase + (int64_t)(k0 + r) * a.v.s2, row_bytes, &full[s]);
+          }
+          issued = t + 1;
+        }
+      }
+    }
+    if (ROPE && first_new >= ntiles) bar_sync(kBarRope, kThreads);  // the consumers always arrive once
+    // every copy issued must land before the CTA may exit
+    if (lane == 0)
+      for (int t = (issued > stages ? issued - stages : 0); t < issued; t++) mbar_wait(&full[t % stages], (t / stages) & 1);
+  } else {
+    // ---------------- consumers
+    constexpr int kCT = 32 * kConsumers;
+    if (ROPE) {
+      if (kend > 0) {
+        // the new key/value rows in this CTA's key range go into the caches (rotated keys) before their tiles load
+        for (int t = threadIdx.x; t < a.S * half; t += kCT) {
+          int s = t / half, j = t - s * half, pos = pos_offset + s;
+          if (pos < j0 || pos >= j1) continue;
+          const float* kr = a.kn.p + (int64_t)b * a.kn.s0 + (int64_t)kvh * a.kn.s1 + (int64_t)s * a.kn.s2;
+          const float* vr = a.vn.p + (int64_t)b * a.vn.s0 + (int64_t)kvh * a.vn.s1 + (int64_t)s * a.vn.s2;
+          float* kd = const_cast<float*>(kbase) + (int64_t)pos * a.k.s2;
+          float* vd = const_cast<float*>(vbase) + (int64_t)pos * a.v.s2;
+          float y0, y1;
+          rope_pair(kr[j], kr[j + half], a.cos + (int64_t)pos * a.tab_stride, a.sin + (int64_t)pos * a.tab_stride, j, half,
+                    y0, y1);
+          kd[j] = y0;
+          kd[j + half] = y1;
+          vd[j] = vr[j];
+          vd[j + half] = vr[j + half];
+        }
+      }
+      // the writes above are read back by bulk copies (the async proxy)
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      bar_arrive(kBarRope, kThreads);
+    }
+    // query rows of this kv head's group, pre-scaled: row r = (head hg of the group, position s)
+    for (int t = threadIdx.x; t < R * kMaxD; t += kCT) {
+      int r = t / kMaxD, d = t - r * kMaxD;
+      float val = 0.0f;
+      if (r < rows && d < a.D) {
+        int hg = r / a.S, s = r - hg * a.S, h = kvh * a.g + hg;
+        const float* qr = a.q.p + (int64_t)b * a.q.s0 + (int64_t)h * a.q.s1 + (int64_t)s * a.q.s2;
+        if (ROPE) {
+          int pos = pos_offset + s, j = d < half ? d : d - half;
+          float y0, y1;
+          rope_pair(qr[j], qr[j + half], a.cos + (int64_t)pos * a.tab_stride, a.sin + (int64_t)pos * a.tab_stride, j, half,
+                    y0, y1);
+          val = d < half ? y0 : y1;
+        } else {
+          val = qr[d];
+        }
+        val = val * a.scale;
+      }
+      qs[r][d] = val;
+    }
+    bar_sync(kBarConsumers, kCT);
+
+    const int kk = lane & 15, hf = lane >> 4;  // QKᵀ: this lane's key in the tile and half of the head dims
+    const int d0 = 2 * lane;                   // PV: this lane's head-dim pair
+    float m[R], l[R], acc0[R], acc1[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) { m[r] = -INFINITY; l[r] = 0.0f; acc0[r] = 0.0f; acc1[r] = 0.0f; }
+
+    for (int t = warp; t < ntiles; t += kConsumers) {
+      const int s = t % stages;
+      if (!warp_wait(&full[s], (t / stages) & 1)) {
+        if (lane == 0) { atomicExch(a.error_flag, 67); s_abort = 1; }
+        break;
+      }
+      const float* kt = reinterpret_cast<const float*>(smem + s * kStageBytes);
+      const float* vt = reinterpret_cast<const float*>(smem + s * kStageBytes + kHalfStage);
+      const int k0 = j0 + t * kTile, nk = min(kTile, j1 - k0);
+      float sc[R];
+#pragma unroll
+      for (int r = 0; r < R; r++) sc[r] = 0.0f;
+      if (DC == 64) {
+        // lane-rotated float4 order: the 8 lanes of each shared-memory phase hit 8 distinct bank groups
+        const float4* kr = reinterpret_cast<const float4*>(kt + kk * 64) + hf * 8;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const int d4 = (i + kk) & 7;
+          float4 kv = kr[d4];
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            float4 qv = reinterpret_cast<const float4*>(&qs[r][0])[hf * 8 + d4];
+            sc[r] = fmaf(qv.x, kv.x, sc[r]);
+            sc[r] = fmaf(qv.y, kv.y, sc[r]);
+            sc[r] = fmaf(qv.z, kv.z, sc[r]);
+            sc[r] = fmaf(qv.w, kv.w, sc[r]);
+          }
+        }
+      } else {
+        const float4* kr = reinterpret_cast<const float4*>(kt + kk * D);
+        for (int d4 = hf; d4 < (D >> 2); d4 += 2) {
+          float4 kv = kr[d4];
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            float4 qv = reinterpret_cast<const float4*>(&qs[r][0])[d4];
+            sc[r] = fmaf(qv.x, kv.x, sc[r]);
+            sc[r] = fmaf(qv.y, kv.y, sc[r]);
+            sc[r] = fmaf(qv.z, kv.z, sc[r]);
+            sc[r] = fmaf(qv.w, kv.w, sc[r]);
+          }
+        }
+      }
+      const int j = k0 + kk;
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        float sv = sc[r] + __shfl_xor_sync(0xffffffffu, sc[r], 16);
+        bool vis = kk < nk && r < rows && (!a.causal || j <= pos_offset + (r % a.S));
+        sv = vis ? sv : -INFINITY;
+        float mn = fmaxf(m[r], hmax(sv));
+        // mn stays -inf only for a row with no visible key so far; it then keeps its zero state
+        float alpha = (m[r] == -INFINITY) ? 0.0f : expf(m[r] - mn);
+        float p = vis ? expf(sv - mn) : 0.0f;
+        float rs = hsum(p);
+        l[r] = l[r] * alpha + rs;
+        acc0[r] *= alpha;
+        acc1[r] *= alpha;
+        m[r] = mn;
+        if (lane < kTile) ps[warp][r][kk] = p;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j4 = 0; j4 < kTile / 4; j4++) {
+        float2 vv[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++)  // rows past the tile's end hold stale data: read as zero (their p is 0)
+          vv[e] = (4 * j4 + e < nk && d0 < D) ? *reinterpret_cast<const float2*>(vt + (4 * j4 + e) * D + d0)
+                                              : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          float4 p4 = reinterpret_cast<const float4*>(&ps[warp][r][0])[j4];
+          acc0[r] = fmaf(p4.x, vv[0].x, acc0[r]);
+          acc1[r] = fmaf(p4.x, vv[0].y, acc1[r]);
+          acc0[r] = fmaf(p4.y, vv[1].x, acc0[r]);
+          acc1[r] = fmaf(p4.y, vv[1].y, acc1[r]);
+          acc0[r] = fmaf(p4.z, vv[2].x, acc0[r]);
+          acc1[r] = fmaf(p4.z, vv[2].y, acc1[r]);
+          acc0[r] = fmaf(p4.w, vv[3].x, acc0[r]);
+          acc1[r] = fmaf(p4.w, vv[3].y, acc1[r]);
+        }
+      }
+      __syncwarp();  // every lane is done with the stage and with ps
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // merge the warps (fixed order) into this CTA's partial
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      if (lane == 0) { wm[warp][r] = m[r]; wl[warp][r] = l[r]; }
+      wacc[warp][r][d0] = acc0[r];
+      wacc[warp][r][d0 + 1] = acc1[r];
+    }
+    bar_sync(kBarConsumers, kCT);
+    for (int t = threadIdx.x; t < rows * kMaxD; t += kCT) {
+      int r = t / kMaxD, d = t - r * kMaxD;
+      float M = -INFINITY;
+      for (int w = 0; w < kConsumers; w++) M = fmaxf(M, wm[w][r]);
+      float L = 0.0f, A = 0.0f;
+      if (M != -INFINITY) {
+        for (int w = 0; w < kConsumers; w++) {
+          float e = wm[w][r] == -INFINITY ? 0.0f : expf(wm[w][r] - M);
+          L += wl[w][r] * e;
+          A += wacc[w][r][d] * e;
+        }
+      }
+      ca[r][d] = A;
+      if (d == 0) { cm[r] = M; cl[r] = L; }
+    }
+  }
+  // rank 0 merges the cluster's partials in rank order; the second barrier keeps every CTA's shared memory alive
+  // until rank 0 has read it
+  cluster.sync();
+  if (cluster.block_rank() == 0) {
+    const int n = (int)cluster.num_blocks();
+    for (int t = threadIdx.x; t < rows * kMaxD; t += kThreads) {
+      int r = t / kMaxD, d = t - r * kMaxD;
+      float M = -INFINITY;
+      for (int c = 0; c < n; c++) M = fmaxf(M, *cluster.map_shared_rank(&cm[r], c));
+      float L = 0.0f, A = 0.0f;
+      if (M != -INFINITY) {
+        for (int c = 0; c < n; c++) {
+          float mc = *cluster.map_shared_rank(&cm[r], c);
+          if (mc == -INFINITY) continue;
+          float e = expf(mc - M);
+          L += *cluster.map_shared_rank(&cl[r], c) * e;
+          A += *cluster.map_shared_rank(&ca[r][d], c) * e;
+        }
+      }
+      store_row(a, b, kvh, r, d, A, M, L);
+    }
+  }
+  cluster.sync();
+}
+
+// max / sum over a whole warp
+__device__ __forceinline__ float wmax32(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float wsum32(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// The latency variant for few (batch, kv head) pairs (small decode batches), where each warp gets about one tile and
+// the streaming ring cannot pay for itself: no producer warp, every warp loads its own 32-key tile straight from
+// global memory (lane j dots key j; V rows prefetched before the QK step), and the kernel may launch early behind the
+// previous kernel (programmatic dependent launch). One CTA per (key split, kv head, batch); the splits of one
+// (batch, kv head) form a cluster. Each of the 4 warps
+// takes 32-key tiles of the CTA's key range; the warps merge in shared memory and cluster rank 0 merges the CTAs'
+// partials through distributed shared memory, in rank order.
+// DC: the head dim when known at compile time (64), else 0 (read from the arguments). ROPE: fused RoPE + append.
+template <int R, int DC, bool ROPE>
+__global__ void __launch_bounds__(kDirectThreads) k_attn_decode_direct(const Args a) {
+  const int D = DC ? DC : a.D;
+  __shared__ __align__(16) float qs[R][kMaxD];
+  __shared__ float wm[kDirectWarps][R], wl[kDirectWarps][R];
+  __shared__ float wacc[kDirectWarps][R][kMaxD];
   __shared__ float cm[R], cl[R];            // this CTA's merged partial, read by rank 0
   __shared__ float ca[R][kMaxD];
   cg::cluster_group cluster = cg::this_cluster();
@@ -118,7 +440,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
 
   if (ROPE && kend > 0) {
     // the new key/value rows in this CTA's key range go into the caches first (rotated keys)
-    for (int t = threadIdx.x; t < a.S * half; t += kThreads) {
+    for (int t = threadIdx.x; t < a.S * half; t += kDirectThreads) {
       int s = t / half, j = t - s * half, pos = pos_offset + s;
       if (pos < j0 || pos >= j1) continue;
       const float* kr = a.kn.p + (int64_t)b * a.kn.s0 + (int64_t)kvh * a.kn.s1 + (int64_t)s * a.kn.s2;
@@ -134,7 +456,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
     }
   }
   // query rows of this kv head's group, pre-scaled: row r = (head hg of the group, position s)
-  for (int t = threadIdx.x; t < R * kMaxD; t += kThreads) {
+  for (int t = threadIdx.x; t < R * kMaxD; t += kDirectThreads) {
     int r = t / kMaxD, d = t - r * kMaxD;
     float val = 0.0f;
     if (r < rows && d < a.D) {
@@ -159,14 +481,14 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
 #pragma unroll
   for (int r = 0; r < R; r++) { m[r] = -INFINITY; l[r] = 0.0f; acc0[r] = 0.0f; acc1[r] = 0.0f; }
 
-  for (int t0 = j0 + warp * kTile; t0 < j1; t0 += kWarps * kTile) {
+  for (int t0 = j0 + warp * kDirectTile; t0 < j1; t0 += kDirectWarps * kDirectTile) {
     const int j = t0 + lane;
     const bool in = j < j1;
-    const int nk = min(kTile, j1 - t0);
+    const int nk = min(kDirectTile, j1 - t0);
     // this lane's head-dim pair of every V row of the tile, issued first so the loads overlap the QK step
-    float2 vv[kTile];
+    float2 vv[kDirectTile];
 #pragma unroll
-    for (int jj = 0; jj < kTile; jj++)
+    for (int jj = 0; jj < kDirectTile; jj++)
       vv[jj] = (jj < nk && d0 < D) ? *reinterpret_cast<const float2*>(vbase + (int64_t)(t0 + jj) * a.v.s2 + d0)
                                    : make_float2(0.f, 0.f);
     float s[R];
@@ -193,12 +515,12 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
     for (int r = 0; r < R; r++) {
       bool vis = in && r < rows && (!a.causal || j <= pos_offset + (r % a.S));
       float sv = vis ? s[r] : -INFINITY;
-      float mx = wmax(sv);
+      float mx = wmax32(sv);
       float mn = fmaxf(m[r], mx);
       // mn stays -inf only for a row with no visible key so far; it then keeps its zero state
       float alpha = (m[r] == -INFINITY) ? 0.0f : expf(m[r] - mn);
       p[r] = vis ? expf(sv - mn) : 0.0f;
-      float rs = wsum(p[r]);
+      float rs = wsum32(p[r]);
       l[r] = l[r] * alpha + rs;
       acc0[r] *= alpha;
       acc1[r] *= alpha;
@@ -206,7 +528,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
     }
     // keys past the tile's end have p = 0 and zero V rows
 #pragma unroll
-    for (int jj = 0; jj < kTile; jj++) {
+    for (int jj = 0; jj < kDirectTile; jj++) {
 #pragma unroll
       for (int r = 0; r < R; r++) {
         float pj = __shfl_sync(0xffffffffu, p[r], jj);
@@ -224,13 +546,13 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
     wacc[warp][r][d0 + 1] = acc1[r];
   }
   __syncthreads();
-  for (int t = threadIdx.x; t < rows * kMaxD; t += kThreads) {
+  for (int t = threadIdx.x; t < rows * kMaxD; t += kDirectThreads) {
     int r = t / kMaxD, d = t - r * kMaxD;
     float M = -INFINITY;
-    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wm[w][r]);
+    for (int w = 0; w < kDirectWarps; w++) M = fmaxf(M, wm[w][r]);
     float L = 0.0f, A = 0.0f;
     if (M != -INFINITY) {
-      for (int w = 0; w < kWarps; w++) {
+      for (int w = 0; w < kDirectWarps; w++) {
         float e = wm[w][r] == -INFINITY ? 0.0f : expf(wm[w][r] - M);
         L += wl[w][r] * e;
         A += wacc[w][r][d] * e;
@@ -244,7 +566,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
   cluster.sync();
   if (cluster.block_rank() == 0) {
     const int n = (int)cluster.num_blocks();
-    for (int t = threadIdx.x; t < rows * kMaxD; t += kThreads) {
+    for (int t = threadIdx.x; t < rows * kMaxD; t += kDirectThreads) {
       int r = t / kMaxD, d = t - r * kMaxD;
       float M = -INFINITY;
       for (int c = 0; c < n; c++) M = fmaxf(M, *cluster.map_shared_rank(&cm[r], c));
@@ -266,16 +588,55 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
 
 }  // namespace dec
 
+template <int R, int DC, bool ROPE>
+static cudaError_t launch_decode_r(pai_ctx* ctx, const dec::Args& a, dim3 grid) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(dec::k_attn_decode<R, DC, ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)dec::smem_bytes(dec::kStages));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  // A plain cluster launch: the kernel starts once the previous kernel has finished (its griddepcontrol.wait is then a
+  // no-op) but still lets the next kernel launch early. Launched early itself, behind the q/k/v product, it made
+  // the decode step slower (batch 1: 1.05 against 0.93 ms per step of the 16-layer model).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(dec::kThreads);
+  cfg.dynamicSmemBytes = dec::smem_bytes(a.stages);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute la[1];
+  la[0].id = cudaLaunchAttributeClusterDimension;
+  la[0].val.clusterDim.x = (unsigned)a.splits;
+  la[0].val.clusterDim.y = 1;
+  la[0].val.clusterDim.z = 1;
+  cfg.attrs = la;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, dec::k_attn_decode<R, DC, ROPE>, a);
+}
+
+// The latency variant is launched early behind the previous kernel (programmatic dependent launch).
+template <int R, int DC, bool ROPE>
+static cudaError_t launch_direct_r(pai_ctx* ctx, const dec::Args& a, dim3 grid) {
+  return launch_pdl_cluster(dec::k_attn_decode_direct<R, DC, ROPE>, grid, dim3(dec::kDirectThreads), 0, ctx->stream,
+                            (unsigned)a.splits, a);
+}
+
 template <int DC, bool ROPE>
-static cudaError_t launch_decode(pai_ctx* ctx, const dec::Args& a, dim3 grid) {
+static cudaError_t launch_decode(pai_ctx* ctx, const dec::Args& a, dim3 grid, bool direct) {
   int R = a.rows;
-  dim3 blk(dec::kThreads);
-  unsigned cl = (unsigned)a.splits;
-  if (R <= 1) return launch_pdl_cluster(dec::k_attn_decode<1, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
-  if (R <= 2) return launch_pdl_cluster(dec::k_attn_decode<2, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
-  if (R <= 4) return launch_pdl_cluster(dec::k_attn_decode<4, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
-  if (R <= 8) return launch_pdl_cluster(dec::k_attn_decode<8, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
-  return launch_pdl_cluster(dec::k_attn_decode<16, DC, ROPE>, grid, blk, 0, ctx->stream, cl, a);
+  if (direct) {
+    if (R <= 1) return launch_direct_r<1, DC, ROPE>(ctx, a, grid);
+    if (R <= 2) return launch_direct_r<2, DC, ROPE>(ctx, a, grid);
+    if (R <= 4) return launch_direct_r<4, DC, ROPE>(ctx, a, grid);
+    if (R <= 8) return launch_direct_r<8, DC, ROPE>(ctx, a, grid);
+    return launch_direct_r<16, DC, ROPE>(ctx, a, grid);
+  }
+  if (R <= 1) return launch_decode_r<1, DC, ROPE>(ctx, a, grid);
+  if (R <= 2) return launch_decode_r<2, DC, ROPE>(ctx, a, grid);
+  if (R <= 4) return launch_decode_r<4, DC, ROPE>(ctx, a, grid);
+  if (R <= 8) return launch_decode_r<8, DC, ROPE>(ctx, a, grid);
+  return launch_decode_r<16, DC, ROPE>(ctx, a, grid);
 }
 
 static bool aligned_view(const pai_tensor& t, int vec) {
@@ -288,30 +649,45 @@ static bool aligned_view(const pai_tensor& t, int vec) {
 }
 
 // True when the decode kernel handles this call: at most 16 query rows per kv head, head dim <= 64 (a multiple of
-// 4), and K/V views whose positions are 16-byte aligned rows.
+// 4), and K/V views whose rows start on 16-byte boundaries (the bulk copies' alignment).
 bool attn_decode_fits(const pai_tensor& q, const pai_tensor& k, const pai_tensor& v, int H, int KVH, int S, int D) {
   int g = H / KVH;
   if (g * S > dec::kMaxRows || D > dec::kMaxD || D % 4) return false;
-  return q.strides[3] == 1 && aligned_view(k, 4) && aligned_view(v, 2);
+  return q.strides[3] == 1 && aligned_view(k, 4) && aligned_view(v, 4);
 }
 
 // pos_dev: when set, the query position is read on the device and k, v are the whole caches (L = capacity); the
-// key splits are then sized for the capacity and splits past the filled prefix contribute nothing.
+// splits then divide the filled prefix on the device.
 // rope: fused RoPE + cache append (q, kn, vn unrotated; a.k / a.v are the caches the new rows are written into).
 pai_status attn_decode_run(pai_ctx* ctx, dec::Args& a, bool rope) {
   int kend = (a.causal && !a.pos_dev) ? std::min(a.L, a.pos_offset + a.S) : a.L;
   if (kend < 1) kend = 1;
-  // one 32-key tile per warp (128 keys per CTA) while a cluster of at most 8 CTAs covers the keys, else longer splits
-  int kps = dec::kWarps * dec::kTile;
-  int need = (kend + dec::kMaxCluster - 1) / dec::kMaxCluster;
-  if (need > kps) kps = (need + kps - 1) / kps * kps;
-  a.keys_per_split = kps;
-  a.splits = (kend + kps - 1) / kps;
   a.error_flag = ctx->d_error_flag;
+  const int pairs = std::max(1, a.B * a.KVH);
+  const bool direct = pairs < dec::kDirectMinPairs;
+  if (direct) {
+    // latency variant: one 32-key tile per warp (128 keys per CTA) while a cluster of at most 8 CTAs covers the keys,
+    // else longer splits
+    int kps = dec::kDirectWarps * dec::kDirectTile;
+    int need = (kend + dec::kMaxCluster - 1) / dec::kMaxCluster;
+    if (need > kps) kps = (need + kps - 1) / kps * kps;
+    a.keys_per_split = kps;
+    a.splits = (kend + kps - 1) / kps;
+  } else {
+    // streaming variant. splits: as many as keep the whole grid resident in one wave (3 CTAs per SM fit in shared
+    // memory with up to 4 query rows, 2 with 8 or 16), at most one cluster of 8, and at most one per 16-key tile
+    const int per_sm = a.rows <= 4 ? 3 : 2;
+    int splits = std::max(1, std::min(dec::kMaxCluster, per_sm * ctx->sm_count / pairs));
+    a.splits = std::min(splits, (kend + dec::kTile - 1) / dec::kTile);
+    // ring depth: a multiple of the consumer count, so each stage is always read by the same warp (tile t sits in
+    // stage t % stages and is read by warp t % kConsumers) and its barrier phases are awaited in order
+    const int max_tiles = ((kend + a.splits - 1) / a.splits + dec::kTile - 1) / dec::kTile;
+    a.stages = max_tiles <= dec::kConsumers ? dec::kConsumers : dec::kStages;
+  }
   dim3 grid((unsigned)a.splits, (unsigned)a.KVH, (unsigned)a.B);
   cudaError_t e;
-  if (a.D == 64) e = rope ? launch_decode<64, true>(ctx, a, grid) : launch_decode<64, false>(ctx, a, grid);
-  else e = rope ? launch_decode<0, true>(ctx, a, grid) : launch_decode<0, false>(ctx, a, grid);
+  if (a.D == 64) e = rope ? launch_decode<64, true>(ctx, a, grid, direct) : launch_decode<64, false>(ctx, a, grid, direct);
+  else e = rope ? launch_decode<0, true>(ctx, a, grid, direct) : launch_decode<0, false>(ctx, a, grid, direct);
   PAI_PDL_LAUNCH(e, "attn decode");
   return PAI_OK;
 }

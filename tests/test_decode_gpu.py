@@ -54,7 +54,9 @@ def lse_ref(q, k, scale, pos_offset):
 
 
 @pytest.mark.parametrize("B,H,KVH,S,L", [(1, 32, 8, 1, 1), (1, 32, 8, 1, 100), (4, 32, 8, 1, 1000), (2, 16, 4, 3, 517),
-                                         (3, 12, 12, 1, 2000), (1, 8, 1, 2, 64)])
+                                         (3, 12, 12, 1, 2000), (1, 8, 1, 2, 64),
+                                         # 64+ (batch, kv head) pairs: the streaming kernel, up to 16 query rows
+                                         (8, 32, 8, 1, 1000), (16, 16, 4, 3, 517), (64, 8, 1, 2, 300), (32, 64, 4, 1, 2048)])
 def test_decode_attention_over_cache_views(cuda, B, H, KVH, S, L):
     D, max_seq = 64, 2048
     q = rnd(40, B, H, S, D)
@@ -88,7 +90,8 @@ def _ids(seed, n, vocab):
 
 
 @pytest.mark.parametrize("cfg,batch,fused", [(GQA16, 3, True), (HD64, 2, True), (HD64, 1, True), (GQA16, 7, True),
-                                             (HD64, 20, True), (GQA16, 3, False), (HD64, 6, False)])
+                                             (HD64, 20, True), (GQA16, 3, False), (HD64, 6, False),
+                                             (GQA16, 32, True), (HD64, 32, False)])
 def test_graph_decode_steps_match_eager_steps(cfg, batch, fused):
     """GraphDecoder (device ids/position, captured once, replayed) against LlamaModel.forward with the KV cache for the
     same tokens: logits within 1e-4·max|logit| (the decode attention splits the keys differently), greedy ids equal."""
@@ -221,7 +224,10 @@ def test_rope_append_equals_rotary_at_and_kv_append():
 
 
 @pytest.mark.parametrize("B,NH,KV,D,T,pos", [(1, 32, 8, 64, 768, 517), (3, 8, 2, 16, 200, 130), (2, 16, 4, 64, 2048, 1500),
-                                          (4, 8, 8, 32, 64, 0)])
+                                          (4, 8, 8, 32, 64, 0),
+                                          # 64+ (batch, kv head) pairs: the streaming kernel (bulk-copied K/V ring)
+                                          (16, 32, 8, 64, 768, 517), (32, 8, 2, 16, 100, 77), (8, 64, 8, 64, 2048, 1999),
+                                          (64, 4, 1, 64, 40, 0)])
 def test_attn_decode_step_equals_rope_append_then_sdpa_decode(B, NH, KV, D, T, pos):
     """The fused decode-step attention (RoPE + cache append + attention, cluster-merged key splits) against the two
     separate ops: bit-identical outputs and caches; and against float64 attention over the filled cache prefix."""
