@@ -328,6 +328,20 @@ __global__ void k_gather_rows_view(const float* __restrict__ src, pai::DView rv,
   }
 }
 
+// k_gather_rows_view with one thread per 16-byte group: every row start 16-byte aligned and len % 4 == 0.
+__global__ void k_gather_rows_view4(const float* __restrict__ src, pai::DView rv, float* __restrict__ dst, int64_t rows,
+                                    int len) {
+  const int q = len >> 2;
+  const int64_t total = rows * q;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / q;
+    const int c = (int)(i - r * q) * 4;
+    int64_t off, o2, o3;
+    row_offsets3(rv, rv, rv, (uint32_t)r, off, o2, o3);
+    *reinterpret_cast<float4*>(dst + r * len + c) = *reinterpret_cast<const float4*>(src + off + c);
+  }
+}
+
 pai_status gather_dense(pai_ctx* ctx, const pai_tensor& src, float* dst) {
   int64_t n = numel(src);
   if (n == 0) return PAI_OK;
@@ -344,7 +358,13 @@ pai_status gather_dense(pai_ctx* ctx, const pai_tensor& src, float* dst) {
     DView rv = dv;
     rv.rank = dv.rank - 1;
     int64_t rows = n / len;
-    k_gather_rows_view<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(fptr(src), rv, dst, rows, len);
+    bool vec4 = len % 4 == 0 && (uintptr_t)fptr(src) % 16 == 0 && (uintptr_t)dst % 16 == 0;
+    for (int i = 0; i < rv.rank && vec4; i++)
+      if (rv.dims[i] > 1 && rv.strides[i] % 4) vec4 = false;
+    if (vec4)
+      k_gather_rows_view4<<<grid_for(ctx, n / 4, 256), 256, 0, ctx->stream>>>(fptr(src), rv, dst, rows, len);
+    else
+      k_gather_rows_view<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(fptr(src), rv, dst, rows, len);
   } else {
     k_gather<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(fptr(src), dv, dst, n);
   }

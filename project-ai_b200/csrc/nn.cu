@@ -240,6 +240,50 @@ __global__ void k_rotary_rows(const float* __restrict__ x, DView xr, const float
   }
 }
 
+// k_rotary_rows with one thread per 4 consecutive pairs (j..j+3, j+h..j+h+3) of a row: 16-byte loads of x, cos and
+// sin and 16-byte stores, all independent, so the pass streams at memory speed. Needs d % 8 == 0 and every row
+// start of x, cos and sin 16-byte aligned; the same element operations as k_rotary_rows.
+__global__ void k_rotary_rows4(const float* __restrict__ x, DView xr, const float* __restrict__ cs, DView cr,
+                               const float* __restrict__ sn, DView sr, float* __restrict__ y, int64_t rows, int d,
+                               RopeShift shift) {
+  const int half = d >> 1, hq = d >> 3;  // float4 groups per half row
+  int64_t dc = 0, ds = 0;
+  if (shift.pos) {
+    float pf = shift.pos[0];
+    int p = (int)pf;
+    if (!(pf >= 0.0f) || p + shift.seq > shift.table_rows) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(shift.error_flag, 61);
+      return;
+    }
+    dc = (int64_t)p * shift.stride_c;
+    ds = (int64_t)p * shift.stride_s;
+  }
+  const int64_t total = rows * hq;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / hq;
+    const int j = (int)(i - r * hq) * 4;
+    int64_t xo, co, so;
+    row_offsets3(xr, cr, sr, (uint32_t)r, xo, co, so);
+    co += dc;
+    so += ds;
+    const float4 x0 = *reinterpret_cast<const float4*>(x + xo + j), x1 = *reinterpret_cast<const float4*>(x + xo + j + half);
+    const float4 c0 = *reinterpret_cast<const float4*>(cs + co + j), c1 = *reinterpret_cast<const float4*>(cs + co + j + half);
+    const float4 s0 = *reinterpret_cast<const float4*>(sn + so + j), s1 = *reinterpret_cast<const float4*>(sn + so + j + half);
+    float4 y0, y1;
+    y0.x = __fadd_rn(__fmul_rn(x0.x, c0.x), __fmul_rn(-x1.x, s0.x));
+    y0.y = __fadd_rn(__fmul_rn(x0.y, c0.y), __fmul_rn(-x1.y, s0.y));
+    y0.z = __fadd_rn(__fmul_rn(x0.z, c0.z), __fmul_rn(-x1.z, s0.z));
+    y0.w = __fadd_rn(__fmul_rn(x0.w, c0.w), __fmul_rn(-x1.w, s0.w));
+    y1.x = __fadd_rn(__fmul_rn(x1.x, c1.x), __fmul_rn(x0.x, s1.x));
+    y1.y = __fadd_rn(__fmul_rn(x1.y, c1.y), __fmul_rn(x0.y, s1.y));
+    y1.z = __fadd_rn(__fmul_rn(x1.z, c1.z), __fmul_rn(x0.z, s1.z));
+    y1.w = __fadd_rn(__fmul_rn(x1.w, c1.w), __fmul_rn(x0.w, s1.w));
+    float* yr = y + r * d;
+    *reinterpret_cast<float4*>(yr + j) = y0;
+    *reinterpret_cast<float4*>(yr + j + half) = y1;
+  }
+}
+
 // ---------------------------------------------------------------- SwiGLU gate
 __device__ __forceinline__ float silu_mul_elem(float gv, float u) { return silu_mul_value(gv, u); }
 
@@ -469,9 +513,23 @@ static pai_status rotary_impl(pai_ctx* ctx, const pai_tensor* x, const pai_tenso
     if (unit_last) {
       collapse(rank - 1, x->dims, views, 3, dv);  // leading (row) dims only
       int64_t rows = n / d;
-      k_rotary_rows<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(
-          static_cast<const float*>(x->base), dv[0], static_cast<const float*>(cs->base), dv[1],
-          static_cast<const float*>(sn->base), dv[2], fptr(r), rows, d, shift);
+      // 16-byte path: every row start of x, cos and sin (any position shift included) on a 16-byte boundary
+      bool vec4 = d % 8 == 0 && (shift.stride_c % 4 == 0) && (shift.stride_s % 4 == 0);
+      const void* bases[3] = {x->base, cs->base, sn->base};
+      for (int v = 0; v < 3 && vec4; v++) {
+        if ((uintptr_t)bases[v] % 16 || dv[v].offset % 4) vec4 = false;
+        for (int i = 0; i < dv[v].rank; i++)
+          if (dv[v].dims[i] > 1 && dv[v].strides[i] % 4) vec4 = false;
+      }
+      if (vec4) {
+        k_rotary_rows4<<<grid_for(ctx, rows * (d / 8), 256), 256, 0, ctx->stream>>>(
+            static_cast<const float*>(x->base), dv[0], static_cast<const float*>(cs->base), dv[1],
+            static_cast<const float*>(sn->base), dv[2], fptr(r), rows, d, shift);
+      } else {
+        k_rotary_rows<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(
+            static_cast<const float*>(x->base), dv[0], static_cast<const float*>(cs->base), dv[1],
+            static_cast<const float*>(sn->base), dv[2], fptr(r), rows, d, shift);
+      }
     } else if (shift.pos) {
       raw_free(ctx, r.base);
       return set_error(PAI_ERR_UNSUPPORTED, "RotaryAt: rows must be contiguous");
