@@ -113,18 +113,29 @@ __global__ void k_rmsnorm_bwd(const float* __restrict__ x, const float* __restri
 
 // The same rule with each row held in registers (d = 128·C): one read of x and g, dx written once, and each lane
 // accumulating its own columns of dw across the rows its warp visits; partials reduced per block in shared memory.
+// Rows longer than 1024 (C > 8) keep the dw partials in the warp's shared-memory row and read w through the
+// read-only cache instead of holding both in registers (x, g, w and the partials at C = 16 would need ~256
+// registers and spill); the per-element operations and their order are the same.
 template <int C>
 __global__ void __launch_bounds__(256) k_rmsnorm_bwd_reg(const float* __restrict__ x, const float* __restrict__ w,
                                                          const float* __restrict__ g, float* __restrict__ dx,
                                                          float* __restrict__ dw_part, int64_t rows, float eps) {
   extern __shared__ float s_dw[];  // [warps][d]
   constexpr int d = 128 * C;
+  constexpr bool kSmemAcc = C > 8;
+  constexpr int CR = kSmemAcc ? 1 : C;  // register-held w and dw partials
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  float4 wv[C], acc[C];
+  float4* my_acc = reinterpret_cast<float4*>(s_dw + (size_t)wid * d);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 wv[CR], acc[CR];
 #pragma unroll
-  for (int c = 0; c < C; c++) {
-    wv[c] = reinterpret_cast<const float4*>(w)[c * 32 + lane];
+  for (int c = 0; c < CR; c++) {
+    wv[c] = kSmemAcc ? make_float4(0.f, 0.f, 0.f, 0.f) : w4[c * 32 + lane];
     acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (kSmemAcc) {
+#pragma unroll
+    for (int c = 0; c < C; c++) my_acc[c * 32 + lane] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int64_t r = (int64_t)blockIdx.x * nw + wid; r < rows; r += (int64_t)gridDim.x * nw) {
     const float4* px = reinterpret_cast<const float4*>(x + r * d);
@@ -143,26 +154,33 @@ __global__ void __launch_bounds__(256) k_rmsnorm_bwd_reg(const float* __restrict
     float dot = 0.0f;
 #pragma unroll
     for (int c = 0; c < C; c++) {
-      dot = fmaf(gv[c].x, xv[c].x * inv * wv[c].x, dot); dot = fmaf(gv[c].y, xv[c].y * inv * wv[c].y, dot);
-      dot = fmaf(gv[c].z, xv[c].z * inv * wv[c].z, dot); dot = fmaf(gv[c].w, xv[c].w * inv * wv[c].w, dot);
+      const float4 wc = kSmemAcc ? __ldg(w4 + c * 32 + lane) : wv[kSmemAcc ? 0 : c];
+      dot = fmaf(gv[c].x, xv[c].x * inv * wc.x, dot); dot = fmaf(gv[c].y, xv[c].y * inv * wc.y, dot);
+      dot = fmaf(gv[c].z, xv[c].z * inv * wc.z, dot); dot = fmaf(gv[c].w, xv[c].w * inv * wc.w, dot);
     }
     dot = warp_sum(dot);
     float coef = inv * inv / (float)d;
     float4* pdx = reinterpret_cast<float4*>(dx + r * d);
 #pragma unroll
     for (int c = 0; c < C; c++) {
+      const float4 wc = kSmemAcc ? __ldg(w4 + c * 32 + lane) : wv[kSmemAcc ? 0 : c];
       float4 o;
-      o.x = (gv[c].x * wv[c].x) * inv - (coef * xv[c].x) * dot;
-      o.y = (gv[c].y * wv[c].y) * inv - (coef * xv[c].y) * dot;
-      o.z = (gv[c].z * wv[c].z) * inv - (coef * xv[c].z) * dot;
-      o.w = (gv[c].w * wv[c].w) * inv - (coef * xv[c].w) * dot;
+      o.x = (gv[c].x * wc.x) * inv - (coef * xv[c].x) * dot;
+      o.y = (gv[c].y * wc.y) * inv - (coef * xv[c].y) * dot;
+      o.z = (gv[c].z * wc.z) * inv - (coef * xv[c].z) * dot;
+      o.w = (gv[c].w * wc.w) * inv - (coef * xv[c].w) * dot;
       pdx[c * 32 + lane] = o;
-      acc[c].x += gv[c].x * (xv[c].x * inv); acc[c].y += gv[c].y * (xv[c].y * inv);
-      acc[c].z += gv[c].z * (xv[c].z * inv); acc[c].w += gv[c].w * (xv[c].w * inv);
+      float4 a = kSmemAcc ? my_acc[c * 32 + lane] : acc[kSmemAcc ? 0 : c];
+      a.x += gv[c].x * (xv[c].x * inv); a.y += gv[c].y * (xv[c].y * inv);
+      a.z += gv[c].z * (xv[c].z * inv); a.w += gv[c].w * (xv[c].w * inv);
+      if (kSmemAcc) my_acc[c * 32 + lane] = a;
+      else acc[kSmemAcc ? 0 : c] = a;
     }
   }
+  if (!kSmemAcc) {
 #pragma unroll
-  for (int c = 0; c < C; c++) reinterpret_cast<float4*>(s_dw + (size_t)wid * d)[c * 32 + lane] = acc[c];
+    for (int c = 0; c < CR; c++) my_acc[c * 32 + lane] = acc[c];
+  }
   __syncthreads();
   for (int j = threadIdx.x; j < d; j += blockDim.x) {
     float s = 0.0f;
