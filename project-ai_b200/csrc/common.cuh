@@ -211,24 +211,32 @@ inline int grid_for(pai_ctx* ctx, int64_t n, int threads, int per_thread = 1, in
 }  // namespace pai
 
 // Logical row-major index -> element offset of a collapsed view.
+// The loops below run over the fixed maximum rank with constant indices (the inactive dims are skipped): a loop
+// bounded by v.rank indexes the kernel parameter arrays dynamically, which copies them to per-thread local memory.
 __device__ __forceinline__ int64_t dview_offset(const pai::DView& v, int64_t i) {
   int64_t off = v.offset;
-  for (int d = v.rank - 1; d >= 0; d--) {
-    int64_t dim = v.dims[d];
-    int64_t q = i / dim;
-    off += (i - q * dim) * v.strides[d];
-    i = q;
+#pragma unroll
+  for (int d = PAI_MAX_RANK - 1; d >= 0; d--) {
+    if (d < v.rank) {
+      int64_t dim = v.dims[d];
+      int64_t q = i / dim;
+      off += (i - q * dim) * v.strides[d];
+      i = q;
+    }
   }
   return off;
 }
 
 __device__ __forceinline__ int64_t dview_offset32(const pai::DView& v, uint32_t i) {
   int64_t off = v.offset;
-  for (int d = v.rank - 1; d >= 0; d--) {
-    uint32_t dim = (uint32_t)v.dims[d];
-    uint32_t q = i / dim;
-    off += (int64_t)(i - q * dim) * v.strides[d];
-    i = q;
+#pragma unroll
+  for (int d = PAI_MAX_RANK - 1; d >= 0; d--) {
+    if (d < v.rank) {
+      uint32_t dim = (uint32_t)v.dims[d];
+      uint32_t q = i / dim;
+      off += (int64_t)(i - q * dim) * v.strides[d];
+      i = q;
+    }
   }
   return off;
 }
@@ -239,14 +247,17 @@ __device__ __forceinline__ void row_offsets3(const pai::DView& a, const pai::DVi
   oa = a.offset;
   ob = b.offset;
   oc = c.offset;
-  for (int d = a.rank - 1; d >= 0; d--) {
-    uint32_t dim = (uint32_t)a.dims[d];
-    uint32_t q = r / dim;
-    int64_t i = (int64_t)(r - q * dim);
-    oa += i * a.strides[d];
-    ob += i * b.strides[d];
-    oc += i * c.strides[d];
-    r = q;
+#pragma unroll
+  for (int d = PAI_MAX_RANK - 1; d >= 0; d--) {
+    if (d < a.rank) {
+      uint32_t dim = (uint32_t)a.dims[d];
+      uint32_t q = r / dim;
+      int64_t i = (int64_t)(r - q * dim);
+      oa += i * a.strides[d];
+      ob += i * b.strides[d];
+      oc += i * c.strides[d];
+      r = q;
+    }
   }
 }
 
