@@ -133,9 +133,12 @@ Tensor Autograd::detach_leaf(const Tensor& x) {
 }
 
 // Checkpoint (Autograd.cs:120-147): a no-grad forward in its own scope, and a backward that recomputes the segment
-// from a detached copy of the input inside a scope, seeds it through the surrogate Σ(recomputed ⊙ upstream), and keeps
+// from a detached copy of the input inside a scope, runs the segment's backward from the upstream gradient, and keeps
 // the input grad and the segment's parameter grads alive one level up. `on_grads_ready` runs once those parameter
 // grads are final (the data-parallel bucket hook).
+// The reference seeds that backward through the surrogate loss Σ(recomputed ⊙ upstream); the surrogate's gradient
+// with respect to the recomputed output is 1·upstream, exactly upstream, so seeding the walk with upstream gives the
+// same gradients bit for bit without computing the surrogate's (unused) value.
 Tensor Autograd::checkpoint(const std::function<Tensor(const Tensor&)>& segment, const Tensor& input,
                             const std::vector<Tensor>& parameters, const std::function<void()>& on_grads_ready) {
   Tensor output;
@@ -161,7 +164,7 @@ Tensor Autograd::checkpoint(const std::function<Tensor(const Tensor&)>& segment,
         GradMode::Guard enabled(false);
         recomputed = segment(leaf);
       }
-      sum_all(mul(recomputed, upstream))->backward();
+      recomputed->backward(upstream);
       input_grad = leaf->grad ? leaf->grad : be->allocate(input->shape);
       be->keep_alive(input_grad);
       for (const auto& p : parameters)

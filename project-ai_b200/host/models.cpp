@@ -296,7 +296,16 @@ Tensor LlamaModel::forward(const Tensor& ids, const ForwardContext& fctx) {
     }
   }
   h = final_norm->forward(h);
-  return ag().matmul(h, embedding->weight, true);
+  // tied head MatMul(h, Emb.W, transposeB) (Modules.cs:278-287) on the rows [B·S, D], as Linear flattens its input:
+  // the same logits, and the weight gradient comes out of one K = B·S product instead of B per-sequence products
+  // summed by ReduceGradToShape
+  if (h->rank() == 2) return ag().matmul(h, embedding->weight, true);
+  const int d = h->shape.back();
+  const int rows = (int)(h->numel() / d);
+  Dims lead(h->shape.begin(), h->shape.end() - 1);
+  Tensor y = ag().matmul(ag().reshape(ag().contiguous(h), {rows, d}), embedding->weight, true);
+  lead.push_back(embedding->weight->shape[0]);
+  return ag().reshape(y, lead);
 }
 
 // ---------------------------------------------------------------- KvCache (Modules.cs:301-370)

@@ -79,6 +79,8 @@ struct TensorImpl {
   Tensor slice(int axis, int start, int length) const;
   Tensor broadcast_to(const Dims& target) const;
   void backward();  // Tensor.Backward (Tensor.cs:213-252)
+  // The same walk seeded with a given gradient of this tensor's shape instead of the scalar 1.
+  void backward(const Tensor& seed);
 };
 
 Tensor make_view(const TensorImpl& t, Dims shape, std::vector<int64_t> strides, int64_t offset);

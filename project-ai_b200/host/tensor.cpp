@@ -158,6 +158,15 @@ void TensorImpl::backward() {
   if (!backend) throw InvalidOperationError("Backward requires a tensor produced by the Autograd facade (no graph/backend recorded).");
   if (numel() != 1)
     throw InvalidOperationError("Backward expects a scalar loss; this tensor has shape " + dims_str(shape) + ". Reduce to a scalar first.");
+  Tensor seed = backend->add_scalar(backend->allocate(shape), 1.0f);
+  seed->known = 1.0f;
+  backward(seed);
+}
+
+void TensorImpl::backward(const Tensor& seed) {
+  if (!backend) throw InvalidOperationError("Backward requires a tensor produced by the Autograd facade (no graph/backend recorded).");
+  if (!seed || seed->shape != shape)
+    throw ArgumentError("Backward seed must have the tensor's shape " + dims_str(shape) + ".");
   NativeBackend& be = *backend;
   std::vector<TensorImpl*> topo;
   std::vector<Tensor> keep;  // holds every node alive during the walk
@@ -182,8 +191,6 @@ void TensorImpl::backward() {
   }
   for (TensorImpl* n : topo)
     if (n->grad_fn) n->grad.reset();
-  Tensor seed = be.add_scalar(be.allocate(shape), 1.0f);
-  seed->known = 1.0f;
   grad = seed;
   for (int i = (int)topo.size() - 1; i >= 0; i--) {
     TensorImpl* node = topo[(size_t)i];
