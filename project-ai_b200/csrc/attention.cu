@@ -429,9 +429,12 @@ PAI_API pai_status pai_sdpa_bwd(pai_ctx* ctx, const pai_tensor* q, const pai_ten
   if (!is_dense(*out) || !is_dense(*lse)) return set_error(PAI_ERR_ARGUMENT, "sdpa_bwd: out and lse must be the forward's results");
   int32_t qd[4] = {a.B, a.H, a.S, a.D}, kd[4] = {a.B, a.KVH, a.L, a.D};
   pai_tensor rq, rk, rv;
-  PAI_TRY(alloc_tensor(ctx, 4, qd, q->dtype, true, &rq));
-  PAI_TRY(alloc_tensor(ctx, 4, kd, q->dtype, true, &rk));
-  PAI_TRY(alloc_tensor(ctx, 4, kd, q->dtype, true, &rv));
+  // the tensor-core kernels write every element of dq, dk and dv; the CUDA-core kernels and empty key ranges start
+  // from zeros
+  const bool zero = attn_force_simt() || a.L == 0;
+  PAI_TRY(alloc_tensor(ctx, 4, qd, q->dtype, zero, &rq));
+  PAI_TRY(alloc_tensor(ctx, 4, kd, q->dtype, zero, &rk));
+  PAI_TRY(alloc_tensor(ctx, 4, kd, q->dtype, zero, &rv));
   if (numel(rq) > 0 && a.L > 0) {
     static bool attr = false;
     if (!attr) {

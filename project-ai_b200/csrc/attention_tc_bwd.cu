@@ -276,11 +276,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
       }
     }
     if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) ok = false;
-    if (ok && N > 0) {
-      fence_after();
+    if (ok || N == 0) {
+      // keys that no query sees (N == 0) get zero gradients: every output row is written
       float dvv[32], dkk[32];
-      tmem_ld32(tmem + lane_off + cDV + col, dvv);
-      tmem_ld32(tmem + lane_off + cDK + col, dkk);
+      if (N > 0) {
+        fence_after();
+        tmem_ld32(tmem + lane_off + cDV + col, dvv);
+        tmem_ld32(tmem + lane_off + cDK + col, dkk);
+      } else {
+#pragma unroll
+        for (int d = 0; d < 32; d++) { dvv[d] = 0.0f; dkk[d] = 0.0f; }
+      }
       if (key < a.L) {
         int64_t base = (((int64_t)b * a.KVH + kvh) * a.L + key) * a.D;
 #pragma unroll
@@ -432,10 +438,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
       }
     }
     if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) ok = false;
-    if (ok && N > 0) {
-      fence_after();
+    if (ok || N == 0) {
+      // queries that see no key (N == 0) get zero gradients: every output row is written
       float dq[32];
-      tmem_ld32(tmem + lane_off + cDQ + col, dq);
+      if (N > 0) {
+        fence_after();
+        tmem_ld32(tmem + lane_off + cDQ + col, dq);
+      } else {
+#pragma unroll
+        for (int d = 0; d < 32; d++) dq[d] = 0.0f;
+      }
       if (qi < a.S) {
         int64_t base = (((int64_t)b * a.H + h) * a.S + qi) * a.D;
 #pragma unroll

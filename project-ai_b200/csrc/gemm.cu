@@ -126,9 +126,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 }
 
 // ---------------------------------------------------------------- pack
+// Up to this many batch matrices travel inside the kernel parameters (read through a __grid_constant__ parameter, so
+// in place); more take a device array uploaded per call. Inline arrays keep the host-to-device copies (each one a
+// copy-engine operation serialised between kernels on the stream) off the per-product path.
+constexpr int kInlineBatches = 16;
+
 struct PackDesc {
   const float* src;
-  const int64_t* batch_off;  // element offset of each batch matrix (device array)
+  const int64_t* batch_off;  // element offset of each batch matrix (device array), or null: boff_inline holds them
+  int64_t boff_inline[kInlineBatches];
   int64_t sr, sk;            // element strides along rows and along k
   int rows, k;               // logical extent
   int kt, rt_pad;            // k tiles, row tiles (padded)
@@ -136,11 +142,12 @@ struct PackDesc {
 };
 
 // grid (kt, rt_pad, batches); 256 threads. Writes one 128x32 hi tile and one lo tile.
-__global__ void __launch_bounds__(256) k_pack(PackDesc d, float* __restrict__ hi, float* __restrict__ lo) {
+__global__ void __launch_bounds__(256) k_pack(const __grid_constant__ PackDesc d, float* __restrict__ hi, float* __restrict__ lo) {
   __shared__ float tile[kBM][kBK + 1];
   int kt = blockIdx.x, rt = blockIdx.y, b = blockIdx.z;
   int tid = threadIdx.x;
-  const float* src = d.src + d.batch_off[b];
+  const int64_t* boffs = d.batch_off ? d.batch_off : d.boff_inline;
+  const float* src = d.src + boffs[b];
   int r0 = rt * kBM, k0 = kt * kBK;
   if (d.vec && d.sk == 1) {
     for (int idx = tid; idx < kBM * (kBK / 4); idx += 256) {
@@ -195,8 +202,10 @@ __global__ void __launch_bounds__(256) k_pack(PackDesc d, float* __restrict__ hi
 struct GemmArgs {
   const float* a_hi; const float* a_lo;  // packed A: [batch_a][kt][mt][tile]
   const float* b_hi; const float* b_lo;  // packed B: [batch_b][kt][nt_pad][tile]
-  const int32_t* a_index;                // output batch -> A batch
+  const int32_t* a_index;                // output batch -> A batch (device array), or null: the inline arrays
   const int32_t* b_index;                // output batch -> B batch
+  int32_t a_index_inline[kInlineBatches];
+  int32_t b_index_inline[kInlineBatches];
   float* c;                              // [batch][m][n] (or split partials [split][batch][m][n])
   int m, n, kt;                          // rows, cols, k tiles
   int mt, nt_pad;                        // A row tiles, B row tiles (padded)
@@ -235,7 +244,7 @@ struct GemmSmem {
 };
 
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1) k_gemm_tc(GemmArgs g) {
+__global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ GemmArgs g) {
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -273,7 +282,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(GemmArgs g) {
       for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
         int split, bt, mb, nb;
         tile_coords(g, t, split, bt, mb, nb);
-        int ba = g.a_index[bt], bb = g.b_index[bt];
+        int ba = (g.a_index ? g.a_index : g.a_index_inline)[bt], bb = (g.b_index ? g.b_index : g.b_index_inline)[bt];
         int k0 = split * g.kt_per_split;
         int k1 = min(g.kt, k0 + g.kt_per_split);
         for (int kb = k0; kb < k1; kb++) {
@@ -471,7 +480,7 @@ static pai_status pack_operand(pai_ctx* ctx, const float* base, const std::vecto
   PAI_TRY(scratch(ctx, floats * 4, hi));
   PAI_TRY(scratch(ctx, floats * 4, lo));
   Scratch doff;
-  PAI_TRY(upload(ctx, boffs.data(), boffs.size() * 8, &doff));
+  if (boffs.size() > (size_t)kInlineBatches) PAI_TRY(upload(ctx, boffs.data(), boffs.size() * 8, &doff));
   // 16-byte loads along the unit-stride axis: every batch matrix and row start 16-byte aligned, and the unit-stride
   // extent a multiple of 4 so a vector never crosses the edge.
   bool aligned = (reinterpret_cast<uintptr_t>(base) & 15) == 0;
@@ -479,7 +488,12 @@ static pai_status pack_operand(pai_ctx* ctx, const float* base, const std::vecto
   int vec = 0;
   if (aligned && sk == 1 && sr % 4 == 0 && k % 4 == 0) vec = 1;
   else if (aligned && sr == 1 && sk % 4 == 0 && rows % 4 == 0) vec = 1;
-  PackDesc d{base, static_cast<const int64_t*>(doff.p), sr, sk, rows, k, kt, rt_pad, vec};
+  PackDesc d{};
+  d.src = base;
+  d.batch_off = static_cast<const int64_t*>(doff.p);
+  if (!d.batch_off)
+    for (size_t i = 0; i < boffs.size(); i++) d.boff_inline[i] = boffs[i];
+  d.sr = sr; d.sk = sk; d.rows = rows; d.k = k; d.kt = kt; d.rt_pad = rt_pad; d.vec = vec;
   dim3 grid((unsigned)kt, (unsigned)rt_pad, (unsigned)boffs.size());
   k_pack<<<grid, 256, 0, ctx->stream>>>(d, static_cast<float*>(hi->p), static_cast<float*>(lo->p));
   PAI_LAUNCH_CHECK("gemm pack");
@@ -615,8 +629,10 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   Scratch ahi, alo, bhi, blo, dai, dbi, part;
   PAI_TRY(pack_operand(ctx, abase, a_distinct, sam, sak, m, k, mt, &ahi, &alo));
   PAI_TRY(pack_operand(ctx, bbase, b_distinct, sbn, sbk, n, k, nt_pad, &bhi, &blo));
-  PAI_TRY(upload(ctx, a_idx.data(), a_idx.size() * 4, &dai));
-  PAI_TRY(upload(ctx, b_idx.data(), b_idx.size() * 4, &dbi));
+  if (batch > kInlineBatches) {
+    PAI_TRY(upload(ctx, a_idx.data(), a_idx.size() * 4, &dai));
+    PAI_TRY(upload(ctx, b_idx.data(), b_idx.size() * 4, &dbi));
+  }
 
   int tiles = mt * tiles_n * (int)batch;
   int splits = 1;
@@ -636,6 +652,8 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   g.a_hi = static_cast<float*>(ahi.p); g.a_lo = static_cast<float*>(alo.p);
   g.b_hi = static_cast<float*>(bhi.p); g.b_lo = static_cast<float*>(blo.p);
   g.a_index = static_cast<int32_t*>(dai.p); g.b_index = static_cast<int32_t*>(dbi.p);
+  if (batch <= kInlineBatches)
+    for (int64_t i = 0; i < batch; i++) { g.a_index_inline[i] = a_idx[(size_t)i]; g.b_index_inline[i] = b_idx[(size_t)i]; }
   g.c = cdst; g.m = m; g.n = n; g.kt = kt; g.mt = mt; g.nt_pad = nt_pad;
   g.tiles_m = mt; g.tiles_n = tiles_n; g.batches = (int)batch; g.splits = splits; g.kt_per_split = kt_per_split;
   g.error_flag = ctx->d_error_flag;

@@ -405,9 +405,9 @@ PAI_API pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_
     return set_error(PAI_ERR_ARGUMENT, "RmsNormBackward: shapes disagree (%s, %s, %s)", shape_str(*x).c_str(),
                      shape_str(*w).c_str(), shape_str(*g).c_str());
   pai_tensor rdx, rdw;
-  PAI_TRY(alloc_tensor(ctx, x->rank, x->dims, x->dtype, false, &rdx));
-  PAI_TRY(alloc_tensor(ctx, 1, &d, x->dtype, true, &rdw));
   int64_t rows = d ? numel(*x) / d : 0;
+  PAI_TRY(alloc_tensor(ctx, x->rank, x->dims, x->dtype, false, &rdx));
+  PAI_TRY(alloc_tensor(ctx, 1, &d, x->dtype, rows == 0, &rdw));  // the column sum writes every entry
   if (rows > 0) {
     const float *xp, *wp, *gp;
     Scratch hx, hw, hg, part;

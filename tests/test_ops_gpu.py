@@ -100,7 +100,9 @@ def attention_grads(q, k, v, do, scale, pos_offset):
 
 
 @pytest.mark.parametrize("B,H,KVH,S,L,D,off", [(2, 4, 2, 70, 70, 32, 0), (1, 2, 1, 1, 9, 16, 8), (1, 4, 4, 5, 12, 8, 7),
-                                               (2, 12, 12, 130, 130, 64, 0), (1, 8, 2, 64, 64, 64, 0)])
+                                               (2, 12, 12, 130, 130, 64, 0), (1, 8, 2, 64, 64, 64, 0),
+                                               # keys 164..299 are visible to no query: their dK/dV rows must be zeros
+                                               (1, 2, 1, 64, 300, 64, 100)])
 def test_sdpa_forward_backward(cuda, B, H, KVH, S, L, D, off):
     q = rnd(10, B, H, S, D)
     k = rnd(11, B, KVH, L, D)
