@@ -256,7 +256,10 @@ Tensor Autograd::rms_norm(const Tensor& x, const Tensor& w, float eps) {
 
 // RotaryEmbedding (Autograd.cs:250-255).
 Tensor Autograd::rotary(const Tensor& x, const Tensor& cos, const Tensor& sin) {
-  Tensor neg_sin = be->mul_scalar(sin, -1.0f);
+  return rotary(x, cos, sin, be->mul_scalar(sin, -1.0f));
+}
+
+Tensor Autograd::rotary(const Tensor& x, const Tensor& cos, const Tensor& sin, const Tensor& neg_sin) {
   Tensor y = be->rotary(x, cos, sin);
   return record(y, "rope", {x}, [this, cos, neg_sin](const Tensor& g) {
     return std::vector<Tensor>{be->rotary(g, cos, neg_sin)};

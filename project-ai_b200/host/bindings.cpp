@@ -179,7 +179,8 @@ PYBIND11_MODULE(_paihost, m) {
       .def("contiguous", &Autograd::contiguous).def("sum_all", &Autograd::sum_all).def("mean", &Autograd::mean)
       .def("embedding", &Autograd::embedding).def("cross_entropy", &Autograd::cross_entropy)
       .def("softmax", &Autograd::softmax).def("silu", &Autograd::silu).def("rms_norm", &Autograd::rms_norm)
-      .def("rotary", &Autograd::rotary).def("transpose", &Autograd::transpose).def("permute", &Autograd::permute)
+      .def("rotary", static_cast<Tensor (Autograd::*)(const Tensor&, const Tensor&, const Tensor&)>(&Autograd::rotary))
+      .def("transpose", &Autograd::transpose).def("permute", &Autograd::permute)
       .def("reshape", [](Autograd& ag, const Tensor& x, const py::sequence& d) { return ag.reshape(x, to_dims(d)); })
       .def("slice", &Autograd::slice)
       .def("broadcast_to", [](Autograd& ag, const Tensor& x, const py::sequence& d) { return ag.broadcast_to(x, to_dims(d)); })

@@ -152,6 +152,8 @@ RotaryEmbedding::RotaryEmbedding(ParameterContext ctx, int hd, float theta, int 
     }
   cos = be().from_host(c.data(), (int64_t)c.size(), {ms, hd});
   sin = be().from_host(s.data(), (int64_t)s.size(), {ms, hd});
+  for (auto& v : s) v = -v;
+  neg_sin = be().from_host(s.data(), (int64_t)s.size(), {ms, hd});
 }
 
 Tensor RotaryEmbedding::apply_at_offset(const Tensor& x, int offset) {
@@ -159,7 +161,18 @@ Tensor RotaryEmbedding::apply_at_offset(const Tensor& x, int offset) {
   if (offset < 0 || offset + seq > max_seq)
     throw OutOfRangeError("RoPE positions " + std::to_string(offset) + ".." + std::to_string(offset + seq - 1) +
                           " exceed the table length " + std::to_string(max_seq) + ".");
-  return ag().rotary(x, cos->slice(0, offset, seq), sin->slice(0, offset, seq));
+  return ag().rotary(x, cos->slice(0, offset, seq), sin->slice(0, offset, seq), neg_sin->slice(0, offset, seq));
+}
+
+Tensor RotaryEmbedding::apply_seq_major(const Tensor& x, int offset) {
+  if (x->rank() != 4) throw ArgumentError("RoPE on [b, s, heads, dh] expects a rank-4 tensor; got " + dims_str(x->shape) + ".");
+  int seq = x->shape[1], hd = x->shape[3];
+  if (offset < 0 || offset + seq > max_seq)
+    throw OutOfRangeError("RoPE positions " + std::to_string(offset) + ".." + std::to_string(offset + seq - 1) +
+                          " exceed the table length " + std::to_string(max_seq) + ".");
+  // table rows offset .. offset+seq-1 as [seq, 1, dh]: broadcast over the heads axis
+  auto rows = [&](const Tensor& t) { return t->slice(0, offset, seq)->reshape({seq, 1, hd}); };
+  return ag().rotary(x, rows(cos), rows(sin), rows(neg_sin));
 }
 
 // ---------------------------------------------------------------- SwiGLU (Modules.cs:84-109)
@@ -202,11 +215,19 @@ Tensor Attention::forward(const Tensor& x, const ForwardContext& fctx) {
   int h = cfg.head_count, kvh = cfg.kv_head_count, dh = cfg.head_dim(), g = h / kvh;
   int pos_offset = cache ? cache->length(layer) : 0;
   Autograd& A = ag();
-  Tensor qh = A.transpose(A.reshape(wq->forward(x), {b, s, h, dh}), 1, 2);
-  Tensor kh = A.transpose(A.reshape(wk->forward(x), {b, s, kvh, dh}), 1, 2);
+  Tensor qh, kh;
   Tensor vh = A.transpose(A.reshape(wv->forward(x), {b, s, kvh, dh}), 1, 2);
-  qh = rope->apply_at_offset(qh, pos_offset);
-  kh = rope->apply_at_offset(kh, pos_offset);
+  if (!cache) {
+    // RoPE on the projections' [b, s, heads, dh] layout, then the head-major views attention reads. The rotation of
+    // each element is the one RotaryEmbedding applies to the head-major view (same pair, same table row), and the
+    // backward's rotated gradient comes out dense in [b, s, heads, dh], so folding it back into the projection's
+    // [b, s, heads·dh] rows is a reshape, not a copy.
+    qh = A.transpose(rope->apply_seq_major(A.reshape(wq->forward(x), {b, s, h, dh}), pos_offset), 1, 2);
+    kh = A.transpose(rope->apply_seq_major(A.reshape(wk->forward(x), {b, s, kvh, dh}), pos_offset), 1, 2);
+  } else {
+    qh = rope->apply_at_offset(A.transpose(A.reshape(wq->forward(x), {b, s, h, dh}), 1, 2), pos_offset);
+    kh = rope->apply_at_offset(A.transpose(A.reshape(wk->forward(x), {b, s, kvh, dh}), 1, 2), pos_offset);
+  }
   int key_len = s;
   if (cache) {
     auto kv = cache->append(layer, kh, vh);

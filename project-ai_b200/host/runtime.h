@@ -234,6 +234,8 @@ class Autograd {
   Tensor silu(const Tensor& x);
   Tensor rms_norm(const Tensor& x, const Tensor& w, float eps);
   Tensor rotary(const Tensor& x, const Tensor& cos, const Tensor& sin);
+  // with the backward's −sin table supplied (no per-call negation)
+  Tensor rotary(const Tensor& x, const Tensor& cos, const Tensor& sin, const Tensor& neg_sin);
   Tensor transpose(const Tensor& x, int a0, int a1);
   Tensor permute(const Tensor& x, const std::vector<int>& p);
   Tensor reshape(const Tensor& x, const Dims& d);
@@ -341,7 +343,10 @@ class RotaryEmbedding : public Module {
  public:
   RotaryEmbedding(ParameterContext ctx, int head_dim, float theta, int max_seq);
   Tensor apply_at_offset(const Tensor& x, int offset);
+  // The same rotation of x [b, s, heads, dh] (positions on axis 1), the tables broadcast over the heads.
+  Tensor apply_seq_major(const Tensor& x, int offset);
   Tensor cos, sin;
+  Tensor neg_sin;  // −sin, the backward's table (RotaryEmbedding's backward, Autograd.cs:250-255), built once
   int max_seq;
 };
 
