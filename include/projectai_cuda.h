@@ -119,6 +119,11 @@ pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tensor* b, in
 pai_status pai_sum(pai_ctx* ctx, const pai_tensor* x, int32_t axis, int32_t keep_dims, pai_tensor* out);
 pai_status pai_mean(pai_ctx* ctx, const pai_tensor* x, int32_t axis, int32_t keep_dims, pai_tensor* out);
 pai_status pai_max(pai_ctx* ctx, const pai_tensor* x, int32_t axis, int32_t keep_dims, pai_tensor* out);
+/* Index of the largest entry of each row of a [rows..., n] view (last axis unit-stride, leading axes collapsing to
+ * one row stride), as float indices in a new [rows] tensor, with the rules of ArgMax (ProjectAI.Models/Sampling.cs:
+ * 15-31, used by GreedySampler, :33-38): NaN entries are skipped, ties resolve to the lowest index, and a row without
+ * a number gives 0. Greedy decoding then reads one index per sequence instead of each sequence's logits row. */
+pai_status pai_argmax_rows(pai_ctx* ctx, const pai_tensor* x, pai_tensor* out);
 
 /* ---- Transformer primitives (IComputeBackend.cs:45-49; CpuComputeBackend.cs:322-420) ---- */
 pai_status pai_softmax(pai_ctx* ctx, const pai_tensor* x, int32_t axis, pai_tensor* out);

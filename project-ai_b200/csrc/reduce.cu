@@ -198,7 +198,88 @@ __global__ void k_softmax_cols(const float* __restrict__ x, float* __restrict__ 
 
 }  // namespace pai
 
+// ---------------------------------------------------------------- row argmax (greedy decoding)
+// ArgMax of Sampling.cs:15-31 per row: NaN entries are skipped, ties resolve to the lowest index, and a row with no
+// number gives index 0. Each thread scans its entries in index order keeping the first maximum; the block then keeps
+// the larger value and, between equal values, the lower index, which is the sequential scan's answer.
+__device__ __forceinline__ void argmax_keep(float v2, int i2, float& v1, int& i1) {
+  if (i2 >= 0 && (i1 < 0 || v2 > v1 || (v2 == v1 && i2 < i1))) { v1 = v2; i1 = i2; }
+}
+
+__global__ void __launch_bounds__(256) k_argmax_rows(const float* __restrict__ x, int64_t row_stride, int n, int vec,
+                                                     float* __restrict__ out) {
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  const float* p = x + (int64_t)blockIdx.x * row_stride;
+  float bv = -INFINITY;
+  int bi = -1;
+  if (vec) {
+    for (int i4 = threadIdx.x; i4 < (n >> 2); i4 += blockDim.x) {
+      float4 q = reinterpret_cast<const float4*>(p)[i4];
+      float e[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        if (!isnan(e[j]) && (bi < 0 || e[j] > bv)) { bv = e[j]; bi = 4 * i4 + j; }
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float v = p[i];
+      if (!isnan(v) && (bi < 0 || v > bv)) { bv = v; bi = i; }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    argmax_keep(ov, oi, bv, bi);
+  }
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) { sv[w] = bv; si[w] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = sv[0];
+    int i = si[0];
+    for (int k = 1; k < nw; k++) argmax_keep(sv[k], si[k], v, i);
+    out[blockIdx.x] = (float)(i < 0 ? 0 : i);
+  }
+}
+
 using namespace pai;
+
+PAI_API pai_status pai_argmax_rows(pai_ctx* ctx, const pai_tensor* x, pai_tensor* out) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> g(ctx->mu);
+  PAI_TRY(check_view(ctx, x, "x"));
+  if (x->rank < 1 || x->dims[x->rank - 1] < 1 || x->strides[x->rank - 1] != 1)
+    return set_error(PAI_ERR_ARGUMENT, "ArgMaxRows: the last axis must be non-empty and unit-stride; got %s",
+                     shape_str(*x).c_str());
+  const int n = x->dims[x->rank - 1];
+  // the leading axes must address the rows with one stride: consecutive non-unit axes nest, and the innermost one's
+  // stride steps a row
+  int64_t rows = 1, row_stride = n;
+  int prev = -1;
+  for (int i = 0; i < x->rank - 1; i++) {
+    rows *= x->dims[i];
+    if (x->dims[i] == 1) continue;
+    if (prev >= 0 && x->strides[prev] != x->strides[i] * x->dims[i])
+      return set_error(PAI_ERR_UNSUPPORTED, "ArgMaxRows: the leading axes of %s do not collapse to one row stride",
+                       shape_str(*x).c_str());
+    prev = i;
+  }
+  if (prev >= 0) row_stride = x->strides[prev];
+  if (rows > INT32_MAX) return set_error(PAI_ERR_UNSUPPORTED, "ArgMaxRows: too many rows");
+  int32_t od[1] = {(int32_t)rows};
+  pai_tensor r;
+  PAI_TRY(alloc_tensor(ctx, 1, od, x->dtype, false, &r));
+  if (rows > 0) {
+    const float* base = fptr(*x);
+    int vec = (n % 4 == 0) && (reinterpret_cast<uintptr_t>(base) % 16 == 0) && (row_stride % 4 == 0);
+    k_argmax_rows<<<(unsigned)rows, 256, 0, ctx->stream>>>(base, row_stride, n, vec, fptr(r));
+    PAI_LAUNCH_CHECK("argmax rows");
+  }
+  *out = r;
+  return PAI_OK;
+}
 
 PAI_API pai_status pai_sum(pai_ctx* c, const pai_tensor* x, int32_t a, int32_t k, pai_tensor* o) { return reduce<kRSum>(c, x, a, k, o); }
 PAI_API pai_status pai_mean(pai_ctx* c, const pai_tensor* x, int32_t a, int32_t k, pai_tensor* o) { return reduce<kRMean>(c, x, a, k, o); }

@@ -140,6 +140,8 @@ PYBIND11_MODULE(_paihost, m) {
       .def("rotary_at", &NativeBackend::rotary_at)
       .def("kv_append", &NativeBackend::kv_append)
       .def("sdpa_decode", &NativeBackend::sdpa_decode)
+      .def_property_readonly("has_argmax_rows", &NativeBackend::has_argmax_rows)
+      .def("argmax_rows", &NativeBackend::argmax_rows)
       .def("linear_fused", &NativeBackend::linear_fused, py::arg("x"), py::arg("weights"), py::arg("mode"),
            py::arg("residual") = nullptr, py::arg("norm_weight") = nullptr, py::arg("eps") = 0.0f)
       .def("rope_append", &NativeBackend::rope_append)

@@ -160,6 +160,9 @@ class NativeBackend {
   Tensor sdpa_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& pos, float scale);
   // fused decode-step ops: x·Wᵀ over several weights with a store / residual / SiLU·mul epilogue, and RoPE + KV append
   bool has_decode_fusions() const;
+  // index of each row's largest entry (ArgMax's rules, Sampling.cs:15-31) as a [rows] float tensor; optional op
+  bool has_argmax_rows() const;
+  Tensor argmax_rows(const Tensor& x);
   Tensor linear_fused(const Tensor& x, const std::vector<Tensor>& weights, int mode, const Tensor& residual = nullptr,
                       const Tensor& norm_weight = nullptr, float eps = 0.0f);
   Tensor rope_append(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos_table, const Tensor& sin_table,

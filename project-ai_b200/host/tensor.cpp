@@ -288,7 +288,8 @@ void TensorImpl::backward(const Tensor& seed) {
   X(graph_begin, int (*)(pai_ctx*))                                                                                      \
   X(graph_end, int (*)(pai_ctx*, pai_graph**))                                                                           \
   X(graph_launch, int (*)(pai_ctx*, pai_graph*))                                                                         \
-  X(graph_destroy, int (*)(pai_ctx*, pai_graph*))
+  X(graph_destroy, int (*)(pai_ctx*, pai_graph*))                                                                       \
+  X(argmax_rows, int (*)(pai_ctx*, const pai_tensor*, pai_tensor*))
 
 template <class T>
 using Fn = T;
@@ -355,6 +356,7 @@ bool NativeBackend::has_graphs() const {
 }
 
 bool NativeBackend::has_decode_fusions() const { return fn_->linear_fused && fn_->rope_append && fn_->attn_decode_step; }
+bool NativeBackend::has_argmax_rows() const { return fn_->argmax_rows != nullptr; }
 
 Tensor NativeBackend::wrap(const pai_tensor& d) {
   auto st = std::make_shared<Storage>();
@@ -711,6 +713,13 @@ Tensor NativeBackend::sdpa_decode(const Tensor& q, const Tensor& k_cache, const 
   need((void*)fn_->sdpa_decode, "sdpa_decode");
   pai_tensor dq = q->desc(), dk = k_cache->desc(), dv = v_cache->desc(), dp = pos->desc(), o;
   check(fn_->sdpa_decode(ctx_, &dq, &dk, &dv, &dp, scale, &o));
+  return wrap(o);
+}
+
+Tensor NativeBackend::argmax_rows(const Tensor& x) {
+  need((void*)fn_->argmax_rows, "argmax_rows");
+  pai_tensor dx = x->desc(), o;
+  check(fn_->argmax_rows(ctx_, &dx, &o));
   return wrap(o);
 }
 

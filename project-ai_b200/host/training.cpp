@@ -321,12 +321,20 @@ GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<
   GradMode::Guard nograd(true);
   int vocab = cfg.vocab_size;
   std::vector<float> last_rows((size_t)batch * vocab);
+  const bool device_argmax = !sampler && be->has_argmax_rows();
+  std::vector<float> picked((size_t)batch);
   auto pick = [&](const Tensor& logits, std::vector<int>& out) {
     int rows = logits->shape[1];
     out.clear();
+    out.resize((size_t)batch);
+    if (device_argmax) {
+      // greedy: the argmax of every sequence's last row on the device (ArgMax's rules), one index per sequence back
+      be->to_host(be->argmax_rows(logits->slice(1, rows - 1, 1)), picked.data(), (int64_t)batch);
+      for (int bi = 0; bi < batch; bi++) out[(size_t)bi] = (int)picked[(size_t)bi];
+      return;
+    }
     // one download of every sequence's last row [batch, vocab]; rows are then sampled in batch order
     be->to_host(logits->slice(1, rows - 1, 1), last_rows.data(), (int64_t)last_rows.size());
-    out.resize((size_t)batch);
     if (sampler) {
       sampler->sample_rows(last_rows.data(), batch, vocab, out.data());
     } else {

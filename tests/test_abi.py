@@ -49,7 +49,7 @@ def test_oracle_exports_contract_ops():
                   "nccl_unique_id", "nccl_init", "allreduce_bucket", "allreduce_wait", "nccl_abort", "check_device_error",
                   "timer_start", "timer_stop", "launch_count", "kernel_timing", "kernel_stats", "rmsnorm_bwd_noalloc",
                   "write", "gather_dev", "rotary_at", "kv_append", "sdpa_decode", "graph_begin", "graph_end",
-                  "graph_launch", "graph_destroy", "linear_fused", "rope_append", "attn_decode_step"}:
+                  "graph_launch", "graph_destroy", "linear_fused", "rope_append", "attn_decode_step", "argmax_rows"}:
             continue  # fused extensions and diagnostics are CUDA-only
         assert "oracle_" + op in syms, op
 

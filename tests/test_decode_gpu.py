@@ -119,6 +119,29 @@ def test_graph_decode_steps_match_eager_steps(cfg, batch, fused):
     be.check_device_error()
 
 
+@pytest.mark.parametrize("rows,n", [(32, 32000), (5, 1001), (1, 4), (3, 1)])
+def test_device_argmax_follows_the_reference_rules(rows, n):
+    """pai_argmax_rows against the host ArgMax (Sampling.cs:15-31): NaN skipped, ties to the lowest index, a row of
+    NaN gives 0; on a dense [rows, n] tensor and on the last-position view of a [rows, 3, n] tensor."""
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", 0)
+    rs = np.random.RandomState(rows * 7 + n)
+    x = rs.standard_normal((rows, 3, n)).astype(np.float32)
+    last = x[:, 2]
+    if n >= 4:
+        last[0, rs.randint(0, n, size=max(1, n // 10))] = np.nan      # NaNs never win
+        top = last[min(1, rows - 1)].max()
+        last[min(1, rows - 1), [n - 1, n // 2]] = top + 1.0            # a tie: the lower index wins
+        last[rows - 1, : n // 2] = -np.inf
+    if rows >= 3:
+        last[2, :] = np.nan                                            # no number: index 0
+    expect = [H.argmax(last[r].copy()) for r in range(rows)]
+    full = be.from_host(x)
+    got_view = be.to_host(be.argmax_rows(full.slice(1, 2, 1)))  # [rows, 1, n], row stride 3·n
+    got_dense = be.to_host(be.argmax_rows(be.from_host(np.ascontiguousarray(last))))
+    assert [int(v) for v in got_view] == expect
+    assert [int(v) for v in got_dense] == expect
+
+
 def test_generate_replays_a_graph_with_the_eager_tokens(monkeypatch):
     be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", 0)
     m = H.LlamaModel(be, H.ModelConfig(**GQA16), seed=4)
