@@ -7,7 +7,8 @@
 // of lo leave a relative error near 2^-21 per product, well inside the 1e-4 conformance tolerance.
 //
 // Pipeline:
-//   1. k_pack: reads the operand view once (any strides, batch offsets), splits hi/lo, and writes 128-row x 32-k
+//   1. k_pack: both operands in one launch (the smaller one's tiles first); reads each operand view once (any
+//      strides, batch offsets), splits hi/lo, and writes 128-row x 32-k
 //      tiles already in the tcgen05 K-major SWIZZLE_128B shared-memory layout, so the GEMM moves each tile with
 //      one plain bulk copy (cp.async.bulk) and no tensor map.
 //   2. k_gemm_tc: persistent kernel, one CTA per SM, warp-specialised:
@@ -141,10 +142,10 @@ struct PackDesc {
   int vec;                   // 1: 16-byte loads along the unit-stride axis are aligned and never straddle an edge
 };
 
-// grid (kt, rt_pad, batches); 256 threads. Writes one 128x32 hi tile and one lo tile.
-__global__ void __launch_bounds__(256) k_pack(const __grid_constant__ PackDesc d, float* __restrict__ hi, float* __restrict__ lo) {
+// One CTA (256 threads) writes one 128x32 hi tile and one lo tile: k tile kt, row tile rt, batch matrix b.
+__device__ __forceinline__ void pack_tile(const PackDesc& d, int kt, int rt, int b, float* __restrict__ hi,
+                                          float* __restrict__ lo) {
   __shared__ float tile[kBM][kBK + 1];
-  int kt = blockIdx.x, rt = blockIdx.y, b = blockIdx.z;
   int tid = threadIdx.x;
   const int64_t* boffs = d.batch_off ? d.batch_off : d.boff_inline;
   const float* src = d.src + boffs[b];
@@ -196,6 +197,28 @@ __global__ void __launch_bounds__(256) k_pack(const __grid_constant__ PackDesc d
     h4[phys] = make_float4(vh[0], vh[1], vh[2], vh[3]);
     l4[phys] = make_float4(vl[0], vl[1], vl[2], vl[3]);
   }
+}
+
+// Both operands of a product in one launch: CTAs [0, tiles0) pack operand 0, the rest operand 1, each walking its
+// (k tile, row tile, batch) space k tile fastest. The weight operand goes first, so its small pack overlaps the
+// activation's instead of paying a launch of its own.
+struct PackPair {
+  PackDesc d[2];
+  float* hi[2];
+  float* lo[2];
+  int64_t tiles0;
+};
+
+__global__ void __launch_bounds__(256) k_pack(const __grid_constant__ PackPair p) {
+  int64_t i = blockIdx.x;
+  const int o = i < p.tiles0 ? 0 : 1;
+  if (o) i -= p.tiles0;
+  const PackDesc& d = p.d[o];
+  const int kt = (int)(i % d.kt);
+  const int64_t rest = i / d.kt;
+  const int rt = (int)(rest % d.rt_pad);
+  const int b = (int)(rest / d.rt_pad);
+  pack_tile(d, kt, rt, b, p.hi[o], p.lo[o]);
 }
 
 // ---------------------------------------------------------------- tcgen05 GEMM
@@ -473,14 +496,15 @@ static pai_status launch_tc(pai_ctx* ctx, GemmArgs& g) {
 }
 
 // Packs one operand (batched 2-D view) into hi/lo tiles.
-static pai_status pack_operand(pai_ctx* ctx, const float* base, const std::vector<int64_t>& boffs, int64_t sr, int64_t sk,
-                               int rows, int k, int rt_pad, Scratch* hi, Scratch* lo) {
+// Allocates the packed hi/lo planes of one operand (batched 2-D view) and fills its pack descriptor; `doff` holds
+// the batch offsets when there are more than fit inline and must outlive the launch.
+static pai_status prepare_pack(pai_ctx* ctx, const float* base, const std::vector<int64_t>& boffs, int64_t sr, int64_t sk,
+                               int rows, int k, int rt_pad, Scratch* hi, Scratch* lo, Scratch* doff, PackDesc* out) {
   int kt = (k + kBK - 1) / kBK;
   size_t floats = (size_t)boffs.size() * kt * rt_pad * kTileFloats;
   PAI_TRY(scratch(ctx, floats * 4, hi));
   PAI_TRY(scratch(ctx, floats * 4, lo));
-  Scratch doff;
-  if (boffs.size() > (size_t)kInlineBatches) PAI_TRY(upload(ctx, boffs.data(), boffs.size() * 8, &doff));
+  if (boffs.size() > (size_t)kInlineBatches) PAI_TRY(upload(ctx, boffs.data(), boffs.size() * 8, doff));
   // 16-byte loads along the unit-stride axis: every batch matrix and row start 16-byte aligned, and the unit-stride
   // extent a multiple of 4 so a vector never crosses the edge.
   bool aligned = (reinterpret_cast<uintptr_t>(base) & 15) == 0;
@@ -490,12 +514,31 @@ static pai_status pack_operand(pai_ctx* ctx, const float* base, const std::vecto
   else if (aligned && sr == 1 && sk % 4 == 0 && rows % 4 == 0) vec = 1;
   PackDesc d{};
   d.src = base;
-  d.batch_off = static_cast<const int64_t*>(doff.p);
+  d.batch_off = static_cast<const int64_t*>(doff->p);
   if (!d.batch_off)
     for (size_t i = 0; i < boffs.size(); i++) d.boff_inline[i] = boffs[i];
   d.sr = sr; d.sk = sk; d.rows = rows; d.k = k; d.kt = kt; d.rt_pad = rt_pad; d.vec = vec;
-  dim3 grid((unsigned)kt, (unsigned)rt_pad, (unsigned)boffs.size());
-  k_pack<<<grid, 256, 0, ctx->stream>>>(d, static_cast<float*>(hi->p), static_cast<float*>(lo->p));
+  *out = d;
+  return PAI_OK;
+}
+
+// Packs both operands of a product with one launch (k_pack), the operand with fewer tiles first.
+static pai_status pack_operands(pai_ctx* ctx, const PackDesc& da, int batches_a, const Scratch& ahi, const Scratch& alo,
+                                const PackDesc& db, int batches_b, const Scratch& bhi, const Scratch& blo) {
+  const int64_t ta = (int64_t)da.kt * da.rt_pad * batches_a, tb = (int64_t)db.kt * db.rt_pad * batches_b;
+  const bool b_first = tb <= ta;
+  PackPair p{};
+  p.d[0] = b_first ? db : da;
+  p.d[1] = b_first ? da : db;
+  p.hi[0] = static_cast<float*>(b_first ? bhi.p : ahi.p);
+  p.lo[0] = static_cast<float*>(b_first ? blo.p : alo.p);
+  p.hi[1] = static_cast<float*>(b_first ? ahi.p : bhi.p);
+  p.lo[1] = static_cast<float*>(b_first ? alo.p : blo.p);
+  p.tiles0 = b_first ? tb : ta;
+  const int64_t total = ta + tb;
+  if (total <= 0) return PAI_OK;
+  if (total > INT32_MAX) return set_error(PAI_ERR_UNSUPPORTED, "MatMul: %lld operand tiles exceed one launch", (long long)total);
+  k_pack<<<(unsigned)total, 256, 0, ctx->stream>>>(p);
   PAI_LAUNCH_CHECK("gemm pack");
   return PAI_OK;
 }
@@ -627,8 +670,11 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   int tiles_n = (n + BN - 1) / BN;
   int nt_pad = tiles_n * (BN / kBM);
   Scratch ahi, alo, bhi, blo, dai, dbi, part;
-  PAI_TRY(pack_operand(ctx, abase, a_distinct, sam, sak, m, k, mt, &ahi, &alo));
-  PAI_TRY(pack_operand(ctx, bbase, b_distinct, sbn, sbk, n, k, nt_pad, &bhi, &blo));
+  Scratch aoff, boff;
+  PackDesc pda, pdb;
+  PAI_TRY(prepare_pack(ctx, abase, a_distinct, sam, sak, m, k, mt, &ahi, &alo, &aoff, &pda));
+  PAI_TRY(prepare_pack(ctx, bbase, b_distinct, sbn, sbk, n, k, nt_pad, &bhi, &blo, &boff, &pdb));
+  PAI_TRY(pack_operands(ctx, pda, (int)a_distinct.size(), ahi, alo, pdb, (int)b_distinct.size(), bhi, blo));
   if (batch > kInlineBatches) {
     PAI_TRY(upload(ctx, a_idx.data(), a_idx.size() * 4, &dai));
     PAI_TRY(upload(ctx, b_idx.data(), b_idx.size() * 4, &dbi));
