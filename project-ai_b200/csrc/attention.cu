@@ -180,6 +180,30 @@ __global__ void k_attn_dot(AttnDims a, V4 dout, const float* __restrict__ out, f
   if (lane == 0) dv[w] = acc;
 }
 
+// k_attn_dot for D % 4 == 0, D <= 64 and 16-byte aligned dout rows: a half-warp per row (lane l holds float4 l of
+// the row), 32-bit row decomposition, two rows per warp.
+__global__ void k_attn_dot4(AttnDims a, V4 dout, const float* __restrict__ out, float* __restrict__ dv) {
+  const int half = (threadIdx.x >> 4) & 1, l = threadIdx.x & 15;
+  const int64_t rows = (int64_t)a.B * a.H * a.S;
+  const int64_t w = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * 2 + half;
+  const bool live = w < rows;
+  float acc = 0.0f;
+  if (live && l < (a.D >> 2)) {
+    const uint32_t r = (uint32_t)w;
+    const uint32_t i = r % (uint32_t)a.S, bh = r / (uint32_t)a.S;
+    const uint32_t h = bh % (uint32_t)a.H, b = bh / (uint32_t)a.H;
+    const float4 g = *reinterpret_cast<const float4*>(dout.p + b * dout.s0 + i * dout.s1 + h * dout.s2 + 4 * l);
+    const float4 o = *reinterpret_cast<const float4*>(out + (((int64_t)b * a.S + i) * a.H + h) * a.D + 4 * l);
+    acc = fmaf(g.x, o.x, acc);
+    acc = fmaf(g.y, o.y, acc);
+    acc = fmaf(g.z, o.z, acc);
+    acc = fmaf(g.w, o.w, acc);
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (live && l == 0) dv[w] = acc;
+}
+
 // dK, dV for one 64-key tile of one KV head, summed over the GQA group and all query tiles that see it.
 __global__ void __launch_bounds__(256) k_attn_bwd_kv(AttnDims a, V4 q, V4 k, V4 v, V4 dout, const float* __restrict__ lse,
                                                      const float* __restrict__ dvec, float* __restrict__ dk,
@@ -446,7 +470,14 @@ PAI_API pai_status pai_sdpa_bwd(pai_ctx* ctx, const pai_tensor* q, const pai_ten
     int64_t rows = (int64_t)a.B * a.H * a.S;
     PAI_TRY(scratch(ctx, (size_t)rows * 4, &dvec));
     KernelTimerScope timer(ctx, "attn_bwd", 2.5 * attn_fwd_flops(a));
-    k_attn_dot<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, ctx->stream>>>(a, v4(*dout), fptr(*out), static_cast<float*>(dvec.p));
+    const V4 dov = v4(*dout);
+    const bool dot4 = a.D % 4 == 0 && a.D <= 64 && dov.s3 == 1 && (reinterpret_cast<uintptr_t>(dov.p) % 16 == 0) &&
+                      dov.s0 % 4 == 0 && dov.s1 % 4 == 0 && dov.s2 % 4 == 0 && (reinterpret_cast<uintptr_t>(fptr(*out)) % 16 == 0) &&
+                      rows < (1ll << 31);
+    if (dot4)
+      k_attn_dot4<<<(unsigned)((rows * 16 + 255) / 256), 256, 0, ctx->stream>>>(a, dov, fptr(*out), static_cast<float*>(dvec.p));
+    else
+      k_attn_dot<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, ctx->stream>>>(a, dov, fptr(*out), static_cast<float*>(dvec.p));
     PAI_LAUNCH_CHECK("sdpa_bwd dot");
     if (!attn_force_simt()) {
       PAI_TRY(attn_tc_bwd(ctx, *q, *k, *v, *dout, fptr(*lse), static_cast<float*>(dvec.p), a.B, a.H, a.KVH, a.S, a.L, a.D,

@@ -189,6 +189,30 @@ __global__ void __launch_bounds__(256) k_rmsnorm_bwd_reg(const float* __restrict
   }
 }
 
+// Deterministic column sum of [parts, d] partials with more loads in flight: a CTA takes 32 columns, its 8 warps each
+// add a contiguous slice of the parts in order, and the 8 slice sums are added in slice order. Launch: (d + 31) / 32
+// CTAs of 256 threads.
+__global__ void __launch_bounds__(256) k_colsum_sliced(const float* __restrict__ part, float* __restrict__ out, int parts,
+                                                       int d) {
+  __shared__ float s[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int j = blockIdx.x * 32 + lane;
+  const int per = (parts + 7) / 8;
+  const int p0 = w * per, p1 = min(parts, p0 + per);
+  float acc = 0.0f;
+  if (j < d) {
+#pragma unroll 4
+    for (int p = p0; p < p1; p++) acc += part[(size_t)p * d + j];
+  }
+  s[w][lane] = acc;
+  __syncthreads();
+  if (w == 0 && j < d) {
+    float t = s[0][lane];
+    for (int k = 1; k < 8; k++) t += s[k][lane];
+    out[j] = t;
+  }
+}
+
 // Deterministic column sum of [parts, d] partials.
 __global__ void k_colsum(const float* __restrict__ part, float* __restrict__ out, int parts, int d) {
   int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -436,7 +460,7 @@ PAI_API pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_
       }
 #undef RMS_REG
       PAI_LAUNCH_CHECK("rmsnorm_bwd");
-      k_colsum<<<(d + 255) / 256, 256, 0, ctx->stream>>>(pp, fptr(rdw), blocks, d);
+      k_colsum_sliced<<<(d + 31) / 32, 256, 0, ctx->stream>>>(pp, fptr(rdw), blocks, d);
       PAI_LAUNCH_CHECK("rmsnorm_bwd colsum");
       *dx = rdx;
       *dw = rdw;
@@ -454,7 +478,7 @@ PAI_API pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_
     if (smem > 48 * 1024) cudaFuncSetAttribute(k_rmsnorm_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_rmsnorm_bwd<<<blocks, threads, smem, ctx->stream>>>(xp, wp, gp, fptr(rdx), static_cast<float*>(part.p), rows, d, eps, rpb);
     PAI_LAUNCH_CHECK("rmsnorm_bwd");
-    k_colsum<<<(d + 255) / 256, 256, 0, ctx->stream>>>(static_cast<float*>(part.p), fptr(rdw), blocks, d);
+    k_colsum_sliced<<<(d + 31) / 32, 256, 0, ctx->stream>>>(static_cast<float*>(part.p), fptr(rdw), blocks, d);
     PAI_LAUNCH_CHECK("rmsnorm_bwd colsum");
   }
   *dx = rdx;
