@@ -4,7 +4,8 @@
 // scores = (q·scale)·kᵀ with q rounded to fp32 after scaling, keys j <= pos_offset + i, online softmax, ·v, output in
 // the merged-heads layout [B,S,H,D] plus the row log-sum-exp for the backward.
 //
-// Per CTA: 128 queries of one (batch, head), key blocks of 64, head dim padded to 64.
+// Per work item: 128 queries of one (batch, head), key blocks of 64, head dim padded to 64; one persistent CTA per SM
+// walks its items.
 //   pre-pass k_attn_pack: q·scale, k and vᵀ split into tf32 hi/lo and written as SWIZZLE_128B K-major tiles;
 //   warp 0      bulk-copies the Q tile once and K/Vᵀ blocks into a 2-stage ring;
 //   warp 1      allocates TMEM and issues S = Q·Kᵀ (3 MMAs per k-step, M=128 N=64) into a double-buffered TMEM S,
@@ -122,6 +123,44 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// One work item: a 128-query tile of one (batch, head).
+struct FwdItem {
+  int qt, h, b, kvh, q0, nblk;
+};
+
+// Item t in longest-first order (the query tile slowest and reversed, then head, then batch); false when the tile
+// sees no key.
+__device__ __forceinline__ bool fwd_item(const AttnTcArgs& a, int t, FwdItem& it) {
+  const int hb = a.H * a.B;
+  it.qt = a.q_tiles - 1 - t / hb;
+  const int rem = t % hb;
+  it.h = rem % a.H;
+  it.b = rem / a.H;
+  it.kvh = it.h / (a.H / a.KVH);
+  it.q0 = it.qt * kQT;
+  int kend = a.L;
+  if (a.causal) kend = min(a.L, a.pos_offset + it.q0 + kQT);
+  it.nblk = kend > 0 ? (kend + kKB - 1) / kKB : 0;
+  return it.nblk > 0;
+}
+
+// This CTA's next item from round r on: rounds are bands of gridDim.x consecutive items, walked forward in even
+// rounds and backward in odd ones (CTA c takes band position c, then gridDim.x - 1 - c), so a CTA that drew a long
+// tile in one band draws a short one in the next. Returns false when the CTA has no further item; r is left at the
+// round of the item returned.
+__device__ __forceinline__ bool next_fwd_item(const AttnTcArgs& a, int n_items, int& r, FwdItem& it) {
+  const int G = gridDim.x, c = blockIdx.x;
+  for (; r * G < n_items; r++) {
+    const int t = r * G + ((r & 1) ? G - 1 - c : c);
+    if (t < n_items && fwd_item(a, t, it)) return true;
+  }
+  return false;
+}
+
+// Persistent: one CTA per SM walks its items (next_fwd_item). Barrier phases, ring slots and TMEM slots follow a
+// running block counter J over the CTA's items, so a tile's last blocks and the next tile's first loads overlap: the
+// next K block is fetched while this tile finishes, and the next Q tile as soon as this tile's last S product has
+// read Q (q_empty).
 __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -130,7 +169,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
   uint8_t* sV = sK + kKStages * kKBytes;        // [kVStages] Vᵀ hi/lo blocks
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVStages * kKBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;                     // [kKStages]
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;                     // [kKStages]
   uint64_t* k_empty = k_full + kKStages;           // [kKStages]
   uint64_t* v_full = k_empty + kKStages;           // [kVStages]
   uint64_t* v_empty = v_full + kVStages;           // [kVStages]
@@ -144,18 +184,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
   __shared__ float s_l[2][kQT];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the query tile is the slowest grid index, in reverse: CTAs start in launch order, so every head's longest causal
-  // tile runs in the first wave and the short tiles fill in behind them
-  const int qt = a.q_tiles - 1 - (int)blockIdx.z;
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int kvh = h / (a.H / a.KVH);
-  const int q0 = qt * kQT;
-  int kend = a.L;
-  if (a.causal) kend = min(a.L, a.pos_offset + q0 + kQT);
-  const int nblk = kend > 0 ? (kend + kKB - 1) / kKB : 0;
+  const int n_items = a.q_tiles * a.H * a.B;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < kKStages; i++) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -182,41 +215,65 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0 && nblk > 0) {
-      const float* qsrc = a.qp + ((size_t)(b * a.H + h) * a.q_tiles + qt) * (kQBytes / 4);
-      mbar_expect_tx(q_full, kQBytes);
-      bulk_g2s(sQ, qsrc, kQBytes, q_full);
-      const size_t head_off = (size_t)(b * a.KVH + kvh) * a.k_blocks;
-      // loads in the order the MMA warp consumes them: K0, then per block K_{j+1} before Vᵀ_j
-      auto load_k = [&](int j) {
-        int st = j % kKStages;
-        if (!mbar_wait(&k_empty[st], ((j / kKStages) & 1) ^ 1)) return false;
+    if (lane == 0) {
+      // loads in the order the MMA warp consumes them: K of the first block, then per block the next block's K
+      // (possibly the next tile's first) before this block's Vᵀ; each tile's Q once the previous tile's S products
+      // are done with the Q buffer
+      auto load_k = [&](int J, const FwdItem& it, int j) {
+        const int st = J % kKStages;
+        if (!mbar_wait(&k_empty[st], ((J / kKStages) & 1) ^ 1)) return false;
+        const size_t head_off = (size_t)(it.b * a.KVH + it.kvh) * a.k_blocks;
         mbar_expect_tx(&k_full[st], kKBytes);
         bulk_g2s(sK + st * kKBytes, a.kp + (head_off + j) * (kKBytes / 4), kKBytes, &k_full[st]);
         return true;
       };
-      auto load_v = [&](int j) {
-        int st = j % kVStages;
-        if (!mbar_wait(&v_empty[st], ((j / kVStages) & 1) ^ 1)) return false;
+      auto load_v = [&](int J, const FwdItem& it, int j) {
+        const int st = J % kVStages;
+        if (!mbar_wait(&v_empty[st], ((J / kVStages) & 1) ^ 1)) return false;
+        const size_t head_off = (size_t)(it.b * a.KVH + it.kvh) * a.k_blocks;
         mbar_expect_tx(&v_full[st], kKBytes);
         bulk_g2s(sV + st * kKBytes, a.vp + (head_off + j) * (kKBytes / 4), kKBytes, &v_full[st]);
         return true;
       };
-      if (!load_k(0)) { atomicExch(a.error_flag, 11); s_abort = 1; }
-      for (int j = 0; j < nblk && !s_abort; j++) {
-        if ((j + 1 < nblk && !load_k(j + 1)) || !load_v(j)) { atomicExch(a.error_flag, 11); s_abort = 1; break; }
+      int r = 0, J0 = 0, ord = 0;
+      FwdItem cur;
+      bool have = next_fwd_item(a, n_items, r, cur);
+      bool ok = !have || load_k(0, cur, 0);
+      while (have && ok && !s_abort) {
+        if (ord > 0 && !mbar_wait(q_empty, (ord - 1) & 1)) { ok = false; break; }
+        mbar_expect_tx(q_full, kQBytes);
+        bulk_g2s(sQ, a.qp + ((size_t)(cur.b * a.H + cur.h) * a.q_tiles + cur.qt) * (kQBytes / 4), kQBytes, q_full);
+        int rn = r + 1;
+        FwdItem nxt;
+        const bool have_next = next_fwd_item(a, n_items, rn, nxt);
+        for (int j = 0; j < cur.nblk && ok && !s_abort; j++) {
+          const int J = J0 + j;
+          if (j + 1 < cur.nblk) ok = load_k(J + 1, cur, j + 1);
+          else if (have_next) ok = load_k(J + 1, nxt, 0);
+          if (ok) ok = load_v(J, cur, j);
+        }
+        J0 += cur.nblk;
+        ord++;
+        cur = nxt;
+        r = rn;
+        have = have_next;
       }
+      if (!ok) { atomicExch(a.error_flag, 11); s_abort = 1; }
       // drain: every issued load must land (and be consumed) before the CTA exits
-      for (int j = nblk; j < nblk + kKStages; j++) mbar_wait(&k_empty[j % kKStages], ((j / kKStages) & 1) ^ 1);
-      for (int j = nblk; j < nblk + kVStages; j++) mbar_wait(&v_empty[j % kVStages], ((j / kVStages) & 1) ^ 1);
+      for (int J = J0; J < J0 + kKStages; J++) mbar_wait(&k_empty[J % kKStages], ((J / kKStages) & 1) ^ 1);
+      for (int J = J0; J < J0 + kVStages; J++) mbar_wait(&v_empty[J % kVStages], ((J / kVStages) & 1) ^ 1);
     }
   } else if (warp == 1) {
-    if (lane == 0 && nblk > 0) {
+    if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(128, 64);
       const uint32_t q_hi = smem_u32(sQ), q_lo = q_hi + kQBytes / 2;
-      auto issue_s = [&](int j) {
-        int st = j & 1;
-        uint32_t k_hi = smem_u32(sK + (j % kKStages) * kKBytes), k_lo = k_hi + kKBytes / 2;
+      // S_J = Q·K_Jᵀ into S slot J & 1, once K_J has landed and the softmax warps have read S_{J-2} from that slot
+      auto wait_s = [&](int J) {
+        return mbar_wait(&k_full[J % kKStages], (J / kKStages) & 1) && mbar_wait(&s_free[J & 1], ((J >> 1) & 1) ^ 1);
+      };
+      auto issue_s = [&](int J) {
+        const int st = J & 1;
+        uint32_t k_hi = smem_u32(sK + (J % kKStages) * kKBytes), k_lo = k_hi + kKBytes / 2;
         uint32_t d = tmem + (st ? kColS1 : kColS0);
 #pragma unroll
         for (int ks = 0; ks < kDP / 8; ks++) {
@@ -227,42 +284,46 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
           mma_ss(d, desc_sw128(q_hi + qo), desc_sw128(k_hi + ko), idesc, 1u);
         }
         commit(&s_full[st]);
-        commit(&k_empty[j % kKStages]);  // the K block is free once these MMAs have read it
+        commit(&k_empty[J % kKStages]);  // the K block is free once these MMAs have read it
       };
-      bool ok = mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
-      if (!ok) { atomicExch(a.error_flag, 12); s_abort = 1; }
-      if (ok) {
+      int r = 0, J0 = 0, ord = 0;
+      FwdItem it;
+      bool ok = true;
+      while (ok && !s_abort && next_fwd_item(a, n_items, r, it)) {
+        if (!mbar_wait(q_full, ord & 1) || !wait_s(J0)) { atomicExch(a.error_flag, 12); s_abort = 1; break; }
         fence_after();
-        issue_s(0);
-      }
-      for (int j = 0; j < nblk && ok && !s_abort; j++) {
-        if (j + 1 < nblk) {
-          int st = (j + 1) & 1;
-          if (!mbar_wait(&k_full[(j + 1) % kKStages], ((j + 1) / kKStages) & 1) ||
-              !mbar_wait(&s_free[st], (((j + 1) >> 1) & 1) ^ 1)) {
-            atomicExch(a.error_flag, 13); s_abort = 1; break;
+        issue_s(J0);
+        if (it.nblk == 1) commit(q_empty);  // this tile's S products are all issued: Q may be replaced after them
+        for (int j = 0; j < it.nblk; j++) {
+          const int J = J0 + j;
+          if (j + 1 < it.nblk) {
+            if (!wait_s(J + 1)) { atomicExch(a.error_flag, 13); s_abort = 1; ok = false; break; }
+            fence_after();
+            issue_s(J + 1);
+            if (j + 2 == it.nblk) commit(q_empty);
+          }
+          const int ps = J & 1;  // P / P·V slot of this block
+          const int vs = J % kVStages;
+          if (!mbar_wait(&p_full[ps], (J >> 1) & 1) || !mbar_wait(&v_full[vs], (J / kVStages) & 1)) {
+            atomicExch(a.error_flag, 14); s_abort = 1; ok = false; break;
           }
           fence_after();
-          issue_s(j + 1);
-        }
-        const int ps = j & 1;  // P / P·V slot of this block
-        const int vs = j % kVStages;
-        if (!mbar_wait(&p_full[ps], (j >> 1) & 1) || !mbar_wait(&v_full[vs], (j / kVStages) & 1)) {
-          atomicExch(a.error_flag, 14); s_abort = 1; break;
-        }
-        fence_after();
-        uint32_t v_hi = smem_u32(sV + vs * kKBytes), v_lo = v_hi + kKBytes / 2;
-        uint32_t d = tmem + col_pv(ps);
+          uint32_t v_hi = smem_u32(sV + vs * kKBytes), v_lo = v_hi + kKBytes / 2;
+          uint32_t d = tmem + col_pv(ps);
 #pragma unroll
-        for (int ks = 0; ks < kKB / 8; ks++) {
-          uint32_t vo = (ks >> 2) * (kDP * 128) + (ks & 3) * 32;  // Vᵀ kb (32 keys) stride 8 KB
-          uint32_t pc = (uint32_t)(ks * 8);
-          mma_ts(d, tmem + col_plo(ps) + pc, desc_sw128(v_hi + vo), idesc, ks > 0 ? 1u : 0u);
-          mma_ts(d, tmem + col_phi(ps) + pc, desc_sw128(v_lo + vo), idesc, 1u);
-          mma_ts(d, tmem + col_phi(ps) + pc, desc_sw128(v_hi + vo), idesc, 1u);
+          for (int ks = 0; ks < kKB / 8; ks++) {
+            uint32_t vo = (ks >> 2) * (kDP * 128) + (ks & 3) * 32;  // Vᵀ kb (32 keys) stride 8 KB
+            uint32_t pc = (uint32_t)(ks * 8);
+            mma_ts(d, tmem + col_plo(ps) + pc, desc_sw128(v_hi + vo), idesc, ks > 0 ? 1u : 0u);
+            mma_ts(d, tmem + col_phi(ps) + pc, desc_sw128(v_lo + vo), idesc, 1u);
+            mma_ts(d, tmem + col_phi(ps) + pc, desc_sw128(v_hi + vo), idesc, 1u);
+          }
+          commit(&pv_full[ps]);
+          commit(&v_empty[vs]);
         }
-        commit(&pv_full[ps]);
-        commit(&v_empty[vs]);
+        J0 += it.nblk;
+        ord++;
+        r++;
       }
     }
   } else {
@@ -271,120 +332,129 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
     const int quad = warp & 3;
     const int half = sw >> 2;
     const int row = quad * 32 + lane;
-    const int qi = q0 + row;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t col = (uint32_t)(32 * half);
     const float kLog2e = 1.4426950408889634f;
-    float o[32];
+    // After a timed-out wait `ok` turns false for good: the warp skips all further TMEM and barrier work but still
+    // reaches every named barrier, so its partner warp never waits on it.
+    bool ok = true;
+    int r = 0, J0 = 0;
+    FwdItem it;
+    while (next_fwd_item(a, n_items, r, it)) {
+      const int q0 = it.q0, nblk = it.nblk;
+      const int qi = q0 + row;
+      float o[32];
 #pragma unroll
-    for (int d = 0; d < 32; d++) o[d] = 0.0f;
-    float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
-    // After a timed-out wait `ok` turns false: the warp skips all further TMEM and barrier work but still reaches
-    // every named barrier, so its partner warp never waits on it.
-    bool ok = nblk > 0;
-    for (int j = 0; j < nblk; j++) {
-      int st = j & 1;
-      float s[32];
+      for (int d = 0; d < 32; d++) o[d] = 0.0f;
+      float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
+      for (int j = 0; j < nblk; j++) {
+        const int J = J0 + j;
+        const int st = J & 1;
+        float s[32];
 #pragma unroll
-      for (int c = 0; c < 32; c++) s[c] = 0.0f;
-      if (ok && !warp_wait(&s_full[st], (j >> 1) & 1)) ok = false;
-      if (ok) {
-        fence_after();
-        tmem_ld32(tmem + lane_off + (st ? kColS1 : kColS0) + col, s);
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[st]);
-      }
-      const int k0 = j * kKB;
-      // Masking is needed only where the block crosses the causal diagonal or the end of the keys.
-      const bool need_mask = (k0 + kKB > a.L) || (a.causal && k0 + kKB - 1 > a.pos_offset + q0);
-      float mx = -INFINITY;
-      if (need_mask) {
+        for (int c = 0; c < 32; c++) s[c] = 0.0f;
+        if (ok && !warp_wait(&s_full[st], (J >> 1) & 1)) ok = false;
+        if (ok) {
+          fence_after();
+          tmem_ld32(tmem + lane_off + (st ? kColS1 : kColS0) + col, s);
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[st]);
+        }
+        const int k0 = j * kKB;
+        // Masking is needed only where the block crosses the causal diagonal or the end of the keys.
+        const bool need_mask = (k0 + kKB > a.L) || (a.causal && k0 + kKB - 1 > a.pos_offset + q0);
+        float mx = -INFINITY;
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < 32; c++) {
+            int kj = k0 + (int)col + c;
+            bool vis = kj < a.L && (!a.causal || kj <= a.pos_offset + qi);
+            if (!vis) s[c] = -INFINITY;
+            mx = fmaxf(mx, s[c]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; c++) mx = fmaxf(mx, s[c]);
+        }
+        // The row max over both halves: exchange through shared memory with the partner warp of this quadrant.
+        s_max[st][half][row] = mx;
+        named_sync(1 + quad, 64);
+        mx = fmaxf(mx, s_max[st][half ^ 1][row]);
+        float mn = fmaxf(m, mx);
+        float alpha = (m == -INFINITY) ? 0.0f : __expf(m - mn);
+        if (mn == -INFINITY) alpha = 1.0f;
+        const float mn2 = mn * kLog2e;
+        float sum = 0.0f;
 #pragma unroll
         for (int c = 0; c < 32; c++) {
-          int kj = k0 + (int)col + c;
-          bool vis = kj < a.L && (!a.causal || kj <= a.pos_offset + qi);
-          if (!vis) s[c] = -INFINITY;
-          mx = fmaxf(mx, s[c]);
+          float p = (s[c] == -INFINITY) ? 0.0f : exp2f(fmaf(s[c], kLog2e, -mn2));
+          s[c] = p;
+          sum += p;
         }
-      } else {
+        l = l * alpha + sum;
+        m = mn;
+        // o holds the blocks up to j-3 in units of the running max. P_{j-2}·V_{j-2} (units of m_{j-2}) sits in this
+        // block's slot: fold it in (factor exp(m_{j-2} - m_j) = alpha_{j-1}·alpha_j) before P_j takes the slot.
+        const int ps = J & 1;
 #pragma unroll
-        for (int c = 0; c < 32; c++) mx = fmaxf(mx, s[c]);
+        for (int d = 0; d < 32; d++) o[d] *= alpha;
+        if (ok && j >= 2) {
+          if (!warp_wait(&pv_full[ps], ((J - 2) >> 1) & 1)) {
+            ok = false;
+          } else {
+            fence_after();
+            float pv[32];
+            tmem_ld32(tmem + lane_off + col_pv(ps) + col, pv);
+            const float f = alpha_prev * alpha;
+#pragma unroll
+            for (int d = 0; d < 32; d++) o[d] = fmaf(pv[d], f, o[d]);
+          }
+        }
+        alpha_prev = alpha;
+        if (ok) {
+          // P_j -> TMEM as hi/lo (the A operand of P·V)
+          float hi[32], lo[32];
+#pragma unroll
+          for (int c = 0; c < 32; c++) split_tf32_fast(s[c], hi[c], lo[c]);
+          tmem_st32(tmem + lane_off + col_phi(ps) + col, hi);
+          tmem_st32(tmem + lane_off + col_plo(ps) + col, lo);
+          tmem_st_wait();
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[ps]);
+        }
       }
-      // The row max over both halves: exchange through shared memory with the partner warp of this quadrant.
-      s_max[st][half][row] = mx;
-      named_sync(1 + quad, 64);
-      mx = fmaxf(mx, s_max[st][half ^ 1][row]);
-      float mn = fmaxf(m, mx);
-      float alpha = (m == -INFINITY) ? 0.0f : __expf(m - mn);
-      if (mn == -INFINITY) alpha = 1.0f;
-      const float mn2 = mn * kLog2e;
-      float sum = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 32; c++) {
-        float p = (s[c] == -INFINITY) ? 0.0f : exp2f(fmaf(s[c], kLog2e, -mn2));
-        s[c] = p;
-        sum += p;
-      }
-      l = l * alpha + sum;
-      m = mn;
-      // o holds the blocks up to j-3 in units of the running max. P_{j-2}·V_{j-2} (units of m_{j-2}) sits in this
-      // block's slot: fold it in (factor exp(m_{j-2} - m_j) = alpha_{j-1}·alpha_j) before P_j takes the slot.
-      const int ps = j & 1;
-#pragma unroll
-      for (int d = 0; d < 32; d++) o[d] *= alpha;
-      if (ok && j >= 2) {
-        if (!warp_wait(&pv_full[ps], ((j - 2) >> 1) & 1)) {
+      // the last two blocks' P·V products: P_{n-2}·V_{n-2} (units of m_{n-2}: factor alpha_{n-1}) and P_{n-1}·V_{n-1}
+      for (int jj = (nblk >= 2 ? nblk - 2 : 0); ok && jj < nblk; jj++) {
+        const int Jj = J0 + jj;
+        const int ps = Jj & 1;
+        if (!warp_wait(&pv_full[ps], (Jj >> 1) & 1)) {
           ok = false;
-        } else {
-          fence_after();
-          float pv[32];
-          tmem_ld32(tmem + lane_off + col_pv(ps) + col, pv);
-          const float f = alpha_prev * alpha;
-#pragma unroll
-          for (int d = 0; d < 32; d++) o[d] = fmaf(pv[d], f, o[d]);
+          break;
         }
-      }
-      alpha_prev = alpha;
-      if (ok) {
-        // P_j -> TMEM as hi/lo (the A operand of P·V)
-        float hi[32], lo[32];
+        fence_after();
+        float pv[32];
+        tmem_ld32(tmem + lane_off + col_pv(ps) + col, pv);
+        const float f = (jj == nblk - 1) ? 1.0f : alpha_prev;
 #pragma unroll
-        for (int c = 0; c < 32; c++) split_tf32_fast(s[c], hi[c], lo[c]);
-        tmem_st32(tmem + lane_off + col_phi(ps) + col, hi);
-        tmem_st32(tmem + lane_off + col_plo(ps) + col, lo);
-        tmem_st_wait();
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[ps]);
+        for (int d = 0; d < 32; d++) o[d] = fmaf(pv[d], f, o[d]);
       }
-    }
-    // the last two blocks' P·V products: P_{J-1}·V_{J-1} (units of m_{J-1}: factor alpha_J) and P_J·V_J (units of m_J)
-    for (int jj = (nblk >= 2 ? nblk - 2 : 0); ok && jj < nblk; jj++) {
-      const int ps = jj & 1;
-      if (!warp_wait(&pv_full[ps], (jj >> 1) & 1)) {
-        ok = false;
-        break;
+      s_l[half][row] = l;
+      named_sync(1 + quad, 64);
+      float lt = s_l[0][row] + s_l[1][row];
+      if (ok && qi < a.S) {
+        float inv = 1.0f / lt;
+        float* orow = a.out + (((int64_t)it.b * a.S + qi) * a.H + it.h) * a.D;
+#pragma unroll
+        for (int d = 0; d < 32; d++)
+          if ((int)col + d < a.D) orow[col + d] = o[d] * inv;
+        if (half == 0) a.lse[((int64_t)it.b * a.H + it.h) * a.S + qi] = m + logf(lt);
       }
-      fence_after();
-      float pv[32];
-      tmem_ld32(tmem + lane_off + col_pv(ps) + col, pv);
-      const float f = (jj == nblk - 1) ? 1.0f : alpha_prev;
-#pragma unroll
-      for (int d = 0; d < 32; d++) o[d] = fmaf(pv[d], f, o[d]);
+      J0 += nblk;
+      r++;
     }
-    s_l[half][row] = l;
-    named_sync(1 + quad, 64);
-    float lt = s_l[0][row] + s_l[1][row];
-    if (ok && nblk > 0 && qi < a.S) {
-      float inv = 1.0f / lt;
-      float* orow = a.out + (((int64_t)b * a.S + qi) * a.H + h) * a.D;
-#pragma unroll
-      for (int d = 0; d < 32; d++)
-        if ((int)col + d < a.D) orow[col + d] = o[d] * inv;
-      if (half == 0) a.lse[((int64_t)b * a.H + h) * a.S + qi] = m + logf(lt);
-    }
-    if (!ok && nblk > 0 && lane == 0) { atomicExch(a.error_flag, 15); s_abort = 1; }
+    if (!ok && lane == 0) { atomicExch(a.error_flag, 15); s_abort = 1; }
   }
   fence_before();
   __syncthreads();
@@ -424,8 +494,9 @@ pai_status attn_tc_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   }
   AttnTcArgs args{static_cast<float*>(qp.p), static_cast<float*>(kp.p), static_cast<float*>(vp.p), out, lse,
                   B, H, KVH, S, L, D, pos_offset, causal, q_tiles, k_blocks, ctx->d_error_flag};
-  dim3 grid((unsigned)H, (unsigned)B, (unsigned)q_tiles);
-  k_attn_fwd_tc<<<grid, kFwdThreads, kFwdSmemBytes, ctx->stream>>>(args);
+  const int n_items = q_tiles * H * B;
+  const int grid = n_items < ctx->sm_count ? n_items : ctx->sm_count;  // persistent: one CTA per SM
+  if (grid > 0) k_attn_fwd_tc<<<grid, kFwdThreads, kFwdSmemBytes, ctx->stream>>>(args);
   PAI_LAUNCH_CHECK("attention fwd (tcgen05)");
   return PAI_OK;
 }
