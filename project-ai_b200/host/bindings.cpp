@@ -78,7 +78,8 @@ PYBIND11_MODULE(_paihost, m) {
       .def_property_readonly("grad_fn", [](const Tensor& t) { return t->grad_fn ? py::cast(t->grad_fn->op) : py::none(); })
       .def("numel", [](const Tensor& t) { return t->numel(); })
       .def("is_contiguous", [](const Tensor& t) { return t->is_contiguous(); })
-      .def("backward", [](const Tensor& t) { t->backward(); })
+      .def("backward", [](const Tensor& t, const Tensor& seed) { if (seed) t->backward(seed); else t->backward(); },
+           py::arg("seed") = Tensor())
       .def("reshape", [](const Tensor& t, const py::sequence& d) { return t->reshape(to_dims(d)); })
       .def("transpose", [](const Tensor& t, int a, int b) { return t->transpose(a, b); })
       .def("permute", [](const Tensor& t, std::vector<int> p) { return t->permute(p); })

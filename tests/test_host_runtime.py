@@ -149,6 +149,44 @@ def param_grads(be, model, ids, targets, checkpoint):
     return {n: be.to_host(p.grad).copy() for n, p in model.named_parameters()}
 
 
+def test_seeded_backward_equals_the_checkpoint_surrogate(be):
+    """Autograd.Checkpoint seeds the recomputed segment's backward through Σ(recomputed ⊙ upstream)
+    (Autograd.cs:143-144); the host runtime runs the walk from upstream directly. The leaf gradients agree bit for bit."""
+    ag = H.Autograd(be)
+    rs = np.random.RandomState(3)
+    xs = rs.standard_normal((4, 6)).astype(np.float32)
+    ws = rs.standard_normal((5, 6)).astype(np.float32)
+    up = rs.standard_normal((4, 5)).astype(np.float32)
+
+    def grads(seeded):
+        x, w = be.from_host(xs), be.from_host(ws)
+        x.requires_grad = w.requires_grad = True
+        y = ag.silu(ag.matmul(x, w, True))
+        u = be.from_host(up)
+        if seeded:
+            y.backward(u)
+        else:
+            ag.sum_all(ag.mul(y, u)).backward()
+        return be.to_host(x.grad), be.to_host(w.grad)
+
+    (sx, sw), (rx, rw) = grads(True), grads(False)
+    assert np.array_equal(sx, rx) and np.array_equal(sw, rw)
+
+
+def test_rope_on_the_sequence_major_layout_equals_the_head_major_rope(be):
+    """RoPE on [b, s, heads, dh] with the tables broadcast over heads ([s, 1, dh]) gives, element for element, the
+    values RotaryEmbedding gives on the head-major view [b, heads, s, dh] (RotaryEmbedding, Modules.cs:43-60)."""
+    b, s, h, d = 2, 5, 3, 8
+    rs = np.random.RandomState(4)
+    x = rs.standard_normal((b, s, h, d)).astype(np.float32)
+    cos = rs.standard_normal((s, d)).astype(np.float32)
+    sin = rs.standard_normal((s, d)).astype(np.float32)
+    tx = be.from_host(x)
+    head_major = be.to_host(be.rotary(tx.transpose(1, 2), be.from_host(cos), be.from_host(sin)))
+    seq_major = be.to_host(be.rotary(tx, be.from_host(cos.reshape(s, 1, d)), be.from_host(sin.reshape(s, 1, d))))
+    assert np.array_equal(np.swapaxes(head_major, 1, 2), seq_major)
+
+
 def test_checkpointed_gradients_match_standard(be):
     model = H.LlamaModel(be, small_config(), seed=0)
     ids = (np.arange(12) % 16).astype(np.float32).reshape(2, 6)
