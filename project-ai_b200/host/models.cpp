@@ -1,10 +1,15 @@
 // PcgRng and Init (ProjectAI.Core/Rng.cs, Init.cs), Module (Module.cs), the Llama modules (ProjectAI.Models/Modules.cs,
 // Linear.cs, Embedding.cs, Loss.cs), the KV cache (Modules.cs:290-370) and the samplers (Sampling.cs).
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <condition_variable>
+#include <functional>
 #include <mutex>
 #include <numeric>
 #include <thread>
+
+#include <unistd.h>
 
 #include "runtime.h"
 
@@ -468,26 +473,98 @@ int TopKTopPSampler::sample(const float* logits, int vocab) {
   return draw(p);
 }
 
+// Process-wide worker threads for per-row host work, started once (decode samples every step, and starting threads
+// per step cost about as much as the work): run(n, fn) calls fn(i) for every i in [0, n) on the workers and the
+// calling thread and returns when all are done, rethrowing the first exception. One job runs at a time. The workers
+// are detached and never stopped, so process exit does not wait for them. A forked child has none of its parent's
+// threads, so a process that is not the pool's owner starts its own pool.
+namespace {
+class RowPool {
+ public:
+  static RowPool& instance() {
+    static std::mutex m;
+    static RowPool* pool = nullptr;
+    static pid_t owner = 0;
+    std::lock_guard<std::mutex> g(m);
+    if (!pool || owner != getpid()) {
+      pool = new RowPool((int)std::max(1u, std::thread::hardware_concurrency()) - 1);
+      owner = getpid();
+    }
+    return *pool;
+  }
+
+  void run(int n, const std::function<void(int)>& fn) {
+    std::lock_guard<std::mutex> job(job_mu_);
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      fn_ = &fn;
+      n_ = n;
+      next_.store(0);
+      done_ = 0;
+      err_ = nullptr;
+      gen_++;
+    }
+    cv_.notify_all();
+    work();
+    std::unique_lock<std::mutex> g(mu_);
+    done_cv_.wait(g, [&] { return done_ == workers_; });  // every worker has finished this job
+    fn_ = nullptr;
+    if (err_) std::rethrow_exception(err_);
+  }
+
+ private:
+  explicit RowPool(int workers) : workers_(workers) {
+    for (int i = 0; i < workers; i++) std::thread([this] { loop(); }).detach();
+  }
+
+  void loop() {
+    uint64_t seen = 0;
+    for (;;) {
+      {
+        std::unique_lock<std::mutex> g(mu_);
+        cv_.wait(g, [&] { return gen_ != seen; });
+        seen = gen_;
+      }
+      work();
+      {
+        std::lock_guard<std::mutex> g(mu_);
+        done_++;
+      }
+      done_cv_.notify_one();
+    }
+  }
+
+  void work() {
+    for (int i = next_.fetch_add(1); i < n_; i = next_.fetch_add(1)) {
+      try {
+        (*fn_)(i);
+      } catch (...) {
+        std::lock_guard<std::mutex> g(mu_);
+        if (!err_) err_ = std::current_exception();
+      }
+    }
+  }
+
+  const int workers_;
+  std::mutex job_mu_, mu_;
+  std::condition_variable cv_, done_cv_;
+  const std::function<void(int)>* fn_ = nullptr;
+  int n_ = 0;
+  std::atomic<int> next_{0};
+  int done_ = 0;
+  uint64_t gen_ = 0;
+  std::exception_ptr err_;
+};
+}  // namespace
+
 void TopKTopPSampler::sample_rows(const float* rows, int batch, int vocab, int* out) {
-  std::vector<Prepared> prep((size_t)batch);
-  int threads = (int)std::min<unsigned>((unsigned)batch, std::max(1u, std::thread::hardware_concurrency()));
-  if (threads <= 1) {
+  if (rows_.size() < (size_t)batch) rows_.resize((size_t)batch);
+  std::vector<Prepared>& prep = rows_;
+  if (batch <= 1) {
     for (int b = 0; b < batch; b++) prepare(rows + (size_t)b * vocab, vocab, prep[(size_t)b]);
   } else {
-    std::vector<std::thread> pool;
-    std::exception_ptr err;
-    std::mutex err_mu;
-    for (int t = 0; t < threads; t++)
-      pool.emplace_back([&, t] {
-        try {
-          for (int b = t; b < batch; b += threads) prepare(rows + (size_t)b * vocab, vocab, prep[(size_t)b]);
-        } catch (...) {
-          std::lock_guard<std::mutex> g(err_mu);
-          err = std::current_exception();
-        }
-      });
-    for (auto& th : pool) th.join();
-    if (err) std::rethrow_exception(err);
+    // rows are independent: prepared in any order on the pool; the draws below stay in row order
+    RowPool::instance().run(batch, [&](int b) { prepare(rows + (size_t)b * vocab, vocab, prep[(size_t)b]); });
   }
   for (int b = 0; b < batch; b++) out[b] = draw(prep[(size_t)b]);
 }

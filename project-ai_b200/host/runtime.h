@@ -453,6 +453,9 @@ class TopKTopPSampler {
   float temperature;
   int top_k;
   float top_p;
+
+ private:
+  std::vector<Prepared> rows_;  // per-row buffers kept across sample_rows calls (a decode step reuses their storage)
 };
 
 // ---------------------------------------------------------------- optimizer (Optimizers.cs)

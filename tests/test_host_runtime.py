@@ -316,7 +316,8 @@ def reference_topk_topp(logits, rng, temperature, top_k, top_p):
 
 def test_topk_partial_sort_and_batched_rows_match_the_reference_sampler():
     rs = np.random.RandomState(1)
-    rows = np.stack([rs.permutation(2000).astype(np.float32) * 0.01 for _ in range(6)])  # distinct logits per row
+    rows = np.stack([rs.permutation(2000).astype(np.float32) * 0.01 for _ in range(6)] +   # distinct logits per row
+                    [rs.randint(0, 30, size=2000).astype(np.float32) * 0.1 for _ in range(4)])  # many exact ties
     for k, p in [(40, 1.0), (5, 0.9), (0, 0.5)]:
         s = H.TopKTopPSampler(9, 0.8, k, p)
         ref_rng = H.PcgRng(9)
