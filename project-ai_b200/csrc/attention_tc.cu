@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "tc_common.cuh"
+#include "attention_pack.cuh"
 
 namespace pai {
 
@@ -31,21 +32,10 @@ constexpr int kSoftmaxWarps = 8;
 constexpr int kFwdThreads = 64 + 32 * kSoftmaxWarps;
 
 // ---------------------------------------------------------------- pack pre-pass
-struct AttnPackArgs {
-  const float* src;
-  int64_t s_b, s_x, s_r, s_d;  // element strides of the [B, X, R, D] view
-  int X, R, D;
-  int blk;        // sequence positions per packed tile (128 for Q, 64 for K/V)
-  int transpose;  // 0: tile rows = positions, cols = d;  1: tile rows = d, cols = positions
-  float scale;
-  int nblk;
-  float* out;
-};
-
-// grid (nblk, B*X). Output per tile: [hi kb0][hi kb1][lo kb0][lo kb1], kb = 32 columns, rows x 32 floats each.
-__global__ void __launch_bounds__(256) k_attn_pack(AttnPackArgs a) {
+// One tile (bi of the nblk along R) of one (batch, head) row bx of an operand. Output per tile: [hi kb0][hi kb1]
+// [lo kb0][lo kb1], kb = 32 columns, rows x 32 floats each.
+__device__ __forceinline__ void attn_pack_tile(const AttnPackArgs& a, int bi, int bx) {
   __shared__ float tile[kQT][kDP + 1];
-  int bi = blockIdx.x, bx = blockIdx.y;
   int b = bx / a.X, x = bx % a.X;
   const float* src = a.src + b * a.s_b + x * a.s_x;
   int rows = a.transpose ? kDP : a.blk;
@@ -92,6 +82,43 @@ __global__ void __launch_bounds__(256) k_attn_pack(AttnPackArgs a) {
     reinterpret_cast<float4*>(out + (size_t)kb * rows * 32)[phys] = make_float4(hi[0], hi[1], hi[2], hi[3]);
     reinterpret_cast<float4*>(out + (size_t)(2 + kb) * rows * 32)[phys] = make_float4(lo[0], lo[1], lo[2], lo[3]);
   }
+}
+
+// Several operands in one launch: CTAs [start[i], start[i+1]) pack operand i, its tiles in (bx, bi) order.
+struct AttnPackSet {
+  AttnPackArgs p[kAttnPackMax];
+  int64_t start[kAttnPackMax + 1];
+  int n;
+};
+
+__global__ void __launch_bounds__(256) k_attn_pack(const __grid_constant__ AttnPackSet s) {
+  const int64_t i = blockIdx.x;
+  int k = 0;
+#pragma unroll
+  for (int j = 1; j < kAttnPackMax; j++)
+    if (j < s.n && i >= s.start[j]) k = j;
+  const AttnPackArgs& a = *(&s.p[0] + k);
+  const int64_t local = i - *(&s.start[0] + k);
+  attn_pack_tile(a, (int)(local % a.nblk), (int)(local / a.nblk));
+}
+
+pai_status attn_pack_launch(pai_ctx* ctx, const AttnPackArgs* packs, int n, int B) {
+  if (n < 1 || n > kAttnPackMax) return set_error(PAI_ERR_ARGUMENT, "attention pack: %d operands (1..%d)", n, kAttnPackMax);
+  AttnPackSet s{};
+  int64_t total = 0;
+  for (int i = 0; i < n; i++) {
+    s.p[i] = packs[i];
+    s.start[i] = total;
+    total += (int64_t)packs[i].nblk * B * packs[i].X;
+  }
+  s.start[n] = total;
+  s.n = n;
+  if (total > INT32_MAX) return set_error(PAI_ERR_UNSUPPORTED, "attention pack: %lld tiles exceed one launch", (long long)total);
+  if (total > 0) {
+    k_attn_pack<<<(unsigned)total, 256, 0, ctx->stream>>>(s);
+    PAI_LAUNCH_CHECK("attention pack");
+  }
+  return PAI_OK;
 }
 
 // ---------------------------------------------------------------- forward kernel
@@ -476,17 +503,13 @@ pai_status attn_tc_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   PAI_TRY(scratch(ctx, (size_t)B * H * q_tiles * kQBytes, &qp));
   PAI_TRY(scratch(ctx, (size_t)B * KVH * k_blocks * kKBytes, &kp));
   PAI_TRY(scratch(ctx, (size_t)B * KVH * k_blocks * kKBytes, &vp));
-  auto pack = [&](const pai_tensor& t, int X, int R, int blk, int transpose, float sc, int nblk, void* dst) -> pai_status {
-    AttnPackArgs p{static_cast<const float*>(t.base) + t.offset, t.strides[0], t.strides[1], t.strides[2], t.strides[3],
-                   X, R, D, blk, transpose, sc, nblk, static_cast<float*>(dst)};
-    dim3 grid((unsigned)nblk, (unsigned)(B * X));
-    k_attn_pack<<<grid, 256, 0, ctx->stream>>>(p);
-    PAI_LAUNCH_CHECK("attention pack");
-    return PAI_OK;
+  auto pack = [&](const pai_tensor& t, int X, int R, int blk, int transpose, float sc, int nblk, void* dst) {
+    return AttnPackArgs{static_cast<const float*>(t.base) + t.offset, t.strides[0], t.strides[1], t.strides[2],
+                        t.strides[3], X, R, D, blk, transpose, sc, nblk, static_cast<float*>(dst)};
   };
-  PAI_TRY(pack(q, H, S, kQT, 0, scale, q_tiles, qp.p));
-  PAI_TRY(pack(k, KVH, L, kKB, 0, 1.0f, k_blocks, kp.p));
-  PAI_TRY(pack(v, KVH, L, kKB, 1, 1.0f, k_blocks, vp.p));
+  const AttnPackArgs packs[3] = {pack(q, H, S, kQT, 0, scale, q_tiles, qp.p), pack(k, KVH, L, kKB, 0, 1.0f, k_blocks, kp.p),
+                                 pack(v, KVH, L, kKB, 1, 1.0f, k_blocks, vp.p)};
+  PAI_TRY(attn_pack_launch(ctx, packs, 3, B));
   static bool attr = false;
   if (!attr) {
     PAI_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmemBytes));

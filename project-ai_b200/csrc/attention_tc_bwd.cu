@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "tc_common.cuh"
+#include "attention_pack.cuh"
 
 namespace pai {
 
@@ -467,19 +468,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
 
 }  // namespace bwd
 
-// k_attn_pack lives in attention_tc.cu
-struct AttnPackArgs {
-  const float* src;
-  int64_t s_b, s_x, s_r, s_d;
-  int X, R, D;
-  int blk;
-  int transpose;
-  float scale;
-  int nblk;
-  float* out;
-};
-__global__ void k_attn_pack(AttnPackArgs a);
-
 }  // namespace pai
 
 using namespace pai;
@@ -501,12 +489,12 @@ pai_status attn_tc_bwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   PAI_TRY(scratch(ctx, (size_t)B * KVH * nk2 * tf, &vp));
   PAI_TRY(scratch(ctx, (size_t)B * KVH * nk * tf, &kT));
   // [B, X, R, D] view strides of each operand (dout is [B,S,H,D]: its head axis is 2, its row axis 1).
+  AttnPackArgs packs[kAttnPackMax];
+  int npack = 0;
   auto pack = [&](const float* base, int64_t sb, int64_t sx, int64_t sr, int64_t sd, int X, int R, int transpose,
                   float sc, int nblk, void* dst) -> pai_status {
-    AttnPackArgs p{base, sb, sx, sr, sd, X, R, D, kBlk, transpose, sc, nblk, static_cast<float*>(dst)};
-    dim3 grid((unsigned)nblk, (unsigned)(B * X));
-    k_attn_pack<<<grid, 256, 0, ctx->stream>>>(p);
-    PAI_LAUNCH_CHECK("attention backward pack");
+    if (npack == kAttnPackMax) return set_error(PAI_ERR_ARGUMENT, "attention backward: too many packed operands");
+    packs[npack++] = AttnPackArgs{base, sb, sx, sr, sd, X, R, D, kBlk, transpose, sc, nblk, static_cast<float*>(dst)};
     return PAI_OK;
   };
   const float* qb = static_cast<const float*>(q.base) + q.offset;
@@ -520,6 +508,7 @@ pai_status attn_tc_bwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   PAI_TRY(pack(kb, k.strides[0], k.strides[1], k.strides[2], k.strides[3], KVH, L, 0, 1.0f, nk2, kp.p));
   PAI_TRY(pack(kb, k.strides[0], k.strides[1], k.strides[2], k.strides[3], KVH, L, 1, 1.0f, nk, kT.p));
   PAI_TRY(pack(vb, v.strides[0], v.strides[1], v.strides[2], v.strides[3], KVH, L, 0, 1.0f, nk2, vp.p));
+  PAI_TRY(attn_pack_launch(ctx, packs, npack, B));  // all seven operands in one launch
   static bool attr = false;
   if (!attr) {
     PAI_CUDA(cudaFuncSetAttribute(k_attn_bwd_kv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
