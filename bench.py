@@ -2,11 +2,16 @@
 
 One step = one pass of the reference trainer's step (ProjectAI.Training/Training.cs:87-113) through the host runtime
 and the C ABI: forward with per-block gradient checkpointing, cross-entropy, backward with recompute, fused AdamW.
-Workload at N=1 (and per GPU at N>1, weak scaling): ~125M Llama-style decoder, fp32 — vocab 32000, d_model 768,
-12 layers, 12 heads (head_dim 64), SwiGLU FFN 2048, RMSNorm, RoPE, tied embeddings, weights N(0, 0.02) from a seed;
-synthetic token ids uniform in [0, 32000) from PcgRng(rank*1000 + step), targets shifted by one; seq 1024 x batch 8.
+Workload at N=1 (and per GPU at N>1, weak scaling): ~1B Llama-style decoder, fp32 — vocab 32000, d_model 2048,
+16 layers, 32 query heads over 8 KV heads (head_dim 64), SwiGLU FFN 5632, RMSNorm, RoPE base 10000, tied embeddings,
+weights N(0, 0.02) from a seed; synthetic token ids uniform in [0, 32000) from PcgRng(rank*1000 + step), targets
+shifted by one; seq 2048 x batch 4 per GPU. At N=1 the line also carries the same model without recompute (tokens/s
+and peak memory), the ~125M config (vocab 32000, d_model 768, 12 layers, 12 heads, FFN 2048, seq 1024 x batch 8) as
+an extra key, and KV-cache decode of the ~1B model.
 
 value  — device-resident batches (uploaded before the timed region), timed with CUDA events on the library's stream.
+mfu / hfu — model flops per token (3 x forward: linear layers, tied LM head, causal attention) and hardware flops per
+         token (plus the recomputed block forwards) times tokens/s, over the 3xTF32 tensor ceiling.
 e2e    — the same step through the public host-buffer entry (Trainer.step with host arrays: the ids H2D copy and the
          loss D2H read are inside the timed region).
 roofline — the dominant kernel (the 3xTF32 tcgen05 GEMM): algorithmic 2·M·N·K flops per launch over its average
@@ -153,22 +158,55 @@ def ncu_traffic():
     return None
 
 
-def cpu_baseline(cfg_name, sample_tokens, threads):
-    """Times the oracle (CPU restatement of the reference backend) on one step of a bounded sample of the workload."""
+# Tokens per step of the bounded CPU samples (batch 1): the oracle's scalar loops take ~7 GFLOP per token of the
+# ~1B model, and its composed AdamW makes ~20 passes over the 787 M parameters whatever the token count.
+CPU_SAMPLE_SEQ = {"1b": 16, "125m": 64, "tiny": 64}
+
+
+def flops_per_token(c, seq):
+    """(model, hardware) flops per trained token. Forward: 2 flops per weight of the linear layers and the tied LM
+    head, plus causal attention (QKᵀ and P·V over the (S+1)/2 keys a query sees on average: 2·(S+1)·d per layer).
+    Model = 3 x forward (forward + backward); hardware adds the per-block recompute (the blocks' forward again)."""
+    d, f, v, h, kvh, layers = (c["embedding_dim"], c["ffn_hidden"], c["vocab_size"], c["head_count"],
+                               c["kv_head_count"], c["layer_count"])
+    hd = d // h
+    linear = 2 * d * h * hd + 2 * d * kvh * hd + 3 * d * f  # wq, wo, wk, wv, gate, up, down
+    block = 2.0 * linear + 2.0 * (seq + 1) * h * hd
+    fwd = layers * block + 2.0 * v * d
+    return 3.0 * fwd, 3.0 * fwd + layers * block
+
+
+def cpu_train_sample(cfg_name, seq, threads, steps=1, warmup=0):
+    """Times the oracle (CPU restatement of the reference backend) on `steps` training steps of the full model at
+    batch 1 x seq `seq` (a bounded sample of the workload), after `warmup` untimed steps. Returns (tokens/s, seconds)."""
     import ctypes
     ctypes.CDLL(str(ORACLE_LIB)).oracle_set_threads(threads)
     c = CONFIGS[cfg_name]
-    seq = min(sample_tokens, c["seq"])
+    seq = min(seq, c["seq"])
     be = H.Backend(str(ORACLE_LIB), "oracle_", 0)
     m = H.LlamaModel(be, model_config(c, seq), seed=0, init="normal0.02")
-    tc = H.TrainingConfig(batch_size=1, sequence_length=seq, learning_rate=3e-4, weight_decay=0.1, max_steps=10,
-                          gradient_checkpointing=True, warmup_steps=0)
+    tc = H.TrainingConfig(batch_size=1, sequence_length=seq, learning_rate=3e-4, weight_decay=0.1,
+                          max_steps=steps + warmup + 10, gradient_checkpointing=True, warmup_steps=0)
     tr = H.Trainer(be, m, tc, 0.9, 0.95)
-    x, y = synthetic_batch(0, 0, 1, seq, c["vocab_size"])
+    for w in range(warmup):
+        x, y = synthetic_batch(0, w, 1, seq, c["vocab_size"])
+        tr.step([x], [y])
     t0 = time.perf_counter()
-    tr.step([x], [y])
+    for k in range(steps):
+        x, y = synthetic_batch(0, warmup + k, 1, seq, c["vocab_size"])
+        tr.step([x], [y])
     dt = time.perf_counter() - t0
-    return seq / dt, dt, seq
+    return seq * steps / dt, dt
+
+
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 def decode_bench(local, cfg_name="1b", prompt_len=512, gen=256, batches=(1, 32)):
@@ -238,35 +276,26 @@ def decode_bench(local, cfg_name="1b", prompt_len=512, gen=256, batches=(1, 32))
 
 
 def reference_arm(args):
+    """The reference's CPU path on the host cores: the oracle port of CpuComputeBackend under the same host runtime,
+    all threads, each step one full-model training step at batch 1 x seq CPU_SAMPLE_SEQ (a bounded sample: the
+    workload's batch x seq per GPU would take hours per step on the CPU). The config block states that sample."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # under torchrun only rank 0 times the CPU reference
     c = CONFIGS[args.config]
     threads = os.cpu_count() or 1
-    import ctypes
-    ctypes.CDLL(str(ORACLE_LIB)).oracle_set_threads(threads)
-    seq = min(args.cpu_sample_tokens, c["seq"])
-    be = H.Backend(str(ORACLE_LIB), "oracle_", 0)
-    m = H.LlamaModel(be, model_config(c, seq), seed=0, init="normal0.02")
-    tc = H.TrainingConfig(batch_size=1, sequence_length=seq, learning_rate=3e-4, weight_decay=0.1, max_steps=1000,
-                          gradient_checkpointing=True, warmup_steps=0)
-    tr = H.Trainer(be, m, tc, 0.9, 0.95)
-    for w in range(args.warmup):
-        x, y = synthetic_batch(0, w, 1, seq, c["vocab_size"])
-        tr.step([x], [y])
-    t0 = time.perf_counter()
-    for k in range(args.steps):
-        x, y = synthetic_batch(0, args.warmup + k, 1, seq, c["vocab_size"])
-        tr.step([x], [y])
-    dt = time.perf_counter() - t0
-    value = seq * args.steps / dt
-    sample = (f"{args.config} model, per-block recompute, batch 1 x seq {seq} per step "
-              f"(the workload is batch {c['batch']} x seq {c['seq']})")
+    seq = min(args.cpu_sample_tokens or CPU_SAMPLE_SEQ[args.config], c["seq"])
+    value, dt = cpu_train_sample(args.config, seq, threads, steps=args.steps, warmup=args.warmup)
+    sample = (f"{args.config} model (all parameters, AdamW over all of them), per-block recompute, batch 1 x seq {seq} "
+              f"per step; the GPU workload is batch {c['batch']} x seq {c['seq']} per GPU")
+    cfg = workload_config(args.config, 1, True)
+    cfg.update({"seq_len": seq, "batch_per_gpu": 1, "global_batch": 1, "parallelism": "cpu, one process",
+                "sample_of": f"llama-{args.config} train step at batch {c['batch']} x seq {c['seq']} per GPU"})
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(args.config, args.gpus),
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample,
+                             "cpu": cpu_model()},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -402,16 +431,84 @@ def workload_config(name, n, recompute=True):
             "l2": "working set above L2 (weights alone 4 B x params), no flush needed"}
 
 
+def device_resident_run(be, tr, rank, c, step0, steps):
+    """Uploads `steps` synthetic batches, then times them through Trainer.step_tensors with CUDA events on the
+    library's stream. Returns (ms, last loss)."""
+    batches = []
+    for k in range(steps):
+        x, y = synthetic_batch(rank, step0 + k, c["batch"], c["seq"], c["vocab_size"])
+        batches.append((be.from_host(x), be.from_host(y)))
+    be.sync()
+    be.timer_start()
+    loss = None
+    for x, y in batches:
+        loss = tr.step_tensors([x], [y])
+    return be.timer_stop(), loss
+
+
+def side_runs(be, m, args, c, peak_tf32):
+    """N=1 extras: the same model without per-block recompute (tokens/s and the allocator's peak), then the ~125M
+    config. Each on device-resident batches after its own warm-up steps."""
+    out = {}
+    steps = max(3, min(args.steps, 10))
+    tc = H.TrainingConfig(batch_size=c["batch"], sequence_length=c["seq"], learning_rate=3e-4, weight_decay=0.1,
+                          max_steps=100, gradient_checkpointing=False, warmup_steps=0)
+    tr = H.Trainer(be, m, tc, 0.9, 0.95)
+    tr.set_constant_lr(3e-4)
+    for w in range(2):
+        x, y = synthetic_batch(0, 500 + w, c["batch"], c["seq"], c["vocab_size"])
+        tr.step([x], [y])
+    be.sync()
+    be.reset_peak()
+    ms, _ = device_resident_run(be, tr, 0, c, 600, steps)
+    peak = be.memory_stats()[1]
+    tokens = c["batch"] * c["seq"] * steps
+    mf, _ = flops_per_token(c, c["seq"])
+    out["no_recompute"] = {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms / steps, "steps": steps,
+                           "peak_allocated_gb": peak / 1e9,
+                           "mfu": mf * tokens / (ms * 1e-3) / 1e12 / (peak_tf32 / 3.0)}
+    del tr
+    be.sync()
+    return out
+
+
+def small_config_run(be, args, name, peak_tf32):
+    """tokens/s of another config (per-block recompute) on device-resident batches, value only."""
+    c = CONFIGS[name]
+    m = H.LlamaModel(be, model_config(c, c["seq"]), seed=0, init="normal0.02")
+    tc = H.TrainingConfig(batch_size=c["batch"], sequence_length=c["seq"], learning_rate=3e-4, weight_decay=0.1,
+                          max_steps=100, gradient_checkpointing=True, warmup_steps=0)
+    tr = H.Trainer(be, m, tc, 0.9, 0.95)
+    tr.set_constant_lr(3e-4)
+    for w in range(3):
+        x, y = synthetic_batch(0, w, c["batch"], c["seq"], c["vocab_size"])
+        tr.step([x], [y])
+    steps = max(3, args.steps)
+    be.reset_peak()
+    ms, loss = device_resident_run(be, tr, 0, c, 3, steps)
+    tokens = c["batch"] * c["seq"] * steps
+    mf, hf = flops_per_token(c, c["seq"])
+    res = {"workload": workload_config(name, 1)["workload"], "value": tokens / (ms * 1e-3), "unit": "tokens/s",
+           "ms_per_step": ms / steps, "steps": steps, "peak_allocated_gb": be.memory_stats()[1] / 1e9,
+           "mfu": mf * tokens / (ms * 1e-3) / 1e12 / (peak_tf32 / 3.0),
+           "hfu": hf * tokens / (ms * 1e-3) / 1e12 / (peak_tf32 / 3.0), "final_loss": loss}
+    del tr, m
+    be.sync()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    ap.add_argument("--config", default="125m", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="1b", choices=sorted(CONFIGS))
     ap.add_argument("--no-recompute", action="store_true")
-    ap.add_argument("--cpu-sample-tokens", type=int, default=64)
+    ap.add_argument("--cpu-sample-tokens", type=int, default=None,
+                    help="tokens per CPU sample step (default: 16 for 1b, 64 for 125m and tiny)")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-extra", action="store_true", help="leave the no-recompute and 125M runs out of the N=1 line")
     ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm", "decode"],
                     help="op-level sweep instead of the training step")
     ap.add_argument("--shape", default=None, help="M,K,N for --op gemm; rows,K,N for --op decode; B,H,S,D for --op attention")
@@ -473,6 +570,8 @@ def main():
     step += args.steps
     barrier()
     be.reset_peak()
+    if world > 1:
+        be.dp_stats()  # clears the warm-up steps' exposed all-reduce time
     launches0 = be.launch_count()
     losses = []
     with ClockSampler(local) as clocks:
@@ -481,6 +580,7 @@ def main():
             losses.append(tr.step_tensors([x], [y]))
         ms = be.timer_stop()
     launches = be.launch_count() - launches0
+    exposed_ms, exposed_steps = be.dp_stats() if world > 1 else (0.0, 0)
     mem_in_use, mem_peak, mem_reserved = be.memory_stats()
     be.check_device_error()
     barrier()
@@ -507,13 +607,14 @@ def main():
 
     if dist:
         import torch
-        t = torch.tensor([ms, ms_e2e], device=f"cuda:{local}")
+        t = torch.tensor([ms, ms_e2e, exposed_ms / max(exposed_steps, 1)], device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_e2e = t.tolist()
+        ms, ms_e2e, exposed_per_step = t.tolist()
 
     tokens = c["batch"] * c["seq"] * world * args.steps
     value = tokens / (ms * 1e-3)
     e2e = tokens / (ms_e2e * 1e-3)
+    line = None
     if rank == 0:
         g_launches, g_ms, g_flops = kstats["gemm"]
         avg_ms = g_ms / max(g_launches, 1)
@@ -536,33 +637,65 @@ def main():
                     "share_of_step": g_ms / ms_timed}
         kernels = {f: {"launches": v[0], "ms": v[1], "tflops": (v[2] / (v[1] * 1e-3) / 1e12) if v[1] else None,
                        "share_of_step": v[1] / ms_timed} for f, v in kstats.items()}
-        step_flops = (kstats["gemm"][2] + kstats["attn_fwd"][2] + kstats["attn_bwd"][2]) / args.steps
+        mf, hf = flops_per_token(c, c["seq"])
+        if args.no_recompute:
+            hf = mf
+        per_gpu = value / world
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (PcgRng token ids, N(0,0.02) weights)",
                 "config": workload_config(args.config, world, not args.no_recompute), "roofline": roofline,
+                "mfu": mf * per_gpu / 1e12 / peak, "hfu": hf * per_gpu / 1e12 / peak,
+                "flops_per_token": {"model": mf, "hardware": hf,
+                                    "note": "model = 3 x forward (linear layers, tied LM head, causal attention); "
+                                            "hardware adds the recomputed block forwards; mfu/hfu are per GPU over "
+                                            "the 3xTF32 ceiling (roofline.peak)"},
                 "memory": {"peak_allocated_gb": mem_peak / 1e9, "reserved_gb": mem_reserved / 1e9,
                            "note": "device bytes held by tensors at the peak of the timed steps (weights, AdamW "
                                    "moments, gradients and activations), from the library's allocator"},
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * c["batch"] * c["seq"] * 4,
                         "d2h_bytes_per_step": 4, "ms_per_step": ms_e2e / args.steps},
                 "gpu_launches": launches, "kernels": kernels,
-                "model_tflops_per_s": step_flops * args.steps / (ms * 1e-3) / 1e12,
+                "model_tflops_per_s": mf * per_gpu / 1e12,
                 "recompute": not args.no_recompute, "final_loss": losses[-1],
                 "clocks": clocks.summary(), "peak_tf32_tflops": peak_tf32}
-        if world == 1 and not args.skip_cpu_baseline:
-            threads = os.cpu_count() or 1
-            v, dt, seq = cpu_baseline(args.config, args.cpu_sample_tokens, threads)
-            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                    "sample": f"one training step of the {args.config} model at batch 1 x seq {seq} "
-                                              f"({dt:.1f} s) on the CPU oracle"}
-    del tr, m
-    if rank == 0:
-        if world == 1 and not args.skip_decode:
+        if world > 1:
+            line["dp"] = {"exposed_allreduce_ms_per_step": exposed_per_step,
+                          "exposed_share_of_step": exposed_per_step / (ms / args.steps),
+                          "steps_counted": exposed_steps,
+                          "note": "device time from the end of a step's backward (compute stream) to the end of its "
+                                  "last NCCL all-reduce (communication stream), max over ranks; the per-block buckets "
+                                  "before it overlap the backward"}
+    del tr
+    if rank == 0 and world == 1:
+        if not args.skip_extra and not args.no_recompute:
+            try:
+                line.update(side_runs(be, m, args, c, peak_tf32))
+                line["memory"]["no_recompute_peak_allocated_gb"] = line["no_recompute"]["peak_allocated_gb"]
+            except Exception as e:  # the main line still prints; the failure is reported in its place
+                line["no_recompute"] = {"error": f"{type(e).__name__}: {e}"}
+        del m
+        be.sync()
+        if not args.skip_extra and args.config != "125m":
+            try:
+                line["extra_125m"] = small_config_run(be, args, "125m", peak_tf32)
+            except Exception as e:
+                line["extra_125m"] = {"error": f"{type(e).__name__}: {e}"}
+        if not args.skip_decode:
             try:
                 line["decode"] = decode_bench(local, gen=args.decode_tokens)
-            except Exception as e:  # the training line still prints; the failure is reported in its place
+            except Exception as e:
                 line["decode"] = {"error": f"{type(e).__name__}: {e}"}
+        if not args.skip_cpu_baseline:
+            threads = os.cpu_count() or 1
+            seq = min(args.cpu_sample_tokens or CPU_SAMPLE_SEQ[args.config], c["seq"])
+            v, dt = cpu_train_sample(args.config, seq, threads)
+            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "cpu": cpu_model(),
+                                    "sample": f"one training step of the {args.config} model (all parameters, AdamW "
+                                              f"over all of them) at batch 1 x seq {seq} ({dt:.1f} s) on the CPU oracle"}
+    else:
+        del m
+    if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
