@@ -186,7 +186,8 @@ pai_status pai_adamw_step(pai_ctx* ctx, const pai_tensor* p, const pai_tensor* g
  * loading the library holds until exit. The first call on a device resolves that array's address
  * (cudaGetSymbolAddress), so make it before any stream capture. Calls share the array: calls that overlap on the
  * GPU race, while calls ordered on one stream are safe. Rows longer than 8192 elements are rejected with
- * PAI_ERR_OUT_OF_RANGE. Results match pai_rmsnorm_bwd. */
+ * PAI_ERR_OUT_OF_RANGE. Results match pai_rmsnorm_bwd within float rounding (1e-4): the dw partials are summed in
+ * a different order, so the two are not bit-identical. */
 pai_status pai_rmsnorm_bwd_noalloc(pai_ctx* ctx, const pai_tensor* x, const pai_tensor* weight, const pai_tensor* g,
                                    float eps, const pai_tensor* dx, const pai_tensor* dw);
 
@@ -247,9 +248,14 @@ pai_status pai_nccl_init(pai_ctx* ctx, const uint8_t id[128], int32_t rank, int3
 /* Sum-all-reduce a bucket of contiguous F32 tensors in place on the communication stream, ordered after all
  * work queued so far on the compute stream; later compute-stream work that touches the bucket waits for it. */
 pai_status pai_allreduce_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n_tensors);
-/* Makes the compute stream wait for every all-reduce issued so far. */
+/* Waits on the host, under the communicator's timeout, for every all-reduce issued so far, then orders the compute
+ * stream after them. A failed or unfinished exchange (a peer left) aborts the communicator and returns PAI_ERR_NCCL or
+ * PAI_ERR_TIMEOUT. Extends the step of ProjectAI.Training/Training.cs:87-113 with the cross-rank gradient sum. */
 pai_status pai_allreduce_wait(pai_ctx* ctx);
 pai_status pai_nccl_abort(pai_ctx* ctx);
+/* Exposed exchange time since the last call: summed device milliseconds by which the last all-reduce of each step
+ * ended after the step's backward (0 for a step whose exchange was hidden), and the number of steps counted. */
+pai_status pai_dp_stats(pai_ctx* ctx, double* exposed_ms, int64_t* steps);
 
 /* ==== Diagnostics (no counterpart in the reference; used by the benchmark and tests) ==== */
 /* Reads and clears the device flag that bounded waits inside kernels set on a timeout (PAI_ERR_TIMEOUT if set). */

@@ -1,8 +1,11 @@
 // Data parallelism: one process per GPU, gradient buckets summed with NCCL all-reduce on a dedicated stream so the
 // exchange of one transformer block's gradients overlaps the backward of the blocks before it.
 // The reference is single-device; this is the data-parallel extension of its trainer.
-// The communicator is created non-blocking and every NCCL call is polled under a host deadline, so a dead peer
-// ends in PAI_ERR_NCCL / PAI_ERR_TIMEOUT (after ncclCommAbort) instead of a hang.
+// The communicator is created non-blocking. Every NCCL call is polled under a host deadline (ncclInProgress), and
+// pai_allreduce_wait polls the completion of the enqueued all-reduces under the same deadline together with
+// ncclCommGetAsyncError. A peer that died before or during an exchange therefore ends in PAI_ERR_NCCL or
+// PAI_ERR_TIMEOUT: the communicator is aborted, which ends its kernels, so the compute stream is not left waiting
+// on a collective that cannot finish.
 #include <nccl.h>
 
 #include <chrono>
@@ -12,6 +15,11 @@
 
 namespace pai {
 
+// Exposed exchange time: per step, the device time from the end of the backward on the compute stream (recorded as
+// pai_allreduce_wait is called) to the end of the last all-reduce on the communication stream; zero when the exchange
+// finished first. A ring of event pairs is read back lazily by pai_dp_stats once both events of a pair completed.
+constexpr int kStatRing = 64;
+
 struct NcclState {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
@@ -19,24 +27,75 @@ struct NcclState {
   cudaEvent_t ready = nullptr;  // compute stream -> comm stream
   cudaEvent_t done = nullptr;   // comm stream -> compute stream
   bool pending = false;
+  cudaEvent_t bwd_end[kStatRing] = {};  // timing events on the compute stream
+  cudaEvent_t ar_end[kStatRing] = {};   // timing events on the comm stream
+  int64_t recorded = 0, read = 0;       // pairs recorded / pairs accounted
+  double exposed_ms = 0.0;
+  int64_t exposed_steps = 0;
 };
+
+static void abort_comm(NcclState* s) {
+  if (s->comm) {
+    ncclCommAbort(s->comm);
+    s->comm = nullptr;
+  }
+}
 
 static pai_status nccl_wait(NcclState* s, ncclResult_t r, const char* what) {
   auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(s->timeout_ms);
   while (r == ncclInProgress) {
     if (std::chrono::steady_clock::now() > deadline) {
-      ncclCommAbort(s->comm);
-      s->comm = nullptr;
+      abort_comm(s);
       return set_error(PAI_ERR_TIMEOUT, "NCCL %s did not complete within %d ms; communicator aborted", what, s->timeout_ms);
     }
     std::this_thread::sleep_for(std::chrono::microseconds(50));
     ncclCommGetAsyncError(s->comm, &r);
   }
   if (r != ncclSuccess) {
-    if (s->comm) { ncclCommAbort(s->comm); s->comm = nullptr; }
+    abort_comm(s);
     return set_error(PAI_ERR_NCCL, "NCCL %s failed: %s", what, ncclGetErrorString(r));
   }
   return PAI_OK;
+}
+
+// Host-side wait for `ev` (recorded on the comm stream after the last all-reduce) under the deadline, checking the
+// communicator's asynchronous error between polls.
+static pai_status wait_done(NcclState* s, cudaEvent_t ev) {
+  auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(s->timeout_ms);
+  for (;;) {
+    cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return PAI_OK;
+    if (q != cudaErrorNotReady) {
+      abort_comm(s);
+      return set_error(PAI_ERR_CUDA, "all-reduce completion: %s", cudaGetErrorString(q));
+    }
+    ncclResult_t r = ncclSuccess;
+    if (s->comm) ncclCommGetAsyncError(s->comm, &r);
+    if (r != ncclSuccess && r != ncclInProgress) {
+      abort_comm(s);
+      return set_error(PAI_ERR_NCCL, "NCCL all-reduce failed: %s; communicator aborted", ncclGetErrorString(r));
+    }
+    if (std::chrono::steady_clock::now() > deadline) {
+      abort_comm(s);
+      return set_error(PAI_ERR_TIMEOUT, "NCCL all-reduce did not complete within %d ms (a peer left?); communicator aborted",
+                       s->timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+// Accounts every recorded (backward end, all-reduce end) pair whose events have completed.
+static void read_stats(NcclState* s) {
+  while (s->read < s->recorded) {
+    const int i = (int)(s->read % kStatRing);
+    if (cudaEventQuery(s->bwd_end[i]) != cudaSuccess || cudaEventQuery(s->ar_end[i]) != cudaSuccess) break;
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, s->bwd_end[i], s->ar_end[i]) == cudaSuccess) {
+      s->exposed_ms += ms > 0.0f ? ms : 0.0f;
+      s->exposed_steps++;
+    }
+    s->read++;
+  }
 }
 
 }  // namespace pai
@@ -48,6 +107,10 @@ void pai_dp_destroy(pai_ctx* ctx) {
   if (ctx->nccl->comm) ncclCommDestroy(ctx->nccl->comm);
   if (ctx->nccl->ready) cudaEventDestroy(ctx->nccl->ready);
   if (ctx->nccl->done) cudaEventDestroy(ctx->nccl->done);
+  for (int i = 0; i < kStatRing; i++) {
+    if (ctx->nccl->bwd_end[i]) cudaEventDestroy(ctx->nccl->bwd_end[i]);
+    if (ctx->nccl->ar_end[i]) cudaEventDestroy(ctx->nccl->ar_end[i]);
+  }
   delete ctx->nccl;
   ctx->nccl = nullptr;
 }
@@ -79,6 +142,10 @@ PAI_API pai_status pai_nccl_init(pai_ctx* ctx, const uint8_t id[128], int32_t ra
   if (st != PAI_OK) { delete s; return st; }
   cudaEventCreateWithFlags(&s->ready, cudaEventDisableTiming);
   cudaEventCreateWithFlags(&s->done, cudaEventDisableTiming);
+  for (int i = 0; i < kStatRing; i++) {
+    cudaEventCreate(&s->bwd_end[i]);
+    cudaEventCreate(&s->ar_end[i]);
+  }
   ctx->nccl = s;
   return PAI_OK;
 }
@@ -115,17 +182,42 @@ PAI_API pai_status pai_allreduce_wait(pai_ctx* ctx) {
   std::lock_guard<std::recursive_mutex> lk(ctx->mu);
   NcclState* s = ctx->nccl;
   if (!s || !s->pending) return PAI_OK;
-  PAI_CUDA(cudaStreamWaitEvent(ctx->stream, s->done, 0));
   s->pending = false;
+  read_stats(s);
+  if (s->recorded - s->read < kStatRing) {
+    const int i = (int)(s->recorded % kStatRing);
+    PAI_CUDA(cudaEventRecord(s->bwd_end[i], ctx->stream));
+    PAI_CUDA(cudaEventRecord(s->ar_end[i], ctx->comm_stream));
+    s->recorded++;
+  }
+  // The host waits (bounded) for the exchange before the compute stream is ordered after it: a dead peer surfaces
+  // here as an error instead of as a compute stream blocked behind a collective that cannot complete.
+  PAI_TRY(wait_done(s, s->done));
+  PAI_CUDA(cudaStreamWaitEvent(ctx->stream, s->done, 0));
+  return PAI_OK;
+}
+
+PAI_API pai_status pai_dp_stats(pai_ctx* ctx, double* exposed_ms, int64_t* steps) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  NcclState* s = ctx->nccl;
+  double e = 0.0;
+  int64_t n = 0;
+  if (s) {
+    read_stats(s);
+    e = s->exposed_ms;
+    n = s->exposed_steps;
+    s->exposed_ms = 0.0;
+    s->exposed_steps = 0;
+  }
+  if (exposed_ms) *exposed_ms = e;
+  if (steps) *steps = n;
   return PAI_OK;
 }
 
 PAI_API pai_status pai_nccl_abort(pai_ctx* ctx) {
   if (!ctx) return set_error(PAI_ERR_ARGUMENT, "null context");
   std::lock_guard<std::recursive_mutex> lk(ctx->mu);
-  if (ctx->nccl && ctx->nccl->comm) {
-    ncclCommAbort(ctx->nccl->comm);
-    ctx->nccl->comm = nullptr;
-  }
+  if (ctx->nccl) abort_comm(ctx->nccl);
   return PAI_OK;
 }

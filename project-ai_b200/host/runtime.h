@@ -10,6 +10,7 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <functional>
 #include <map>
 #include <memory>
@@ -150,6 +151,8 @@ class NativeBackend {
   void nccl_init(const uint8_t id[128], int rank, int world, int timeout_ms);
   void allreduce(const std::vector<Tensor>& grads);
   void allreduce_wait();
+  // Exposed all-reduce device time (ms summed over steps) and the step count since the last call.
+  std::pair<double, int64_t> dp_stats();
   int dp_world = 1, dp_rank = 0;
   // decode steps with device-side ids and position, replayed as CUDA graphs (CUDA library only)
   bool has_graphs() const;

@@ -265,6 +265,7 @@ void TensorImpl::backward(const Tensor& seed) {
   X(nccl_init, int (*)(pai_ctx*, const uint8_t*, int32_t, int32_t, int32_t))                                             \
   X(allreduce_bucket, int (*)(pai_ctx*, const pai_tensor*, int32_t))                                                     \
   X(allreduce_wait, int (*)(pai_ctx*))                                                                                  \
+  X(dp_stats, int (*)(pai_ctx*, double*, int64_t*))                                                                      \
   X(timer_start, int (*)(pai_ctx*))                                                                                      \
   X(timer_stop, int (*)(pai_ctx*, float*))                                                                               \
   X(launch_count, int (*)(pai_ctx*, int64_t*))                                                                           \
@@ -664,6 +665,13 @@ void NativeBackend::allreduce(const std::vector<Tensor>& grads) {
   d.reserve(grads.size());
   for (const auto& g : grads) d.push_back(g->desc());
   check(fn_->allreduce_bucket(ctx_, d.data(), (int32_t)d.size()));
+}
+
+std::pair<double, int64_t> NativeBackend::dp_stats() {
+  double ms = 0.0;
+  int64_t n = 0;
+  if (fn_->dp_stats) check(fn_->dp_stats(ctx_, &ms, &n));
+  return {ms, n};
 }
 
 void NativeBackend::allreduce_wait() {
