@@ -590,13 +590,8 @@ __global__ void __launch_bounds__(kDirectThreads) k_attn_decode_direct(const Arg
 
 template <int R, int DC, bool ROPE>
 static cudaError_t launch_decode_r(pai_ctx* ctx, const dec::Args& a, dim3 grid) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(dec::k_attn_decode<R, DC, ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)dec::smem_bytes(dec::kStages));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  cudaError_t e = smem_limit(ctx, dec::k_attn_decode<R, DC, ROPE>, (int)dec::smem_bytes(dec::kStages));
+  if (e != cudaSuccess) return e;
   // A plain cluster launch: the kernel starts once the previous kernel has finished (its griddepcontrol.wait is then a
   // no-op) but still lets the next kernel launch early. Launched early itself, behind the q/k/v product, it made
   // the decode step slower (batch 1: 1.05 against 0.93 ms per step of the 16-layer model).

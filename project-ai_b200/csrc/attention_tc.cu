@@ -1,6 +1,6 @@
 // Tensor-core (tcgen05, 3xTF32) fused causal attention forward.
 //
-// Same contract and semantics as the CUDA-core kernel in attention.cu (the composed chain of Modules.cs:169-203):
+// Semantics of the composed chain of Modules.cs:169-203 (entry point pai_sdpa_fwd in attention.cu):
 // scores = (q·scale)·kᵀ with q rounded to fp32 after scaling, keys j <= pos_offset + i, online softmax, ·v, output in
 // the merged-heads layout [B,S,H,D] plus the row log-sum-exp for the backward.
 //
@@ -510,11 +510,7 @@ pai_status attn_tc_fwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   const AttnPackArgs packs[3] = {pack(q, H, S, kQT, 0, scale, q_tiles, qp.p), pack(k, KVH, L, kKB, 0, 1.0f, k_blocks, kp.p),
                                  pack(v, KVH, L, kKB, 1, 1.0f, k_blocks, vp.p)};
   PAI_TRY(attn_pack_launch(ctx, packs, 3, B));
-  static bool attr = false;
-  if (!attr) {
-    PAI_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmemBytes));
-    attr = true;
-  }
+  PAI_CUDA(smem_limit(ctx, k_attn_fwd_tc, kFwdSmemBytes));
   AttnTcArgs args{static_cast<float*>(qp.p), static_cast<float*>(kp.p), static_cast<float*>(vp.p), out, lse,
                   B, H, KVH, S, L, D, pos_offset, causal, q_tiles, k_blocks, ctx->d_error_flag};
   const int n_items = q_tiles * H * B;

@@ -509,12 +509,8 @@ pai_status attn_tc_bwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   PAI_TRY(pack(kb, k.strides[0], k.strides[1], k.strides[2], k.strides[3], KVH, L, 1, 1.0f, nk, kT.p));
   PAI_TRY(pack(vb, v.strides[0], v.strides[1], v.strides[2], v.strides[3], KVH, L, 0, 1.0f, nk2, vp.p));
   PAI_TRY(attn_pack_launch(ctx, packs, npack, B));  // all seven operands in one launch
-  static bool attr = false;
-  if (!attr) {
-    PAI_CUDA(cudaFuncSetAttribute(k_attn_bwd_kv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-    PAI_CUDA(cudaFuncSetAttribute(k_attn_bwd_q_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-    attr = true;
-  }
+  PAI_CUDA(smem_limit(ctx, k_attn_bwd_kv_tc, kSmem));
+  PAI_CUDA(smem_limit(ctx, k_attn_bwd_q_tc, kSmem));
   Args args{static_cast<float*>(qs.p), static_cast<float*>(dO.p), static_cast<float*>(qsT.p), static_cast<float*>(dOT.p),
             static_cast<float*>(kp.p), static_cast<float*>(vp.p), static_cast<float*>(kT.p), lse, dvec, dq, dk, dv,
             B, H, KVH, S, L, D, pos_offset, causal, nq, nq2, nk, nk2, scale, ctx->d_error_flag};

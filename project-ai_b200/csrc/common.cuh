@@ -97,9 +97,24 @@ struct pai_ctx {
   pai_graph* capture = nullptr;
   int64_t capture_launches0 = 0;
   std::unordered_map<void*, pai_graph*> graph_owner;
+  // kernels whose dynamic shared-memory limit was raised on this context's device, with the bytes set
+  std::unordered_map<const void*, int> smem_attr;
 };
 
 namespace pai {
+// Raises a kernel's dynamic shared-memory limit to `bytes`. The attribute belongs to the device that is current (a
+// CUDA context per device), so it is set once per library context, which is bound to one device and entered (device
+// made current) by every entry point, and only under the context's lock.
+template <class Kernel>
+inline cudaError_t smem_limit(pai_ctx* ctx, Kernel* kernel, int bytes) {
+  const void* key = reinterpret_cast<const void*>(kernel);
+  auto it = ctx->smem_attr.find(key);
+  if (it != ctx->smem_attr.end() && it->second >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) ctx->smem_attr[key] = bytes;
+  return e;
+}
+
 // Brackets one launch with events on the compute stream when kernel timing is on (pai_kernel_timing).
 struct KernelTimerScope {
   pai_ctx* ctx;

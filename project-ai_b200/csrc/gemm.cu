@@ -417,76 +417,16 @@ __global__ void k_splitk_reduce(const float* __restrict__ part, float* __restric
   }
 }
 
-// ---------------------------------------------------------------- SIMT reference GEMM (exact fp32 FMA)
-struct SimtArgs {
-  const float* a; const float* b; float* c;
-  const int64_t* a_off; const int64_t* b_off;  // per output batch
-  int64_t sam, sak, sbn, sbk;
-  int m, n, k;
-};
-
-__global__ void __launch_bounds__(256) k_gemm_simt(SimtArgs g) {
-  __shared__ float As[16][64 + 1];
-  __shared__ float Bs[16][64 + 1];
-  int bt = blockIdx.z;
-  const float* a = g.a + g.a_off[bt];
-  const float* b = g.b + g.b_off[bt];
-  int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-  int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < g.k; k0 += 16) {
-    for (int idx = threadIdx.x; idx < 16 * 64; idx += 256) {
-      int kk = idx / 64, mm = idx % 64;
-      int gm = m0 + mm, gk = k0 + kk;
-      As[kk][mm] = (gm < g.m && gk < g.k) ? a[gm * g.sam + gk * g.sak] : 0.0f;
-      int gn = n0 + mm;
-      Bs[kk][mm] = (gn < g.n && gk < g.k) ? b[gn * g.sbn + gk * g.sbk] : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < 16; kk++) {
-      float av[4], bv[4];
-#pragma unroll
-      for (int i = 0; i < 4; i++) { av[i] = As[kk][ty * 4 + i]; bv[i] = Bs[kk][tx * 4 + i]; }
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-  float* c = g.c + (size_t)bt * g.m * g.n;
-#pragma unroll
-  for (int i = 0; i < 4; i++)
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      int gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + j;
-      if (gm < g.m && gn < g.n) c[(size_t)gm * g.n + gn] = acc[i][j];
-    }
-}
-
 // ---------------------------------------------------------------- host side
 // gemv.cu: the small-M weight-streaming path (PAI_GEMV=0 turns it off)
 bool gemv_enabled();
 pai_status gemv_tn(pai_ctx* ctx, const float* x, const int64_t* xoff, int rows, const float* w, int64_t sw, int n, int k,
                    float* y);
 
-static int gemm_mode() {
-  static int mode = [] {
-    const char* e = getenv("PAI_GEMM");
-    return (e && strcmp(e, "simt") == 0) ? 1 : 0;
-  }();
-  return mode;
-}
-
 template <int BN, int STAGES>
 static pai_status launch_tc(pai_ctx* ctx, GemmArgs& g) {
   using S = GemmSmem<BN, STAGES>;
-  static bool attr_set = false;  // per process; every device gets the same attribute
-  if (!attr_set) {
-    PAI_CUDA(cudaFuncSetAttribute(k_gemm_tc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
-    attr_set = true;
-  }
+  PAI_CUDA(smem_limit(ctx, k_gemm_tc<BN, STAGES>, S::kBytes));
   int total = g.tiles_m * g.tiles_n * g.batches * g.splits;
   int grid = total < ctx->sm_count ? total : ctx->sm_count;
   KernelTimerScope timer(ctx, "gemm", 2.0 * g.m * g.n * (double)g.k_elems * g.batches);
@@ -633,24 +573,12 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
 
   // Decode-sized x · Wᵀ (at most 32 rows against one weight matrix): weight-streaming kernel (gemv.cu).
   const int64_t rows_total = batch * (int64_t)m;
-  if (tb && gemm_mode() != 1 && gemv_enabled() && b_distinct.size() == 1 && rows_total <= 32 && sak == 1 && sbk == 1) {
+  if (tb && gemv_enabled() && b_distinct.size() == 1 && rows_total <= 32 && sak == 1 && sbk == 1) {
     int64_t xo[32];
     int idx = 0;
     for (int64_t bi = 0; bi < batch; bi++)
       for (int i = 0; i < m; i++) xo[idx++] = a_off[(size_t)bi] + (int64_t)i * sam;
     PAI_TRY(gemv_tn(ctx, abase, xo, (int)rows_total, bbase + b_distinct[0], sbn, n, k, fptr(r)));
-    *out = r;
-    return PAI_OK;
-  }
-
-  if (gemm_mode() == 1) {
-    Scratch dao, dbo;
-    PAI_TRY(upload(ctx, a_off.data(), a_off.size() * 8, &dao));
-    PAI_TRY(upload(ctx, b_off.data(), b_off.size() * 8, &dbo));
-    SimtArgs s{abase, bbase, fptr(r), static_cast<int64_t*>(dao.p), static_cast<int64_t*>(dbo.p), sam, sak, sbn, sbk, m, n, k};
-    dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
-    k_gemm_simt<<<grid, 256, 0, ctx->stream>>>(s);
-    PAI_LAUNCH_CHECK("simt gemm");
     *out = r;
     return PAI_OK;
   }

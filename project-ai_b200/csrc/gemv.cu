@@ -553,18 +553,10 @@ static pai_status gemv_tc_segment(pai_ctx* ctx, const float* xh, const float* xl
   *splits_out = (splits > 1 || force_partial) ? splits : 0;
   dim3 grid((unsigned)n_tiles, (unsigned)splits);
   if (np == 16) {
-    static bool attr = false;
-    if (!attr) {
-      PAI_CUDA(cudaFuncSetAttribute(k_gemv_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<16>()));
-      attr = true;
-    }
+    PAI_CUDA(smem_limit(ctx, k_gemv_tc<16>, (int)smem_bytes<16>()));
     PAI_PDL_LAUNCH(launch_pdl(k_gemv_tc<16>, grid, dim3(kThreads), smem_bytes<16>(), ctx->stream, map, a), "gemv tc");
   } else {
-    static bool attr = false;
-    if (!attr) {
-      PAI_CUDA(cudaFuncSetAttribute(k_gemv_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<32>()));
-      attr = true;
-    }
+    PAI_CUDA(smem_limit(ctx, k_gemv_tc<32>, (int)smem_bytes<32>()));
     PAI_PDL_LAUNCH(launch_pdl(k_gemv_tc<32>, grid, dim3(kThreads), smem_bytes<32>(), ctx->stream, map, a), "gemv tc");
   }
   return PAI_OK;

@@ -447,7 +447,7 @@ PAI_API pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_
       float* pp = static_cast<float*>(part.p);
 #define RMS_REG(C)                                                                                              \
   do {                                                                                                          \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k_rmsnorm_bwd_reg<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (smem > 48 * 1024) PAI_CUDA(smem_limit(ctx, k_rmsnorm_bwd_reg<C>, (int)smem));                                  \
     k_rmsnorm_bwd_reg<C><<<blocks, 256, smem, ctx->stream>>>(xp, wp, gp, fptr(rdx), pp, rows, eps);            \
   } while (0)
       switch (chunks) {
@@ -475,7 +475,7 @@ PAI_API pai_status pai_rmsnorm_bwd(pai_ctx* ctx, const pai_tensor* x, const pai_
     if (rpb < nw) rpb = nw;
     blocks = (int)((rows + rpb - 1) / rpb);
     PAI_TRY(scratch(ctx, (size_t)blocks * d * 4, &part));
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k_rmsnorm_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > 48 * 1024) PAI_CUDA(smem_limit(ctx, k_rmsnorm_bwd, (int)smem));
     k_rmsnorm_bwd<<<blocks, threads, smem, ctx->stream>>>(xp, wp, gp, fptr(rdx), static_cast<float*>(part.p), rows, d, eps, rpb);
     PAI_LAUNCH_CHECK("rmsnorm_bwd");
     k_colsum_sliced<<<(d + 31) / 32, 256, 0, ctx->stream>>>(static_cast<float*>(part.p), fptr(rdw), blocks, d);

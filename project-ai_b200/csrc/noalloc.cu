@@ -91,7 +91,7 @@ PAI_API pai_status pai_rmsnorm_bwd_noalloc(pai_ctx* ctx, const pai_tensor* x, co
   int rpb = (int)((rows + blocks - 1) / blocks);
   if (rpb < nw) rpb = nw;
   blocks = (int)((rows + rpb - 1) / rpb);  // <= kNoAllocMaxBlocks, so blocks * d fits the array
-  if (smem > 48 * 1024) PAI_CUDA(cudaFuncSetAttribute(k_rmsnorm_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (smem > 48 * 1024) PAI_CUDA(smem_limit(ctx, k_rmsnorm_bwd, (int)smem));
   k_rmsnorm_bwd<<<blocks, threads, smem, ctx->stream>>>(fptr(*x), fptr(*w), fptr(*g), fptr(*dx), part, rows, d, eps, rpb);
   PAI_LAUNCH_CHECK("rmsnorm_bwd (no allocation)");
   k_colsum<<<(d + 255) / 256, 256, 0, ctx->stream>>>(part, fptr(*dw), blocks, d);

@@ -9,7 +9,10 @@
 #include <numeric>
 #include <thread>
 
+#include <pthread.h>
 #include <unistd.h>
+
+#include <new>
 
 #include "runtime.h"
 
@@ -476,20 +479,21 @@ int TopKTopPSampler::sample(const float* logits, int vocab) {
 // Process-wide worker threads for per-row host work, started once (decode samples every step, and starting threads
 // per step cost about as much as the work): run(n, fn) calls fn(i) for every i in [0, n) on the workers and the
 // calling thread and returns when all are done, rethrowing the first exception. One job runs at a time. The workers
-// are detached and never stopped, so process exit does not wait for them. A forked child has none of its parent's
-// threads, so a process that is not the pool's owner starts its own pool.
+// are detached and never stopped, so process exit does not wait for them.
+//
+// Fork: a child has only the thread that called fork(), and any mutex another parent thread held at that moment is
+// copied locked. A pthread_atfork child handler therefore forgets the parent's pool (its memory is never touched again
+// in the child: its locks may be held by threads that do not exist there) and re-creates the creation lock, so the
+// child's first instance() starts a pool of its own whichever thread of the parent forked and whatever it held.
 namespace {
 class RowPool {
  public:
   static RowPool& instance() {
-    static std::mutex m;
-    static RowPool* pool = nullptr;
-    static pid_t owner = 0;
-    std::lock_guard<std::mutex> g(m);
-    if (!pool || owner != getpid()) {
-      pool = new RowPool((int)std::max(1u, std::thread::hardware_concurrency()) - 1);
-      owner = getpid();
-    }
+    static std::once_flag hook;
+    std::call_once(hook, [] { pthread_atfork(nullptr, nullptr, &RowPool::after_fork_child); });
+    std::lock_guard<std::mutex> g(create_lock());
+    RowPool*& pool = slot();
+    if (!pool) pool = new RowPool((int)std::max(1u, std::thread::hardware_concurrency()) - 1);
     return *pool;
   }
 
@@ -513,6 +517,19 @@ class RowPool {
   }
 
  private:
+  static std::mutex& create_lock() {
+    static std::mutex m;
+    return m;
+  }
+  static RowPool*& slot() {
+    static RowPool* p = nullptr;
+    return p;
+  }
+  static void after_fork_child() {
+    new (&create_lock()) std::mutex();  // unlocked again, whatever its state at the fork
+    slot() = nullptr;                   // the parent's pool stays allocated and unused
+  }
+
   explicit RowPool(int workers) : workers_(workers) {
     for (int i = 0; i < workers; i++) std::thread([this] { loop(); }).detach();
   }
