@@ -421,13 +421,14 @@ def op_sweep(args):
     be.close()
 
 
-def workload_config(name, n, recompute=True):
+def workload_config(name, n, recompute=True, zero1=False):
     c = CONFIGS[name]
     mode = "per-block recompute" if recompute else "stored activations, no recompute"
     return {"workload": f"llama-{name} train step (fwd + {mode} + bwd + AdamW), fp32 semantics",
             "vocab": c["vocab_size"], "d_model": c["embedding_dim"], "layers": c["layer_count"], "heads": c["head_count"],
             "kv_heads": c["kv_head_count"], "ffn": c["ffn_hidden"], "seq_len": c["seq"], "batch_per_gpu": c["batch"],
-            "global_batch": c["batch"] * n, "params": param_count(c), "parallelism": f"dp{n}",
+            "global_batch": c["batch"] * n, "params": param_count(c),
+            "parallelism": f"dp{n}" + (" zero1 (AdamW state sharded)" if zero1 else ""),
             "l2": "working set above L2 (weights alone 4 B x params), no flush needed"}
 
 
@@ -505,6 +506,7 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--config", default="1b", choices=sorted(CONFIGS))
     ap.add_argument("--no-recompute", action="store_true")
+    ap.add_argument("--zero1", action="store_true", help="N>1: shard the AdamW state over the ranks (ZeRO-1)")
     ap.add_argument("--cpu-sample-tokens", type=int, default=None,
                     help="tokens per CPU sample step (default: 16 for 1b, 64 for 125m and tiny)")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
@@ -550,6 +552,7 @@ def main():
                           warmup_steps=0)
     tr = H.Trainer(be, m, tc, 0.9, 0.95)
     tr.set_constant_lr(3e-4)
+    tr.zero1 = args.zero1 and world > 1
 
     def barrier():
         be.sync()
@@ -644,7 +647,8 @@ def main():
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (PcgRng token ids, N(0,0.02) weights)",
-                "config": workload_config(args.config, world, not args.no_recompute), "roofline": roofline,
+                "config": workload_config(args.config, world, not args.no_recompute, args.zero1 and world > 1),
+                "roofline": roofline,
                 "mfu": mf * per_gpu / 1e12 / peak, "hfu": hf * per_gpu / 1e12 / peak,
                 "flops_per_token": {"model": mf, "hardware": hf,
                                     "note": "model = 3 x forward (linear layers, tied LM head, causal attention); "

@@ -248,6 +248,13 @@ pai_status pai_nccl_init(pai_ctx* ctx, const uint8_t id[128], int32_t rank, int3
 /* Sum-all-reduce a bucket of contiguous F32 tensors in place on the communication stream, ordered after all
  * work queued so far on the compute stream; later compute-stream work that touches the bucket waits for it. */
 pai_status pai_allreduce_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n_tensors);
+/* ZeRO-1 exchanges (sharded AdamW state; the reference's AdamW, Optimizers.cs:81-123, keeps every moment on every
+ * device). Rank r owns elements [r·n/W, (r+1)·n/W) of each tensor; n must divide by the world size W. reduce_scatter
+ * sums every rank's tensor and leaves the sum of this rank's shard in place (other elements are unspecified
+ * afterwards); allgather copies each rank's shard into every rank's tensor. Ordered like pai_allreduce_bucket and
+ * completed by pai_allreduce_wait. */
+pai_status pai_reduce_scatter_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n_tensors);
+pai_status pai_allgather_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n_tensors);
 /* Waits on the host, under the communicator's timeout, for every all-reduce issued so far, then orders the compute
  * stream after them. A failed or unfinished exchange (a peer left) aborts the communicator and returns PAI_ERR_NCCL or
  * PAI_ERR_TIMEOUT. Extends the step of ProjectAI.Training/Training.cs:87-113 with the cross-rank gradient sum. */

@@ -150,31 +150,64 @@ PAI_API pai_status pai_nccl_init(pai_ctx* ctx, const uint8_t id[128], int32_t ra
   return PAI_OK;
 }
 
-PAI_API pai_status pai_allreduce_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n) {
-  PAI_TRY(enter(ctx));
-  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+// Enqueues one group of NCCL calls on the communication stream, ordered after the work queued so far on the compute
+// stream; `done` marks its end for pai_allreduce_wait.
+template <class Calls>
+static pai_status exchange(pai_ctx* ctx, const pai_tensor* tensors, int32_t n, bool shard, const char* what, Calls calls) {
   NcclState* s = ctx->nccl;
-  if (!s || !s->comm) return set_error(PAI_ERR_INVALID_OP, "all-reduce without an initialised communicator");
+  if (!s || !s->comm) return set_error(PAI_ERR_INVALID_OP, "%s without an initialised communicator", what);
   for (int i = 0; i < n; i++) {
     PAI_TRY(check_view(ctx, &tensors[i], "bucket tensor"));
-    if (!is_dense(tensors[i])) return set_error(PAI_ERR_ARGUMENT, "all-reduce tensors must be contiguous");
+    if (!is_dense(tensors[i])) return set_error(PAI_ERR_ARGUMENT, "%s tensors must be contiguous", what);
+    if (shard && numel(tensors[i]) % s->world != 0)
+      return set_error(PAI_ERR_ARGUMENT, "%s: %lld elements do not split into %d equal shards", what,
+                       (long long)numel(tensors[i]), s->world);
   }
   if (s->world == 1) return PAI_OK;
   PAI_CUDA(cudaEventRecord(s->ready, ctx->stream));
   PAI_CUDA(cudaStreamWaitEvent(ctx->comm_stream, s->ready, 0));
   ncclResult_t r = ncclGroupStart();
   if (r == ncclSuccess) {
-    for (int i = 0; i < n && r == ncclSuccess; i++) {
-      float* p = fptr(tensors[i]);
-      r = ncclAllReduce(p, p, (size_t)numel(tensors[i]), ncclFloat, ncclSum, s->comm, ctx->comm_stream);
-    }
+    for (int i = 0; i < n && r == ncclSuccess; i++) r = calls(s, tensors[i]);
     ncclResult_t r2 = ncclGroupEnd();
     if (r == ncclSuccess) r = r2;
   }
-  PAI_TRY(nccl_wait(s, r, "all-reduce"));
+  PAI_TRY(nccl_wait(s, r, what));
   PAI_CUDA(cudaEventRecord(s->done, ctx->comm_stream));
   s->pending = true;
   return PAI_OK;
+}
+
+PAI_API pai_status pai_allreduce_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  return exchange(ctx, tensors, n, false, "all-reduce", [&](NcclState* s, const pai_tensor& t) {
+    float* p = fptr(t);
+    return ncclAllReduce(p, p, (size_t)numel(t), ncclFloat, ncclSum, s->comm, ctx->comm_stream);
+  });
+}
+
+// ZeRO-1: rank r owns elements [r·n/W, (r+1)·n/W) of every tensor. The reduce-scatter leaves the cross-rank sum of
+// that shard in place (the rest of the tensor is unspecified afterwards); the all-gather copies every rank's shard
+// into all ranks' tensors. Both are NCCL's in-place forms (the shard at offset rank x shard size).
+PAI_API pai_status pai_reduce_scatter_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  return exchange(ctx, tensors, n, true, "reduce-scatter", [&](NcclState* s, const pai_tensor& t) {
+    float* p = fptr(t);
+    const size_t shard = (size_t)(numel(t) / s->world);
+    return ncclReduceScatter(p, p + shard * (size_t)s->rank, shard, ncclFloat, ncclSum, s->comm, ctx->comm_stream);
+  });
+}
+
+PAI_API pai_status pai_allgather_bucket(pai_ctx* ctx, const pai_tensor* tensors, int32_t n) {
+  PAI_TRY(enter(ctx));
+  std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+  return exchange(ctx, tensors, n, true, "all-gather", [&](NcclState* s, const pai_tensor& t) {
+    float* p = fptr(t);
+    const size_t shard = (size_t)(numel(t) / s->world);
+    return ncclAllGather(p + shard * (size_t)s->rank, p, shard, ncclFloat, s->comm, ctx->comm_stream);
+  });
 }
 
 PAI_API pai_status pai_allreduce_wait(pai_ctx* ctx) {

@@ -749,6 +749,28 @@ public sealed unsafe class CudaComputeBackend : IComputeBackend
         }
     }
 
+    /// <summary>
+    /// ZeRO-1: sums these gradients across ranks leaving this rank's shard (elements [r·n/W, (r+1)·n/W) of each
+    /// flattened tensor) in place, for an AdamW step on the shard alone. Every tensor's element count must divide by
+    /// the world size.
+    /// </summary>
+    public void GradientShardsReady(IReadOnlyList<Tensor> gradients) => ShardExchange(gradients, scatter: true);
+
+    /// <summary>ZeRO-1: copies every rank's updated shard into all ranks' parameters (after the sharded AdamW step).</summary>
+    public void GatherParameterShards(IReadOnlyList<Tensor> parameters) => ShardExchange(parameters, scatter: false);
+
+    private void ShardExchange(IReadOnlyList<Tensor> tensors, bool scatter)
+    {
+        lock (_gate)
+        {
+            Drain();
+            var ds = new PaiTensor[tensors.Count];
+            for (int i = 0; i < ds.Length; i++) ds[i] = Desc(tensors[i]);
+            fixed (PaiTensor* p = ds)
+                Native.Check(scatter ? Native.ReduceScatterBucket(Ctx, p, ds.Length) : Native.AllgatherBucket(Ctx, p, ds.Length));
+        }
+    }
+
     /// <summary>Waits (bounded) for every exchange issued so far; the optimizer step comes after.</summary>
     public void WaitForGradients()
     {

@@ -101,6 +101,8 @@ internal static unsafe partial class Native
     [LibraryImport(Lib, EntryPoint = "pai_nccl_unique_id")] internal static partial int NcclUniqueId(byte* idOut);
     [LibraryImport(Lib, EntryPoint = "pai_nccl_init")] internal static partial int NcclInit(IntPtr ctx, byte* id, int rank, int worldSize, int timeoutMs);
     [LibraryImport(Lib, EntryPoint = "pai_allreduce_bucket")] internal static partial int AllreduceBucket(IntPtr ctx, PaiTensor* tensors, int nTensors);
+    [LibraryImport(Lib, EntryPoint = "pai_reduce_scatter_bucket")] internal static partial int ReduceScatterBucket(IntPtr ctx, PaiTensor* tensors, int nTensors);
+    [LibraryImport(Lib, EntryPoint = "pai_allgather_bucket")] internal static partial int AllgatherBucket(IntPtr ctx, PaiTensor* tensors, int nTensors);
     [LibraryImport(Lib, EntryPoint = "pai_allreduce_wait")] internal static partial int AllreduceWait(IntPtr ctx);
     [LibraryImport(Lib, EntryPoint = "pai_nccl_abort")] internal static partial int NcclAbort(IntPtr ctx);
     [LibraryImport(Lib, EntryPoint = "pai_dp_stats")] internal static partial int DpStats(IntPtr ctx, double* exposedMs, long* steps);

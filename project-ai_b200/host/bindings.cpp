@@ -341,6 +341,27 @@ PYBIND11_MODULE(_paihost, m) {
           fn(grads);
         };
         t.trainer->allreduce_wait = [] {};
+      })
+      // ZeRO-1 (sharded AdamW state); with CPU collectives substituted for the backend's NCCL exchanges in tests
+      .def_property("zero1", [](PyTrainer& t) { return t.trainer->zero1; },
+                    [](PyTrainer& t, bool v) { t.trainer->zero1 = v; })
+      .def_property("rank", [](PyTrainer& t) { return t.trainer->rank; },
+                    [](PyTrainer& t, int v) { t.trainer->rank = v; })
+      .def("set_shard_exchange", [](PyTrainer& t, py::function reduce_scatter, py::function allgather) {
+        t.trainer->reduce_scatter = [reduce_scatter](const std::vector<Tensor>& g) {
+          py::gil_scoped_acquire gil;
+          reduce_scatter(g);
+        };
+        t.trainer->allgather = [allgather](const std::vector<Tensor>& p) {
+          py::gil_scoped_acquire gil;
+          allgather(p);
+        };
+      })
+      .def("moment_elements", [](PyTrainer& t) {
+        int64_t n = 0;
+        for (auto& kv : t.trainer->optimizer->state)
+          if (kv.second.m) n += kv.second.m->numel() + kv.second.v->numel();
+        return n;
       });
 
   py::class_<TopKTopPSampler>(m, "TopKTopPSampler")

@@ -151,6 +151,10 @@ class NativeBackend {
   void nccl_init(const uint8_t id[128], int rank, int world, int timeout_ms);
   void allreduce(const std::vector<Tensor>& grads);
   void allreduce_wait();
+  // ZeRO-1 exchanges: in-place NCCL reduce-scatter / all-gather of contiguous tensors whose element count divides by
+  // the world size (rank r's shard is elements [r·n/W, (r+1)·n/W)); completed by allreduce_wait.
+  void reduce_scatter(const std::vector<Tensor>& grads);
+  void allgather(const std::vector<Tensor>& params);
   // Exposed all-reduce device time (ms summed over steps) and the step count since the last call.
   std::pair<double, int64_t> dp_stats();
   int dp_world = 1, dp_rank = 0;
@@ -472,6 +476,11 @@ class AdamW {
   float lr, b1, b2, eps, wd;
   int step_count = 0;
   float grad_scale = 1.0f;  // 1/world for a data-parallel sum
+  // ZeRO-1: with shard_world > 1 this rank updates only its shard of each parameter whose element count divides by
+  // shard_world (elements [r·n/W, (r+1)·n/W) of the flattened tensor) and keeps moments for that shard alone; the
+  // others are updated whole. The caller exchanges the shards (reduce-scatter before, all-gather after).
+  int shard_rank = 0, shard_world = 1;
+  bool sharded(const Tensor& p) const { return shard_world > 1 && p->numel() % shard_world == 0; }
   struct State { Tensor m, v; int t = 0; };
   std::map<TensorImpl*, State> state;
 
@@ -508,8 +517,15 @@ class Trainer {
   // Data parallel: the number of ranks and the bucket exchange. Default: the backend's NCCL communicator
   // (world = backend.dp_world); callers may substitute another sum-all-reduce (e.g. a CPU collective in tests).
   int world = 0;  // 0: take the backend's dp_world
+  int rank = -1;  // -1: take the backend's dp_rank
   std::function<void(const std::vector<Tensor>&)> allreduce;
   std::function<void()> allreduce_wait;
+  // ZeRO-1 (optimizer state sharded over the ranks): gradients of shardable parameters are reduce-scattered instead
+  // of all-reduced, AdamW updates this rank's shard, and the parameters are all-gathered after the update. The
+  // exchanges default to the backend's NCCL communicator; tests substitute CPU collectives.
+  bool zero1 = false;
+  std::function<void(const std::vector<Tensor>&)> reduce_scatter;
+  std::function<void(const std::vector<Tensor>&)> allgather;
 
  private:
   NativeBackend* be_;

@@ -266,6 +266,8 @@ void TensorImpl::backward(const Tensor& seed) {
   X(allreduce_bucket, int (*)(pai_ctx*, const pai_tensor*, int32_t))                                                     \
   X(allreduce_wait, int (*)(pai_ctx*))                                                                                  \
   X(dp_stats, int (*)(pai_ctx*, double*, int64_t*))                                                                      \
+  X(reduce_scatter_bucket, int (*)(pai_ctx*, const pai_tensor*, int32_t))                                                \
+  X(allgather_bucket, int (*)(pai_ctx*, const pai_tensor*, int32_t))                                                     \
   X(timer_start, int (*)(pai_ctx*))                                                                                      \
   X(timer_stop, int (*)(pai_ctx*, float*))                                                                               \
   X(launch_count, int (*)(pai_ctx*, int64_t*))                                                                           \
@@ -665,6 +667,25 @@ void NativeBackend::allreduce(const std::vector<Tensor>& grads) {
   d.reserve(grads.size());
   for (const auto& g : grads) d.push_back(g->desc());
   check(fn_->allreduce_bucket(ctx_, d.data(), (int32_t)d.size()));
+}
+
+void NativeBackend::reduce_scatter(const std::vector<Tensor>& grads) {
+  if (dp_world <= 1 || grads.empty()) return;
+  if (!fn_->reduce_scatter_bucket) throw BackendError("backend has no reduce-scatter");
+  std::vector<pai_tensor> d;
+  for (const auto& g : grads) d.push_back(g->desc());
+  check(fn_->reduce_scatter_bucket(ctx_, d.data(), (int32_t)d.size()));
+}
+
+void NativeBackend::allgather(const std::vector<Tensor>& params) {
+  if (dp_world <= 1 || params.empty()) return;
+  if (!fn_->allgather_bucket) throw BackendError("backend has no all-gather");
+  std::vector<pai_tensor> d;
+  for (const auto& p : params) {
+    d.push_back(p->desc());
+    invalidate_shadow(p);
+  }
+  check(fn_->allgather_bucket(ctx_, d.data(), (int32_t)d.size()));
 }
 
 std::pair<double, int64_t> NativeBackend::dp_stats() {

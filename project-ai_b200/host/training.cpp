@@ -13,7 +13,15 @@ namespace paihost {
 AdamW::AdamW(std::vector<Tensor> params, NativeBackend* be, float lr_, float b1_, float b2_, float eps_, float wd_)
     : lr(lr_), b1(b1_), b2(b2_), eps(eps_), wd(wd_), params_(std::move(params)), be_(be) {}
 
+// This rank's shard of a flattened parameter (or gradient): elements [r·n/W, (r+1)·n/W).
+static Tensor shard_of(const Tensor& t, int rank, int world) {
+  const int64_t n = t->numel(), s = n / world;
+  return t->reshape({(int)n})->slice(0, (int)(rank * s), (int)s);
+}
+
 // AdamW.Step (Optimizers.cs:81-123). The fused path runs the same per-element operations in one kernel, in place.
+// Under ZeRO-1 (shard_world > 1) a shardable parameter is updated through views of its shard (the same element
+// operations on fewer elements), with moments of the shard's size.
 void AdamW::step() {
   step_count++;
   float cur_lr = schedule ? schedule(step_count) : lr;
@@ -23,24 +31,29 @@ void AdamW::step() {
     for (const auto& p : params_) {
       if (!p->grad) continue;
       State& s = state[p.get()];
+      const bool sh = sharded(p);
+      const Tensor pv = sh ? shard_of(p, shard_rank, shard_world) : p;
+      const Tensor gv = sh ? shard_of(p->grad, shard_rank, shard_world) : p->grad;
       if (!s.m) {
-        s.m = be_->allocate(p->shape);  // zero-initialised moments, persisting across steps
-        s.v = be_->allocate(p->shape);
+        s.m = be_->allocate(pv->shape);  // zero-initialised moments, persisting across steps
+        s.v = be_->allocate(pv->shape);
         be_->keep_alive(s.m);
         be_->keep_alive(s.v);
       }
       s.t += 1;
-      be_->adamw_step(p, p->grad, s.m, s.v, cur_lr, b1, b2, eps, wd, s.t, grad_scale);
+      be_->adamw_step(pv, gv, s.m, s.v, cur_lr, b1, b2, eps, wd, s.t, grad_scale);
     }
     return;
   }
   be_->begin_scope();
   try {
-    for (const auto& p : params_) {
-      if (!p->grad) continue;
-      Tensor g = p->grad;
+    for (const auto& param : params_) {
+      if (!param->grad) continue;
+      const bool sh = sharded(param);
+      const Tensor p = sh ? shard_of(param, shard_rank, shard_world) : param;
+      Tensor g = sh ? shard_of(param->grad, shard_rank, shard_world) : param->grad;
       if (grad_scale != 1.0f) g = be_->mul_scalar(g, grad_scale);
-      State& s = state[p.get()];
+      State& s = state[param.get()];
       Tensor prev_m = s.m, prev_v = s.v;
       if (!s.m) s.m = be_->allocate(p->shape);
       if (!s.v) s.v = be_->allocate(p->shape);
@@ -126,11 +139,23 @@ float Trainer::step_tensors(const std::vector<Tensor>& inputs, const std::vector
   int micro_steps = std::max(1, (int)inputs.size());
   if ((int)targets.size() != micro_steps) throw ArgumentError("inputs and targets must hold the same number of micro-batches");
   const int ranks = world > 0 ? world : be_->dp_world;
+  const int my_rank = rank >= 0 ? rank : be_->dp_rank;
   const bool dp = ranks > 1;
-  auto exchange = [this](const std::vector<Tensor>& g) {
+  const bool shard = dp && zero1;
+  optimizer->shard_world = shard ? ranks : 1;
+  optimizer->shard_rank = shard ? my_rank : 0;
+  auto exchange = [this, shard](const std::vector<Tensor>& g) {
     if (g.empty()) return;
-    if (allreduce) allreduce(g);
-    else be_->allreduce(g);
+    std::vector<Tensor> whole, split;
+    for (const auto& t : g) (shard && t->numel() % optimizer->shard_world == 0 ? split : whole).push_back(t);
+    if (!whole.empty()) {
+      if (allreduce) allreduce(whole);
+      else be_->allreduce(whole);
+    }
+    if (!split.empty()) {
+      if (reduce_scatter) reduce_scatter(split);
+      else be_->reduce_scatter(split);
+    }
   };
   optimizer->grad_scale = dp ? 1.0f / (float)ranks : 1.0f;
   optimizer->zero_grad();
@@ -177,6 +202,16 @@ float Trainer::step_tensors(const std::vector<Tensor>& inputs, const std::vector
     else if (!allreduce) be_->allreduce_wait();
   }
   optimizer->step();
+  if (shard) {
+    // every rank updated its shards: gather them so all replicas hold the full new parameters
+    std::vector<Tensor> split;
+    for (const auto& p : params_)
+      if (p->grad && optimizer->sharded(p)) split.push_back(p);
+    if (allgather) allgather(split);
+    else be_->allgather(split);
+    if (allreduce_wait) allreduce_wait();
+    else if (!allgather) be_->allreduce_wait();
+  }
   return step_loss;
 }
 

@@ -46,7 +46,7 @@ def test_oracle_exports_contract_ops():
     for n in declared():
         op = n[len("pai_"):]
         if op in {"sdpa_fwd", "sdpa_bwd", "rmsnorm_bwd", "silu_mul_fwd", "silu_mul_bwd", "cross_entropy_fused", "adamw_step",
-                  "nccl_unique_id", "nccl_init", "allreduce_bucket", "allreduce_wait", "nccl_abort", "dp_stats", "check_device_error",
+                  "nccl_unique_id", "nccl_init", "allreduce_bucket", "allreduce_wait", "nccl_abort", "dp_stats", "reduce_scatter_bucket", "allgather_bucket", "check_device_error",
                   "timer_start", "timer_stop", "launch_count", "kernel_timing", "kernel_stats", "rmsnorm_bwd_noalloc",
                   "write", "gather_dev", "rotary_at", "kv_append", "sdpa_decode", "graph_begin", "graph_end",
                   "graph_launch", "graph_destroy", "linear_fused", "rope_append", "attn_decode_step", "argmax_rows"}:

@@ -131,7 +131,7 @@ def test_dead_rank_fails_the_collective_instead_of_hanging(tmp_path):
     assert str(r0["status"]).startswith("error"), str(r0["status"])
 
 
-def _nccl_rank(rank, world, port, out_dir):
+def _nccl_rank(rank, world, port, out_dir, zero1=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
     torch.cuda.set_device(rank)
@@ -146,10 +146,12 @@ def _nccl_rank(rank, world, port, out_dir):
     dist.broadcast_object_list(uid, src=0)
     be.nccl_init(uid[0], rank, world, 60000)
     m, tr = make_trainer(H, be, world)
+    tr.zero1 = zero1
     x, y = full_batch()
     per = 4 // world
     tr.step([x[rank * per:(rank + 1) * per].copy()], [y[rank * per:(rank + 1) * per].copy()])
-    np.savez(out_dir / f"rank{rank}.npz", **{"p_" + n: be.to_host(p) for n, p in m.named_parameters()},
+    tag = "zero1_" if zero1 else ""
+    np.savez(out_dir / f"{tag}rank{rank}.npz", **{"p_" + n: be.to_host(p) for n, p in m.named_parameters()},
              **{"g_" + n: be.to_host(p.grad) for n, p in m.named_parameters()})
     dist.barrier()
     dist.destroy_process_group()
@@ -170,3 +172,97 @@ def test_nccl_two_gpus_match_full_batch(tmp_path):
         np.testing.assert_array_equal(r0["g_" + n], r1["g_" + n])
         np.testing.assert_allclose(r0["g_" + n] / 2, ref_g[n], rtol=1e-4, atol=1e-4 * np.abs(ref_g[n]).max(), err_msg=n)
         np.testing.assert_array_equal(r0["p_" + n], r1["p_" + n])
+
+
+# ---------------------------------------------------------------- ZeRO-1 (sharded AdamW state)
+def _zero1_rank(rank, world, port, out_dir):
+    """Two steps of the same data-parallel training, once with replicated AdamW (all-reduce) and once with ZeRO-1
+    (reduce-scatter, AdamW on this rank's shard, all-gather), from the same initial weights."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(ROOT / "oracle" / "build" / "liboracle.so"), "oracle_", 0)
+
+    def allreduce(grads):
+        for t in grads:
+            host = torch.from_numpy(be.to_host(t).copy())
+            dist.all_reduce(host)
+            be.copy(be.from_host(host.numpy()), t)
+
+    def shard_view(t):
+        n = t.numel()
+        return t.reshape([n]).slice(0, rank * (n // world), n // world)
+
+    def reduce_scatter(grads):
+        for t in grads:
+            full = torch.from_numpy(be.to_host(t).copy()).reshape(-1)
+            mine = torch.empty(full.numel() // world)
+            dist.reduce_scatter_tensor(mine, full)
+            be.copy(be.from_host(mine.numpy()), shard_view(t))
+
+    def allgather(params):
+        for p in params:
+            mine = torch.from_numpy(be.to_host(shard_view(p)).copy())
+            full = torch.empty(mine.numel() * world)
+            dist.all_gather_into_tensor(full, mine)
+            be.copy(be.from_host(full.numpy().reshape(be.to_host(p).shape)), p)
+
+    x, y = full_batch()
+    per = 4 // world
+    out = {}
+    for mode in ("replicated", "zero1"):
+        m, tr = make_trainer(H, be, world)
+        tr.world = world
+        tr.rank = rank
+        tr.set_allreduce(allreduce)
+        if mode == "zero1":
+            tr.zero1 = True
+            tr.set_shard_exchange(reduce_scatter, allgather)
+        for step in range(2):
+            xs = np.roll(x, step, axis=0)[rank * per:(rank + 1) * per].copy()
+            ys = np.roll(y, step, axis=0)[rank * per:(rank + 1) * per].copy()
+            tr.step([xs], [ys])
+        out.update({f"{mode}_p_{n}": be.to_host(p) for n, p in m.named_parameters()})
+        out[f"{mode}_moments"] = np.array(tr.moment_elements())
+        out["params"] = np.array(sum(be.to_host(p).size for _, p in m.named_parameters()))
+    np.savez(out_dir / f"zero1_rank{rank}.npz", **out)
+    dist.destroy_process_group()
+
+
+def test_zero1_matches_replicated_adamw_bit_for_bit(tmp_path):
+    port = free_port()
+    mp.spawn(_zero1_rank, args=(2, port, tmp_path), nprocs=2, join=True)
+    r0 = np.load(tmp_path / "zero1_rank0.npz")
+    r1 = np.load(tmp_path / "zero1_rank1.npz")
+    names = [k[len("replicated_p_"):] for k in r0.files if k.startswith("replicated_p_")]
+    assert names
+    for n in names:
+        # the shards each rank updated, gathered, equal the replicated update bit for bit on both ranks
+        np.testing.assert_array_equal(r0["zero1_p_" + n].view(np.uint32), r0["replicated_p_" + n].view(np.uint32), n)
+        np.testing.assert_array_equal(r1["zero1_p_" + n].view(np.uint32), r0["zero1_p_" + n].view(np.uint32), n)
+    # every parameter of the tiny model splits in two: each rank holds the moments of half of them
+    assert int(r0["replicated_moments"]) == 2 * int(r0["params"])
+    assert int(r0["zero1_moments"]) == int(r0["params"])
+
+
+@pytest.mark.gpu
+def test_nccl_zero1_two_gpus_matches_replicated(tmp_path):
+    """ZeRO-1 over NCCL (in-place reduce-scatter, AdamW on the shard, in-place all-gather) gives the replicated
+    update bit for bit: with two ranks both exchanges sum the same two values."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    port = free_port()
+    mp.spawn(_nccl_rank, args=(2, port, tmp_path, False), nprocs=2, join=True)
+    port = free_port()
+    mp.spawn(_nccl_rank, args=(2, port, tmp_path, True), nprocs=2, join=True)
+    for r in (0, 1):
+        a = np.load(tmp_path / f"rank{r}.npz")
+        b = np.load(tmp_path / f"zero1_rank{r}.npz")
+        for k in a.files:
+            if k.startswith("p_"):
+                np.testing.assert_array_equal(a[k].view(np.uint32), b[k].view(np.uint32), k)

@@ -97,7 +97,7 @@ def test_1b_greedy_decode_teacher_forced(backends):
     seqn = np.array([prompt + toks[:-1]], np.float32)  # position prompt_len-1+i predicts toks[i]
     with H.no_grad():
         lc = cuda.to_host(mc.forward(cuda.from_host(seqn)))[0, prompt_len - 1:]
-    assert cuda.check_device_error() == 0
+    cuda.check_device_error()  # raises if a kernel's bounded wait timed out
     del mc
     mo = H.LlamaModel(oracle, cfg, seed=0, init="normal0.02")
     with H.no_grad():
