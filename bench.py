@@ -363,14 +363,14 @@ def op_sweep(args):
             be.scope_end()
             for t in (q, k, v, do):
                 be.release(t)
-    if args.op in ("all", "decode"):
+    if args.op in ("all", "decode", "decode-attn"):
         # 1B decode: every weight shape of a layer plus the LM head, x·Wᵀ for 1 and 32 rows; enough weight copies are
         # cycled that each timed call reads its W from HBM, not L2 (--shape rows,k,n: that product only)
         gemv_shapes = [((n, k), (1, 32)) for n, k in ((2048, 2048), (512, 2048), (5632, 2048), (2048, 5632), (32000, 2048))]
         if args.op == "decode" and args.shape:
             r0, k0, n0 = (int(v) for v in args.shape.split(","))
             gemv_shapes = [((n0, k0), (r0,))]
-        for (n, k), row_counts in gemv_shapes:
+        for (n, k), row_counts in (gemv_shapes if args.op != "decode-attn" else []):
             copies = max(1, -(-300_000_000 // (n * k * 4)))
             ws = [randt(n, k) for _ in range(copies)]
             for rows_ in row_counts:
@@ -385,8 +385,13 @@ def op_sweep(args):
                 be.release(x)
             for t in ws:
                 be.release(t)
-        for B in (() if (args.op == "decode" and args.shape) else (1, 32)):
-            Hh, KV, D, L = 32, 8, 64, 768
+        attn_batches = (1, 32)
+        if args.op == "decode" and args.shape:
+            attn_batches = ()
+        elif args.op == "decode-attn" and args.shape:
+            attn_batches = (int(args.shape),)
+        for B in attn_batches:
+            Hh, KV, D, L = 32, 8, 64, args.decode_cache_len
             q = randt(B, Hh, 1, D)
             kc, vc = randt(B, KV, L, D), randt(B, KV, L, D)
             be.scope_begin()
@@ -405,6 +410,8 @@ def op_sweep(args):
         xv = cabi.transpose(xr, 1, 2)
         emit("rope (strided q view)", [4, 32, 2048, 64], timed(lambda: be.rotary(xv, cs, sn), args.steps), 2 * 8192 * 2048 * 4, "GB/s", hbm)
         emit("swiglu silu(gate)*up", [8192, 2048], timed(lambda: be.silu_mul_fwd(x, g), args.steps), 3 * 8192 * 2048 * 4, "GB/s", hbm)
+        emit("swiglu backward", [8192, 2048], timed(lambda: be.silu_mul_bwd(x, g, x), args.steps), 5 * 8192 * 2048 * 4, "GB/s", hbm)
+        emit("residual add", [8192, 2048], timed(lambda: be.add(x, g), args.steps), 3 * 8192 * 2048 * 4, "GB/s", hbm)
         be.scope_end()
         logits = randt(8192, 32000)
         targets = rng.randint(0, 32000, size=8192).astype(np.int32)
@@ -413,7 +420,7 @@ def op_sweep(args):
              2 * 8192 * 32000 * 4, "GB/s", hbm)
         be.scope_end()
         be.release(logits)
-        n = 1_100_000_000 if args.op == "hbm" or args.op == "all" else 100_000_000
+        n = args.adamw_elements
         p = be.allocate((n,))
         gg, mm, vv = be.allocate((n,)), be.allocate((n,)), be.allocate((n,))
         emit("adamw (fused, in place)", [n], timed(lambda: be.adamw_step(p, gg, mm, vv, 3e-4, 0.9, 0.95, 1e-8, 0.1, 1),
@@ -511,9 +518,12 @@ def main():
                     help="tokens per CPU sample step (default: 16 for 1b, 64 for 125m and tiny)")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--skip-extra", action="store_true", help="leave the no-recompute and 125M runs out of the N=1 line")
-    ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm", "decode"],
+    ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm", "decode", "decode-attn"],
                     help="op-level sweep instead of the training step")
-    ap.add_argument("--shape", default=None, help="M,K,N for --op gemm; rows,K,N for --op decode; B,H,S,D for --op attention")
+    ap.add_argument("--shape", default=None, help="M,K,N for --op gemm; rows,K,N for --op decode; B,H,S,D for --op attention; "
+                                                  "the batch for --op decode-attn")
+    ap.add_argument("--adamw-elements", type=int, default=1_100_000_000, help="--op hbm: AdamW parameter count")
+    ap.add_argument("--decode-cache-len", type=int, default=768, help="--op decode: cached positions for decode attention")
     ap.add_argument("--skip-decode", action="store_true", help="leave the ~1B decode measurement out of the N=1 line")
     ap.add_argument("--decode-only", action="store_true", help="print only the decode measurement")
     ap.add_argument("--decode-tokens", type=int, default=256)

@@ -161,6 +161,7 @@ PYBIND11_MODULE(_paihost, m) {
         return py::bytes(reinterpret_cast<char*>(id), 128);
       })
       .def("dp_stats", [](NativeBackend& be) { return be.dp_stats(); })
+      .def("nccl_abort", &NativeBackend::nccl_abort)
       .def("nccl_init", [](NativeBackend& be, py::bytes id, int rank, int world, int timeout_ms) {
         std::string s = id;
         if (s.size() != 128) throw ArgumentError("NCCL unique id must be 128 bytes");

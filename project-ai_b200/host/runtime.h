@@ -151,6 +151,8 @@ class NativeBackend {
   void nccl_init(const uint8_t id[128], int rank, int world, int timeout_ms);
   void allreduce(const std::vector<Tensor>& grads);
   void allreduce_wait();
+  // Aborts the communicator (no wait for peers): a rank leaving a job, or after a failed exchange.
+  void nccl_abort();
   // ZeRO-1 exchanges: in-place NCCL reduce-scatter / all-gather of contiguous tensors whose element count divides by
   // the world size (rank r's shard is elements [r·n/W, (r+1)·n/W)); completed by allreduce_wait.
   void reduce_scatter(const std::vector<Tensor>& grads);

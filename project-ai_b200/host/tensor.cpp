@@ -266,6 +266,7 @@ void TensorImpl::backward(const Tensor& seed) {
   X(allreduce_bucket, int (*)(pai_ctx*, const pai_tensor*, int32_t))                                                     \
   X(allreduce_wait, int (*)(pai_ctx*))                                                                                  \
   X(dp_stats, int (*)(pai_ctx*, double*, int64_t*))                                                                      \
+  X(nccl_abort, int (*)(pai_ctx*))                                                                                       \
   X(reduce_scatter_bucket, int (*)(pai_ctx*, const pai_tensor*, int32_t))                                                \
   X(allgather_bucket, int (*)(pai_ctx*, const pai_tensor*, int32_t))                                                     \
   X(timer_start, int (*)(pai_ctx*))                                                                                      \
@@ -667,6 +668,10 @@ void NativeBackend::allreduce(const std::vector<Tensor>& grads) {
   d.reserve(grads.size());
   for (const auto& g : grads) d.push_back(g->desc());
   check(fn_->allreduce_bucket(ctx_, d.data(), (int32_t)d.size()));
+}
+
+void NativeBackend::nccl_abort() {
+  if (fn_->nccl_abort) check(fn_->nccl_abort(ctx_));
 }
 
 void NativeBackend::reduce_scatter(const std::vector<Tensor>& grads) {

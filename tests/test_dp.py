@@ -266,3 +266,60 @@ def test_nccl_zero1_two_gpus_matches_replicated(tmp_path):
         for k in a.files:
             if k.startswith("p_"):
                 np.testing.assert_array_equal(a[k].view(np.uint32), b[k].view(np.uint32), k)
+
+
+def _nccl_leave_rank(rank, world, port, out_dir):
+    """Step 1 on both ranks; then rank 1 leaves (no further collective, nothing in flight) and rank 0 starts step 2.
+    Rank 1 stays alive, its memory still mapped, until rank 0 has reported, then aborts its own communicator."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    pai = __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", rank)
+    uid = [be.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    be.nccl_init(uid[0], rank, world, 5000)  # every exchange is bounded by 5 s
+    m, tr = make_trainer(H, be, world)
+    x, y = full_batch()
+    per = 4 // world
+    xs, ys = x[rank * per:(rank + 1) * per].copy(), y[rank * per:(rank + 1) * per].copy()
+    tr.step([xs], [ys])
+    be.sync()
+    dist.barrier()  # host-side (gloo): both ranks finished step 1, no kernel or collective in flight
+    done = out_dir / "survivor_done"
+    if rank == 1:
+        for _ in range(1200):  # left the job; waits (at most 120 s) for the survivor's verdict
+            if done.exists():
+                break
+            time.sleep(0.1)
+        be.nccl_abort()
+        return
+    t0 = time.time()
+    try:
+        tr.step([xs], [ys])
+        status = "ok"
+    except Exception as e:  # the exchange with the departed peer must fail within the deadline
+        status = f"error: {type(e).__name__}: {e}"
+    np.savez(out_dir / "leave_rank0.npz", status=status, elapsed=time.time() - t0)
+    done.touch()
+
+
+@pytest.mark.gpu
+def test_nccl_peer_leaving_between_steps_fails_within_the_deadline(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    port = free_port()
+    ctx = mp.start_processes(_nccl_leave_rank, args=(2, port, tmp_path), nprocs=2, join=False, start_method="spawn")
+    for p in ctx.processes:
+        p.join(180)
+        assert not p.is_alive(), "a rank hung"
+    r0 = np.load(tmp_path / "leave_rank0.npz")
+    status = str(r0["status"])
+    assert status.startswith("error"), status
+    assert "timeout" in status.lower() or "nccl" in status.lower(), status
+    assert float(r0["elapsed"]) < 60.0, float(r0["elapsed"])
