@@ -15,6 +15,10 @@
 //                     ring (K, V, Kᵀ); dS goes to TMEM as the A operand of dQ += dS·K.
 // All operands are 64-row SWIZZLE_128B hi/lo tiles from k_attn_pack; 128-row A operands are assembled in shared
 // memory from two 64-row tiles. Every wait is bounded (device error flag on timeout).
+// Accuracy: the gradient products of each streamed block go into a fresh TMEM accumulator, which the element-wise
+// warps add into fp32 registers (IEEE round-to-nearest) before the next block's products overwrite it: the tensor
+// core's own accumulation over the hundreds of blocks a long sequence streams (x the GQA group) drifts from the
+// float64 result far more than a rounded fp32 sum does.
 #include <math.h>
 
 #include "common.cuh"
@@ -114,12 +118,34 @@ __device__ __forceinline__ void kv_ring_item(int i, int N, int& n, int& type) {
   }
 }
 
+// 16 registers per thread -> 16 consecutive TMEM columns of this warp's lanes (completion: tmem_st_wait()).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
 __device__ __forceinline__ void store_hilo(uint32_t hi_addr, uint32_t lo_addr, const float* x) {
-  float hi[32], lo[32];
 #pragma unroll
-  for (int c = 0; c < 32; c++) split_tf32_fast(x[c], hi[c], lo[c]);
-  tmem_st32(hi_addr, hi);
-  tmem_st32(lo_addr, lo);
+  for (int h = 0; h < 2; h++) {
+    float hi[16], lo[16];
+#pragma unroll
+    for (int c = 0; c < 16; c++) split_tf32_fast(x[16 * h + c], hi[c], lo[c]);
+    tmem_st16(hi_addr + 16 * h, hi);
+    tmem_st16(lo_addr + 16 * h, lo);
+  }
+}
+
+// acc += 32 TMEM columns of this warp's lanes (one block's partial gradient rows).
+__device__ __forceinline__ void add_partial(uint32_t taddr, float* acc) {
+  float v[32];
+  tmem_ld32(taddr, v);
+#pragma unroll
+  for (int c = 0; c < 32; c++) acc[c] += v[c];
 }
 
 // ---------------------------------------------------------------- dK, dV
@@ -225,8 +251,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[t2 % kSlots], (t2 / kSlots) & 1) ||
             !mbar_wait(&ring_full[t3 % kSlots], (t3 / kSlots) & 1)) { ok = false; break; }
         fence_after();
-        mma_tmem_tile(tmem + cDV, tmem + cPhi, tmem + cPlo, ring + (t2 % kSlots) * kTile, idesc, n > 0);    // dV += Pᵀ·dO
-        mma_tmem_tile(tmem + cDK, tmem + cDShi, tmem + cDSlo, ring + (t3 % kSlots) * kTile, idesc, n > 0);  // dK += dSᵀ·qs
+        mma_tmem_tile(tmem + cDV, tmem + cPhi, tmem + cPlo, ring + (t2 % kSlots) * kTile, idesc, false);    // dV_n = Pᵀ·dO
+        mma_tmem_tile(tmem + cDK, tmem + cDShi, tmem + cDSlo, ring + (t3 % kSlots) * kTile, idesc, false);  // dK_n = dSᵀ·qs
         commit(pd_free);
         commit(&ring_empty[t2 % kSlots]);
         commit(&ring_empty[t3 % kSlots]);
@@ -241,6 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
     const uint32_t col = (uint32_t)(32 * half);
     const float kLog2e = 1.4426950408889634f;
     bool ok = N > 0;
+    float dvv[32], dkk[32];  // this thread's dV, dK row slice, summed block by block in fp32
+#pragma unroll
+    for (int d = 0; d < 32; d++) { dvv[d] = 0.0f; dkk[d] = 0.0f; }
     for (int n = 0; n < N; n++) {
       const int h = head_of(n), q0 = qblk_of(n) * kBlk + (int)col;
       float s[32], dp[32];
@@ -267,6 +296,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         dp[c] = p * (dp[c] - dvq);
       }
       if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) ok = false;
+      if (ok && n > 0) {
+        // block n-1's products are done: fold them in before block n's P / dS (and then its products) reuse TMEM
+        fence_after();
+        add_partial(tmem + lane_off + cDV + col, dvv);
+        add_partial(tmem + lane_off + cDK + col, dkk);
+      }
       if (ok) {
         store_hilo(tmem + lane_off + cPhi + col, tmem + lane_off + cPlo + col, s);
         store_hilo(tmem + lane_off + cDShi + col, tmem + lane_off + cDSlo + col, dp);
@@ -279,14 +314,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
     if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) ok = false;
     if (ok || N == 0) {
       // keys that no query sees (N == 0) get zero gradients: every output row is written
-      float dvv[32], dkk[32];
       if (N > 0) {
         fence_after();
-        tmem_ld32(tmem + lane_off + cDV + col, dvv);
-        tmem_ld32(tmem + lane_off + cDK + col, dkk);
-      } else {
-#pragma unroll
-        for (int d = 0; d < 32; d++) { dvv[d] = 0.0f; dkk[d] = 0.0f; }
+        add_partial(tmem + lane_off + cDV + col, dvv);
+        add_partial(tmem + lane_off + cDK + col, dkk);
       }
       if (key < a.L) {
         int64_t base = (((int64_t)b * a.KVH + kvh) * a.L + key) * a.D;
@@ -392,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
         }
         if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[2], n & 1)) { ok = false; break; }
         fence_after();
-        mma_tmem_tile(tmem + cDQ, tmem + cDShi, tmem + cDSlo, ring + 2 * kTile, idesc, n > 0);  // dQ += dS·K
+        mma_tmem_tile(tmem + cDQ, tmem + cDShi, tmem + cDSlo, ring + 2 * kTile, idesc, false);  // dQ_n = dS·K
         commit(pd_free);
         commit(&ring_empty[2]);
       }
@@ -408,6 +439,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
     const float lse2 = qi < a.S ? a.lse[((int64_t)b * a.H + h) * a.S + qi] * kLog2e : 0.0f;
     const float dvq = qi < a.S ? a.dvec[((int64_t)b * a.H + h) * a.S + qi] : 0.0f;
     bool ok = N > 0;
+    float dq[32];  // this thread's dQ row slice, summed block by block in fp32
+#pragma unroll
+    for (int d = 0; d < 32; d++) dq[d] = 0.0f;
     for (int n = 0; n < N; n++) {
       float s[32], dp[32];
 #pragma unroll
@@ -430,6 +464,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
         dp[c] = p * (dp[c] - dvq);
       }
       if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) ok = false;
+      if (ok && n > 0) {
+        fence_after();
+        add_partial(tmem + lane_off + cDQ + col, dq);  // block n-1's dS·K, before block n's dS and product
+      }
       if (ok) {
         store_hilo(tmem + lane_off + cDShi + col, tmem + lane_off + cDSlo + col, dp);
         tmem_st_wait();
@@ -441,13 +479,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
     if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) ok = false;
     if (ok || N == 0) {
       // queries that see no key (N == 0) get zero gradients: every output row is written
-      float dq[32];
       if (N > 0) {
         fence_after();
-        tmem_ld32(tmem + lane_off + cDQ + col, dq);
-      } else {
-#pragma unroll
-        for (int d = 0; d < 32; d++) dq[d] = 0.0f;
+        add_partial(tmem + lane_off + cDQ + col, dq);
       }
       if (qi < a.S) {
         int64_t base = (((int64_t)b * a.H + h) * a.S + qi) * a.D;

@@ -99,6 +99,8 @@ struct pai_ctx {
   std::unordered_map<void*, pai_graph*> graph_owner;
   // kernels whose dynamic shared-memory limit was raised on this context's device, with the bytes set
   std::unordered_map<const void*, int> smem_attr;
+  // two-CTA clusters of the CTA-pair GEMM resident at once on this device (0: not queried yet, -1: unavailable)
+  int gemm_pair_slots = 0;
 };
 
 namespace pai {

@@ -20,6 +20,11 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
 #include <vector>
 
 #include "common.cuh"
@@ -87,13 +92,13 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: kind::tf32, fp32 accumulate, A and B K-major, M=128, N=bn.
-__host__ __device__ constexpr uint32_t umma_idesc_tf32(int bn) {
+// Instruction descriptor: kind::tf32, fp32 accumulate, A and B K-major, M = bm (128, or 256 for a CTA pair), N = bn.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int bn, int bm = kBM) {
   return (1u << 4)                    // D format: f32
          | (2u << 7)                  // A format: tf32
          | (2u << 10)                 // B format: tf32
          | ((uint32_t)(bn >> 3) << 17)  // N >> 3
-         | ((uint32_t)(kBM >> 4) << 24);  // M >> 4
+         | ((uint32_t)(bm >> 4) << 24);  // M >> 4
 }
 
 __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
@@ -124,6 +129,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 consecutive TMEM columns of this warp's 32 lanes -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
 // ---------------------------------------------------------------- pack
@@ -223,7 +241,7 @@ __global__ void __launch_bounds__(256) k_pack(const __grid_constant__ PackPair p
 
 // ---------------------------------------------------------------- tcgen05 GEMM
 struct GemmArgs {
-  const float* a_hi; const float* a_lo;  // packed A: [batch_a][kt][mt][tile]
+  const float* a_hi; const float* a_lo;  // packed A: [batch_a][kt][mt_pad][tile]
   const float* b_hi; const float* b_lo;  // packed B: [batch_b][kt][nt_pad][tile]
   const int32_t* a_index;                // output batch -> A batch (device array), or null: the inline arrays
   const int32_t* b_index;                // output batch -> B batch
@@ -231,16 +249,40 @@ struct GemmArgs {
   int32_t b_index_inline[kInlineBatches];
   float* c;                              // [batch][m][n] (or split partials [split][batch][m][n])
   int m, n, kt;                          // rows, cols, k tiles
-  int mt, nt_pad;                        // A row tiles, B row tiles (padded)
-  int tiles_m, tiles_n, batches, splits;
+  int mt_pad, nt_pad;                    // 128-row tiles of the packed A and B
+  int tiles_m, tiles_n, batches, splits; // output tiles (kTileM x kTileN) per batch, K splits
   int kt_per_split;
   int* error_flag;
   int k_elems;                           // logical K (for the work count only)
 };
 
+// The CTA-pair kernel reads the same packed planes through 2-D tensor maps ([rows, 32] fp32, 128-row boxes, no
+// swizzle: each box is one pre-swizzled tile copied verbatim), so the partner CTA's copies can signal the leader's
+// barrier (the .cta_group::2 form of the tensor copy).
+struct PairMaps {
+  CUtensorMap a_hi, a_lo, b_hi, b_lo;
+};
+
+constexpr int kTileN = 256;        // output columns per tile (one MMA's N)
+constexpr int kEpiWarps = 8;       // two per TMEM lane quadrant, each owning half of a row's 256 columns
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr uint32_t kPartialCols = 256;  // one TMEM partial accumulator (128 lanes x 256 fp32 columns); two stages
+constexpr int kPromoteKt = 1;           // k tiles (32 wide) summed in TMEM before the epilogue folds the partial into fp32
+
+template <bool PAIR>
+struct GemmShape {
+  static constexpr int kTileM = PAIR ? 256 : 128;   // output rows per tile (a CTA pair computes 256 x 256)
+  static constexpr int kBRows = PAIR ? 128 : 256;   // B rows (output columns) each CTA stages per k tile
+  static constexpr int kA = kBM * kBK * 4;          // 16 KiB
+  static constexpr int kB = kBRows * kBK * 4;       // 16 or 32 KiB
+  static constexpr int kStage = 2 * kA + 2 * kB;    // hi and lo planes of both operands
+  static constexpr int kStages = PAIR ? 3 : 2;
+  static constexpr int kBytes = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+};
+
 // Tile order: split-K slice, then batch, then a grouped raster over (m, n) — kGroupM row tiles walked first inside
-// each column band — so the ~148 tiles in flight at once share a few A row-blocks and B column-blocks in L2 instead
-// of each streaming its own operands from HBM.
+// each column band — so the tiles in flight at once share a few A row-blocks and B column-blocks in L2 instead of each
+// streaming its own operands from HBM.
 constexpr int kGroupM = 16;
 
 __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& split, int& bt, int& mb, int& nb) {
@@ -258,153 +300,273 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& split
   nb = within / gsize;
 }
 
-template <int BN, int STAGES>
-struct GemmSmem {
-  static constexpr int kA = kBM * kBK * 4;          // 16 KiB
-  static constexpr int kB = BN * kBK * 4;           // BN/128 tiles
-  static constexpr int kStage = 2 * kA + 2 * kB;
-  static constexpr int kBytes = STAGES * kStage + 1024 /*align*/ + 256 /*barriers*/;
-};
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// mbar_wait with cluster-scope acquire: the barrier also receives arrivals from the partner CTA.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kWaitLimit; i++) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+// Lane 0 polls, the warp follows (keeps the .sync.aligned TMEM loads convergent on every path).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+// One 128-row box of a packed plane into this CTA's shared memory; the bytes count on the leader CTA's barrier.
+__device__ __forceinline__ void tma_pair_load(void* dst, const CUtensorMap* map, int row, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(bar_cluster)
+      : "memory");
+}
+template <bool PAIR>
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  if (PAIR)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  else
+    umma_tf32(d_tmem, a, b, idesc, accumulate);
+}
+// Completion of the MMAs issued so far arrives on `bar` (PAIR: on the barrier at that offset in both CTAs).
+template <bool PAIR>
+__device__ __forceinline__ void umma_commit_all(uint64_t* bar) {
+  if (PAIR)
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(smem_u32(bar)), "h"((uint16_t)3) : "memory");
+  else
+    umma_commit(bar);
+}
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ GemmArgs g) {
-  using S = GemmSmem<BN, STAGES>;
+// Persistent, warp-specialised 3xTF32 GEMM. PAIR = false: one CTA per SM, 128 x 256 output tiles. PAIR = true: a
+// cluster of two CTAs (one per SM) computes 256 x 256 tiles with cta_group::2 MMAs (M = 256: each CTA holds 128 rows
+// of A and of the accumulator, and stages half of B's 256 columns, so each SM reads half of B per MMA).
+//   warp 0      copies A and B tiles (hi and lo planes) into a ring of shared-memory stages;
+//   warp 1      allocates TMEM and (the leader CTA's lane 0) issues the MMAs;
+//   warps 2-9   accumulate and store the result.
+// Accuracy: the tensor core sums into its fp32 accumulator with a rounding that does not average out over thousands of
+// accumulations (at K = 5632 a single accumulator lands ~30x further from the float64 result than a sequential fp32
+// loop). So every kPromoteKt k tiles go into a fresh TMEM partial (two stages, ping-pong), with the small cross terms
+// (a_lo·b_hi, a_hi·b_lo) issued before the large a_hi·b_hi, and the epilogue warps add each partial into fp32
+// registers with IEEE round-to-nearest: per-partial errors have random signs and average out across the partials.
+template <bool PAIR>
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_constant__ GemmArgs g,
+                                                             const __grid_constant__ PairMaps maps) {
+  using S = GemmShape<PAIR>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStage);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* acc_full = empty_bar + STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStage);
+  uint64_t* empty_bar = full_bar + S::kStages;
+  uint64_t* part_full = empty_bar + S::kStages;
+  uint64_t* part_empty = part_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_empty + 2);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-    for (int a = 0; a < 2; a++) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], 4); }
+    for (int s = 0; s < S::kStages; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+    for (int a = 0; a < 2; a++) { mbar_init(&part_full[a], 1); mbar_init(&part_empty[a], PAIR ? 2 * kEpiWarps : kEpiWarps); }
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(2 * BN));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(2 * kPartialCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(2 * kPartialCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // both CTAs' barriers exist before any copy or commit targets them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int total = g.tiles_m * g.tiles_n * g.batches * g.splits;
   const int tiles_per_split = g.tiles_m * g.tiles_n * g.batches;
-  const int total = tiles_per_split * g.splits;
-  constexpr uint32_t kStageBytes = (uint32_t)S::kStage;
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
+      const uint32_t lead_full = PAIR ? mapa_rank(smem_u32(&full_bar[0]), 0) : 0u;
+      for (int t = unit; t < total && !s_abort; t += units) {
         int split, bt, mb, nb;
         tile_coords(g, t, split, bt, mb, nb);
-        int ba = (g.a_index ? g.a_index : g.a_index_inline)[bt], bb = (g.b_index ? g.b_index : g.b_index_inline)[bt];
-        int k0 = split * g.kt_per_split;
-        int k1 = min(g.kt, k0 + g.kt_per_split);
+        const int ba = (g.a_index ? g.a_index : g.a_index_inline)[bt];
+        const int bb = (g.b_index ? g.b_index : g.b_index_inline)[bt];
+        const int k0 = split * g.kt_per_split, k1 = min(g.kt, k0 + g.kt_per_split);
         for (int kb = k0; kb < k1; kb++) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { atomicExch(g.error_flag, 1); s_abort = 1; break; }
           uint8_t* st = smem + stage * S::kStage;
-          mbar_expect_tx(&full_bar[stage], kStageBytes);
-          size_t aoff = ((size_t)(ba * g.kt + kb) * g.mt + mb) * kTileFloats;
-          size_t boff = ((size_t)(bb * g.kt + kb) * g.nt_pad + (size_t)nb * (BN / kBM)) * kTileFloats;
-          bulk_g2s(st, g.a_hi + aoff, S::kA, &full_bar[stage]);
-          bulk_g2s(st + S::kA, g.a_lo + aoff, S::kA, &full_bar[stage]);
-          bulk_g2s(st + 2 * S::kA, g.b_hi + boff, S::kB, &full_bar[stage]);
-          bulk_g2s(st + 2 * S::kA + S::kB, g.b_lo + boff, S::kB, &full_bar[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (PAIR) {
+            if (leader) mbar_expect_tx(&full_bar[stage], 2u * (uint32_t)S::kStage);
+            const uint32_t bar = lead_full + (uint32_t)(stage * 8);
+            const int arow = ((ba * g.kt + kb) * g.mt_pad + mb * 2 + (int)rank) * kBM;
+            const int brow = ((bb * g.kt + kb) * g.nt_pad + nb * 2 + (int)rank) * kBM;
+            tma_pair_load(st, &maps.a_hi, arow, bar);
+            tma_pair_load(st + S::kA, &maps.a_lo, arow, bar);
+            tma_pair_load(st + 2 * S::kA, &maps.b_hi, brow, bar);
+            tma_pair_load(st + 2 * S::kA + S::kB, &maps.b_lo, brow, bar);
+          } else {
+            mbar_expect_tx(&full_bar[stage], (uint32_t)S::kStage);
+            const size_t aoff = ((size_t)(ba * g.kt + kb) * g.mt_pad + mb) * kTileFloats;
+            const size_t boff = ((size_t)(bb * g.kt + kb) * g.nt_pad + (size_t)nb * 2) * kTileFloats;
+            bulk_g2s(st, g.a_hi + aoff, S::kA, &full_bar[stage]);
+            bulk_g2s(st + S::kA, g.a_lo + aoff, S::kA, &full_bar[stage]);
+            bulk_g2s(st + 2 * S::kA, g.b_hi + boff, S::kB, &full_bar[stage]);
+            bulk_g2s(st + 2 * S::kA + S::kB, g.b_lo + boff, S::kB, &full_bar[stage]);
+          }
+          if (++stage == S::kStages) { stage = 0; phase ^= 1; }
         }
       }
       // Drain: every stage issued must have landed (and been consumed) before the CTA may exit.
-      for (int s = 0; s < STAGES; s++) {
+      for (int s = 0; s < S::kStages; s++) {
         mbar_wait(&empty_bar[stage], phase ^ 1);
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == S::kStages) { stage = 0; phase ^= 1; }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_tf32(BN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = umma_idesc_tf32(kTileN, S::kTileM);
       int stage = 0;
       uint32_t phase = 0;
-      int local = 0;
-      for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x, local++) {
-        int split = t / tiles_per_split;
-        int k0 = split * g.kt_per_split;
-        int k1 = min(g.kt, k0 + g.kt_per_split);
-        int acc = local & 1;
-        uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) { atomicExch(g.error_flag, 2); s_abort = 1; break; }
-        tc_fence_after();
-        uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+      uint32_t J = 0;  // running partial count: partial stage J & 1, its barrier phase (J >> 1) & 1
+      for (int t = unit; t < total && !s_abort; t += units) {
+        const int split = t / tiles_per_split;
+        const int k0 = split * g.kt_per_split, k1 = min(g.kt, k0 + g.kt_per_split);
         for (int kb = k0; kb < k1; kb++) {
+          const int ps = (int)(J & 1);
+          const bool first = (kb - k0) % kPromoteKt == 0;
+          const bool last = (kb - k0) % kPromoteKt == kPromoteKt - 1 || kb == k1 - 1;
           if (!mbar_wait(&full_bar[stage], phase)) { atomicExch(g.error_flag, 3); s_abort = 1; break; }
+          if (first) {
+            const bool freed = PAIR ? mbar_wait_cluster(&part_empty[ps], ((J >> 1) & 1) ^ 1)
+                                    : mbar_wait(&part_empty[ps], ((J >> 1) & 1) ^ 1);
+            if (!freed) { atomicExch(g.error_flag, 2); s_abort = 1; break; }
+          }
           tc_fence_after();
           uint8_t* st = smem + stage * S::kStage;
-          uint32_t a_hi = smem_u32(st), a_lo = a_hi + S::kA, b_hi = a_hi + 2 * S::kA, b_lo = b_hi + S::kB;
+          const uint32_t a_hi = smem_u32(st), a_lo = a_hi + S::kA, b_hi = a_hi + 2 * S::kA, b_lo = b_hi + S::kB;
+          const uint32_t d = tmem_base + (uint32_t)ps * kPartialCols;
 #pragma unroll
           for (int ks = 0; ks < kBK / 8; ks++) {
-            uint32_t koff = ks * 32;  // 8 tf32 = 32 bytes along K inside the 128-byte swizzle row
-            uint32_t accum = (kb > k0 || ks > 0) ? 1u : 0u;
-            umma_tf32(d_tmem, umma_desc_sw128(a_lo + koff), umma_desc_sw128(b_hi + koff), idesc, accum);
-            umma_tf32(d_tmem, umma_desc_sw128(a_hi + koff), umma_desc_sw128(b_lo + koff), idesc, 1u);
-            umma_tf32(d_tmem, umma_desc_sw128(a_hi + koff), umma_desc_sw128(b_hi + koff), idesc, 1u);
+            const uint32_t ko = (uint32_t)ks * 32;  // 8 tf32 = 32 bytes along K inside the 128-byte swizzle row
+            umma<PAIR>(d, umma_desc_sw128(a_lo + ko), umma_desc_sw128(b_hi + ko), idesc, (first && ks == 0) ? 0u : 1u);
+            umma<PAIR>(d, umma_desc_sw128(a_hi + ko), umma_desc_sw128(b_lo + ko), idesc, 1u);
           }
-          umma_commit(&empty_bar[stage]);  // frees the stage once these MMAs have read it
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+#pragma unroll
+          for (int ks = 0; ks < kBK / 8; ks++) {
+            const uint32_t ko = (uint32_t)ks * 32;
+            umma<PAIR>(d, umma_desc_sw128(a_hi + ko), umma_desc_sw128(b_hi + ko), idesc, 1u);
+          }
+          umma_commit_all<PAIR>(&empty_bar[stage]);  // frees the stage (in both CTAs) once these MMAs have read it
+          if (last) {
+            umma_commit_all<PAIR>(&part_full[ps]);
+            J++;
+          }
+          if (++stage == S::kStages) { stage = 0; phase ^= 1; }
         }
-        umma_commit(&acc_full[acc]);
       }
     }
   } else {
-    // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.
+    // Epilogue warps 2..9: TMEM lane quadrant = warp % 4, column half = (warp - 2) / 4 (128 of the tile's 256).
     const int quad = warp & 3;
-    const int row_in_tile = quad * 32 + lane;
-    int local = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * (kTileN / 2));
+    const uint32_t lead_part_empty = PAIR ? mapa_rank(smem_u32(&part_empty[0]), 0) : 0u;
+    bool ok = true;
+    uint32_t J = 0;
+    for (int t = unit; t < total && ok; t += units) {
       int split, bt, mb, nb;
       tile_coords(g, t, split, bt, mb, nb);
-      int acc = local & 1;
-      uint32_t acc_phase = (local >> 1) & 1;
-      bool ok = mbar_wait(&acc_full[acc], acc_phase);
-      if (!ok) { atomicExch(g.error_flag, 4); s_abort = 1; break; }
-      tc_fence_after();
-      int row = mb * kBM + row_in_tile;
-      float* crow = g.c + ((size_t)split * g.batches + bt) * (size_t)g.m * g.n + (size_t)row * g.n;
-      bool vec_ok = (g.n & 3) == 0;
-#pragma unroll 1
-      for (int cc = 0; cc < BN / 32; cc++) {
-        float v[32];
-        uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + cc * 32);
-        tmem_ld32(taddr, v);
-        int col0 = nb * BN + cc * 32;
-        if (row < g.m) {
-          if (vec_ok && col0 + 32 <= g.n) {
-            float4* dst = reinterpret_cast<float4*>(crow + col0);
+      const int k0 = split * g.kt_per_split, k1 = min(g.kt, k0 + g.kt_per_split);
+      float acc[kTileN / 2];
 #pragma unroll
-            for (int j = 0; j < 8; j++) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else {
+      for (int j = 0; j < kTileN / 2; j++) acc[j] = 0.0f;
+      const int parts = (k1 - k0 + kPromoteKt - 1) / kPromoteKt;
+      for (int pi = 0; pi < parts; pi++, J++) {
+        const int ps = (int)(J & 1);
+        if (!warp_wait(&part_full[ps], (J >> 1) & 1)) {
+          if (lane == 0) { atomicExch(g.error_flag, 4); s_abort = 1; }
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
-            for (int j = 0; j < 32; j++)
-              if (col0 + j < g.n) crow[col0 + j] = v[j];
-          }
+        for (int cc = 0; cc < kTileN / 2 / 16; cc++) {
+          float v[16];
+          tmem_ld16(lane_base + (uint32_t)ps * kPartialCols + (uint32_t)(cc * 16), v);
+#pragma unroll
+          for (int j = 0; j < 16; j++) acc[cc * 16 + j] += v[j];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (PAIR && !leader) mbar_arrive_remote(lead_part_empty + (uint32_t)(ps * 8));
+          else mbar_arrive(&part_empty[ps]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (!ok) break;
+      const int row = mb * S::kTileM + (int)rank * kBM + quad * 32 + lane;
+      const int col0 = nb * kTileN + half * (kTileN / 2);
+      if (row < g.m) {
+        float* crow = g.c + ((size_t)split * g.batches + bt) * (size_t)g.m * g.n + (size_t)row * g.n;
+        if ((g.n & 3) == 0 && col0 + kTileN / 2 <= g.n) {
+          float4* dst = reinterpret_cast<float4*>(crow + col0);
+#pragma unroll
+          for (int j = 0; j < kTileN / 8; j++) dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kTileN / 2; j++)
+            if (col0 + j < g.n) crow[col0 + j] = acc[j];
+        }
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // the partner's MMAs and reads of this CTA's TMEM and shared memory are over
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * BN));
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * kPartialCols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * kPartialCols));
   }
 }
 
@@ -423,15 +585,74 @@ bool gemv_enabled();
 pai_status gemv_tn(pai_ctx* ctx, const float* x, const int64_t* xoff, int rows, const float* w, int64_t sw, int n, int k,
                    float* y);
 
-template <int BN, int STAGES>
-static pai_status launch_tc(pai_ctx* ctx, GemmArgs& g) {
-  using S = GemmSmem<BN, STAGES>;
-  PAI_CUDA(smem_limit(ctx, k_gemm_tc<BN, STAGES>, S::kBytes));
-  int total = g.tiles_m * g.tiles_n * g.batches * g.splits;
-  int grid = total < ctx->sm_count ? total : ctx->sm_count;
+// gemv.cu: the driver's cuTensorMapEncodeTiled, or null.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+// A packed plane ([tiles x 128 rows] x 32 fp32, 128-byte rows) as a 2-D tensor map with one-tile boxes.
+static pai_status plane_map(const float* plane, int64_t rows, CUtensorMap* map) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)kBK, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kBK * 4};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult cr = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(plane), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for a packed plane", (int)cr);
+  return PAI_OK;
+}
+
+// How many two-CTA clusters of the pair kernel fit on the device at once (queried once per context).
+static int pair_slots(pai_ctx* ctx) {
+  if (ctx->gemm_pair_slots == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (ctx->sm_count / 2));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = GemmShape<true>::kBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (smem_limit(ctx, k_gemm_tc<true>, GemmShape<true>::kBytes) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, k_gemm_tc<true>, &cfg) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = -1;  // the pair kernel is not used on this device
+    }
+    ctx->gemm_pair_slots = n;
+  }
+  return ctx->gemm_pair_slots;
+}
+
+static pai_status launch_gemm(pai_ctx* ctx, const GemmArgs& g, bool pair, const PairMaps& maps) {
+  const int total = g.tiles_m * g.tiles_n * g.batches * g.splits;
   KernelTimerScope timer(ctx, "gemm", 2.0 * g.m * g.n * (double)g.k_elems * g.batches);
-  k_gemm_tc<BN, STAGES><<<grid, 192, S::kBytes, ctx->stream>>>(g);
-  PAI_LAUNCH_CHECK("tcgen05 gemm");
+  if (pair) {
+    PAI_CUDA(smem_limit(ctx, k_gemm_tc<true>, GemmShape<true>::kBytes));
+    const int pairs = std::min(total, pair_slots(ctx));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = GemmShape<true>::kBytes;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    PAI_PDL_LAUNCH(cudaLaunchKernelEx(&cfg, k_gemm_tc<true>, g, maps), "tcgen05 gemm (CTA pairs)");
+  } else {
+    PAI_CUDA(smem_limit(ctx, k_gemm_tc<false>, GemmShape<false>::kBytes));
+    const int grid = std::min(total, ctx->sm_count);
+    k_gemm_tc<false><<<grid, kGemmThreads, GemmShape<false>::kBytes, ctx->stream>>>(g, maps);
+    PAI_LAUNCH_CHECK("tcgen05 gemm");
+  }
   return PAI_OK;
 }
 
@@ -585,38 +806,41 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
 
   int kt = (k + kBK - 1) / kBK;
   int mt = (m + kBM - 1) / kBM;
-  // N tile: 256 columns (2-stage ring) by default; 128 columns (3-stage ring, same shared memory) when the persistent
-  // CTAs then share the tiles more evenly. A product's time is set by the CTA with the most tiles, so the figure of
-  // merit is tiles / (SMs x the largest per-CTA tile count); 128-column tiles reuse each A tile half as often, which the
-  // 0.92 factor charges for.
-  auto balance = [&](int bn) {
-    int64_t t = (int64_t)mt * ((n + bn - 1) / bn) * batch;
-    int64_t per = (t + ctx->sm_count - 1) / ctx->sm_count;
-    return (double)t / ((double)ctx->sm_count * (double)per);
-  };
-  const int BN = (0.92 * balance(128) > balance(256)) ? 128 : 256;
-  int tiles_n = (n + BN - 1) / BN;
-  int nt_pad = tiles_n * (BN / kBM);
+  const int tn = (n + kTileN - 1) / kTileN;
+  // Tile shape by the rounds the persistent CTAs take: 128 x 256 tiles on every SM, or 256 x 256 tiles on two-SM
+  // clusters (same work per SM and round, but each SM reads half of B per MMA, which shared-memory bandwidth limits
+  // in the one-CTA kernel to ~0.8 of the tensor pipe). Split-K products (few tiles, deep K) stay on one CTA each.
+  const int64_t tiles1 = (int64_t)mt * tn * batch;
+  const int64_t tiles2 = (int64_t)((m + 255) / 256) * tn * batch;
+  int splits = 1;
+  if (tiles1 * 2 <= ctx->sm_count && kt >= 16) {
+    splits = ctx->sm_count / (int)tiles1;
+    if (splits > kt / 8) splits = kt / 8;
+    if (splits < 1) splits = 1;
+  }
+  int kt_per_split = (kt + splits - 1) / splits;
+  splits = (kt + kt_per_split - 1) / kt_per_split;
+  bool pair = false;
+  if (splits == 1 && m > kBM) {
+    const int slots = pair_slots(ctx);
+    if (slots > 0) {
+      const double rounds1 = std::ceil((double)tiles1 / ctx->sm_count) / 0.8;
+      const double rounds2 = std::ceil((double)tiles2 / slots) * ((double)ctx->sm_count / (2.0 * slots)) / 0.95;
+      pair = rounds2 < rounds1;
+    }
+  }
+  const int mt_pad = pair ? 2 * (int)((m + 255) / 256) : mt;
+  const int nt_pad = tn * (kTileN / kBM);
   Scratch ahi, alo, bhi, blo, dai, dbi, part;
   Scratch aoff, boff;
   PackDesc pda, pdb;
-  PAI_TRY(prepare_pack(ctx, abase, a_distinct, sam, sak, m, k, mt, &ahi, &alo, &aoff, &pda));
+  PAI_TRY(prepare_pack(ctx, abase, a_distinct, sam, sak, m, k, mt_pad, &ahi, &alo, &aoff, &pda));
   PAI_TRY(prepare_pack(ctx, bbase, b_distinct, sbn, sbk, n, k, nt_pad, &bhi, &blo, &boff, &pdb));
   PAI_TRY(pack_operands(ctx, pda, (int)a_distinct.size(), ahi, alo, pdb, (int)b_distinct.size(), bhi, blo));
   if (batch > kInlineBatches) {
     PAI_TRY(upload(ctx, a_idx.data(), a_idx.size() * 4, &dai));
     PAI_TRY(upload(ctx, b_idx.data(), b_idx.size() * 4, &dbi));
   }
-
-  int tiles = mt * tiles_n * (int)batch;
-  int splits = 1;
-  if (tiles * 2 <= ctx->sm_count && kt >= 16) {
-    splits = ctx->sm_count / tiles;
-    if (splits > kt / 8) splits = kt / 8;
-    if (splits < 1) splits = 1;
-  }
-  int kt_per_split = (kt + splits - 1) / splits;
-  splits = (kt + kt_per_split - 1) / kt_per_split;
   float* cdst = fptr(r);
   if (splits > 1) {
     PAI_TRY(scratch(ctx, (size_t)splits * numel(r) * 4, &part));
@@ -628,12 +852,26 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   g.a_index = static_cast<int32_t*>(dai.p); g.b_index = static_cast<int32_t*>(dbi.p);
   if (batch <= kInlineBatches)
     for (int64_t i = 0; i < batch; i++) { g.a_index_inline[i] = a_idx[(size_t)i]; g.b_index_inline[i] = b_idx[(size_t)i]; }
-  g.c = cdst; g.m = m; g.n = n; g.kt = kt; g.mt = mt; g.nt_pad = nt_pad;
-  g.tiles_m = mt; g.tiles_n = tiles_n; g.batches = (int)batch; g.splits = splits; g.kt_per_split = kt_per_split;
+  g.c = cdst; g.m = m; g.n = n; g.kt = kt; g.mt_pad = mt_pad; g.nt_pad = nt_pad;
+  g.tiles_m = pair ? mt_pad / 2 : mt; g.tiles_n = tn; g.batches = (int)batch; g.splits = splits;
+  g.kt_per_split = kt_per_split;
   g.error_flag = ctx->d_error_flag;
   g.k_elems = k;
-  if (BN == 128) PAI_TRY((launch_tc<128, 3>(ctx, g)));
-  else PAI_TRY((launch_tc<256, 2>(ctx, g)));
+  PairMaps maps;
+  memset(&maps, 0, sizeof maps);
+  if (pair) {
+    const int64_t arows = (int64_t)a_distinct.size() * kt * mt_pad * kBM, brows = (int64_t)b_distinct.size() * kt * nt_pad * kBM;
+    if (arows > INT32_MAX || brows > INT32_MAX) {
+      pair = false;  // tensor-map coordinates are 32-bit; the packed A (pairs of row tiles) serves the one-CTA kernel too
+      g.tiles_m = mt;
+    } else {
+      PAI_TRY(plane_map(g.a_hi, arows, &maps.a_hi));
+      PAI_TRY(plane_map(g.a_lo, arows, &maps.a_lo));
+      PAI_TRY(plane_map(g.b_hi, brows, &maps.b_hi));
+      PAI_TRY(plane_map(g.b_lo, brows, &maps.b_lo));
+    }
+  }
+  PAI_TRY(launch_gemm(ctx, g, pair, maps));
   if (splits > 1) {
     int64_t nn = numel(r);
     k_splitk_reduce<<<grid_for(ctx, nn, 256), 256, 0, ctx->stream>>>(cdst, fptr(r), nn, splits);

@@ -490,7 +490,7 @@ __global__ void k_gemv_finish(const float* __restrict__ pa, int sa, const float*
 
 }  // namespace gtc
 
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
