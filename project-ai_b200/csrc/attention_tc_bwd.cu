@@ -272,6 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
     for (int d = 0; d < 32; d++) { dvv[d] = 0.0f; dkk[d] = 0.0f; }
     for (int n = 0; n < N; n++) {
       const int h = head_of(n), q0 = qblk_of(n) * kBlk + (int)col;
+      // the block's 32 query statistics: one load per lane, issued before the wait, broadcast by shuffles below
+      const int ql = q0 + lane;
+      const float lse_l = ql < a.S ? a.lse[((int64_t)b * a.H + h) * a.S + ql] * kLog2e : 0.0f;
+      const float dv_l = ql < a.S ? a.dvec[((int64_t)b * a.H + h) * a.S + ql] : 0.0f;
       float s[32], dp[32];
 #pragma unroll
       for (int c = 0; c < 32; c++) { s[c] = 0.0f; dp[c] = 0.0f; }
@@ -284,14 +288,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         __syncwarp();
         if (lane == 0) mbar_arrive(st_free);
       }
-      const float* lse_row = a.lse + ((int64_t)b * a.H + h) * a.S;
-      const float* dv_row = a.dvec + ((int64_t)b * a.H + h) * a.S;
 #pragma unroll
       for (int c = 0; c < 32; c++) {
         int q = q0 + c;
+        const float lse2 = __shfl_sync(0xffffffffu, lse_l, c);
+        const float dvc = __shfl_sync(0xffffffffu, dv_l, c);
         bool vis = q < a.S && key < a.L && (!a.causal || key <= a.pos_offset + q);
-        float p = vis ? exp2f(fmaf(s[c], kLog2e, -lse_row[q] * kLog2e)) : 0.0f;
-        float dvq = vis ? dv_row[q] : 0.0f;
+        float p = vis ? exp2f(fmaf(s[c], kLog2e, -lse2)) : 0.0f;
+        float dvq = vis ? dvc : 0.0f;
         s[c] = p;
         dp[c] = p * (dp[c] - dvq);
       }
