@@ -267,7 +267,7 @@ constexpr int kTileN = 256;        // output columns per tile (one MMA's N)
 constexpr int kEpiWarps = 8;       // two per TMEM lane quadrant, each owning half of a row's 256 columns
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kPartialCols = 256;  // one TMEM partial accumulator (128 lanes x 256 fp32 columns); two stages
-constexpr int kPromoteKt = 4;           // k tiles (32 wide) summed in TMEM before the epilogue folds the partial into fp32
+constexpr int kPromoteKt = 8;           // k tiles (32 wide) summed in TMEM before the epilogue folds the partial into fp32
 
 template <bool PAIR>
 struct GemmShape {
