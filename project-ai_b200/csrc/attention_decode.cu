@@ -669,15 +669,25 @@ pai_status attn_decode_run(pai_ctx* ctx, dec::Args& a, bool rope) {
     a.keys_per_split = kps;
     a.splits = (kend + kps - 1) / kps;
   } else {
-    // streaming variant. splits: as many as keep the whole grid resident in one wave (3 CTAs per SM fit in shared
-    // memory with up to 4 query rows, 2 with 8 or 16), at most one cluster of 8, and at most one per 16-key tile
-    const int per_sm = a.rows <= 4 ? 3 : 2;
-    int splits = std::max(1, std::min(dec::kMaxCluster, per_sm * ctx->sm_count / pairs));
-    a.splits = std::min(splits, (kend + dec::kTile - 1) / dec::kTile);
+    // streaming variant. splits: as many as keep the whole grid resident in one wave, at most one cluster of 8, and
+    // at most one per 16-key tile. With up to 4 query rows, 3 CTAs per SM fit in shared memory with the 8-stage ring
+    // and 5 with a 4-stage ring (32 KB); the consumer warps' QKᵀ / softmax / PV chain is latency-bound, so the
+    // shallower ring is taken whenever it lets the grid hold more CTAs (batch 32 x 8 kv heads: 2 splits, 512 CTAs,
+    // instead of 1). 8 or 16 query rows: 2 CTAs per SM (registers).
+    const int tiles = (kend + dec::kTile - 1) / dec::kTile;
+    auto splits_for = [&](int per_sm) {
+      return std::max(1, std::min(std::min(dec::kMaxCluster, per_sm * ctx->sm_count / pairs), tiles));
+    };
+    int stages = dec::kStages;
+    a.splits = splits_for(a.rows <= 4 ? 3 : 2);
+    if (a.rows <= 4 && splits_for(5) > a.splits) {
+      a.splits = splits_for(5);
+      stages = dec::kConsumers;
+    }
     // ring depth: a multiple of the consumer count, so each stage is always read by the same warp (tile t sits in
     // stage t % stages and is read by warp t % kConsumers) and its barrier phases are awaited in order
     const int max_tiles = ((kend + a.splits - 1) / a.splits + dec::kTile - 1) / dec::kTile;
-    a.stages = max_tiles <= dec::kConsumers ? dec::kConsumers : dec::kStages;
+    a.stages = max_tiles <= dec::kConsumers ? dec::kConsumers : stages;
   }
   dim3 grid((unsigned)a.splits, (unsigned)a.KVH, (unsigned)a.B);
   cudaError_t e;
