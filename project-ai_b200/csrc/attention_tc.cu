@@ -8,8 +8,9 @@
 // walks its items.
 //   pre-pass k_attn_pack: q·scale, k and vᵀ split into tf32 hi/lo and written as SWIZZLE_128B K-major tiles;
 //   warp 0      bulk-copies the Q tile once and K/Vᵀ blocks into a 2-stage ring;
-//   warp 1      allocates TMEM and issues S = Q·Kᵀ (3 MMAs per k-step, M=128 N=64) into a double-buffered TMEM S,
-//               then O_j = P_j·V_j with P read from TMEM as the A operand;
+//   warp 1      allocates TMEM and issues S = Q·Kᵀ (3 MMAs per k-step, M=128 N=64) into a double-buffered TMEM S;
+//   warp 10     issues O_j = P_j·V_j with P read from TMEM as the A operand (a second issuing thread: one thread
+//               issues a tf32 MMA about every 115 cycles whatever its N, and the pipe overlaps two threads' products);
 //   warps 2-9   softmax: two warps per TMEM lane quadrant, so each query row is owned by two threads, each holding
 //               32 of the block's 64 scores (and 32 of the 64 output columns); the pair agrees on the running row
 //               max through shared memory. Each thread masks (diagonal blocks only), exponentiates, splits P into
@@ -29,7 +30,8 @@ constexpr int kQT = 128;  // queries per CTA
 constexpr int kKB = 64;   // keys per block
 constexpr int kDP = 64;   // padded head dim
 constexpr int kSoftmaxWarps = 8;
-constexpr int kFwdThreads = 64 + 32 * kSoftmaxWarps;
+constexpr int kPvWarp = 2 + kSoftmaxWarps;  // the P·V issuer, after the softmax warps
+constexpr int kFwdThreads = 32 * (kPvWarp + 1);
 
 // ---------------------------------------------------------------- pack pre-pass
 // One tile (bi of the nblk along R) of one (batch, head) row bx of an operand. Output per tile: [hi kb0][hi kb1]
@@ -205,7 +207,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
   uint64_t* s_free = s_full + 2;                   // [2]
   uint64_t* p_full = s_free + 2;                   // [2]
   uint64_t* pv_full = p_full + 2;                  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_full + 2);
+  uint64_t* drained = pv_full + 2;                 // [2]: the S and P·V issuers' MMAs have completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 2);
   __shared__ volatile int s_abort;
   __shared__ float s_max[2][2][kQT];  // [block parity][column half][row]
   __shared__ float s_l[2][kQT];
@@ -231,6 +234,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
     for (int i = 0; i < 2; i++) {
       mbar_init(&p_full[i], kSoftmaxWarps);
       mbar_init(&pv_full[i], 1);
+      mbar_init(&drained[i], 1);
     }
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -317,18 +321,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
       FwdItem it;
       bool ok = true;
       while (ok && !s_abort && next_fwd_item(a, n_items, r, it)) {
-        if (!mbar_wait(q_full, ord & 1) || !wait_s(J0)) { atomicExch(a.error_flag, 12); s_abort = 1; break; }
-        fence_after();
-        issue_s(J0);
-        if (it.nblk == 1) commit(q_empty);  // this tile's S products are all issued: Q may be replaced after them
+        if (!mbar_wait(q_full, ord & 1)) { atomicExch(a.error_flag, 12); s_abort = 1; break; }
         for (int j = 0; j < it.nblk; j++) {
           const int J = J0 + j;
-          if (j + 1 < it.nblk) {
-            if (!wait_s(J + 1)) { atomicExch(a.error_flag, 13); s_abort = 1; ok = false; break; }
-            fence_after();
-            issue_s(J + 1);
-            if (j + 2 == it.nblk) commit(q_empty);
-          }
+          if (!wait_s(J)) { atomicExch(a.error_flag, 13); s_abort = 1; ok = false; break; }
+          fence_after();
+          issue_s(J);
+          if (j + 1 == it.nblk) commit(q_empty);  // this tile's S products are all issued: Q may be replaced after them
+        }
+        J0 += it.nblk;
+        ord++;
+        r++;
+      }
+      // every MMA this thread issued completes before the CTA releases its tensor memory
+      commit(&drained[0]);
+      mbar_wait(&drained[0], 0);
+    }
+  } else if (warp == kPvWarp) {
+    // O_J = P_J·V_J, issued by a second thread: one thread issues a tcgen05.mma about every 115 cycles whatever its
+    // N, and the tensor pipe runs two threads' N=64 products side by side, so S and P·V no longer queue behind
+    // each other
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(128, 64);
+      int r = 0, J0 = 0;
+      FwdItem it;
+      bool ok = true;
+      while (ok && !s_abort && next_fwd_item(a, n_items, r, it)) {
+        for (int j = 0; j < it.nblk; j++) {
+          const int J = J0 + j;
           const int ps = J & 1;  // P / P·V slot of this block
           const int vs = J % kVStages;
           if (!mbar_wait(&p_full[ps], (J >> 1) & 1) || !mbar_wait(&v_full[vs], (J / kVStages) & 1)) {
@@ -349,11 +369,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
           commit(&v_empty[vs]);
         }
         J0 += it.nblk;
-        ord++;
         r++;
       }
+      commit(&drained[1]);
+      mbar_wait(&drained[1], 0);
     }
-  } else {
+  } else if (warp < 2 + kSoftmaxWarps) {
     // softmax warps: (quad, half) -> query row quad*32+lane, columns [32*half, 32*half+32) of S, P and O
     const int sw = warp - 2;
     const int quad = warp & 3;

@@ -5,8 +5,10 @@
 //   P = exp(S − lse), dP = dO·Vᵀ, dS = P ⊙ (dP − rowsum(dO ⊙ O)),
 //   dV = Σ_group Pᵀ·dO,  dK = Σ_group dSᵀ·(q·scale),  dQ = scale · dS·K.
 //
-// Two kernels, 320 threads each (warp 0 bulk-copy producer, warp 1 MMA issuer, warps 2-9 element-wise — two warps
-// per TMEM lane quadrant, 32 of each 64-wide block's columns per thread):
+// Two kernels, 352 threads each (warp 0 bulk-copy producer, warp 1 issuer of the score products, warps 2-9
+// element-wise — two warps per TMEM lane quadrant, 32 of each 64-wide block's columns per thread — and warp 10 issuer
+// of the gradient products: one thread issues a tf32 MMA about every 115 cycles whatever its N, and the tensor pipe
+// overlaps two threads' N=64 products):
 //   k_attn_bwd_kv_tc  128 keys of one (batch, kv head) stay resident (K, V as A operands in shared memory); the
 //                     group's heads x 64-query blocks stream through a 3-slot ring (q·scale, dO, dOᵀ, (q·scale)ᵀ);
 //                     Sᵀ and dPᵀ land in TMEM, Pᵀ / dSᵀ go back to TMEM as hi/lo A operands of dV += Pᵀ·dO and
@@ -37,7 +39,8 @@ constexpr int kDP = 64;                  // padded head dim
 constexpr uint32_t kTile = 64 * 64 * 4 * 2;   // one packed 64x64 hi/lo tile: 32 KB
 constexpr uint32_t kA = 2 * kTile;            // a resident 128-row operand: 64 KB
 constexpr int kSlots = 3;
-constexpr int kThreads = 320;
+constexpr int kGradWarp = 10;         // second MMA issuer: the gradient products (after the 8 element-wise warps)
+constexpr int kThreads = 32 * (kGradWarp + 1);
 constexpr int kSmem = 2 * kA + kSlots * kTile + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;
 
@@ -118,16 +121,6 @@ __device__ __forceinline__ void kv_ring_item(int i, int N, int& n, int& type) {
   }
 }
 
-// 16 registers per thread -> 16 consecutive TMEM columns of this warp's lanes (completion: tmem_st_wait()).
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
-      : "memory");
-}
 
 __device__ __forceinline__ void store_hilo(uint32_t hi_addr, uint32_t lo_addr, const float* x) {
 #pragma unroll
@@ -163,7 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
   uint64_t* st_free = bars + 8;
   uint64_t* pd_full = bars + 9;
   uint64_t* pd_free = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* drained = bars + 11;    // [2]: each issuer's MMAs have completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -189,6 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
     mbar_init(st_free, 8);
     mbar_init(pd_full, 8);
     mbar_init(pd_free, 1);
+    mbar_init(&drained[0], 1);
+    mbar_init(&drained[1], 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -240,13 +236,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         commit(&ring_empty[t1 % kSlots]);
         return true;
       };
-      if (ok) ok = issue_st(0);
+      // the scores of block n once the element-wise warps have read block n-1's
       for (int n = 0; n < N && ok && !s_abort; n++) {
-        if (n + 1 < N) {
-          if (!mbar_wait(st_free, n & 1)) { ok = false; break; }
+        if (n > 0) {
+          if (!mbar_wait(st_free, (n - 1) & 1)) { ok = false; break; }
           fence_after();
-          if (!issue_st(n + 1)) { ok = false; break; }
         }
+        if (!issue_st(n)) { ok = false; break; }
+      }
+      if (!ok) { atomicExch(a.error_flag, 22); s_abort = 1; }
+      commit(&drained[0]);
+      mbar_wait(&drained[0], 0);
+    }
+  } else if (warp == kGradWarp) {
+    // the gradient products, issued by a second thread: one thread issues a tf32 MMA about every 115 cycles
+    // whatever its N, and the tensor pipe runs two threads' N=64 products side by side
+    if (lane == 0 && N > 0) {
+      constexpr uint32_t idesc = idesc_tf32(128, 64);
+      const uint32_t ring = smem_u32(sRing);
+      bool ok = true;
+      for (int n = 0; n < N && ok && !s_abort; n++) {
         int t2 = kv_ring_pos(n, 2, N), t3 = kv_ring_pos(n, 3, N);
         if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[t2 % kSlots], (t2 / kSlots) & 1) ||
             !mbar_wait(&ring_full[t3 % kSlots], (t3 / kSlots) & 1)) { ok = false; break; }
@@ -257,7 +266,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         commit(&ring_empty[t2 % kSlots]);
         commit(&ring_empty[t3 % kSlots]);
       }
-      if (!ok) { atomicExch(a.error_flag, 22); s_abort = 1; }
+      if (!ok) { atomicExch(a.error_flag, 24); s_abort = 1; }
+      commit(&drained[1]);
+      mbar_wait(&drained[1], 0);
     }
   } else {
     const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
@@ -355,7 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
   uint64_t* st_free = bars + 8;
   uint64_t* pd_full = bars + 9;
   uint64_t* pd_free = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* drained = bars + 11;    // [2]: each issuer's MMAs have completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -375,6 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
     mbar_init(st_free, 8);
     mbar_init(pd_full, 8);
     mbar_init(pd_free, 1);
+    mbar_init(&drained[0], 1);
+    mbar_init(&drained[1], 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -418,20 +432,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
         commit(&ring_empty[1]);
         return true;
       };
-      if (ok) ok = issue_st(0);
       for (int n = 0; n < N && ok && !s_abort; n++) {
-        if (n + 1 < N) {
-          if (!mbar_wait(st_free, n & 1)) { ok = false; break; }
+        if (n > 0) {
+          if (!mbar_wait(st_free, (n - 1) & 1)) { ok = false; break; }
           fence_after();
-          if (!issue_st(n + 1)) { ok = false; break; }
         }
+        if (!issue_st(n)) { ok = false; break; }
+      }
+      if (!ok) { atomicExch(a.error_flag, 32); s_abort = 1; }
+      commit(&drained[0]);
+      mbar_wait(&drained[0], 0);
+    }
+  } else if (warp == kGradWarp) {
+    if (lane == 0 && N > 0) {
+      constexpr uint32_t idesc = idesc_tf32(128, 64);
+      const uint32_t ring = smem_u32(sRing);
+      bool ok = true;
+      for (int n = 0; n < N && ok && !s_abort; n++) {
         if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[2], n & 1)) { ok = false; break; }
         fence_after();
         mma_tmem_tile(tmem + cDQ, tmem + cDShi, tmem + cDSlo, ring + 2 * kTile, idesc, false);  // dQ_n = dS·K
         commit(pd_free);
         commit(&ring_empty[2]);
       }
-      if (!ok) { atomicExch(a.error_flag, 32); s_abort = 1; }
+      if (!ok) { atomicExch(a.error_flag, 33); s_abort = 1; }
+      commit(&drained[1]);
+      mbar_wait(&drained[1], 0);
     }
   } else {
     const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
