@@ -241,22 +241,27 @@ def decode_bench(local, cfg_name="1b", prompt_len=512, gen=256, batches=(1, 32))
             row[mode] = {"tok_s": n / (ms * 1e-3), "ms": ms, "generated": n, "prefill_ms": res["prefill_seconds"] * 1e3,
                          "decode_tok_s": b * (n // b - 1) / max(res["decode_seconds"], 1e-9)}
         out[f"batch{b}"] = row
-    # per-kernel device time of one greedy batch-1 generation: the weight-streaming GEMV is the dominant kernel
-    r = H.PcgRng(7)
-    prompt = [int(r.next_u32() % c["vocab_size"]) for _ in range(prompt_len)]
-    be.kernel_timing(True)
-    be.timer_start()
-    H.generate(be, m, prompt, 64, None, 1)
-    ms_timed = be.timer_stop()
-    stats = {f: be.kernel_stats(f) for f in ("gemv", "attn_decode", "gemm", "attn_fwd")}
-    be.kernel_timing(False)
-    g_launches, g_ms, g_bytes = stats["gemv"]
-    achieved = (g_bytes / max(g_launches, 1)) / ((g_ms / max(g_launches, 1)) * 1e-3) / 1e9 if g_ms else 0.0
-    out["roofline"] = {"bound": "hbm", "kernel": "k_gemv_tn (weight-streaming x·Wᵀ)", "achieved": achieved, "peak": hbm,
-                       "unit": "GB/s", "frac": achieved / hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
-                       "launches": g_launches, "avg_launch_ms": g_ms / max(g_launches, 1),
-                       "sample": "greedy batch 1, prompt 512 + 64 new tokens (prefill GEMMs excluded: family gemm)"}
-    out["kernels"] = {f: {"launches": v[0], "ms": v[1], "share": v[1] / ms_timed} for f, v in stats.items()}
+    # per-kernel device time of one greedy generation per batch size: the weight-streaming products dominate (batch 1:
+    # k_gemv_tn on the CUDA cores; batch 32: k_gemv_tc on the tensor cores)
+    for b in batches:
+        r = H.PcgRng(7)
+        prompt = [int(r.next_u32() % c["vocab_size"]) for _ in range(b * prompt_len)]
+        be.kernel_timing(True)
+        be.timer_start()
+        H.generate(be, m, prompt, 64, None, b)
+        ms_timed = be.timer_stop()
+        stats = {f: be.kernel_stats(f) for f in ("gemv", "attn_decode", "gemm", "attn_fwd")}
+        be.kernel_timing(False)
+        g_launches, g_ms, g_bytes = stats["gemv"]
+        achieved = (g_bytes / max(g_launches, 1)) / ((g_ms / max(g_launches, 1)) * 1e-3) / 1e9 if g_ms else 0.0
+        kernel = "k_gemv_tn (weight-streaming x·Wᵀ, CUDA cores)" if b <= 4 else "k_gemv_tc (weight-streaming x·Wᵀ, tcgen05 3xTF32)"
+        sfx = "" if b == 1 else f"_batch{b}"
+        out["roofline" + sfx] = {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                                 "frac": achieved / hbm, "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
+                                 "launches": g_launches, "avg_launch_ms": g_ms / max(g_launches, 1),
+                                 "sample": f"greedy batch {b}, prompt 512 + 64 new tokens (timed per call, x pack included; "
+                                           "prefill GEMMs excluded: family gemm)"}
+        out["kernels" + sfx] = {f: {"launches": v[0], "ms": v[1], "share": v[1] / ms_timed} for f, v in stats.items()}
     # whole decode steps against the HBM line: every weight and the cached K/V of every sequence are read once per
     # step (mean cache length over the run: prompt + half the new tokens)
     kv_row = 2 * c["kv_head_count"] * (c["embedding_dim"] // c["head_count"]) * 4 * c["layer_count"]
@@ -527,13 +532,15 @@ def main():
     ap.add_argument("--skip-decode", action="store_true", help="leave the ~1B decode measurement out of the N=1 line")
     ap.add_argument("--decode-only", action="store_true", help="print only the decode measurement")
     ap.add_argument("--decode-tokens", type=int, default=256)
+    ap.add_argument("--decode-batches", default="1,32", help="--decode-only: batch sizes to generate at")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
     if args.op:
         return op_sweep(args)
     if args.decode_only:
-        print(json.dumps(decode_bench(0, gen=args.decode_tokens)), flush=True)
+        print(json.dumps(decode_bench(0, gen=args.decode_tokens, batches=tuple(int(v) for v in args.decode_batches.split(",")))),
+              flush=True)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

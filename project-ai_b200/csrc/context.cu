@@ -30,13 +30,6 @@ pai_status cuda_error(cudaError_t e, const char* what) {
   return set_error(PAI_ERR_CUDA, "CUDA error in %s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("PAI_PDL");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
 
 pai_status enter(pai_ctx* ctx) {
   if (!ctx) return set_error(PAI_ERR_ARGUMENT, "null context");

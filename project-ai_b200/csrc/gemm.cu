@@ -580,8 +580,6 @@ __global__ void k_splitk_reduce(const float* __restrict__ part, float* __restric
 }
 
 // ---------------------------------------------------------------- host side
-// gemv.cu: the small-M weight-streaming path (PAI_GEMV=0 turns it off)
-bool gemv_enabled();
 pai_status gemv_tn(pai_ctx* ctx, const float* x, const int64_t* xoff, int rows, const float* w, int64_t sw, int n, int k,
                    float* y);
 
@@ -794,7 +792,7 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
 
   // Decode-sized x · Wᵀ (at most 32 rows against one weight matrix): weight-streaming kernel (gemv.cu).
   const int64_t rows_total = batch * (int64_t)m;
-  if (tb && gemv_enabled() && b_distinct.size() == 1 && rows_total <= 32 && sak == 1 && sbk == 1) {
+  if (tb && b_distinct.size() == 1 && rows_total <= 32 && sak == 1 && sbk == 1) {
     int64_t xo[32];
     int idx = 0;
     for (int64_t bi = 0; bi < batch; bi++)

@@ -27,6 +27,7 @@ constexpr int kGemvRowsPerWarp = 4;
 constexpr int kGemvThreads = 256;
 
 constexpr int kGemvMaxSegs = 4;
+constexpr int kGemvTcMinRows = 5;  // from 5 rows of x the products run on the tensor cores
 
 // Output epilogues: plain store, residual + x·Wᵀ (TransformerBlock's Add after a Linear), and SiLU(x·W0ᵀ)·(x·W1ᵀ)
 // (SwiGLU's gate and up products combined as SiluMul does).
@@ -530,12 +531,7 @@ static pai_status gemv_tc_segment(pai_ctx* ctx, const float* xh, const float* xl
   if (cr != CUDA_SUCCESS) return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for W [%d, %d]", (int)cr, n, k);
 
   const int n_tiles = (n + kRowsW - 1) / kRowsW;
-  static const int forced_splits = [] {
-    const char* e = getenv("PAI_GEMV_TC_SPLITS");
-    return e ? atoi(e) : 0;
-  }();
   int splits = std::max(1, std::min(2 * ctx->sm_count / n_tiles, kt / 4));
-  if (forced_splits > 0) splits = std::min(forced_splits, kt);
   int ktp = (kt + splits - 1) / splits;
   splits = (kt + ktp - 1) / ktp;
   Args a{};
@@ -583,14 +579,6 @@ static pai_status launch_gemv(pai_ctx* ctx, const GemvArgs& g, bool vec, int gri
   return set_error(PAI_ERR_ARGUMENT, "paired gemv takes at most 16 rows per launch");
 }
 
-bool gemv_enabled() {
-  static int on = [] {
-    const char* e = getenv("PAI_GEMV");
-    return e && e[0] == '0' ? 0 : 1;
-  }();
-  return on != 0;
-}
-
 // rows (<= 32) of x (element offsets xoff, each contiguous along k) against the weight segments, with an epilogue:
 //   store:    y[:, seg_start(s) + j] = x · W_sᵀ   (segments side by side)
 //   residual: y = res + x · W_0ᵀ
@@ -616,12 +604,7 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
   if (norm_w && (uintptr_t)norm_w % 16) vec = false;
   const int n_out = mode == kGemvStore ? n_total : segs[0].n;
   KernelTimerScope timer(ctx, "gemv", wbytes + 4.0 * rows * (k + n_out));
-  static const int tc_min_rows = [] {
-    const char* e = getenv("PAI_GEMV_TC_MIN_ROWS");
-    return e ? atoi(e) : 5;
-  }();
-
-  if (vec && rows >= tc_min_rows) {
+  if (vec && rows >= kGemvTcMinRows) {
     // tensor cores: split x once, one launch per weight segment, then the epilogue with the split-K sum
     using namespace gtc;
     const int np = rows <= 16 ? 16 : 32;

@@ -15,7 +15,10 @@ pytestmark = pytest.mark.gpu
                                       (17, 2048, 5632), (32, 2048, 4000), (2, 130, 99), (5, 1, 3),
                                       # tensor-core range (5..32 rows): ragged n and k, split-K and single-split grids
                                       (5, 100, 130), (12, 2052, 1000), (16, 5632, 2048), (24, 2048, 512),
-                                      (32, 2048, 32000), (32, 36, 129)])
+                                      (32, 2048, 32000), (32, 36, 129),
+                                      # stream-K partition: CTAs that cover several whole tiles, and tiles split over
+                                      # many CTAs (finished by the last to arrive)
+                                      (32, 32, 100000), (20, 96, 50000), (7, 2048, 300), (32, 5632, 2048)])
 def test_gemv_matches_float64(cuda, rows, k, n):
     x = rnd(30, rows, k)
     w = rnd(31, n, k, scale=0.02)
@@ -175,7 +178,35 @@ def test_graph_decoder_rejects_bad_ids_and_overflow():
 
 
 # ---------------------------------------------------------------- fused decode-step ops
-@pytest.mark.parametrize("rows", [1, 3, 8, 20])
+@pytest.mark.parametrize("rows", [5, 32])
+def test_linear_fused_at_the_1b_decode_shapes(rows):
+    """The 1B decode step's products at batch 5 and 32: q/k/v side by side, SwiGLU gate/up with SiLU·mul, the down
+    projection with the residual (k = 5632), against float64."""
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", 0)
+    rs = np.random.RandomState(40 + rows)
+    x = rs.standard_normal((rows, 2048)).astype(np.float32)
+    h = rs.standard_normal((rows, 5632)).astype(np.float32)
+    w = lambda n, k: (rs.standard_normal((n, k)) * 0.02).astype(np.float32)
+    wq, wk, wv, wg, wu, wd = w(2048, 2048), w(512, 2048), w(512, 2048), w(5632, 2048), w(5632, 2048), w(2048, 5632)
+    res = rs.standard_normal((rows, 2048)).astype(np.float32)
+    x64, h64 = x.astype(np.float64), h.astype(np.float64)
+    tx = be.from_host(x)
+    got = be.to_host(be.linear_fused(tx, [be.from_host(t) for t in (wq, wk, wv)], 0))
+    exp = x64 @ np.concatenate([wq, wk, wv]).astype(np.float64).T
+    bound = np.abs(x64) @ np.abs(np.concatenate([wq, wk, wv])).astype(np.float64).T
+    assert np.abs(got - exp).max() <= 1e-5 * bound.max()
+    got = be.to_host(be.linear_fused(tx, [be.from_host(wg), be.from_host(wu)], 2))
+    g, u = x64 @ wg.astype(np.float64).T, x64 @ wu.astype(np.float64).T
+    exp = g / (1 + np.exp(-g)) * u
+    assert np.abs(got - exp).max() <= 1e-4 * np.abs(exp).max()
+    got = be.to_host(be.linear_fused(be.from_host(h), [be.from_host(wd)], 1, be.from_host(res)))
+    exp = res.astype(np.float64) + h64 @ wd.astype(np.float64).T
+    bound = np.abs(h64) @ np.abs(wd).astype(np.float64).T
+    assert np.abs(got - exp).max() <= 1e-5 * bound.max() + 1e-6 * np.abs(exp).max()
+    be.check_device_error()
+
+
+@pytest.mark.parametrize("rows", [1, 3, 8, 20, 32])
 def test_linear_fused_modes_match_float64(rows):
     be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", 0)
     rs = np.random.RandomState(rows)
@@ -202,6 +233,11 @@ def test_linear_fused_modes_match_float64(rows):
     assert np.abs(got - exp).max() <= 1e-4 * max(np.abs(exp).max(), 1e-3)
     with pytest.raises(H.ArgumentError):
         be.linear_fused(tx, [tw[0], tw[1]], 2)  # SiLU·mul needs two weights of one shape
+    # split-K partials are added in a fixed order (the last CTA to arrive sums them by k): repeated calls agree bit for bit
+    for mode, ws_, r_ in ((0, tw, None), (1, [tw[0]], be.from_host(res)), (2, [tw[1], tw[2]], None)):
+        first = be.to_host(be.linear_fused(tx, ws_, mode, r_))
+        for _ in range(3):
+            assert np.array_equal(be.to_host(be.linear_fused(tx, ws_, mode, r_)), first)
     # with a norm weight: the same values as RmsNorm followed by the product (the normalised rows are bit-identical)
     nw = be.from_host((1 + 0.1 * rs.standard_normal(k)).astype(np.float32))
     fused = be.to_host(be.linear_fused(tx, tw, 0, None, nw, 1e-5))
