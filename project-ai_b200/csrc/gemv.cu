@@ -253,13 +253,23 @@ constexpr int kWBytes = kRowsW * kK * 4;
 constexpr int kThreads = 192;    // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 converters / epilogue
 constexpr uint32_t kColAcc = 0;
 
+constexpr int kMaxSegs = kGemvMaxSegs;
+
+// The weight segments of one call share a launch: grid x runs over every segment's 128-row tiles in order.
+struct Maps {
+  CUtensorMap w[kMaxSegs];       // W_s [n_s, k]: 128-row x 32-k boxes, 128-byte swizzle, zero fill
+};
+
 struct Args {
   const float* xhi;              // [kt][rows_pad x 32] pre-split, swizzled x tiles
   const float* xlo;
-  float* out;                    // direct: row m at out + m * ldo; partials: [splits][rows, n] (ldo = n)
-  int64_t ldo;
+  float* out;                    // row m of split q at out + q * split_stride + m * ldo, segment s from column col_start[s]
+  int64_t ldo, split_stride;
   int* error_flag;
-  int rows, rows_pad, n, kt, kt_per_split;
+  int rows, rows_pad, kt, kt_per_split;
+  int tile_start[kMaxSegs + 1];  // first grid-x tile of each segment (unused entries: the tile count)
+  int n_seg[kMaxSegs];           // rows of each W segment
+  int col_start[kMaxSegs];       // output column of each segment's first row
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -271,7 +281,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 }
 
 template <int NP>  // NP: x rows padded to the MMA's N (16 or 32)
-__global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CUtensorMap wmap, const Args a) {
+__global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ Maps maps, const Args a) {
   constexpr uint32_t kColA = 64;
   constexpr uint32_t kTmemCols = 256;
   constexpr int kXBytes = NP * 128;
@@ -287,7 +297,14 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kRowsW;
+  // this CTA's weight segment (selected with constant indices: a dynamic index into the parameters would copy
+  // them to local memory)
+  int seg = 0, seg_tile0 = a.tile_start[0], seg_n = a.n_seg[0], seg_col = a.col_start[0];
+#pragma unroll
+  for (int i = 1; i < kMaxSegs; i++)
+    if ((int)blockIdx.x >= a.tile_start[i]) { seg = i; seg_tile0 = a.tile_start[i]; seg_n = a.n_seg[i]; seg_col = a.col_start[i]; }
+  const CUtensorMap* wmap = &maps.w[0] + seg;
+  const int n0 = ((int)blockIdx.x - seg_tile0) * kRowsW;
   const int split = blockIdx.y;
   const int k0 = split * a.kt_per_split, k1 = min(a.kt, k0 + a.kt_per_split);
   const int nk = k1 - k0;
@@ -307,12 +324,12 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
 
   if (warp == 0) {
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(wmap)) : "memory");
       // the first stages' weight tiles are requested before waiting on the previous kernel (which wrote x's tiles)
       const int pre = nk < kStages ? nk : kStages;
       for (int i = 0; i < pre; i++) {
         mbar_expect_tx(&full[i], kWBytes + 2 * kXBytes);
-        tma_load_2d(smem + i * kStage, &wmap, (k0 + i) * kK, n0, &full[i]);
+        tma_load_2d(smem + i * kStage, wmap, (k0 + i) * kK, n0, &full[i]);
       }
       pdl_wait();
       int issued = 0;
@@ -322,7 +339,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
         if (i >= pre) {
           if (!mbar_wait(&stage_free[s], ((i / kStages) & 1) ^ 1)) { atomicExch(a.error_flag, 41); s_abort = 1; break; }
           mbar_expect_tx(&full[s], kWBytes + 2 * kXBytes);
-          tma_load_2d(st, &wmap, (k0 + i) * kK, n0, &full[s]);
+          tma_load_2d(st, wmap, (k0 + i) * kK, n0, &full[s]);
         }
         size_t xoff = (size_t)(k0 + i) * (kXBytes / 4);
         bulk_g2s(st + kWBytes, a.xhi + xoff, kXBytes, &full[s]);
@@ -393,8 +410,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv_tc(const __grid_constant__ CU
       float v[32];
       tmem_ld32(tmem + lane_base + kColAcc, v);
       const int n = n0 + r;
-      float* dst = a.out + (size_t)split * a.rows * a.ldo;
-      if (n < a.n) {
+      float* dst = a.out + (size_t)split * a.split_stride + seg_col;
+      if (n < seg_n) {
 #pragma unroll
         for (int m = 0; m < NP; m++)
           if (m < a.rows) dst[(size_t)m * a.ldo + n] = v[m];
@@ -466,23 +483,24 @@ constexpr size_t smem_bytes() {
   return (size_t)kStages * (kWBytes + 2 * NP * 128) + 1024 + 256;
 }
 
-// Sums the split-K partials of up to two products in split order and applies the epilogue:
-// y[m, c] = a (store), res[m, c] + a (residual), SiLU(a)·b (SiLU·mul).
-__global__ void k_gemv_finish(const float* __restrict__ pa, int sa, const float* __restrict__ pb, int sb, int rows, int n,
+// Sums the split-K partials (split q of row m at p + q * plane + m * ldp) in split order and applies the epilogue:
+// y[m, c] = a (store), res[m, c] + a (residual), SiLU(a)·b (SiLU·mul; b from column colb + c of the same partials).
+__global__ void k_gemv_finish(const float* __restrict__ p, int splits, int64_t plane, int64_t ldp, int colb, int rows, int n,
                               float* __restrict__ y, int64_t ldy, int mode, const float* __restrict__ res, int64_t ldr) {
   pdl_trigger();
   pdl_wait();
-  const int64_t total = (int64_t)rows * n, plane = total;
+  const int64_t total = (int64_t)rows * n;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     int m = (int)(i / n), c = (int)(i - (int64_t)m * n);
-    float va = pa[i];
-    for (int q = 1; q < sa; q++) va += pa[q * plane + i];
+    const float* pm = p + (int64_t)m * ldp + c;
+    float va = pm[0];
+    for (int q = 1; q < splits; q++) va += pm[q * plane];
     float out = va;
     if (mode == kGemvResidual) {
       out = __fadd_rn(res[(int64_t)m * ldr + c], va);
     } else if (mode == kGemvSiluMul) {
-      float vb = pb[i];
-      for (int q = 1; q < sb; q++) vb += pb[q * plane + i];
+      float vb = pm[colb];
+      for (int q = 1; q < splits; q++) vb += pm[q * plane + colb];
       out = silu_mul_value(va, vb);
     }
     y[(int64_t)m * ldy + c] = out;
@@ -510,50 +528,75 @@ struct LinearSeg {
   int n;
 };
 
-// Tensor-core product of pre-split x tiles against one W: writes y (row m at out + m * ldo) directly when partial is
-// false and one split suffices, else split-K partials [splits][rows, n] into a scratch buffer returned in `part`.
-static pai_status gemv_tc_segment(pai_ctx* ctx, const float* xh, const float* xl, int rows, int np, int k, const LinearSeg& sg,
-                                  float* out, int64_t ldo, bool force_partial, Scratch* part, int* splits_out) {
+// Tensor-core product of pre-split x tiles against all weight segments in one launch (grid x over the segments'
+// 128-row tiles, y over the K splits), then the epilogue: store mode with one split writes y directly (segments side
+// by side); otherwise split-K partials [splits][rows, n_total] go to a scratch buffer that k_gemv_finish sums in split
+// order with the store / residual / SiLU·mul epilogue.
+static pai_status gemv_tc(pai_ctx* ctx, const float* xh, const float* xl, int rows, int np, int k, const LinearSeg* segs,
+                          int nseg, int mode, float* y, int64_t ldy, const float* res, int64_t ldr) {
   using namespace gtc;
   auto encode = tensor_map_encoder();
   if (!encode) return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   const int kt = (k + kK - 1) / kK;
-  const int n = sg.n;
-  // W [n, k] row-major with row stride sw: a 2-D tensor map of 128-row x 32-k boxes, 128-byte swizzle, zero fill
-  CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)n};
-  cuuint64_t strides[1] = {(cuuint64_t)sg.sw * 4};
-  cuuint32_t box[2] = {(cuuint32_t)kK, (cuuint32_t)kRowsW};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(sg.w), dims, strides, box, estr,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for W [%d, %d]", (int)cr, n, k);
-
-  const int n_tiles = (n + kRowsW - 1) / kRowsW;
-  int splits = std::max(1, std::min(2 * ctx->sm_count / n_tiles, kt / 4));
+  Maps maps;
+  memset(&maps, 0, sizeof maps);
+  Args a{};
+  int tiles = 0, n_total = 0;
+  for (int s = 0; s < nseg; s++) {
+    const LinearSeg& sg = segs[s];
+    // W [n, k] row-major with row stride sw: a 2-D tensor map of 128-row x 32-k boxes, 128-byte swizzle, zero fill
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)sg.n};
+    cuuint64_t strides[1] = {(cuuint64_t)sg.sw * 4};
+    cuuint32_t box[2] = {(cuuint32_t)kK, (cuuint32_t)kRowsW};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult cr = encode(&maps.w[s], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(sg.w), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS)
+      return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for W [%d, %d]", (int)cr, sg.n, k);
+    a.tile_start[s] = tiles;
+    a.n_seg[s] = sg.n;
+    a.col_start[s] = n_total;
+    n_total += sg.n;
+    tiles += (sg.n + kRowsW - 1) / kRowsW;
+  }
+  for (int s = nseg; s <= kMaxSegs; s++) a.tile_start[s] = tiles;
+  int splits = std::max(1, std::min(2 * ctx->sm_count / tiles, kt / 4));
   int ktp = (kt + splits - 1) / splits;
   splits = (kt + ktp - 1) / ktp;
-  Args a{};
-  a.xhi = xh; a.xlo = xl;
+  a.xhi = xh;
+  a.xlo = xl;
   a.error_flag = ctx->d_error_flag;
-  a.rows = rows; a.rows_pad = np; a.n = n; a.kt = kt; a.kt_per_split = ktp;
-  if (splits > 1 || force_partial) {
-    PAI_TRY(scratch(ctx, (size_t)splits * rows * n * 4, part));
-    a.out = static_cast<float*>(part->p);
-    a.ldo = n;
+  a.rows = rows;
+  a.rows_pad = np;
+  a.kt = kt;
+  a.kt_per_split = ktp;
+  const bool direct = mode == kGemvStore && splits == 1;
+  Scratch part;
+  if (direct) {
+    a.out = y;
+    a.ldo = ldy;
   } else {
-    a.out = out;
-    a.ldo = ldo;
+    PAI_TRY(scratch(ctx, (size_t)splits * rows * n_total * 4, &part));
+    a.out = static_cast<float*>(part.p);
+    a.ldo = n_total;
+    a.split_stride = (int64_t)rows * n_total;
   }
-  *splits_out = (splits > 1 || force_partial) ? splits : 0;
-  dim3 grid((unsigned)n_tiles, (unsigned)splits);
+  dim3 grid((unsigned)tiles, (unsigned)splits);
   if (np == 16) {
     PAI_CUDA(smem_limit(ctx, k_gemv_tc<16>, (int)smem_bytes<16>()));
-    PAI_PDL_LAUNCH(launch_pdl(k_gemv_tc<16>, grid, dim3(kThreads), smem_bytes<16>(), ctx->stream, map, a), "gemv tc");
+    PAI_PDL_LAUNCH(launch_pdl(k_gemv_tc<16>, grid, dim3(kThreads), smem_bytes<16>(), ctx->stream, maps, a), "gemv tc");
   } else {
     PAI_CUDA(smem_limit(ctx, k_gemv_tc<32>, (int)smem_bytes<32>()));
-    PAI_PDL_LAUNCH(launch_pdl(k_gemv_tc<32>, grid, dim3(kThreads), smem_bytes<32>(), ctx->stream, map, a), "gemv tc");
+    PAI_PDL_LAUNCH(launch_pdl(k_gemv_tc<32>, grid, dim3(kThreads), smem_bytes<32>(), ctx->stream, maps, a), "gemv tc");
+  }
+  if (!direct) {
+    const int n_out = mode == kGemvStore ? n_total : segs[0].n;
+    const int64_t nn = (int64_t)rows * n_out;
+    PAI_PDL_LAUNCH(launch_pdl(k_gemv_finish, dim3(grid_for(ctx, nn, 256)), dim3(256), 0, ctx->stream,
+                              static_cast<const float*>(part.p), splits, (int64_t)rows * n_total, (int64_t)n_total,
+                              mode == kGemvSiluMul ? segs[0].n : 0, rows, n_out, y, ldy, mode, res, ldr),
+                   "gemv finish");
   }
   return PAI_OK;
 }
@@ -605,7 +648,7 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
   const int n_out = mode == kGemvStore ? n_total : segs[0].n;
   KernelTimerScope timer(ctx, "gemv", wbytes + 4.0 * rows * (k + n_out));
   if (vec && rows >= kGemvTcMinRows) {
-    // tensor cores: split x once, one launch per weight segment, then the epilogue with the split-K sum
+    // tensor cores: split x once, one launch over every weight segment, then the epilogue with the split-K sum
     using namespace gtc;
     const int np = rows <= 16 ? 16 : 32;
     const int kt = (k + kK - 1) / kK;
@@ -619,35 +662,8 @@ pai_status linear_rows(pai_ctx* ctx, const float* x, const int64_t* xoff, int ro
     for (int i = 0; i < rows; i++) xp.xoff[i] = xoff[i];
     PAI_PDL_LAUNCH(launch_pdl(k_pack_x, dim3(np), dim3(256), 0, ctx->stream, xp, static_cast<float*>(xh.p),
                               static_cast<float*>(xl.p)), "gemv x pack");
-    const float* xhp = static_cast<const float*>(xh.p);
-    const float* xlp = static_cast<const float*>(xl.p);
-    if (mode == kGemvStore) {
-      int col = 0;
-      for (int s = 0; s < nseg; s++) {
-        Scratch part;
-        int sp = 0;
-        PAI_TRY(gemv_tc_segment(ctx, xhp, xlp, rows, np, k, segs[s], y + col, ldy, false, &part, &sp));
-        if (sp) {
-          int64_t nn = (int64_t)rows * segs[s].n;
-          PAI_PDL_LAUNCH(launch_pdl(k_gemv_finish, dim3(grid_for(ctx, nn, 256)), dim3(256), 0, ctx->stream,
-                                    static_cast<const float*>(part.p), sp, static_cast<const float*>(nullptr), 0, rows,
-                                    segs[s].n, y + col, ldy, (int)kGemvStore, static_cast<const float*>(nullptr), (int64_t)0),
-                         "gemv finish");
-        }
-        col += segs[s].n;
-      }
-      return PAI_OK;
-    }
-    Scratch pa, pb;
-    int sa = 0, sb = 0;
-    PAI_TRY(gemv_tc_segment(ctx, xhp, xlp, rows, np, k, segs[0], nullptr, 0, true, &pa, &sa));
-    if (mode == kGemvSiluMul) PAI_TRY(gemv_tc_segment(ctx, xhp, xlp, rows, np, k, segs[1], nullptr, 0, true, &pb, &sb));
-    int64_t nn = (int64_t)rows * segs[0].n;
-    PAI_PDL_LAUNCH(launch_pdl(k_gemv_finish, dim3(grid_for(ctx, nn, 256)), dim3(256), 0, ctx->stream,
-                              static_cast<const float*>(pa.p), sa, static_cast<const float*>(pb.p), sb, rows, segs[0].n, y,
-                              ldy, mode, res, ldr),
-                   "gemv finish");
-    return PAI_OK;
+    return gemv_tc(ctx, static_cast<const float*>(xh.p), static_cast<const float*>(xl.p), rows, np, k, segs, nseg, mode, y,
+                   ldy, res, ldr);
   }
 
   if (mode == kGemvSiluMul && rows > 16) {
