@@ -5,10 +5,11 @@
 //   P = exp(S − lse), dP = dO·Vᵀ, dS = P ⊙ (dP − rowsum(dO ⊙ O)),
 //   dV = Σ_group Pᵀ·dO,  dK = Σ_group dSᵀ·(q·scale),  dQ = scale · dS·K.
 //
-// Two kernels, 352 threads each (warp 0 bulk-copy producer, warp 1 issuer of the score products, warps 2-9
-// element-wise — two warps per TMEM lane quadrant, 32 of each 64-wide block's columns per thread — and warp 10 issuer
-// of the gradient products: one thread issues a tf32 MMA about every 115 cycles whatever its N, and the tensor pipe
-// overlaps two threads' N=64 products):
+// Two kernels, 352 threads each (warp 0 bulk-copy producer, warps 2-9 element-wise — two warps per TMEM lane quadrant,
+// 32 of each 64-wide block's columns per thread — and MMA issuers: in the dQ kernel lanes 0 and 16 of warp 1 issue S
+// and dP and lane 0 of warp 10 dQ, each from its own ring slot (one thread issues a tf32 MMA about every 115 cycles
+// whatever its N, and the tensor pipe overlaps several threads' N=64 products); the dK/dV kernel's single issuer
+// consumes its shared ring in load order):
 //   k_attn_bwd_kv_tc  128 keys of one (batch, kv head) stay resident (K, V as A operands in shared memory); the
 //                     group's heads x 64-query blocks stream through a 3-slot ring (q·scale, dO, dOᵀ, (q·scale)ᵀ);
 //                     Sᵀ and dPᵀ land in TMEM, Pᵀ / dSᵀ go back to TMEM as hi/lo A operands of dV += Pᵀ·dO and
@@ -122,23 +123,28 @@ __device__ __forceinline__ void kv_ring_item(int i, int N, int& n, int& type) {
 }
 
 
+// 32 values -> TMEM as tf32 hi/lo, 8 columns at a time (the element-wise warps keep their block's scores and both
+// gradient accumulators in registers meanwhile).
 __device__ __forceinline__ void store_hilo(uint32_t hi_addr, uint32_t lo_addr, const float* x) {
 #pragma unroll
-  for (int h = 0; h < 2; h++) {
-    float hi[16], lo[16];
+  for (int h = 0; h < 4; h++) {
+    float hi[8], lo[8];
 #pragma unroll
-    for (int c = 0; c < 16; c++) split_tf32_fast(x[16 * h + c], hi[c], lo[c]);
-    tmem_st16(hi_addr + 16 * h, hi);
-    tmem_st16(lo_addr + 16 * h, lo);
+    for (int c = 0; c < 8; c++) split_tf32_fast(x[8 * h + c], hi[c], lo[c]);
+    tmem_st8(hi_addr + 8 * h, hi);
+    tmem_st8(lo_addr + 8 * h, lo);
   }
 }
 
-// acc += 32 TMEM columns of this warp's lanes (one block's partial gradient rows).
+// acc += 32 TMEM columns of this warp's lanes (one block's partial gradient rows), 8 at a time.
 __device__ __forceinline__ void add_partial(uint32_t taddr, float* acc) {
-  float v[32];
-  tmem_ld32(taddr, v);
 #pragma unroll
-  for (int c = 0; c < 32; c++) acc[c] += v[c];
+  for (int h = 0; h < 4; h++) {
+    float v[8];
+    tmem_ld8(taddr + 8 * h, v);
+#pragma unroll
+    for (int c = 0; c < 8; c++) acc[8 * h + c] += v[c];
+  }
 }
 
 // ---------------------------------------------------------------- dK, dV
@@ -156,8 +162,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
   uint64_t* st_free = bars + 8;
   uint64_t* pd_full = bars + 9;
   uint64_t* pd_free = bars + 10;
-  uint64_t* drained = bars + 11;    // [2]: each issuer's MMAs have completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* drained = bars + 11;    // [4]: each issuer's MMAs have completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -183,8 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
     mbar_init(st_free, 8);
     mbar_init(pd_full, 8);
     mbar_init(pd_free, 1);
-    mbar_init(&drained[0], 1);
-    mbar_init(&drained[1], 1);
+    for (int i = 0; i < 4; i++) mbar_init(&drained[i], 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -207,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         int n, type;
         kv_ring_item(t, N, n, type);
         int slot = t % kSlots;
-        if (!mbar_wait(&ring_empty[slot], ((t / kSlots) & 1) ^ 1)) { atomicExch(a.error_flag, 21); s_abort = 1; break; }
+        if (!mbar_wait(&ring_empty[slot], ((t / kSlots) & 1) ^ 1)) { atomicCAS(a.error_flag, 0, 21); s_abort = 1; break; }
         int h = head_of(n), qb = qblk_of(n);
         const float* src;
         if (type == 0) src = a.qs + ((size_t)(b * a.H + h) * a.nq2 + qb) * (kTile / 4);
@@ -220,6 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
       for (int t = 4 * N; t < 4 * N + kSlots; t++) mbar_wait(&ring_empty[t % kSlots], ((t / kSlots) & 1) ^ 1);
     }
   } else if (warp == 1) {
+    // one issuing thread: the 3-slot ring interleaves four operand streams and must be consumed in its load order (a
+    // second consumer thread could wait on a slot two loads ahead, where the mbarrier's phase parity reads an older
+    // completed phase as this one); warp 10 idles in this kernel
     if (lane == 0 && N > 0) {
       constexpr uint32_t idesc = idesc_tf32(128, 64);
       const uint32_t k_s = smem_u32(sK), v_s = smem_u32(sV), ring = smem_u32(sRing);
@@ -236,26 +244,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         commit(&ring_empty[t1 % kSlots]);
         return true;
       };
-      // the scores of block n once the element-wise warps have read block n-1's
+      if (ok) ok = issue_st(0);
       for (int n = 0; n < N && ok && !s_abort; n++) {
-        if (n > 0) {
-          if (!mbar_wait(st_free, (n - 1) & 1)) { ok = false; break; }
+        if (n + 1 < N) {
+          if (!mbar_wait(st_free, n & 1)) { ok = false; break; }
           fence_after();
+          if (!issue_st(n + 1)) { ok = false; break; }
         }
-        if (!issue_st(n)) { ok = false; break; }
-      }
-      if (!ok) { atomicExch(a.error_flag, 22); s_abort = 1; }
-      commit(&drained[0]);
-      mbar_wait(&drained[0], 0);
-    }
-  } else if (warp == kGradWarp) {
-    // the gradient products, issued by a second thread: one thread issues a tf32 MMA about every 115 cycles
-    // whatever its N, and the tensor pipe runs two threads' N=64 products side by side
-    if (lane == 0 && N > 0) {
-      constexpr uint32_t idesc = idesc_tf32(128, 64);
-      const uint32_t ring = smem_u32(sRing);
-      bool ok = true;
-      for (int n = 0; n < N && ok && !s_abort; n++) {
         int t2 = kv_ring_pos(n, 2, N), t3 = kv_ring_pos(n, 3, N);
         if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[t2 % kSlots], (t2 / kSlots) & 1) ||
             !mbar_wait(&ring_full[t3 % kSlots], (t3 / kSlots) & 1)) { ok = false; break; }
@@ -266,11 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         commit(&ring_empty[t2 % kSlots]);
         commit(&ring_empty[t3 % kSlots]);
       }
-      if (!ok) { atomicExch(a.error_flag, 24); s_abort = 1; }
-      commit(&drained[1]);
-      mbar_wait(&drained[1], 0);
+      if (!ok) { atomicCAS(a.error_flag, 0, 22); s_abort = 1; }
+      // every MMA this thread issued completes before the CTA releases its tensor memory
+      commit(&drained[0]);
+      mbar_wait(&drained[0], 0);
     }
-  } else {
+  } else if (warp < kGradWarp) {  // warp 10 has no role in this kernel
     const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
     const int row = quad * 32 + lane;
     const int key = j0 + row;
@@ -290,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
       float s[32], dp[32];
 #pragma unroll
       for (int c = 0; c < 32; c++) { s[c] = 0.0f; dp[c] = 0.0f; }
-      if (ok && !warp_wait(st_full, n & 1)) ok = false;
+      if (ok && !warp_wait(st_full, n & 1)) { ok = false; if (lane == 0) atomicCAS(a.error_flag, 0, 26 + 0); }
       if (ok) {
         fence_after();
         tmem_ld32(tmem + lane_off + cS + col, s);
@@ -310,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         s[c] = p;
         dp[c] = p * (dp[c] - dvq);
       }
-      if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) ok = false;
+      if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) { ok = false; if (lane == 0) atomicCAS(a.error_flag, 0, 26 + 1); }
       if (ok && n > 0) {
         // block n-1's products are done: fold them in before block n's P / dS (and then its products) reuse TMEM
         fence_after();
@@ -326,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         if (lane == 0) mbar_arrive(pd_full);
       }
     }
-    if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) ok = false;
+    if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) { ok = false; if (lane == 0) atomicCAS(a.error_flag, 0, 26 + 2); }
     if (ok || N == 0) {
       // keys that no query sees (N == 0) get zero gradients: every output row is written
       if (N > 0) {
@@ -341,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
           if ((int)col + d < a.D) { a.dv[base + col + d] = dvv[d]; a.dk[base + col + d] = dkk[d]; }
       }
     }
-    if (!ok && N > 0 && lane == 0) { atomicExch(a.error_flag, 23); s_abort = 1; }
+    if (!ok && N > 0 && lane == 0) s_abort = 1;
   }
   fence_before();
   __syncthreads();
@@ -366,8 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
   uint64_t* st_free = bars + 8;
   uint64_t* pd_full = bars + 9;
   uint64_t* pd_free = bars + 10;
-  uint64_t* drained = bars + 11;    // [2]: each issuer's MMAs have completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* drained = bars + 11;    // [4]: each issuer's MMAs have completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -383,12 +379,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
     for (int i = 0; i < kSlots; i++) { mbar_init(&ring_full[i], 1); mbar_init(&ring_empty[i], 1); }
-    mbar_init(st_full, 1);
+    mbar_init(st_full, 2);   // the S and dP issuers
     mbar_init(st_free, 8);
     mbar_init(pd_full, 8);
     mbar_init(pd_free, 1);
-    mbar_init(&drained[0], 1);
-    mbar_init(&drained[1], 1);
+    for (int i = 0; i < 4; i++) mbar_init(&drained[i], 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -406,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
       load_resident(sDO, a.dO + qbase, a_full);
       for (int n = 0; n < N && !s_abort; n++) {
         for (int type = 0; type < 3; type++) {
-          if (!mbar_wait(&ring_empty[type], (n & 1) ^ 1)) { atomicExch(a.error_flag, 31); s_abort = 1; break; }
+          if (!mbar_wait(&ring_empty[type], (n & 1) ^ 1)) { atomicCAS(a.error_flag, 0, 31); s_abort = 1; break; }
           const float* src;
           if (type == 0) src = a.k + ((size_t)(b * a.KVH + kvh) * a.nk2 + n) * (kTile / 4);
           else if (type == 1) src = a.v + ((size_t)(b * a.KVH + kvh) * a.nk2 + n) * (kTile / 4);
@@ -417,47 +412,36 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
       }
       for (int type = 0; type < 3; type++) mbar_wait(&ring_empty[type], (N & 1) ^ 1);
     }
-  } else if (warp == 1) {
-    if (lane == 0 && N > 0) {
-      constexpr uint32_t idesc = idesc_tf32(128, 64);
-      const uint32_t q_s = smem_u32(sQ), do_s = smem_u32(sDO), ring = smem_u32(sRing);
-      bool ok = mbar_wait(a_full, 0);
-      auto issue_st = [&](int n) -> bool {
-        if (!mbar_wait(&ring_full[0], n & 1) || !mbar_wait(&ring_full[1], n & 1)) return false;
-        fence_after();
-        mma_res_tile(tmem + cS, q_s, ring, idesc);            // S  = (q·scale)·Kᵀ
-        mma_res_tile(tmem + cDP, do_s, ring + kTile, idesc);  // dP = dO·Vᵀ
-        commit(st_full);
-        commit(&ring_empty[0]);
-        commit(&ring_empty[1]);
-        return true;
-      };
-      for (int n = 0; n < N && ok && !s_abort; n++) {
-        if (n > 0) {
-          if (!mbar_wait(st_free, (n - 1) & 1)) { ok = false; break; }
-          fence_after();
-        }
-        if (!issue_st(n)) { ok = false; break; }
-      }
-      if (!ok) { atomicExch(a.error_flag, 32); s_abort = 1; }
-      commit(&drained[0]);
-      mbar_wait(&drained[0], 0);
-    }
-  } else if (warp == kGradWarp) {
-    if (lane == 0 && N > 0) {
+  } else if (warp == 1 || warp == kGradWarp) {
+    // three issuing threads: S and dP from lanes 0 and 16 of warp 1, dQ from lane 0 of warp 10
+    const int role = warp == 1 ? (lane == 16 ? 1 : 0) : 2;  // 0 S, 1 dP, 2 dQ
+    if ((warp == 1 ? (lane == 0 || lane == 16) : lane == 0) && N > 0) {
       constexpr uint32_t idesc = idesc_tf32(128, 64);
       const uint32_t ring = smem_u32(sRing);
       bool ok = true;
-      for (int n = 0; n < N && ok && !s_abort; n++) {
-        if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[2], n & 1)) { ok = false; break; }
-        fence_after();
-        mma_tmem_tile(tmem + cDQ, tmem + cDShi, tmem + cDSlo, ring + 2 * kTile, idesc, false);  // dQ_n = dS·K
-        commit(pd_free);
-        commit(&ring_empty[2]);
+      if (role < 2) {
+        const uint32_t a_s = smem_u32(role == 0 ? sQ : sDO), d = tmem + (role == 0 ? cS : cDP);
+        ok = mbar_wait(a_full, 0);
+        for (int n = 0; n < N && ok && !s_abort; n++) {
+          if (n > 0 && !mbar_wait(st_free, (n - 1) & 1)) { ok = false; break; }
+          if (!mbar_wait(&ring_full[role], n & 1)) { ok = false; break; }
+          fence_after();
+          mma_res_tile(d, a_s, ring + role * kTile, idesc);  // S = (q·scale)·Kᵀ, dP = dO·Vᵀ
+          commit(st_full);
+          commit(&ring_empty[role]);
+        }
+      } else {
+        for (int n = 0; n < N && ok && !s_abort; n++) {
+          if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[2], n & 1)) { ok = false; break; }
+          fence_after();
+          mma_tmem_tile(tmem + cDQ, tmem + cDShi, tmem + cDSlo, ring + 2 * kTile, idesc, false);  // dQ_n = dS·K
+          commit(pd_free);
+          commit(&ring_empty[2]);
+        }
       }
-      if (!ok) { atomicExch(a.error_flag, 33); s_abort = 1; }
-      commit(&drained[1]);
-      mbar_wait(&drained[1], 0);
+      if (!ok) { atomicCAS(a.error_flag, 0, 32 + role); s_abort = 1; }
+      commit(&drained[role]);
+      mbar_wait(&drained[role], 0);
     }
   } else {
     const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
@@ -476,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
       float s[32], dp[32];
 #pragma unroll
       for (int c = 0; c < 32; c++) { s[c] = 0.0f; dp[c] = 0.0f; }
-      if (ok && !warp_wait(st_full, n & 1)) ok = false;
+      if (ok && !warp_wait(st_full, n & 1)) { ok = false; if (lane == 0) atomicCAS(a.error_flag, 0, 36 + 0); }
       if (ok) {
         fence_after();
         tmem_ld32(tmem + lane_off + cS + col, s);
@@ -493,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
         float p = vis ? exp2f(fmaf(s[c], kLog2e, -lse2)) : 0.0f;
         dp[c] = p * (dp[c] - dvq);
       }
-      if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) ok = false;
+      if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) { ok = false; if (lane == 0) atomicCAS(a.error_flag, 0, 36 + 1); }
       if (ok && n > 0) {
         fence_after();
         add_partial(tmem + lane_off + cDQ + col, dq);  // block n-1's dS·K, before block n's dS and product
@@ -506,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
         if (lane == 0) mbar_arrive(pd_full);
       }
     }
-    if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) ok = false;
+    if (ok && N > 0 && !warp_wait(pd_free, (N - 1) & 1)) { ok = false; if (lane == 0) atomicCAS(a.error_flag, 0, 36 + 2); }
     if (ok || N == 0) {
       // queries that see no key (N == 0) get zero gradients: every output row is written
       if (N > 0) {
@@ -520,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
           if ((int)col + d < a.D) a.dq[base + col + d] = dq[d] * a.scale;
       }
     }
-    if (!ok && N > 0 && lane == 0) { atomicExch(a.error_flag, 33); s_abort = 1; }
+    if (!ok && N > 0 && lane == 0) s_abort = 1;
   }
   fence_before();
   __syncthreads();

@@ -285,10 +285,14 @@ __global__ void k_rotary_rows(const float* __restrict__ x, DView xr, const float
 // k_rotary_rows with one thread per 4 consecutive pairs (j..j+3, j+h..j+h+3) of a row: 16-byte loads of x, cos and
 // sin and 16-byte stores, all independent, so the pass streams at memory speed. Needs d % 8 == 0 and every row
 // start of x, cos and sin 16-byte aligned; the same element operations as k_rotary_rows.
+// HQ: float4 groups per half row when it is a compile-time constant (head dim 64: 8), else 0 (runtime d >> 3). Item
+// indices run in 32 bits when they fit (the integer division per item is the kernel's main instruction cost).
+template <int HQ, typename Idx>
 __global__ void k_rotary_rows4(const float* __restrict__ x, DView xr, const float* __restrict__ cs, DView cr,
                                const float* __restrict__ sn, DView sr, float* __restrict__ y, int64_t rows, int d,
                                RopeShift shift) {
-  const int half = d >> 1, hq = d >> 3;  // float4 groups per half row
+  const int hq = HQ ? HQ : d >> 3;
+  const int half = 4 * hq;
   int64_t dc = 0, ds = 0;
   if (shift.pos) {
     float pf = shift.pos[0];
@@ -300,10 +304,10 @@ __global__ void k_rotary_rows4(const float* __restrict__ x, DView xr, const floa
     dc = (int64_t)p * shift.stride_c;
     ds = (int64_t)p * shift.stride_s;
   }
-  const int64_t total = rows * hq;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / hq;
-    const int j = (int)(i - r * hq) * 4;
+  const Idx total = (Idx)(rows * hq);
+  for (Idx i = blockIdx.x * (Idx)blockDim.x + threadIdx.x; i < total; i += (Idx)gridDim.x * blockDim.x) {
+    const Idx r = i / (Idx)hq;
+    const int j = (int)(i - r * (Idx)hq) * 4;
     int64_t xo, co, so;
     row_offsets3(xr, cr, sr, (uint32_t)r, xo, co, so);
     co += dc;
@@ -343,10 +347,17 @@ __global__ void k_silu_mul_fwd(const float* __restrict__ gate, const float* __re
                                int64_t n, bool vec) {
   int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
   int64_t n4 = vec ? n >> 2 : 0;
-  for (int64_t i = tid; i < n4; i += stride) {
+  // two float4 of each input per trip: four 16-byte loads in flight per thread before the first store
+  for (int64_t i = tid; i < n4; i += 2 * stride) {
+    const int64_t i2 = i + stride;
+    const bool two = i2 < n4;
     float4 g4 = reinterpret_cast<const float4*>(gate)[i], u4 = reinterpret_cast<const float4*>(up)[i];
+    float4 g5 = two ? reinterpret_cast<const float4*>(gate)[i2] : g4, u5 = two ? reinterpret_cast<const float4*>(up)[i2] : u4;
     reinterpret_cast<float4*>(o)[i] =
         make_float4(silu_mul_elem(g4.x, u4.x), silu_mul_elem(g4.y, u4.y), silu_mul_elem(g4.z, u4.z), silu_mul_elem(g4.w, u4.w));
+    if (two)
+      reinterpret_cast<float4*>(o)[i2] =
+          make_float4(silu_mul_elem(g5.x, u5.x), silu_mul_elem(g5.y, u5.y), silu_mul_elem(g5.z, u5.z), silu_mul_elem(g5.w, u5.w));
   }
   for (int64_t i = (n4 << 2) + tid; i < n; i += stride) o[i] = silu_mul_elem(gate[i], up[i]);
 }
@@ -564,9 +575,13 @@ static pai_status rotary_impl(pai_ctx* ctx, const pai_tensor* x, const pai_tenso
           if (dv[v].dims[i] > 1 && dv[v].strides[i] % 4) vec4 = false;
       }
       if (vec4) {
-        k_rotary_rows4<<<grid_for(ctx, rows * (d / 8), 256), 256, 0, ctx->stream>>>(
-            static_cast<const float*>(x->base), dv[0], static_cast<const float*>(cs->base), dv[1],
-            static_cast<const float*>(sn->base), dv[2], fptr(r), rows, d, shift);
+        const dim3 g(grid_for(ctx, rows * (d / 8), 256));
+        const bool small = rows * (d / 8) < (int64_t)INT32_MAX;
+        const float *xb = static_cast<const float*>(x->base), *cb = static_cast<const float*>(cs->base),
+                    *sb = static_cast<const float*>(sn->base);
+        if (d == 64 && small) k_rotary_rows4<8, uint32_t><<<g, 256, 0, ctx->stream>>>(xb, dv[0], cb, dv[1], sb, dv[2], fptr(r), rows, d, shift);
+        else if (small) k_rotary_rows4<0, uint32_t><<<g, 256, 0, ctx->stream>>>(xb, dv[0], cb, dv[1], sb, dv[2], fptr(r), rows, d, shift);
+        else k_rotary_rows4<0, int64_t><<<g, 256, 0, ctx->stream>>>(xb, dv[0], cb, dv[1], sb, dv[2], fptr(r), rows, d, shift);
       } else {
         k_rotary_rows<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(
             static_cast<const float*>(x->base), dv[0], static_cast<const float*>(cs->base), dv[1],
