@@ -158,7 +158,8 @@ struct FwdItem {
 };
 
 // Item t in longest-first order (the query tile slowest and reversed, then head, then batch); false when the tile
-// sees no key.
+// sees no key. (Ordering the items by (batch, kv head) groups instead cut the K/V reads from DRAM from 2.0 to 0.5 GB
+// at [4, 32, 2048, 64] but lengthened the kernel, 0.63 -> 0.72 ms: the rounds then mix long and short tiles.)
 __device__ __forceinline__ bool fwd_item(const AttnTcArgs& a, int t, FwdItem& it) {
   const int hb = a.H * a.B;
   it.qt = a.q_tiles - 1 - t / hb;

@@ -168,7 +168,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // key tiles in the slowest grid index: under a causal mask tile 0 is attended by every query, so the longest
-  // tiles start first
+  // tiles start first (ordered by (batch, kv head) instead, the CTAs read 5x less from DRAM but the longest tiles of
+  // the last heads started last and the backward took 15% longer in the 1B step)
   const int kt = blockIdx.z, kvh = blockIdx.x, b = blockIdx.y;
   const int g = a.H / a.KVH;
   const int j0 = kt * kRows;
