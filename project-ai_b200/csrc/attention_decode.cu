@@ -123,7 +123,9 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
   __shared__ __align__(16) float qs[R][kMaxD];
   __shared__ __align__(16) float ps[kConsumers][R][kTile];
   __shared__ float wm[kConsumers][R], wl[kConsumers][R];
-  __shared__ float wacc[kConsumers][R][kMaxD];
+  // the warps' partial outputs, merged after the key loop: they reuse the start of the stage ring (so a 4-stage
+  // CTA fits 6 to an SM), written only once every consumer warp is done with its stages
+  float (*wacc)[R][kMaxD] = reinterpret_cast<float (*)[R][kMaxD]>(smem);
   __shared__ float cm[R], cl[R];  // this CTA's merged partial, read by cluster rank 0
   __shared__ float ca[R][kMaxD];
   __shared__ volatile int s_abort;
@@ -336,7 +338,9 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const Args a) {
       if (lane == 0) mbar_arrive(&empty[s]);
     }
 
-    // merge the warps (fixed order) into this CTA's partial
+    // merge the warps (fixed order) into this CTA's partial; the partials overwrite stage memory, so every consumer
+    // warp first finishes with its stages (every issued copy has landed: each one was awaited by its consumer)
+    bar_sync(kBarConsumers, kCT);
 #pragma unroll
     for (int r = 0; r < R; r++) {
       if (lane == 0) { wm[warp][r] = m[r]; wl[warp][r] = l[r]; }
@@ -671,8 +675,8 @@ pai_status attn_decode_run(pai_ctx* ctx, dec::Args& a, bool rope) {
   } else {
     // streaming variant. splits: as many as keep the whole grid resident in one wave, at most one cluster of 8, and
     // at most one per 16-key tile. With up to 4 query rows, 3 CTAs per SM fit in shared memory with the 8-stage ring
-    // and 5 with a 4-stage ring (32 KB); the consumer warps' QKᵀ / softmax / PV chain is latency-bound, so the
-    // shallower ring is taken whenever it lets the grid hold more CTAs (batch 32 x 8 kv heads: 2 splits, 512 CTAs,
+    // and 6 with a 4-stage ring (32 KB); the consumer warps' QKᵀ / softmax / PV chain is latency-bound, so the
+    // shallower ring is taken whenever it lets the grid hold more CTAs (batch 32 x 8 kv heads: 3 splits, 768 CTAs,
     // instead of 1). 8 or 16 query rows: 2 CTAs per SM (registers).
     const int tiles = (kend + dec::kTile - 1) / dec::kTile;
     auto splits_for = [&](int per_sm) {
@@ -680,8 +684,8 @@ pai_status attn_decode_run(pai_ctx* ctx, dec::Args& a, bool rope) {
     };
     int stages = dec::kStages;
     a.splits = splits_for(a.rows <= 4 ? 3 : 2);
-    if (a.rows <= 4 && splits_for(5) > a.splits) {
-      a.splits = splits_for(5);
+    if (a.rows <= 4 && splits_for(6) > a.splits) {
+      a.splits = splits_for(6);
       stages = dec::kConsumers;
     }
     // ring depth: a multiple of the consumer count, so each stage is always read by the same warp (tile t sits in
