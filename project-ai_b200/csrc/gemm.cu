@@ -4,13 +4,17 @@
 // fp32 semantics on the tensor cores (3xTF32): every operand element x is split into hi = tf32(x) and
 // lo = tf32(x − hi) (round-to-nearest, both exactly representable in tf32), and each product is accumulated as
 // a_lo·b_hi + a_hi·b_lo + a_hi·b_hi in an fp32 TMEM accumulator. The dropped a_lo·b_lo term and the tf32 rounding
-// of lo leave a relative error near 2^-21 per product, well inside the 1e-4 conformance tolerance.
+// of lo leave a relative error near 2^-21 per product, well inside the 1e-4 conformance tolerance. The tensor core
+// reads an fp32 operand as tf32 by dropping its low 13 mantissa bits, so for a K-major operand of the two-CTA kernel
+// hi is the operand itself and lo = tf32(x − trunc(x)): one plane is written instead of two (the dropped lo·lo term
+// is then below 2^-20 relative).
 //
 // Pipeline:
 //   1. k_pack: both operands in one launch (the smaller one's tiles first); reads each operand view once (any
 //      strides, batch offsets), splits hi/lo, and writes 128-row x 32-k
 //      tiles already in the tcgen05 K-major SWIZZLE_128B shared-memory layout, so the GEMM moves each tile with
-//      one plain bulk copy (cp.async.bulk) and no tensor map.
+//      one plain bulk copy (cp.async.bulk) and no tensor map. A K-major operand of the two-CTA kernel gets its lo
+//      plane only; its hi tiles come from the operand through a SWIZZLE_128B tensor map.
 //   2. k_gemm_tc: persistent kernel, one CTA per SM, warp-specialised:
 //        warp 0   bulk-copy producer into a STAGES-deep shared-memory ring (mbarrier complete_tx);
 //        warp 1   allocates TMEM and issues tcgen05.mma.kind::tf32 (M=128, N=BN) from one elected lane;
@@ -158,6 +162,8 @@ struct PackDesc {
   int rows, k;               // logical extent
   int kt, rt_pad;            // k tiles, row tiles (padded)
   int vec;                   // 1: 16-byte loads along the unit-stride axis are aligned and never straddle an edge
+  int lo_only;               // 1: the GEMM reads the raw fp32 operand as hi (the tensor core truncates it to tf32),
+                             //    so only lo = tf32(x − trunc(x)) is written
 };
 
 // One CTA (256 threads) writes one 128x32 hi tile and one lo tile: k tile kt, row tile rt, batch matrix b.
@@ -199,8 +205,22 @@ __device__ __forceinline__ void pack_tile(const PackDesc& d, int kt, int rt, int
   }
   __syncthreads();
   size_t base = ((size_t)(b * d.kt + kt) * d.rt_pad + rt) * kTileFloats;
-  float4* h4 = reinterpret_cast<float4*>(hi + base);
   float4* l4 = reinterpret_cast<float4*>(lo + base);
+  if (d.lo_only) {
+    // hi is the raw value as the tensor core reads it (low 13 mantissa bits dropped); x − hi is exact.
+    for (int ch = tid; ch < kBM * 8; ch += 256) {
+      int r = ch >> 3, c = ch & 7;
+      float vl[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float v = tile[r][c * 4 + j];
+        vl[j] = __uint_as_float(to_tf32(v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u)));
+      }
+      l4[r * 8 + (c ^ (r & 7))] = make_float4(vl[0], vl[1], vl[2], vl[3]);
+    }
+    return;
+  }
+  float4* h4 = reinterpret_cast<float4*>(hi + base);
   for (int ch = tid; ch < kBM * 8; ch += 256) {
     int r = ch >> 3, c = ch & 7;
     float v[4], vh[4], vl[4];
@@ -254,11 +274,14 @@ struct GemmArgs {
   int kt_per_split;
   int* error_flag;
   int k_elems;                           // logical K (for the work count only)
+  int a_raw, b_raw;                      // pair kernel: hi is read from the raw operand (its tensor map), not a plane
 };
 
 // The CTA-pair kernel reads the same packed planes through 2-D tensor maps ([rows, 32] fp32, 128-row boxes, no
 // swizzle: each box is one pre-swizzled tile copied verbatim), so the partner CTA's copies can signal the leader's
-// barrier (the .cta_group::2 form of the tensor copy).
+// barrier (the .cta_group::2 form of the tensor copy). A K-major operand's hi map may instead cover the raw operand
+// ([rows, k] fp32, 32 x 128 boxes, SWIZZLE_128B): the copy then lays the tile out as the pack would, and rows or k
+// past the edge read as zeros, as the pack pads them.
 struct PairMaps {
   CUtensorMap a_hi, a_lo, b_hi, b_lo;
 };
@@ -339,11 +362,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity) ? 1 : 0;
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
-// One 128-row box of a packed plane into this CTA's shared memory; the bytes count on the leader CTA's barrier.
-__device__ __forceinline__ void tma_pair_load(void* dst, const CUtensorMap* map, int row, uint32_t bar_cluster) {
+// One 128-row box (at element x of the row, a multiple of 32) into this CTA's shared memory; the bytes count on the
+// leader CTA's barrier.
+__device__ __forceinline__ void tma_pair_load(void* dst, const CUtensorMap* map, int x, int row, uint32_t bar_cluster) {
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(bar_cluster)
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(row), "r"(bar_cluster)
       : "memory");
 }
 template <bool PAIR>
@@ -438,10 +462,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(const __grid_consta
             const uint32_t bar = lead_full + (uint32_t)(stage * 8);
             const int arow = ((ba * g.kt + kb) * g.mt_pad + mb * 2 + (int)rank) * kBM;
             const int brow = ((bb * g.kt + kb) * g.nt_pad + nb * 2 + (int)rank) * kBM;
-            tma_pair_load(st, &maps.a_hi, arow, bar);
-            tma_pair_load(st + S::kA, &maps.a_lo, arow, bar);
-            tma_pair_load(st + 2 * S::kA, &maps.b_hi, brow, bar);
-            tma_pair_load(st + 2 * S::kA + S::kB, &maps.b_lo, brow, bar);
+            if (g.a_raw) tma_pair_load(st, &maps.a_hi, kb * kBK, (mb * 2 + (int)rank) * kBM, bar);
+            else tma_pair_load(st, &maps.a_hi, 0, arow, bar);
+            tma_pair_load(st + S::kA, &maps.a_lo, 0, arow, bar);
+            if (g.b_raw) tma_pair_load(st + 2 * S::kA, &maps.b_hi, kb * kBK, (nb * 2 + (int)rank) * kBM, bar);
+            else tma_pair_load(st + 2 * S::kA, &maps.b_hi, 0, brow, bar);
+            tma_pair_load(st + 2 * S::kA + S::kB, &maps.b_lo, 0, brow, bar);
           } else {
             mbar_expect_tx(&full_bar[stage], (uint32_t)S::kStage);
             const size_t aoff = ((size_t)(ba * g.kt + kb) * g.mt_pad + mb) * kTileFloats;
@@ -601,6 +627,30 @@ static pai_status plane_map(const float* plane, int64_t rows, CUtensorMap* map) 
   return PAI_OK;
 }
 
+// A K-major operand in place ([rows, k] fp32, row stride sr elements) as a 2-D tensor map with 32 x 128 boxes in the
+// SWIZZLE_128B layout of a packed tile; rows and k past the edge read as zeros.
+static pai_status raw_map(const float* base, int rows, int k, int64_t sr, CUtensorMap* map) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)sr * 4};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult cr = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return set_error(PAI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for an operand", (int)cr);
+  return PAI_OK;
+}
+
+// Whether the pair kernel can read an operand's hi straight from the operand: one matrix, unit stride along k, and
+// the base and every row start 16-byte aligned (the tensor map's rules; k a multiple of 4 keeps the row stride legal
+// for any row count).
+static bool raw_operand_ok(const float* base, const std::vector<int64_t>& distinct, int64_t sr, int64_t sk, int k) {
+  if (distinct.size() != 1 || sk != 1 || k % 4 != 0 || sr < k || sr % 4 != 0 || sr >= (int64_t(1) << 36)) return false;
+  return (reinterpret_cast<uintptr_t>(base + distinct[0]) & 15) == 0;
+}
+
 // How many two-CTA clusters of the pair kernel fit on the device at once (queried once per context).
 static int pair_slots(pai_ctx* ctx) {
   if (ctx->gemm_pair_slots == 0) {
@@ -658,10 +708,11 @@ static pai_status launch_gemm(pai_ctx* ctx, const GemmArgs& g, bool pair, const 
 // Allocates the packed hi/lo planes of one operand (batched 2-D view) and fills its pack descriptor; `doff` holds
 // the batch offsets when there are more than fit inline and must outlive the launch.
 static pai_status prepare_pack(pai_ctx* ctx, const float* base, const std::vector<int64_t>& boffs, int64_t sr, int64_t sk,
-                               int rows, int k, int rt_pad, Scratch* hi, Scratch* lo, Scratch* doff, PackDesc* out) {
+                               int rows, int k, int rt_pad, bool lo_only, Scratch* hi, Scratch* lo, Scratch* doff,
+                               PackDesc* out) {
   int kt = (k + kBK - 1) / kBK;
   size_t floats = (size_t)boffs.size() * kt * rt_pad * kTileFloats;
-  PAI_TRY(scratch(ctx, floats * 4, hi));
+  if (!lo_only) PAI_TRY(scratch(ctx, floats * 4, hi));
   PAI_TRY(scratch(ctx, floats * 4, lo));
   if (boffs.size() > (size_t)kInlineBatches) PAI_TRY(upload(ctx, boffs.data(), boffs.size() * 8, doff));
   // 16-byte loads along the unit-stride axis: every batch matrix and row start 16-byte aligned, and the unit-stride
@@ -676,7 +727,7 @@ static pai_status prepare_pack(pai_ctx* ctx, const float* base, const std::vecto
   d.batch_off = static_cast<const int64_t*>(doff->p);
   if (!d.batch_off)
     for (size_t i = 0; i < boffs.size(); i++) d.boff_inline[i] = boffs[i];
-  d.sr = sr; d.sk = sk; d.rows = rows; d.k = k; d.kt = kt; d.rt_pad = rt_pad; d.vec = vec;
+  d.sr = sr; d.sk = sk; d.rows = rows; d.k = k; d.kt = kt; d.rt_pad = rt_pad; d.vec = vec; d.lo_only = lo_only ? 1 : 0;
   *out = d;
   return PAI_OK;
 }
@@ -829,11 +880,17 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   }
   const int mt_pad = pair ? 2 * (int)((m + 255) / 256) : mt;
   const int nt_pad = tn * (kTileN / kBM);
+  const int64_t arows = (int64_t)a_distinct.size() * kt * mt_pad * kBM, brows = (int64_t)b_distinct.size() * kt * nt_pad * kBM;
+  if (pair && (arows > INT32_MAX || brows > INT32_MAX))
+    pair = false;  // tensor-map coordinates are 32-bit; the packed A (pairs of row tiles) serves the one-CTA kernel too
+  // Pair kernel: a K-major operand's hi is the operand itself, so its pack writes lo alone.
+  const bool a_raw = pair && raw_operand_ok(abase, a_distinct, sam, sak, k);
+  const bool b_raw = pair && raw_operand_ok(bbase, b_distinct, sbn, sbk, k);
   Scratch ahi, alo, bhi, blo, dai, dbi, part;
   Scratch aoff, boff;
   PackDesc pda, pdb;
-  PAI_TRY(prepare_pack(ctx, abase, a_distinct, sam, sak, m, k, mt_pad, &ahi, &alo, &aoff, &pda));
-  PAI_TRY(prepare_pack(ctx, bbase, b_distinct, sbn, sbk, n, k, nt_pad, &bhi, &blo, &boff, &pdb));
+  PAI_TRY(prepare_pack(ctx, abase, a_distinct, sam, sak, m, k, mt_pad, a_raw, &ahi, &alo, &aoff, &pda));
+  PAI_TRY(prepare_pack(ctx, bbase, b_distinct, sbn, sbk, n, k, nt_pad, b_raw, &bhi, &blo, &boff, &pdb));
   PAI_TRY(pack_operands(ctx, pda, (int)a_distinct.size(), ahi, alo, pdb, (int)b_distinct.size(), bhi, blo));
   if (batch > kInlineBatches) {
     PAI_TRY(upload(ctx, a_idx.data(), a_idx.size() * 4, &dai));
@@ -855,19 +912,17 @@ PAI_API pai_status pai_matmul(pai_ctx* ctx, const pai_tensor* a, const pai_tenso
   g.kt_per_split = kt_per_split;
   g.error_flag = ctx->d_error_flag;
   g.k_elems = k;
+  g.a_raw = a_raw ? 1 : 0;
+  g.b_raw = b_raw ? 1 : 0;
   PairMaps maps;
   memset(&maps, 0, sizeof maps);
   if (pair) {
-    const int64_t arows = (int64_t)a_distinct.size() * kt * mt_pad * kBM, brows = (int64_t)b_distinct.size() * kt * nt_pad * kBM;
-    if (arows > INT32_MAX || brows > INT32_MAX) {
-      pair = false;  // tensor-map coordinates are 32-bit; the packed A (pairs of row tiles) serves the one-CTA kernel too
-      g.tiles_m = mt;
-    } else {
-      PAI_TRY(plane_map(g.a_hi, arows, &maps.a_hi));
-      PAI_TRY(plane_map(g.a_lo, arows, &maps.a_lo));
-      PAI_TRY(plane_map(g.b_hi, brows, &maps.b_hi));
-      PAI_TRY(plane_map(g.b_lo, brows, &maps.b_lo));
-    }
+    if (a_raw) PAI_TRY(raw_map(abase + a_distinct[0], m, k, sam, &maps.a_hi));
+    else PAI_TRY(plane_map(g.a_hi, arows, &maps.a_hi));
+    PAI_TRY(plane_map(g.a_lo, arows, &maps.a_lo));
+    if (b_raw) PAI_TRY(raw_map(bbase + b_distinct[0], n, k, sbn, &maps.b_hi));
+    else PAI_TRY(plane_map(g.b_hi, brows, &maps.b_hi));
+    PAI_TRY(plane_map(g.b_lo, brows, &maps.b_lo));
   }
   PAI_TRY(launch_gemm(ctx, g, pair, maps));
   if (splits > 1) {

@@ -36,6 +36,25 @@ def test_matmul_matches_float64(cuda, m, k, n, tb):
     assert_close(ref, got, 1e-4, 1e-5 + 1e-6 * scale.max(), f"matmul {m}x{k}x{n} tb={tb}")
 
 
+# Products the two-CTA kernel takes (more than one round of 128 x 256 tiles, no K split): K-major operands feed their
+# raw fp32 tiles as hi through a tensor map and get a lo-only pack. Covered: a k tail (k = 100 reads zeros past the
+# edge), row and column tails of the 256-row tiles, a column-slice view with a 16-byte aligned start (raw) and one
+# with an unaligned start (packed hi and lo), and an MN-major B beside a raw A.
+@pytest.mark.parametrize("m,k,n,tb,col0", [(2048, 100, 2048, True, 0), (1536, 256, 1000, True, 0),
+                                           (2048, 768, 2048, True, 32), (2048, 768, 2048, True, 1),
+                                           (2048, 256, 2048, False, 0)])
+def test_matmul_pair_kernel_raw_operands(cuda, m, k, n, tb, col0):
+    full = rnd(11, m, k + col0 + 8)
+    a = full[:, col0:col0 + k]
+    b = rnd(12, n, k) if tb else rnd(12, k, n)
+    ta = cabi.slice_view(cuda.from_host(full), 1, col0, k)
+    got = cuda.to_host(cuda.matmul(ta, cuda.from_host(b), transpose_b=tb))
+    bt = b.astype(np.float64).T if tb else b.astype(np.float64)
+    ref = a.astype(np.float64) @ bt
+    scale = np.abs(a).astype(np.float64) @ np.abs(bt)
+    assert_close(ref, got, 1e-4, 1e-5 + 1e-6 * scale.max(), f"pair matmul {m}x{k}x{n} tb={tb} col0={col0}")
+
+
 def test_matmul_strided_operands_and_deep_k(cuda):
     # Weight-gradient shape: dW = dYᵀ·X with both operands as transposed views (MN-major), K = 8192 (split-K path).
     dy = rnd(3, 8192, 384, scale=0.05)
