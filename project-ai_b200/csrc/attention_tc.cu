@@ -433,14 +433,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_attn_fwd_tc(AttnTcArgs a) {
         float mn = fmaxf(m, mx);
         float alpha = (m == -INFINITY) ? 0.0f : __expf(m - mn);
         if (mn == -INFINITY) alpha = 1.0f;
-        const float mn2 = mn * kLog2e;
-        float sum = 0.0f;
+        // A masked score (-inf) gives 2^-inf = 0; a row with no visible key yet keeps a zero bias, so no NaN forms.
+        const float mn2 = (mn == -INFINITY) ? 0.0f : mn * kLog2e;
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int c = 0; c < 32; c++) {
-          float p = (s[c] == -INFINITY) ? 0.0f : exp2f(fmaf(s[c], kLog2e, -mn2));
+          float p = ex2_sfu(fmaf(s[c], kLog2e, -mn2));
           s[c] = p;
-          sum += p;
+          part[c & 3] += p;
         }
+        const float sum = (part[0] + part[1]) + (part[2] + part[3]);
         l = l * alpha + sum;
         m = mn;
         // o holds the blocks up to j-3 in units of the running max. P_{j-2}·V_{j-2} (units of m_{j-2}) sits in this

@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
         const float lse2 = __shfl_sync(0xffffffffu, lse_l, c);
         const float dvc = __shfl_sync(0xffffffffu, dv_l, c);
         bool vis = q < a.S && key < a.L && (!a.causal || key <= a.pos_offset + q);
-        float p = vis ? exp2f(fmaf(s[c], kLog2e, -lse2)) : 0.0f;
+        float p = vis ? ex2_sfu(fmaf(s[c], kLog2e, -lse2)) : 0.0f;
         float dvq = vis ? dvc : 0.0f;
         s[c] = p;
         dp[c] = p * (dp[c] - dvq);
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
       for (int c = 0; c < 32; c++) {
         int kj = k0 + c;
         bool vis = qi < a.S && kj < a.L && (!a.causal || kj <= a.pos_offset + qi);
-        float p = vis ? exp2f(fmaf(s[c], kLog2e, -lse2)) : 0.0f;
+        float p = vis ? ex2_sfu(fmaf(s[c], kLog2e, -lse2)) : 0.0f;
         dp[c] = p * (dp[c] - dvq);
       }
       if (ok && n > 0 && !warp_wait(pd_free, (n - 1) & 1)) { ok = false; if (lane == 0) atomicCAS(a.error_flag, 0, 36 + 1); }

@@ -31,6 +31,15 @@ __device__ __forceinline__ void split_tf32_fast(float x, float& hi, float& lo) {
   lo = x - hi;
 }
 
+// 2^x from the special-function unit (the PTX ISA's ex2.approx.ftz.f32, one instruction): 2^-inf = +0 and results
+// below the normal range flush to zero, which a softmax weight may. Used for the attention kernels' per-score
+// exponentials, where a guarded library call would sit on the softmax warps' critical path.
+__device__ __forceinline__ float ex2_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
