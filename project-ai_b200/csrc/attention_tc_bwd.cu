@@ -5,17 +5,19 @@
 //   P = exp(S − lse), dP = dO·Vᵀ, dS = P ⊙ (dP − rowsum(dO ⊙ O)),
 //   dV = Σ_group Pᵀ·dO,  dK = Σ_group dSᵀ·(q·scale),  dQ = scale · dS·K.
 //
-// Two kernels, 352 threads each (warp 0 bulk-copy producer, warps 2-9 element-wise — two warps per TMEM lane quadrant,
-// 32 of each 64-wide block's columns per thread — and MMA issuers: in the dQ kernel lanes 0 and 16 of warp 1 issue S
-// and dP and lane 0 of warp 10 dQ, each from its own ring slot (one thread issues a tf32 MMA about every 115 cycles
-// whatever its N, and the tensor pipe overlaps several threads' N=64 products); the dK/dV kernel's single issuer
+// Two kernels (warp 0 bulk-copy producer, warps 2-9 element-wise — two warps per TMEM lane quadrant, 32 of each
+// 64-wide block's columns per thread — and MMA issuers: the dQ kernel (384 threads) issues S, dP and dQ from lane 0
+// of warps 1, 10 and 11, each consuming its own ring (one thread issues a tf32 MMA about every 115 cycles whatever
+// its N, and the tensor pipe overlaps several threads' N=64 products); the dK/dV kernel's (352 threads) single issuer
 // consumes its shared ring in load order):
 //   k_attn_bwd_kv_tc  128 keys of one (batch, kv head) stay resident (K, V as A operands in shared memory); the
 //                     group's heads x 64-query blocks stream through a 3-slot ring (q·scale, dO, dOᵀ, (q·scale)ᵀ);
 //                     Sᵀ and dPᵀ land in TMEM, Pᵀ / dSᵀ go back to TMEM as hi/lo A operands of dV += Pᵀ·dO and
 //                     dK += dSᵀ·(q·scale).
-//   k_attn_bwd_q_tc   128 queries of one (batch, head) stay resident (q·scale, dO); 64-key blocks stream through the
-//                     ring (K, V, Kᵀ); dS goes to TMEM as the A operand of dQ += dS·K.
+//   k_attn_bwd_q_tc   128 queries of one (batch, head) stay resident: q·scale in shared memory, dO in TMEM (so dP is
+//                     a TS product). 64-key blocks stream through per-operand rings (two K and two V slots, so a
+//                     block's K and V land while the previous block's products run; one Kᵀ slot, a block behind);
+//                     dS goes to TMEM as the A operand of dQ += dS·K.
 // All operands are 64-row SWIZZLE_128B hi/lo tiles from k_attn_pack; 128-row A operands are assembled in shared
 // memory from two 64-row tiles. Every wait is bounded (device error flag on timeout).
 // Accuracy: the gradient products of each streamed block go into a fresh TMEM accumulator, which the element-wise
@@ -349,22 +351,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
 }
 
 // ---------------------------------------------------------------- dQ
-__global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
+// dQ kernel roles (12 warps): 0 producer, 1 S issuer (and TMEM owner), 2-9 element-wise, 10 dP issuer, 11 dQ issuer.
+constexpr int kDpWarpQ = 10, kDqWarpQ = 11;
+constexpr int kThreadsQ = 32 * (kDqWarpQ + 1);
+
+__global__ void __launch_bounds__(kThreadsQ, 1) k_attn_bwd_q_tc(Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // q·scale stays in shared memory (A of S = (q·scale)·Kᵀ); dO stays in TMEM (A of dP = dO·Vᵀ), which leaves room for
+  // two K and two V slots, so each block's K and V land while the previous block's products run.
   uint8_t* sQ = smem;
-  uint8_t* sDO = smem + kA;
-  uint8_t* sRing = smem + 2 * kA;  // slot 0: K tile, 1: V tile, 2: Kᵀ tile
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * kA + kSlots * kTile);
+  uint8_t* sK = smem + kA;              // [2]
+  uint8_t* sV = sK + 2 * kTile;         // [2]
+  uint8_t* sKT = sV + 2 * kTile;        // [1]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKT + kTile);
   uint64_t* a_full = bars;
-  uint64_t* ring_full = bars + 1;   // [3]
-  uint64_t* ring_empty = bars + 4;  // [3]
-  uint64_t* st_full = bars + 7;
-  uint64_t* st_free = bars + 8;
-  uint64_t* pd_full = bars + 9;
-  uint64_t* pd_free = bars + 10;
-  uint64_t* drained = bars + 11;    // [4]: each issuer's MMAs have completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* k_full = bars + 1;      // [2]
+  uint64_t* k_empty = bars + 3;     // [2]
+  uint64_t* v_full = bars + 5;      // [2]
+  uint64_t* v_empty = bars + 7;     // [2]
+  uint64_t* kt_full = bars + 9;
+  uint64_t* kt_empty = bars + 10;
+  uint64_t* do_ready = bars + 11;   // dO is in TMEM
+  uint64_t* st_full = bars + 12;
+  uint64_t* st_free = bars + 13;
+  uint64_t* pd_full = bars + 14;
+  uint64_t* pd_free = bars + 15;
+  uint64_t* drained = bars + 16;    // [3]: each issuer's MMAs have completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -375,16 +389,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
   int kend = a.L;
   if (a.causal) kend = min(a.L, a.pos_offset + q0 + kRows);
   const int N = kend > 0 ? (kend + kBlk - 1) / kBlk : 0;
-  const uint32_t cS = 0, cDP = 64, cDShi = 128, cDSlo = 192, cDQ = 256;
+  const uint32_t cS = 0, cDP = 64, cDShi = 128, cDSlo = 192, cDQ = 256, cDOhi = 320, cDOlo = 384;
+  const size_t qbase = ((size_t)(b * a.H + h) * a.nq2 + 2 * qt) * (kTile / 4);
 
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
-    for (int i = 0; i < kSlots; i++) { mbar_init(&ring_full[i], 1); mbar_init(&ring_empty[i], 1); }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
+    }
+    mbar_init(kt_full, 1);
+    mbar_init(kt_empty, 1);
+    mbar_init(do_ready, 8);
     mbar_init(st_full, 2);   // the S and dP issuers
     mbar_init(st_free, 8);
     mbar_init(pd_full, 8);
     mbar_init(pd_free, 1);
-    for (int i = 0; i < 4; i++) mbar_init(&drained[i], 1);
+    for (int i = 0; i < 3; i++) mbar_init(&drained[i], 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -396,55 +417,70 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
 
   if (warp == 0) {
     if (lane == 0 && N > 0) {
-      size_t qbase = ((size_t)(b * a.H + h) * a.nq2 + 2 * qt) * (kTile / 4);
-      mbar_expect_tx(a_full, 2 * kA);
+      mbar_expect_tx(a_full, kA);
       load_resident(sQ, a.qs + qbase, a_full);
-      load_resident(sDO, a.dO + qbase, a_full);
-      for (int n = 0; n < N && !s_abort; n++) {
-        for (int type = 0; type < 3; type++) {
-          if (!mbar_wait(&ring_empty[type], (n & 1) ^ 1)) { atomicCAS(a.error_flag, 0, 31); s_abort = 1; break; }
-          const float* src;
-          if (type == 0) src = a.k + ((size_t)(b * a.KVH + kvh) * a.nk2 + n) * (kTile / 4);
-          else if (type == 1) src = a.v + ((size_t)(b * a.KVH + kvh) * a.nk2 + n) * (kTile / 4);
-          else src = a.kT + ((size_t)(b * a.KVH + kvh) * a.nk + n) * (kTile / 4);
-          mbar_expect_tx(&ring_full[type], kTile);
-          bulk_g2s(sRing + type * kTile, src, kTile, &ring_full[type]);
+      const size_t kv = (size_t)(b * a.KVH + kvh);
+      // One tile into a slot once its previous fill is released (fill f waits for parity (f & 1) ^ 1).
+      auto load = [&](uint64_t* empty, int fill, uint64_t* full, uint8_t* dst, const float* src) -> bool {
+        if (!mbar_wait(empty, (uint32_t)(fill & 1) ^ 1u)) { atomicCAS(a.error_flag, 0, 31); s_abort = 1; return false; }
+        mbar_expect_tx(full, kTile);
+        bulk_g2s(dst, src, kTile, full);
+        return true;
+      };
+      // K_n and V_n, then Kᵀ_{n-1}: the dQ product of a block runs a block behind its scores, so its tile trails
+      // and never holds up the next block's K and V.
+      bool ok = true;
+      for (int n = 0; n <= N && ok && !s_abort; n++) {
+        if (n < N) {
+          const int sl = n & 1;
+          ok = load(&k_empty[sl], n >> 1, &k_full[sl], sK + sl * kTile, a.k + (kv * a.nk2 + n) * (kTile / 4)) &&
+               load(&v_empty[sl], n >> 1, &v_full[sl], sV + sl * kTile, a.v + (kv * a.nk2 + n) * (kTile / 4));
         }
+        if (ok && n >= 1) ok = load(kt_empty, n - 1, kt_full, sKT, a.kT + (kv * a.nk + (n - 1)) * (kTile / 4));
       }
-      for (int type = 0; type < 3; type++) mbar_wait(&ring_empty[type], (N & 1) ^ 1);
+      // every tile copied has been consumed before the CTA may exit
+      for (int sl = 0; sl < 2; sl++) {
+        const int fills = (N - sl + 1) / 2;
+        mbar_wait(&k_empty[sl], (uint32_t)(fills & 1) ^ 1u);
+        mbar_wait(&v_empty[sl], (uint32_t)(fills & 1) ^ 1u);
+      }
+      mbar_wait(kt_empty, (uint32_t)(N & 1) ^ 1u);
     }
-  } else if (warp == 1 || warp == kGradWarp) {
-    // three issuing threads: S and dP from lanes 0 and 16 of warp 1, dQ from lane 0 of warp 10
-    const int role = warp == 1 ? (lane == 16 ? 1 : 0) : 2;  // 0 S, 1 dP, 2 dQ
-    if ((warp == 1 ? (lane == 0 || lane == 16) : lane == 0) && N > 0) {
+  } else if (warp == 1 || warp == kDpWarpQ || warp == kDqWarpQ) {
+    const int role = warp == 1 ? 0 : (warp == kDpWarpQ ? 1 : 2);  // 0 S, 1 dP, 2 dQ: one ring or barrier each
+    if (lane == 0 && N > 0) {
       constexpr uint32_t idesc = idesc_tf32(128, 64);
-      const uint32_t ring = smem_u32(sRing);
       bool ok = true;
       if (role < 2) {
-        const uint32_t a_s = smem_u32(role == 0 ? sQ : sDO), d = tmem + (role == 0 ? cS : cDP);
-        ok = mbar_wait(a_full, 0);
+        ok = mbar_wait(role == 0 ? a_full : do_ready, 0);
+        uint64_t* full = role == 0 ? k_full : v_full;
+        uint64_t* empty = role == 0 ? k_empty : v_empty;
         for (int n = 0; n < N && ok && !s_abort; n++) {
+          const int sl = n & 1;
           if (n > 0 && !mbar_wait(st_free, (n - 1) & 1)) { ok = false; break; }
-          if (!mbar_wait(&ring_full[role], n & 1)) { ok = false; break; }
+          if (!mbar_wait(&full[sl], (n >> 1) & 1)) { ok = false; break; }
           fence_after();
-          mma_res_tile(d, a_s, ring + role * kTile, idesc);  // S = (q·scale)·Kᵀ, dP = dO·Vᵀ
+          if (role == 0)
+            mma_res_tile(tmem + cS, smem_u32(sQ), smem_u32(sK + sl * kTile), idesc);  // S = (q·scale)·Kᵀ
+          else
+            mma_tmem_tile(tmem + cDP, tmem + cDOhi, tmem + cDOlo, smem_u32(sV + sl * kTile), idesc, false);  // dO·Vᵀ
           commit(st_full);
-          commit(&ring_empty[role]);
+          commit(&empty[sl]);
         }
       } else {
         for (int n = 0; n < N && ok && !s_abort; n++) {
-          if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[2], n & 1)) { ok = false; break; }
+          if (!mbar_wait(pd_full, n & 1) || !mbar_wait(kt_full, n & 1)) { ok = false; break; }
           fence_after();
-          mma_tmem_tile(tmem + cDQ, tmem + cDShi, tmem + cDSlo, ring + 2 * kTile, idesc, false);  // dQ_n = dS·K
+          mma_tmem_tile(tmem + cDQ, tmem + cDShi, tmem + cDSlo, smem_u32(sKT), idesc, false);  // dQ_n = dS·K
           commit(pd_free);
-          commit(&ring_empty[2]);
+          commit(kt_empty);
         }
       }
       if (!ok) { atomicCAS(a.error_flag, 0, 32 + role); s_abort = 1; }
       commit(&drained[role]);
       mbar_wait(&drained[role], 0);
     }
-  } else {
+  } else if (warp >= 2 && warp < 10) {
     const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
     const int row = quad * 32 + lane;
     const int qi = q0 + row;
@@ -454,6 +490,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_q_tc(Args a) {
     const float lse2 = qi < a.S ? a.lse[((int64_t)b * a.H + h) * a.S + qi] * kLog2e : 0.0f;
     const float dvq = qi < a.S ? a.dvec[((int64_t)b * a.H + h) * a.S + qi] : 0.0f;
     bool ok = N > 0;
+    if (N > 0) {
+      // This thread's dO row slice (packed hi/lo, 32 columns) -> TMEM, the A operand of the dP products. In the packed
+      // 64-row tile the (hi|lo, column half) sub-tile is 64 rows of 32 floats with 16-byte chunks XOR (row & 7).
+      const float* t = a.dO + qbase + (size_t)(row >> 6) * (kTile / 4);
+      const int rr = row & 63;
+      float hv[32], lv[32];
+#pragma unroll
+      for (int c4 = 0; c4 < 8; c4++) {
+        const int off = rr * 32 + ((c4 ^ (rr & 7)) << 2);
+        const float4 x = *reinterpret_cast<const float4*>(t + half * 2048 + off);
+        const float4 y = *reinterpret_cast<const float4*>(t + (2 + half) * 2048 + off);
+        hv[4 * c4] = x.x; hv[4 * c4 + 1] = x.y; hv[4 * c4 + 2] = x.z; hv[4 * c4 + 3] = x.w;
+        lv[4 * c4] = y.x; lv[4 * c4 + 1] = y.y; lv[4 * c4 + 2] = y.z; lv[4 * c4 + 3] = y.w;
+      }
+      tmem_st32(tmem + lane_off + cDOhi + col, hv);
+      tmem_st32(tmem + lane_off + cDOlo + col, lv);
+      tmem_st_wait();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(do_ready);
+    }
     float dq[32];  // this thread's dQ row slice, summed block by block in fp32
 #pragma unroll
     for (int d = 0; d < 32; d++) dq[d] = 0.0f;
@@ -567,7 +624,7 @@ pai_status attn_tc_bwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
   k_attn_bwd_kv_tc<<<gkv, kThreads, kSmem, ctx->stream>>>(args);
   PAI_LAUNCH_CHECK("attention bwd dK/dV (tcgen05)");
   dim3 gq((unsigned)H, (unsigned)B, (unsigned)((S + kRows - 1) / kRows));
-  k_attn_bwd_q_tc<<<gq, kThreads, kSmem, ctx->stream>>>(args);
+  k_attn_bwd_q_tc<<<gq, kThreadsQ, kSmem, ctx->stream>>>(args);
   PAI_LAUNCH_CHECK("attention bwd dQ (tcgen05)");
   return PAI_OK;
 }
