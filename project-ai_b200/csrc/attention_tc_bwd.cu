@@ -5,15 +5,14 @@
 //   P = exp(S − lse), dP = dO·Vᵀ, dS = P ⊙ (dP − rowsum(dO ⊙ O)),
 //   dV = Σ_group Pᵀ·dO,  dK = Σ_group dSᵀ·(q·scale),  dQ = scale · dS·K.
 //
-// Two kernels (warp 0 bulk-copy producer, warps 2-9 element-wise — two warps per TMEM lane quadrant, 32 of each
-// 64-wide block's columns per thread — and MMA issuers: the dQ kernel (384 threads) issues S, dP and dQ from lane 0
-// of warps 1, 10 and 11, each consuming its own ring (one thread issues a tf32 MMA about every 115 cycles whatever
-// its N, and the tensor pipe overlaps several threads' N=64 products); the dK/dV kernel's (352 threads) single issuer
-// consumes its shared ring in load order):
+// Two kernels of 384 threads (bulk-copy producers, warps 2-9 element-wise — two warps per TMEM lane quadrant, 32 of
+// each 64-wide block's columns per thread — and MMA issuers, one thread each, every one consuming its own ring or
+// barrier: one thread issues a tf32 MMA about every 115 cycles whatever its N, and the tensor pipe overlaps several
+// threads' N=64 products):
 //   k_attn_bwd_kv_tc  128 keys of one (batch, kv head) stay resident (K, V as A operands in shared memory); the
-//                     group's heads x 64-query blocks stream through a 3-slot ring (q·scale, dO, dOᵀ, (q·scale)ᵀ);
-//                     Sᵀ and dPᵀ land in TMEM, Pᵀ / dSᵀ go back to TMEM as hi/lo A operands of dV += Pᵀ·dO and
-//                     dK += dSᵀ·(q·scale).
+//                     group's heads x 64-query blocks stream through two rings of half tiles, q·scale and dO for the
+//                     score issuer, dOᵀ and (q·scale)ᵀ for the gradient issuer; Sᵀ and dPᵀ land in TMEM, Pᵀ / dSᵀ go
+//                     back to TMEM as hi/lo A operands of dV += Pᵀ·dO and dK += dSᵀ·(q·scale).
 //   k_attn_bwd_q_tc   128 queries of one (batch, head) stay resident: q·scale in shared memory, dO in TMEM (so dP is
 //                     a TS product). 64-key blocks stream through per-operand rings (two K and two V slots, so a
 //                     block's K and V land while the previous block's products run; one Kᵀ slot, a block behind);
@@ -41,10 +40,9 @@ constexpr int kBlk = 64;                 // streamed block (queries or keys)
 constexpr int kDP = 64;                  // padded head dim
 constexpr uint32_t kTile = 64 * 64 * 4 * 2;   // one packed 64x64 hi/lo tile: 32 KB
 constexpr uint32_t kA = 2 * kTile;            // a resident 128-row operand: 64 KB
-constexpr int kSlots = 3;
-constexpr int kGradWarp = 10;         // second MMA issuer: the gradient products (after the 8 element-wise warps)
-constexpr int kThreads = 32 * (kGradWarp + 1);
-constexpr int kSmem = 2 * kA + kSlots * kTile + 1024 + 256;
+// Both kernels: 224 KB of operands (dK/dV: resident K and V + two rings of three half tiles; dQ: resident q·scale +
+// five tile slots), then the alignment slack and the barriers.
+constexpr int kSmem = 2 * kA + 3 * kTile + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;
 
 struct Args {
@@ -105,25 +103,72 @@ __device__ __forceinline__ void mma_tmem_tile(uint32_t d, uint32_t a_hi, uint32_
   }
 }
 
-// The dK/dV kernel's ring carries, per streamed block n, four tiles: 0 = q·scale, 1 = dO (read by the Sᵀ/dPᵀ
-// MMAs), 2 = dOᵀ, 3 = (q·scale)ᵀ (read by the dV/dK MMAs). The MMA warp consumes them in the order
-//   (0,Qs) (0,dO) | (1,Qs) (1,dO) (0,dOᵀ) (0,Qsᵀ) | (2,Qs) (2,dO) (1,dOᵀ) (1,Qsᵀ) | ... | (N-1,dOᵀ) (N-1,Qsᵀ)
-// (the next block's scores are issued before this block's gradient products), and the producer loads in exactly
-// that order, so a slot is always released before the load that reuses it is needed.
-__device__ __forceinline__ int kv_ring_pos(int n, int type, int N) {
-  if (type < 2) return (n == 0 ? 0 : 4 * n - 2) + type;
-  return (n < N - 1 ? 4 * n + 4 : 4 * n + 2) + (type - 2);
-}
-__device__ __forceinline__ void kv_ring_item(int i, int N, int& n, int& type) {
-  if (i < 2) { n = 0; type = i; return; }
-  int r = i - 2, it = r >> 2, w = r & 3;
-  if (it + 1 < N) {
-    if (w < 2) { n = it + 1; type = w; } else { n = it; type = w; }
-  } else {
-    n = it; type = 2 + w;
-  }
+// The dK/dV kernel streams each block's four tiles through two rings of half-tile slots, each with its own producer
+// thread and its own issuing thread (so every ring has one consumer, which takes its slots in load order): the score
+// ring carries q·scale then dO (the Sᵀ and dPᵀ products), the gradient ring dOᵀ then (q·scale)ᵀ (dV and dK). A half
+// is one 32-wide half of the tile's K: its hi and lo 64 x 32 sub-tiles, 16 KB, released once the 12 MMAs that read
+// it complete, so the next tile streams in while the second half's MMAs run.
+constexpr uint32_t kHalf = kTile / 2;
+constexpr int kHalfSlots = 3;
+
+// Item j of a block (0-1: first tile's halves, 2-3: second tile's) of packed tile `tile` into a half slot.
+__device__ __forceinline__ void load_half(uint8_t* dst, const float* tile, int half, uint64_t* bar) {
+  mbar_expect_tx(bar, kHalf);
+  bulk_g2s(dst, tile + half * 2048, 8192, bar);            // hi, K columns [32*half, 32*half + 32)
+  bulk_g2s(dst + 8192, tile + (2 + half) * 2048, 8192, bar);  // lo
 }
 
+// One ring of kHalfSlots half-tile slots, consumed in order by one thread; item i sits in slot i % kHalfSlots.
+struct HalfRing {
+  uint8_t* base;
+  uint64_t* full;
+  uint64_t* empty;
+  __device__ __forceinline__ uint32_t slot_addr(int i) const { return smem_u32(base + (i % kHalfSlots) * kHalf); }
+  __device__ __forceinline__ bool wait_full(int i) const { return mbar_wait(&full[i % kHalfSlots], (uint32_t)(i / kHalfSlots) & 1u); }
+  __device__ __forceinline__ uint64_t* empty_of(int i) const { return &empty[i % kHalfSlots]; }
+};
+
+// S(+)= A(128-row resident, smem) · B(tile in ring items i, i+1)ᵀ; each half's slot is released after its MMAs.
+__device__ __forceinline__ bool mma_res_halves(uint32_t d, uint32_t a, const HalfRing& r, int i, uint32_t idesc) {
+  const uint32_t a_lo = a + kA / 2;
+#pragma unroll
+  for (int hf = 0; hf < 2; hf++) {
+    if (!r.wait_full(i + hf)) return false;
+    fence_after();
+    const uint32_t bh = r.slot_addr(i + hf), bl = bh + 8192;
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      const int ks = 4 * hf + kk;
+      const uint32_t ao = (ks >> 2) * 16384 + kk * 32, bo = kk * 32;
+      mma_ss(d, desc_sw128(a_lo + ao), desc_sw128(bh + bo), idesc, ks > 0 ? 1u : 0u);
+      mma_ss(d, desc_sw128(a + ao), desc_sw128(bl + bo), idesc, 1u);
+      mma_ss(d, desc_sw128(a + ao), desc_sw128(bh + bo), idesc, 1u);
+    }
+    commit(r.empty_of(i + hf));
+  }
+  return true;
+}
+
+// D = A(TMEM hi/lo, 64 columns of K) · B(tile in ring items i, i+1)ᵀ; each half's slot is released after its MMAs.
+__device__ __forceinline__ bool mma_tmem_halves(uint32_t d, uint32_t a_hi, uint32_t a_lo, const HalfRing& r, int i,
+                                                uint32_t idesc) {
+#pragma unroll
+  for (int hf = 0; hf < 2; hf++) {
+    if (!r.wait_full(i + hf)) return false;
+    fence_after();
+    const uint32_t bh = r.slot_addr(i + hf), bl = bh + 8192;
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      const int ks = 4 * hf + kk;
+      const uint32_t c = (uint32_t)(ks * 8), bo = kk * 32;
+      mma_ts(d, a_lo + c, desc_sw128(bh + bo), idesc, ks > 0 ? 1u : 0u);
+      mma_ts(d, a_hi + c, desc_sw128(bl + bo), idesc, 1u);
+      mma_ts(d, a_hi + c, desc_sw128(bh + bo), idesc, 1u);
+    }
+    commit(r.empty_of(i + hf));
+  }
+  return true;
+}
 
 // 32 values -> TMEM as tf32 hi/lo, 8 columns at a time (the element-wise warps keep their block's scores and both
 // gradient accumulators in registers meanwhile).
@@ -150,22 +195,30 @@ __device__ __forceinline__ void add_partial(uint32_t taddr, float* acc) {
 }
 
 // ---------------------------------------------------------------- dK, dV
-__global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
+// dK/dV kernel roles (12 warps): 0 score-ring producer (and the resident K, V), 1 score issuer (Sᵀ, dPᵀ; TMEM owner),
+// 2-9 element-wise, 10 gradient issuer (dV, dK), 11 gradient-ring producer.
+constexpr int kScoreProducerKV = 0, kGradIssuerKV = 10, kGradProducerKV = 11;
+constexpr int kThreadsKV = 32 * (kGradProducerKV + 1);
+
+__global__ void __launch_bounds__(kThreadsKV, 1) k_attn_bwd_kv_tc(Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = smem + kA;
-  uint8_t* sRing = smem + 2 * kA;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * kA + kSlots * kTile);
+  uint8_t* sScore = smem + 2 * kA;                 // score ring: kHalfSlots half tiles
+  uint8_t* sGrad = sScore + kHalfSlots * kHalf;    // gradient ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sGrad + kHalfSlots * kHalf);
   uint64_t* a_full = bars;
-  uint64_t* ring_full = bars + 1;   // [3]
-  uint64_t* ring_empty = bars + 4;  // [3]
-  uint64_t* st_full = bars + 7;
-  uint64_t* st_free = bars + 8;
-  uint64_t* pd_full = bars + 9;
-  uint64_t* pd_free = bars + 10;
-  uint64_t* drained = bars + 11;    // [4]: each issuer's MMAs have completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* sc_full = bars + 1;     // [3]
+  uint64_t* sc_empty = bars + 4;    // [3]
+  uint64_t* gr_full = bars + 7;     // [3]
+  uint64_t* gr_empty = bars + 10;   // [3]
+  uint64_t* st_full = bars + 13;
+  uint64_t* st_free = bars + 14;
+  uint64_t* pd_full = bars + 15;
+  uint64_t* pd_free = bars + 16;
+  uint64_t* drained = bars + 17;    // [2]: each issuer's MMAs have completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -187,12 +240,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
 
   if (threadIdx.x == 0) {
     mbar_init(a_full, 1);
-    for (int i = 0; i < kSlots; i++) { mbar_init(&ring_full[i], 1); mbar_init(&ring_empty[i], 1); }
+    for (int i = 0; i < kHalfSlots; i++) {
+      mbar_init(&sc_full[i], 1); mbar_init(&sc_empty[i], 1);
+      mbar_init(&gr_full[i], 1); mbar_init(&gr_empty[i], 1);
+    }
     mbar_init(st_full, 1);
     mbar_init(st_free, 8);
     mbar_init(pd_full, 8);
     mbar_init(pd_free, 1);
-    for (int i = 0; i < 4; i++) mbar_init(&drained[i], 1);
+    for (int i = 0; i < 2; i++) mbar_init(&drained[i], 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -201,75 +257,67 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_bwd_kv_tc(Args a) {
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
+  const HalfRing score{sScore, sc_full, sc_empty}, grad{sGrad, gr_full, gr_empty};
 
   auto head_of = [&](int n) { return kvh * g + n / max(qb_count, 1); };
   auto qblk_of = [&](int n) { return qb_start + n % max(qb_count, 1); };
 
-  if (warp == 0) {
+  if (warp == kScoreProducerKV || warp == kGradProducerKV) {
     if (lane == 0 && N > 0) {
-      size_t kvbase = ((size_t)(b * a.KVH + kvh) * a.nk2 + 2 * kt) * (kTile / 4);
-      mbar_expect_tx(a_full, 2 * kA);
-      load_resident(sK, a.k + kvbase, a_full);
-      load_resident(sV, a.v + kvbase, a_full);
-      for (int t = 0; t < 4 * N && !s_abort; t++) {
-        int n, type;
-        kv_ring_item(t, N, n, type);
-        int slot = t % kSlots;
-        if (!mbar_wait(&ring_empty[slot], ((t / kSlots) & 1) ^ 1)) { atomicCAS(a.error_flag, 0, 21); s_abort = 1; break; }
-        int h = head_of(n), qb = qblk_of(n);
-        const float* src;
-        if (type == 0) src = a.qs + ((size_t)(b * a.H + h) * a.nq2 + qb) * (kTile / 4);
-        else if (type == 1) src = a.dO + ((size_t)(b * a.H + h) * a.nq2 + qb) * (kTile / 4);
-        else if (type == 2) src = a.dOT + ((size_t)(b * a.H + h) * a.nq + qb) * (kTile / 4);
-        else src = a.qsT + ((size_t)(b * a.H + h) * a.nq + qb) * (kTile / 4);
-        mbar_expect_tx(&ring_full[slot], kTile);
-        bulk_g2s(sRing + slot * kTile, src, kTile, &ring_full[slot]);
+      const bool sc = warp == kScoreProducerKV;
+      const HalfRing& r = sc ? score : grad;
+      if (sc) {
+        size_t kvbase = ((size_t)(b * a.KVH + kvh) * a.nk2 + 2 * kt) * (kTile / 4);
+        mbar_expect_tx(a_full, 2 * kA);
+        load_resident(sK, a.k + kvbase, a_full);
+        load_resident(sV, a.v + kvbase, a_full);
       }
-      for (int t = 4 * N; t < 4 * N + kSlots; t++) mbar_wait(&ring_empty[t % kSlots], ((t / kSlots) & 1) ^ 1);
+      // per block: items 0-1 the halves of q·scale (score) / dOᵀ (gradient), items 2-3 of dO / (q·scale)ᵀ
+      for (int i = 0; i < 4 * N && !s_abort; i++) {
+        const int n = i >> 2, j = i & 3;
+        if (!mbar_wait(r.empty_of(i), ((uint32_t)(i / kHalfSlots) & 1u) ^ 1u)) {
+          atomicCAS(a.error_flag, 0, sc ? 21 : 23);
+          s_abort = 1;
+          break;
+        }
+        const size_t bh = (size_t)(b * a.H + head_of(n));
+        const int qb = qblk_of(n);
+        const float* tile = sc ? (j < 2 ? a.qs : a.dO) + (bh * a.nq2 + qb) * (kTile / 4)
+                               : (j < 2 ? a.dOT : a.qsT) + (bh * a.nq + qb) * (kTile / 4);
+        load_half(r.base + (i % kHalfSlots) * kHalf, tile, j & 1, &r.full[i % kHalfSlots]);
+      }
+      // every half copied has been consumed before the CTA may exit
+      for (int i = 4 * N; i < 4 * N + kHalfSlots; i++)
+        mbar_wait(r.empty_of(i), ((uint32_t)(i / kHalfSlots) & 1u) ^ 1u);
     }
-  } else if (warp == 1) {
-    // one issuing thread: the 3-slot ring interleaves four operand streams and must be consumed in its load order (a
-    // second consumer thread could wait on a slot two loads ahead, where the mbarrier's phase parity reads an older
-    // completed phase as this one); warp 10 idles in this kernel
+  } else if (warp == 1 || warp == kGradIssuerKV) {
     if (lane == 0 && N > 0) {
       constexpr uint32_t idesc = idesc_tf32(128, 64);
-      const uint32_t k_s = smem_u32(sK), v_s = smem_u32(sV), ring = smem_u32(sRing);
-      bool ok = mbar_wait(a_full, 0);
-      auto issue_st = [&](int n) -> bool {
-        int t0 = kv_ring_pos(n, 0, N), t1 = kv_ring_pos(n, 1, N);
-        if (!mbar_wait(&ring_full[t0 % kSlots], (t0 / kSlots) & 1) || !mbar_wait(&ring_full[t1 % kSlots], (t1 / kSlots) & 1))
-          return false;
-        fence_after();
-        mma_res_tile(tmem + cS, k_s, ring + (t0 % kSlots) * kTile, idesc);   // Sᵀ  = K·(q·scale)ᵀ
-        mma_res_tile(tmem + cDP, v_s, ring + (t1 % kSlots) * kTile, idesc);  // dPᵀ = V·dOᵀ
-        commit(st_full);
-        commit(&ring_empty[t0 % kSlots]);
-        commit(&ring_empty[t1 % kSlots]);
-        return true;
-      };
-      if (ok) ok = issue_st(0);
-      for (int n = 0; n < N && ok && !s_abort; n++) {
-        if (n + 1 < N) {
-          if (!mbar_wait(st_free, n & 1)) { ok = false; break; }
-          fence_after();
-          if (!issue_st(n + 1)) { ok = false; break; }
+      const int role = warp == 1 ? 0 : 1;
+      bool ok = true;
+      if (role == 0) {
+        ok = mbar_wait(a_full, 0);
+        for (int n = 0; n < N && ok && !s_abort; n++) {
+          if (n > 0 && !mbar_wait(st_free, (n - 1) & 1)) { ok = false; break; }
+          ok = mma_res_halves(tmem + cS, smem_u32(sK), score, 4 * n, idesc) &&        // Sᵀ  = K·(q·scale)ᵀ
+               mma_res_halves(tmem + cDP, smem_u32(sV), score, 4 * n + 2, idesc);     // dPᵀ = V·dOᵀ
+          if (ok) commit(st_full);
         }
-        int t2 = kv_ring_pos(n, 2, N), t3 = kv_ring_pos(n, 3, N);
-        if (!mbar_wait(pd_full, n & 1) || !mbar_wait(&ring_full[t2 % kSlots], (t2 / kSlots) & 1) ||
-            !mbar_wait(&ring_full[t3 % kSlots], (t3 / kSlots) & 1)) { ok = false; break; }
-        fence_after();
-        mma_tmem_tile(tmem + cDV, tmem + cPhi, tmem + cPlo, ring + (t2 % kSlots) * kTile, idesc, false);    // dV_n = Pᵀ·dO
-        mma_tmem_tile(tmem + cDK, tmem + cDShi, tmem + cDSlo, ring + (t3 % kSlots) * kTile, idesc, false);  // dK_n = dSᵀ·qs
-        commit(pd_free);
-        commit(&ring_empty[t2 % kSlots]);
-        commit(&ring_empty[t3 % kSlots]);
+      } else {
+        for (int n = 0; n < N && ok && !s_abort; n++) {
+          if (!mbar_wait(pd_full, n & 1)) { ok = false; break; }
+          fence_after();
+          ok = mma_tmem_halves(tmem + cDV, tmem + cPhi, tmem + cPlo, grad, 4 * n, idesc) &&        // dV_n = Pᵀ·dO
+               mma_tmem_halves(tmem + cDK, tmem + cDShi, tmem + cDSlo, grad, 4 * n + 2, idesc);    // dK_n = dSᵀ·qs
+          if (ok) commit(pd_free);
+        }
       }
-      if (!ok) { atomicCAS(a.error_flag, 0, 22); s_abort = 1; }
+      if (!ok) { atomicCAS(a.error_flag, 0, 22 + 2 * role); s_abort = 1; }
       // every MMA this thread issued completes before the CTA releases its tensor memory
-      commit(&drained[0]);
-      mbar_wait(&drained[0], 0);
+      commit(&drained[role]);
+      mbar_wait(&drained[role], 0);
     }
-  } else if (warp < kGradWarp) {  // warp 10 has no role in this kernel
+  } else if (warp >= 2 && warp < 10) {
     const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
     const int row = quad * 32 + lane;
     const int key = j0 + row;
@@ -621,7 +669,7 @@ pai_status attn_tc_bwd(pai_ctx* ctx, const pai_tensor& q, const pai_tensor& k, c
             static_cast<float*>(kp.p), static_cast<float*>(vp.p), static_cast<float*>(kT.p), lse, dvec, dq, dk, dv,
             B, H, KVH, S, L, D, pos_offset, causal, nq, nq2, nk, nk2, scale, ctx->d_error_flag};
   dim3 gkv((unsigned)KVH, (unsigned)B, (unsigned)((L + kRows - 1) / kRows));
-  k_attn_bwd_kv_tc<<<gkv, kThreads, kSmem, ctx->stream>>>(args);
+  k_attn_bwd_kv_tc<<<gkv, kThreadsKV, kSmem, ctx->stream>>>(args);
   PAI_LAUNCH_CHECK("attention bwd dK/dV (tcgen05)");
   dim3 gq((unsigned)H, (unsigned)B, (unsigned)((S + kRows - 1) / kRows));
   k_attn_bwd_q_tc<<<gq, kThreadsQ, kSmem, ctx->stream>>>(args);
