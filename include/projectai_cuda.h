@@ -45,7 +45,9 @@ typedef enum pai_status {
   PAI_ERR_CUDA = 5,
   PAI_ERR_NCCL = 6,
   PAI_ERR_TIMEOUT = 7,
-  PAI_ERR_UNSUPPORTED = 8
+  PAI_ERR_UNSUPPORTED = 8,
+  PAI_ERR_IO = 9,           /* IOException / FileNotFoundException: a file could not be opened, read or written */
+  PAI_ERR_INVALID_DATA = 10 /* InvalidDataException: a checkpoint or dataset file is malformed */
 } pai_status;
 
 /* A tensor view (ProjectAI.Core/Tensor.cs:17-48): storage base + element offset + shape + element strides.
@@ -263,6 +265,44 @@ pai_status pai_nccl_abort(pai_ctx* ctx);
 /* Exposed exchange time since the last call: summed device milliseconds by which the last all-reduce of each step
  * ended after the step's backward (0 for a step whose exchange was hidden), and the number of steps counted. */
 pai_status pai_dp_stats(pai_ctx* ctx, double* exposed_ms, int64_t* steps);
+
+/* ==== Checkpoints: the PAICKPT2 format of ProjectAI.Formats/Checkpoint.cs:11-110, byte for byte ==== */
+/* Checkpoint.Save (Checkpoint.cs:23-57): writes `path` with `step`, the metadata bytes and n_tensors F32 tensors, the
+ * i-th named by the i-th NUL-terminated string packed into names[0, names_len). The tensors are copied once into a
+ * device snapshot on the compute stream; a writer thread then streams the snapshot to the file through pinned host
+ * chunks on a copy stream of its own, so the call returns while the file is written and later ops may change the
+ * tensors. pai_ckpt_wait joins the writer and returns its status (PAI_ERR_IO on a failed write); a second save, or
+ * destroying the context, waits for the first. Without device memory for the snapshot the save streams from the
+ * tensors themselves and returns once the file is written. PAI_ERR_UNSUPPORTED for a tensor over 2^31 elements
+ * (Checkpoint.cs:41-42), PAI_ERR_IO when the file cannot be created. */
+pai_status pai_ckpt_save(pai_ctx* ctx, const char* path, int32_t step, const char* metadata, int64_t meta_len,
+                         const char* names, int64_t names_len, const pai_tensor* tensors, int32_t n_tensors);
+pai_status pai_ckpt_wait(pai_ctx* ctx);
+/* Checkpoint.Load / ReadMetadata (Checkpoint.cs:59-139): reads the header (step, metadata length) and, unless
+ * header_only, every tensor onto the device (F32, allocated in the current scope; the file is read chunk by chunk
+ * while the previous chunk crosses to the device). The checks and messages are the reference's: PAI_ERR_INVALID_DATA
+ * for a bad magic, metadata length, tensor count, name length, rank, dimension or payload length, or a truncated
+ * file; PAI_ERR_IO when the file cannot be opened. pai_ckpt_meta copies the metadata bytes; pai_ckpt_tensor returns
+ * the index-th tensor and its name (name_len bytes, no terminator); pai_ckpt_close forgets them (the tensors stay
+ * allocated in their scope). */
+pai_status pai_ckpt_load(pai_ctx* ctx, const char* path, int32_t header_only, int32_t* step, int64_t* meta_len,
+                         int32_t* n_tensors);
+pai_status pai_ckpt_meta(pai_ctx* ctx, char* buf, int64_t cap);
+pai_status pai_ckpt_tensor(pai_ctx* ctx, int32_t index, char* name, int64_t name_cap, int64_t* name_len, pai_tensor* out);
+pai_status pai_ckpt_close(pai_ctx* ctx);
+
+/* ==== Packed token datasets (ProjectAI.Training/PackedBinDataset.cs:43-117, Training.cs:122-141) ==== */
+/* PackedBinDataset.Open after its manifest is read: maps the shard, block_count blocks of seq_len + 1 little-endian ids
+ * of elem_bytes each (2 = "u16", 4 = "u32"). PAI_ERR_INVALID_DATA for another width, seq_len < 1, block_count < 1 or a
+ * shard shorter than the blocks need (PackedBinDataset.cs:62-83); PAI_ERR_IO when the shard cannot be opened. One
+ * dataset per context; opening another replaces it. */
+pai_status pai_dataset_open(pai_ctx* ctx, const char* bin_path, int32_t elem_bytes, int32_t seq_len, int64_t block_count);
+/* NextBatch for the given block indices: inputs and targets [count, seq_len] F32 ids on the device (ids[:, :-1] and
+ * ids[:, 1:] of each block), allocated in the current scope. The blocks are gathered from the mapping into pinned
+ * memory at the shard's width, uploaded with one copy and widened on the device. PAI_ERR_OUT_OF_RANGE for an index
+ * outside [0, block_count) (GetSequence, PackedBinDataset.cs:98-99) or a u32 id above int32 (its checked cast). */
+pai_status pai_dataset_batch(pai_ctx* ctx, const int64_t* indices, int32_t count, pai_tensor* inputs, pai_tensor* targets);
+pai_status pai_dataset_close(pai_ctx* ctx);
 
 /* ==== Diagnostics (no counterpart in the reference; used by the benchmark and tests) ==== */
 /* Reads and clears the device flag that bounded waits inside kernels set on a timeout (PAI_ERR_TIMEOUT if set). */

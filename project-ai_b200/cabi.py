@@ -88,8 +88,16 @@ class UnsupportedError(BackendError, NotImplementedError):
     pass
 
 
+class FileIOError(BackendError, OSError):
+    """IOException / FileNotFoundException: a checkpoint or dataset file could not be opened, read or written."""
+
+
+class InvalidDataError(BackendError, ValueError):
+    """InvalidDataException: a checkpoint or dataset file is malformed (ProjectAI.Formats/Checkpoint.cs:59-139)."""
+
+
 _STATUS = {1: ArgumentError, 2: OutOfRangeError, 3: InvalidOperationError, 4: MemoryError, 5: BackendError,
-           6: BackendError, 7: DeviceTimeoutError, 8: UnsupportedError}
+           6: BackendError, 7: DeviceTimeoutError, 8: UnsupportedError, 9: FileIOError, 10: InvalidDataError}
 
 T = POINTER(PaiTensor)
 _I32P = POINTER(c_int32)
@@ -136,6 +144,15 @@ _SIGS = {
     "allreduce_wait": [c_void_p],
     "nccl_abort": [c_void_p],
     "check_device_error": [c_void_p, _I32P],
+    "ckpt_save": [c_void_p, c_char_p, c_int32, c_char_p, c_int64, c_char_p, c_int64, T, c_int32],
+    "ckpt_wait": [c_void_p],
+    "ckpt_load": [c_void_p, c_char_p, c_int32, _I32P, POINTER(c_int64), _I32P],
+    "ckpt_meta": [c_void_p, c_char_p, c_int64],
+    "ckpt_tensor": [c_void_p, c_int32, c_char_p, c_int64, POINTER(c_int64), T],
+    "ckpt_close": [c_void_p],
+    "dataset_open": [c_void_p, c_char_p, c_int32, c_int32, c_int64],
+    "dataset_batch": [c_void_p, POINTER(c_int64), c_int32, T, T],
+    "dataset_close": [c_void_p],
     "rmsnorm_bwd_noalloc": [c_void_p, T, T, T, c_float, T, T],
     "timer_start": [c_void_p],
     "timer_stop": [c_void_p, POINTER(c_float)],
@@ -357,6 +374,60 @@ class NativeBackend:
         code = c_int32()
         self._c("check_device_error", ctypes.byref(code))
         return code.value
+
+    # --- checkpoints (ProjectAI.Formats/Checkpoint.cs) and packed datasets (ProjectAI.Training/PackedBinDataset.cs)
+    def save_checkpoint(self, path, step: int, tensors, metadata: str = "") -> None:
+        """Checkpoint.Save: `tensors` is a sequence of (name, PaiTensor). Returns once the tensors are snapshotted on
+        the device; the file is written in the background until wait_checkpoint()."""
+        items = list(tensors)
+        names = b"".join(n.encode() + b"\0" for n, _ in items)
+        arr = (PaiTensor * max(1, len(items)))(*[t for _, t in items])
+        meta = metadata.encode()
+        self._c("ckpt_save", str(path).encode(), int(step), meta, len(meta), names, len(names), arr, len(items))
+
+    def wait_checkpoint(self) -> None:
+        self._c("ckpt_wait")
+
+    def _ckpt_header(self, path, header_only):
+        step, mlen, count = c_int32(), c_int64(), c_int32()
+        self._c("ckpt_load", str(path).encode(), int(header_only), ctypes.byref(step), ctypes.byref(mlen), ctypes.byref(count))
+        buf = ctypes.create_string_buffer(max(1, mlen.value))
+        self._c("ckpt_meta", buf, mlen.value)
+        return step.value, buf.raw[:mlen.value].decode(), count.value
+
+    def load_checkpoint(self, path) -> tuple:
+        """Checkpoint.Load: (step, metadata, {name: PaiTensor}) with the tensors on the device in the current scope."""
+        step, meta, count = self._ckpt_header(path, False)
+        out = {}
+        for i in range(count):
+            nlen = c_int64()
+            self._c("ckpt_tensor", i, None, 0, ctypes.byref(nlen), None)
+            name = ctypes.create_string_buffer(max(1, nlen.value))
+            t = PaiTensor()
+            self._c("ckpt_tensor", i, name, nlen.value, None, ctypes.byref(t))
+            out[name.raw[:nlen.value].decode()] = t
+        self._c("ckpt_close")
+        return step, meta, out
+
+    def read_checkpoint_metadata(self, path) -> tuple:
+        """Checkpoint.ReadMetadata: (step, metadata) from the header alone."""
+        step, meta, _ = self._ckpt_header(path, True)
+        self._c("ckpt_close")
+        return step, meta
+
+    def dataset_open(self, bin_path, dtype: str, seq_len: int, block_count: int) -> None:
+        widths = {"u16": 2, "u32": 4}
+        self._c("dataset_open", str(bin_path).encode(), widths.get(dtype, 0), int(seq_len), int(block_count))
+
+    def dataset_batch(self, indices) -> tuple:
+        """NextBatch over the given block indices: (inputs, targets) [len(indices), seq_len] F32 ids on the device."""
+        idx = np.ascontiguousarray(np.asarray(indices, dtype=np.int64))
+        inp, tgt = PaiTensor(), PaiTensor()
+        self._c("dataset_batch", idx.ctypes.data_as(POINTER(c_int64)), idx.size, ctypes.byref(inp), ctypes.byref(tgt))
+        return inp, tgt
+
+    def dataset_close(self) -> None:
+        self._c("dataset_close")
 
 
 # --- view helpers (ProjectAI.Core/Tensor.cs:75-168): metadata only, storage shared

@@ -46,6 +46,7 @@ struct BlockInfo {
 };
 
 struct NcclState;  // defined in dp.cu
+struct IoState;    // defined in io.cu
 
 // Device blocks a captured CUDA graph reads or writes. They stay reserved while the graph exists: blocks freed during
 // or after the capture are parked here instead of returning to the allocator's cache.
@@ -76,6 +77,7 @@ struct pai_ctx {
   // device flag the kernels with bounded waits report into (0 = ok)
   int* d_error_flag = nullptr;
   pai::NcclState* nccl = nullptr;
+  pai::IoState* io = nullptr;  // checkpoint streaming and the open packed dataset (io.cu)
   char name[128] = {0};
   // instrumentation: kernel launches issued, a stream timer, and per-kernel-family event timing
   int64_t launches = 0;

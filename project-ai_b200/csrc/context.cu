@@ -411,6 +411,7 @@ PAI_API pai_status pai_ctx_create(int device, pai_ctx** out) {
 }
 
 void pai_dp_destroy(pai_ctx* ctx);  // dp.cu
+void pai_io_destroy(pai_ctx* ctx);  // io.cu
 
 PAI_API pai_status pai_ctx_destroy(pai_ctx* ctx) {
   if (!ctx) return PAI_OK;
@@ -418,6 +419,7 @@ PAI_API pai_status pai_ctx_destroy(pai_ctx* ctx) {
   cudaStreamSynchronize(ctx->stream);
   cudaStreamSynchronize(ctx->comm_stream);
   pai_dp_destroy(ctx);
+  pai_io_destroy(ctx);  // joins a checkpoint writer still running
   for (auto& kv : ctx->live) cudaFree(kv.first);
   for (auto& kv : ctx->free_blocks)
     for (void* p : kv.second) cudaFree(p);

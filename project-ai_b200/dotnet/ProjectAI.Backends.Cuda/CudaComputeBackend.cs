@@ -794,6 +794,114 @@ public sealed unsafe class CudaComputeBackend : IComputeBackend
         }
     }
 
+    // ------------------------------------------------------------ Checkpoints (ProjectAI.Formats/Checkpoint.cs)
+
+    /// <summary>
+    /// Checkpoint.Save (Checkpoint.cs:23-57) on the device's side of the copy: the tensors are snapshotted on the GPU
+    /// and the PAICKPT2 file is written by a native thread while training continues; <see cref="WaitCheckpoint"/>
+    /// joins it (and throws its IOException). Byte-identical to Checkpoint.Save for F32 tensors.
+    /// </summary>
+    public void SaveCheckpoint(string path, int step, IEnumerable<(string Name, Tensor Tensor)> tensors, string metadata = "")
+    {
+        var items = tensors.ToList();
+        var names = new List<byte>();
+        foreach (var (name, _) in items) { names.AddRange(Encoding.UTF8.GetBytes(name)); names.Add(0); }
+        byte[] nameBytes = names.ToArray(), pathBytes = Encoding.UTF8.GetBytes(path + "\0"), meta = Encoding.UTF8.GetBytes(metadata);
+        lock (_gate)
+        {
+            Drain();
+            var ds = new PaiTensor[Math.Max(1, items.Count)];
+            for (int i = 0; i < items.Count; i++) ds[i] = Desc(items[i].Tensor);
+            fixed (byte* pp = pathBytes) fixed (byte* pm = meta) fixed (byte* pn = nameBytes) fixed (PaiTensor* pt = ds)
+                Native.Check(Native.CkptSave(Ctx, pp, step, pm, meta.Length, pn, nameBytes.Length, pt, items.Count));
+        }
+    }
+
+    public void WaitCheckpoint()
+    {
+        lock (_gate) Native.Check(Native.CkptWait(Ctx));
+    }
+
+    /// <summary>Checkpoint.Load (Checkpoint.cs:59-110): step, metadata and the tensors by name, on this device.</summary>
+    public (int Step, string Metadata, IReadOnlyList<(string Name, Tensor Tensor)> Tensors) LoadCheckpoint(string path)
+    {
+        var (step, meta, count) = ReadCheckpointHeader(path, headerOnly: false);
+        var list = new List<(string, Tensor)>(count);
+        lock (_gate)
+        {
+            for (int i = 0; i < count; i++)
+            {
+                long len;
+                Native.Check(Native.CkptTensor(Ctx, i, null, 0, &len, null));
+                var name = new byte[Math.Max(1, len)];
+                PaiTensor d;
+                fixed (byte* pn = name) Native.Check(Native.CkptTensor(Ctx, i, pn, len, null, &d));
+                list.Add((Encoding.UTF8.GetString(name, 0, (int)len), Wrap(d)));
+            }
+            Native.Check(Native.CkptClose(Ctx));
+        }
+        return (step, meta, list);
+    }
+
+    /// <summary>Checkpoint.ReadMetadata (Checkpoint.cs:113-129): the step and metadata from the header alone.</summary>
+    public (int Step, string Metadata) ReadCheckpointMetadata(string path)
+    {
+        var (step, meta, _) = ReadCheckpointHeader(path, headerOnly: true);
+        lock (_gate) Native.Check(Native.CkptClose(Ctx));
+        return (step, meta);
+    }
+
+    private (int Step, string Metadata, int Count) ReadCheckpointHeader(string path, bool headerOnly)
+    {
+        byte[] pathBytes = Encoding.UTF8.GetBytes(path + "\0");
+        lock (_gate)
+        {
+            Drain();
+            int step, count;
+            long metaLen;
+            fixed (byte* pp = pathBytes) Native.Check(Native.CkptLoad(Ctx, pp, headerOnly ? 1 : 0, &step, &metaLen, &count));
+            var meta = new byte[Math.Max(1, metaLen)];
+            fixed (byte* pm = meta) Native.Check(Native.CkptMeta(Ctx, pm, metaLen));
+            return (step, Encoding.UTF8.GetString(meta, 0, (int)metaLen), count);
+        }
+    }
+
+    // ------------------------------------------------------------ Packed datasets (ProjectAI.Training/PackedBinDataset.cs)
+
+    /// <summary>
+    /// Maps the shard a packed dataset's manifest names (PackedBinDataset.Open, PackedBinDataset.cs:43-95, after the
+    /// manifest is read): dtype "u16" or "u32", blocks of sequenceLength + 1 ids.
+    /// </summary>
+    public void OpenDataset(string shardPath, string dtype, int sequenceLength, long blockCount)
+    {
+        byte[] pathBytes = Encoding.UTF8.GetBytes(shardPath + "\0");
+        int width = dtype switch { "u16" => 2, "u32" => 4, _ => 0 };
+        lock (_gate)
+            fixed (byte* pp = pathBytes) Native.Check(Native.DatasetOpen(Ctx, pp, width, sequenceLength, blockCount));
+    }
+
+    /// <summary>
+    /// Trainer.NextBatch (Training.cs:122-141) for the given block indices, ids straight to the device: the blocks are
+    /// gathered from the mapped shard, uploaded at their on-disk width and widened to the F32 input and target ids on
+    /// the GPU.
+    /// </summary>
+    public (Tensor Input, Tensor Target) NextBatch(IReadOnlyList<long> blockIndices)
+    {
+        var idx = blockIndices.ToArray();
+        lock (_gate)
+        {
+            Drain();
+            PaiTensor i, t;
+            fixed (long* p = idx) Native.Check(Native.DatasetBatch(Ctx, p, idx.Length, &i, &t));
+            return (Wrap(i), Wrap(t));
+        }
+    }
+
+    public void CloseDataset()
+    {
+        lock (_gate) Native.Check(Native.DatasetClose(Ctx));
+    }
+
     // ------------------------------------------------------------ Diagnostics
 
     public void Synchronize()

@@ -34,6 +34,8 @@ internal enum PaiStatus
     Nccl = 6,
     Timeout = 7,
     Unsupported = 8,
+    Io = 9,
+    InvalidData = 10,
 }
 
 internal static unsafe partial class Native
@@ -112,6 +114,15 @@ internal static unsafe partial class Native
     [LibraryImport(Lib, EntryPoint = "pai_launch_count")] internal static partial int LaunchCount(IntPtr ctx, long* n);
     [LibraryImport(Lib, EntryPoint = "pai_kernel_timing")] internal static partial int KernelTiming(IntPtr ctx, int enable);
     [LibraryImport(Lib, EntryPoint = "pai_kernel_stats")] internal static partial int KernelStats(IntPtr ctx, byte* family, long* launches, double* totalMs, double* work);
+    [LibraryImport(Lib, EntryPoint = "pai_ckpt_save")] internal static partial int CkptSave(IntPtr ctx, byte* path, int step, byte* metadata, long metaLen, byte* names, long namesLen, PaiTensor* tensors, int nTensors);
+    [LibraryImport(Lib, EntryPoint = "pai_ckpt_wait")] internal static partial int CkptWait(IntPtr ctx);
+    [LibraryImport(Lib, EntryPoint = "pai_ckpt_load")] internal static partial int CkptLoad(IntPtr ctx, byte* path, int headerOnly, int* step, long* metaLen, int* nTensors);
+    [LibraryImport(Lib, EntryPoint = "pai_ckpt_meta")] internal static partial int CkptMeta(IntPtr ctx, byte* buf, long cap);
+    [LibraryImport(Lib, EntryPoint = "pai_ckpt_tensor")] internal static partial int CkptTensor(IntPtr ctx, int index, byte* name, long nameCap, long* nameLen, PaiTensor* @out);
+    [LibraryImport(Lib, EntryPoint = "pai_ckpt_close")] internal static partial int CkptClose(IntPtr ctx);
+    [LibraryImport(Lib, EntryPoint = "pai_dataset_open")] internal static partial int DatasetOpen(IntPtr ctx, byte* binPath, int elemBytes, int seqLen, long blockCount);
+    [LibraryImport(Lib, EntryPoint = "pai_dataset_batch")] internal static partial int DatasetBatch(IntPtr ctx, long* indices, int count, PaiTensor* inputs, PaiTensor* targets);
+    [LibraryImport(Lib, EntryPoint = "pai_dataset_close")] internal static partial int DatasetClose(IntPtr ctx);
 
 
     /// <summary>The message pai_last_error() holds for this thread.</summary>
@@ -121,8 +132,9 @@ internal static unsafe partial class Native
     /// Maps a status onto the exception ProjectAI's CPU backend throws for the same condition: ArgumentException
     /// (shape, rank, broadcast), ArgumentOutOfRangeException (axis, id, target; CpuComputeBackend.cs:257-258,432,446,
     /// 463), InvalidOperationException, and OutOfMemoryException whose message contains "out of memory"
-    /// (ProjectAI.Trainer/Program.cs:152-157 matches on that text). Device, NCCL and timeout failures are
-    /// InvalidOperationException with the library's message.
+    /// (ProjectAI.Trainer/Program.cs:152-157 matches on that text), and for the checkpoint and dataset files the
+    /// IOException and InvalidDataException of ProjectAI.Formats/Checkpoint.cs and PackedBinDataset.cs. Device, NCCL
+    /// and timeout failures are InvalidOperationException with the library's message.
     /// </summary>
     internal static void Check(int status)
     {
@@ -134,6 +146,8 @@ internal static unsafe partial class Native
             PaiStatus.OutOfRange => new ArgumentOutOfRangeException(null, msg),
             PaiStatus.OutOfMemory => new OutOfMemoryException(msg),
             PaiStatus.Unsupported => new NotSupportedException(msg),
+            PaiStatus.Io => new IOException(msg),
+            PaiStatus.InvalidData => new InvalidDataException(msg),
             _ => new InvalidOperationException(msg),
         };
     }

@@ -20,7 +20,7 @@ PATCH = DOTNET / "Backends.cs.patch"
 C_TO_CS = [
     (r"^(const )?pai_tensor\*$", "PaiTensor*"), (r"^pai_ctx\*$", "IntPtr"), (r"^pai_ctx\*\*$", "IntPtr*"),
     (r"^pai_graph\*$", "IntPtr"), (r"^pai_graph\*\*$", "IntPtr*"), (r"^(const )?float\*$", "float*"),
-    (r"^(const )?int32_t\*$", "int*"), (r"^int64_t\*$", "long*"), (r"^double\*$", "double*"),
+    (r"^(const )?int32_t\*$", "int*"), (r"^(const )?int64_t\*$", "long*"), (r"^double\*$", "double*"),
     (r"^(const )?uint8_t$", "byte*"), (r"^const void\*$", "IntPtr"), (r"^(const )?char\*$", "byte*"),
     (r"^(int32_t|int)$", "int"), (r"^int64_t$", "long"), (r"^float$", "float"),
 ]

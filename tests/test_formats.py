@@ -1,0 +1,188 @@
+"""PAICKPT2 checkpoints and packed token datasets.
+
+CPU: the oracle (oracle/formats.py) against known-answer bytes built by hand from the layout documented in
+ProjectAI.Formats/Checkpoint.cs:11-16, its read checks (Checkpoint.cs:59-124) and the packed-dataset rules of
+ProjectAI.Training/PackedBinDataset.cs and ProjectAI.Tests/PackedDatasetTests.cs (blocks of seq_len + 1 ids, trailing
+remainder dropped, u16 when the vocabulary fits, a truncated shard rejected).
+
+GPU: the native paths of project-ai_b200/csrc/io.cu through the C ABI — a saved file is byte-identical to the oracle's
+for the same tensors (views, a scalar, a payload spanning several staging chunks), a save snapshots the tensors so
+later device writes do not reach the file, a load reproduces the oracle's tensors and raises the reference's errors on
+damaged files, and a dataset batch equals Trainer.NextBatch (Training.cs:122-141) bit for bit.
+"""
+import struct
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+sys.path.insert(0, str(ROOT / "oracle"))
+import formats as F  # noqa: E402  (the oracle, test infrastructure)
+
+from projectai_b200 import cabi  # noqa: E402
+
+
+def known_answer() -> bytes:
+    """step 7, metadata "{}", "w" = [1, -2] and "s" = 0.5 (rank 0), written out field by field."""
+    b = b"PAICKPT2" + struct.pack("<i", 7) + struct.pack("<i", 2) + b"{}" + struct.pack("<i", 2)
+    b += struct.pack("<i", 1) + b"w" + struct.pack("<i", 1) + struct.pack("<i", 2) + struct.pack("<q", 8)
+    b += struct.pack("<f", 1.0) + struct.pack("<f", -2.0)
+    b += struct.pack("<i", 1) + b"s" + struct.pack("<i", 0) + struct.pack("<q", 4) + struct.pack("<f", 0.5)
+    return b
+
+
+# ---------------------------------------------------------------- oracle (CPU)
+def test_oracle_checkpoint_matches_the_documented_layout(tmp_path):
+    tensors = [("w", np.array([1.0, -2.0], np.float32)), ("s", np.array(0.5, np.float32))]
+    assert F.checkpoint_bytes(7, tensors, "{}") == known_answer()
+    p = tmp_path / "k.ckpt"
+    p.write_bytes(known_answer())
+    step, meta, back = F.load_checkpoint(p)
+    assert (step, meta) == (7, "{}")
+    assert [n for n, _ in back] == ["w", "s"] and back[1][1].shape == () and float(back[1][1]) == 0.5
+    assert F.load_checkpoint(p, header_only=True)[:2] == (7, "{}")
+
+
+def damaged_files(good: bytes):
+    """(bytes, message fragment) pairs for each check of Checkpoint.Load (Checkpoint.cs:64-101)."""
+    body = good[8:]
+    meta_end = 8 + 8 + 2
+    w_rank = meta_end + 4 + 4 + 1
+    return [
+        (b"PAICKPT1" + body, "bad magic"),
+        (good[:12] + struct.pack("<i", -1) + good[16:], "bad metadata length (-1)"),
+        (good[:12] + struct.pack("<i", (1 << 24) + 1) + good[16:], "bad metadata length"),
+        (good[:meta_end] + struct.pack("<i", -3) + good[meta_end + 4:], "negative tensor count (-3)"),
+        (good[:meta_end + 4] + struct.pack("<i", -1) + good[meta_end + 8:], "bad name length -1"),
+        (good[:w_rank] + struct.pack("<i", 9) + good[w_rank + 4:], "invalid rank 9"),
+        (good[:w_rank + 4] + struct.pack("<i", -2) + good[w_rank + 8:], "negative dimension -2"),
+        (good[:w_rank + 8] + struct.pack("<q", 12) + good[w_rank + 16:], "payload length 12 != dims product"),
+        (good[:-2], "is truncated"),
+        (good[:14], "is truncated"),
+    ]
+
+
+def test_oracle_checkpoint_rejects_damaged_files(tmp_path):
+    for i, (data, msg) in enumerate(damaged_files(known_answer())):
+        p = tmp_path / f"bad{i}.ckpt"
+        p.write_bytes(data)
+        with pytest.raises(F.InvalidData, match=msg.replace("(", r"\(").replace(")", r"\)")):
+            F.load_checkpoint(p)
+
+
+def test_oracle_packed_dataset_blocks_and_guards(tmp_path):
+    ids = np.random.RandomState(3).randint(0, 259, size=16 * 17 + 5)
+    m = F.pack_dataset(ids, 259, 16, tmp_path / "a")
+    assert (m["Dtype"], m["BlockCount"], m["DroppedTokens"]) == ("u16", 16, 5)
+    man, shard = F.read_manifest(tmp_path / "a")
+    for b in (0, 7, 15):
+        assert np.array_equal(F.get_sequence(man, shard, b), ids[b * 17:(b + 1) * 17])
+    inp, tgt = F.next_batch(man, shard, [3, 0, 3])
+    assert np.array_equal(inp[0], ids[51:67].astype(np.float32)) and np.array_equal(tgt[0], ids[52:68].astype(np.float32))
+    with pytest.raises(IndexError):
+        F.get_sequence(man, shard, 16)
+    assert F.pack_dataset(ids, 70000, 16, tmp_path / "b")["Dtype"] == "u32"
+    with open(shard, "r+b") as f:  # PackedDatasetTests.Open_RejectsTruncatedShard
+        f.truncate(8)
+    with pytest.raises(F.InvalidData, match="bytes but the manifest needs"):
+        F.read_manifest(tmp_path / "a")
+    with pytest.raises(FileNotFoundError):
+        F.read_manifest(tmp_path / "missing")
+
+
+# ---------------------------------------------------------------- native path (GPU)
+def rnd(seed, *shape):
+    return np.random.RandomState(seed).standard_normal(shape).astype(np.float32)
+
+
+@pytest.mark.gpu
+def test_saved_checkpoint_is_byte_identical_to_the_oracle(cuda, tmp_path):
+    a, b, big = rnd(1, 33, 70), rnd(2, 5, 6, 7), rnd(3, 20_000_003)  # big spans three 32 MB staging chunks
+    ta, tb, tbig = cuda.from_host(a), cuda.from_host(b), cuda.from_host(big)
+    ts = cuda.from_host(np.array(0.25, np.float32), shape=())
+    tt = cabi.transpose(ta, 0, 1)  # a strided view is written in its logical (row-major) order
+    named = [("layers.0.w", ta), ("opt.m::layers.0.w", tt), ("b", tb), ("scalar", ts), ("big", tbig)]
+    p = tmp_path / "s.ckpt"
+    cuda.save_checkpoint(p, 42, named, '{"Config": 1}')
+    cuda.wait_checkpoint()
+    want = F.checkpoint_bytes(42, [("layers.0.w", a), ("opt.m::layers.0.w", a.T), ("b", b),
+                                   ("scalar", np.array(0.25, np.float32)), ("big", big)], '{"Config": 1}')
+    got = p.read_bytes()
+    assert len(got) == len(want) and got == want
+
+
+@pytest.mark.gpu
+def test_save_snapshots_the_tensors_before_returning(cuda, tmp_path):
+    x = rnd(4, 4_000_000)
+    t = cuda.from_host(x)
+    p = tmp_path / "snap.ckpt"
+    cuda.save_checkpoint(p, 1, [("x", t)])
+    cuda.copy(cuda.from_host(np.zeros_like(x)), t)  # queued after the snapshot, while the file is being written
+    cuda.wait_checkpoint()
+    assert np.array_equal(F.load_checkpoint(p)[2][0][1], x)
+    assert np.array_equal(cuda.to_host(t), np.zeros_like(x))
+
+
+@pytest.mark.gpu
+def test_load_matches_the_oracle_and_raises_its_errors(cuda, tmp_path):
+    tensors = [("w", rnd(5, 64, 48)), ("v", rnd(6, 9_000_001)), ("s", np.array(-1.5, np.float32)), ("e", np.zeros((0, 3), np.float32))]
+    p = tmp_path / "l.ckpt"
+    F.save_checkpoint(p, 9, tensors, "meta ✓")
+    step, meta, got = cuda.load_checkpoint(p)
+    assert (step, meta) == (9, "meta ✓") and list(got) == [n for n, _ in tensors]
+    for name, arr in tensors:
+        assert got[name].shape == arr.shape
+        assert np.array_equal(cuda.to_host(got[name]), arr)
+    assert cuda.read_checkpoint_metadata(p) == (9, "meta ✓")
+    for i, (data, msg) in enumerate(damaged_files(known_answer())):
+        q = tmp_path / f"bad{i}.ckpt"
+        q.write_bytes(data)
+        with pytest.raises(cabi.InvalidDataError, match=msg.replace("(", r"\(").replace(")", r"\)")):
+            cuda.load_checkpoint(q)
+    with pytest.raises(cabi.FileIOError):
+        cuda.load_checkpoint(tmp_path / "absent.ckpt")
+    with pytest.raises(cabi.FileIOError):
+        cuda.save_checkpoint(tmp_path / "no" / "dir" / "x.ckpt", 0, [("w", cuda.from_host(tensors[0][1]))])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("vocab", [259, 100_000])
+def test_dataset_batch_equals_next_batch(cuda, tmp_path, vocab):
+    seq = 64
+    ids = np.random.RandomState(vocab).randint(0, vocab, size=40 * (seq + 1) + 11)
+    m = F.pack_dataset(ids, vocab, seq, tmp_path)
+    man, shard = F.read_manifest(tmp_path)
+    cuda.dataset_open(shard, man["Dtype"], man["SequenceLength"], man["BlockCount"])
+    for indices in ([0], [39, 3, 3, 17], list(range(40))):
+        inp, tgt = cuda.dataset_batch(indices)
+        want_i, want_t = F.next_batch(man, shard, indices)
+        assert np.array_equal(cuda.to_host(inp), want_i) and np.array_equal(cuda.to_host(tgt), want_t)
+    with pytest.raises(cabi.OutOfRangeError):
+        cuda.dataset_batch([m["BlockCount"]])
+    cuda.dataset_close()
+    with pytest.raises(cabi.InvalidOperationError):
+        cuda.dataset_batch([0])
+
+
+@pytest.mark.gpu
+def test_dataset_open_and_id_guards(cuda, tmp_path):
+    seq = 8
+    ids = np.arange(5 * (seq + 1), dtype=np.int64)
+    F.pack_dataset(ids, 1 << 20, seq, tmp_path / "d")
+    man, shard = F.read_manifest(tmp_path / "d")
+    with pytest.raises(cabi.InvalidDataError, match="bytes but the manifest needs"):
+        cuda.dataset_open(shard, "u32", seq, 6)
+    with pytest.raises(cabi.InvalidDataError, match="unsupported dataset dtype"):
+        cuda.dataset_open(shard, "u8", seq, 5)
+    with pytest.raises(cabi.FileIOError):
+        cuda.dataset_open(tmp_path / "none.bin", "u32", seq, 5)
+    raw = np.fromfile(shard, dtype="<u4")
+    raw[2 * (seq + 1) + 4] = 2**31  # above int32: GetSequence's checked cast throws
+    raw.tofile(shard)
+    cuda.dataset_open(shard, "u32", seq, 5)
+    inp, _ = cuda.dataset_batch([1])
+    assert np.array_equal(cuda.to_host(inp)[0], ids[9:17].astype(np.float32))
+    with pytest.raises(cabi.OutOfRangeError, match="exceeds the int32 range"):
+        cuda.dataset_batch([2])
