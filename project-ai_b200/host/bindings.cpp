@@ -67,6 +67,8 @@ PYBIND11_MODULE(_paihost, m) {
   py::register_exception<InvalidOperationError>(m, "InvalidOperationError", backend_error.ptr());
   py::register_exception<OutOfMemoryError>(m, "OutOfMemoryError", PyExc_MemoryError);
   py::register_exception<DeviceTimeoutError>(m, "DeviceTimeoutError", PyExc_TimeoutError);
+  py::register_exception<FileIOError>(m, "FileIOError", PyExc_OSError);
+  py::register_exception<InvalidDataError>(m, "InvalidDataError", PyExc_ValueError);
 
   py::class_<TensorImpl, Tensor>(m, "Tensor")
       .def_property_readonly("shape", [](const Tensor& t) { return py::tuple(py::cast(t->shape)); })
@@ -138,6 +140,16 @@ PYBIND11_MODULE(_paihost, m) {
         be.write(dst, a.data(), (int64_t)a.size());
       })
       .def("gather_dev", &NativeBackend::gather_dev)
+      .def("save_checkpoint", &NativeBackend::save_checkpoint, py::arg("path"), py::arg("step"), py::arg("tensors"),
+           py::arg("metadata") = "")
+      .def("wait_checkpoint", &NativeBackend::wait_checkpoint, py::call_guard<py::gil_scoped_release>())
+      .def("load_checkpoint", [](NativeBackend& be, const std::string& path, bool header_only) {
+        auto r = be.load_checkpoint(path, header_only);
+        return py::make_tuple(r.step, r.metadata, r.tensors);
+      }, py::arg("path"), py::arg("header_only") = false)
+      .def("dataset_open", &NativeBackend::dataset_open)
+      .def("dataset_batch", &NativeBackend::dataset_batch)
+      .def("dataset_close", &NativeBackend::dataset_close)
       .def("rotary_at", &NativeBackend::rotary_at)
       .def("kv_append", &NativeBackend::kv_append)
       .def("sdpa_decode", &NativeBackend::sdpa_decode)
@@ -327,6 +339,18 @@ PYBIND11_MODULE(_paihost, m) {
       .def("step_tensors", [](PyTrainer& t, std::vector<Tensor> inputs, std::vector<Tensor> targets) {
         py::gil_scoped_release nogil;
         return t.trainer->step_tensors(inputs, targets);
+      })
+      .def("save_checkpoint", [](PyTrainer& t, const std::string& path, int step, const std::string& metadata) {
+        py::gil_scoped_release nogil;
+        t.trainer->save_checkpoint(path, step, metadata);
+      }, py::arg("path"), py::arg("step"), py::arg("metadata") = "")
+      .def("wait_checkpoint", [](PyTrainer& t) {
+        py::gil_scoped_release nogil;
+        t.trainer->wait_checkpoint();
+      })
+      .def("restore", [](PyTrainer& t, const std::string& path) {
+        py::gil_scoped_release nogil;
+        return t.trainer->restore(path);
       })
       .def_property_readonly("optimizer", [](PyTrainer& t) { return t.trainer->optimizer.get(); },
                              py::return_value_policy::reference_internal)

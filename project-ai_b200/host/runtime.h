@@ -31,6 +31,8 @@ struct OutOfRangeError : ArgumentError { using ArgumentError::ArgumentError; };
 struct InvalidOperationError : BackendError { using BackendError::BackendError; };
 struct OutOfMemoryError : BackendError { using BackendError::BackendError; };
 struct DeviceTimeoutError : BackendError { using BackendError::BackendError; };
+struct FileIOError : BackendError { using BackendError::BackendError; };       // IOException
+struct InvalidDataError : BackendError { using BackendError::BackendError; };  // InvalidDataException
 
 using Dims = std::vector<int>;
 int64_t numel(const Dims& d);
@@ -172,6 +174,21 @@ class NativeBackend {
   // index of each row's largest entry (ArgMax's rules, Sampling.cs:15-31) as a [rows] float tensor; optional op
   bool has_argmax_rows() const;
   Tensor argmax_rows(const Tensor& x);
+  // PAICKPT2 checkpoints (Checkpoint.cs:23-139): save returns once the tensors are snapshotted on the device; the file
+  // is written in the background until wait_checkpoint. load returns the tensors in the current scope.
+  void save_checkpoint(const std::string& path, int step, const std::vector<std::pair<std::string, Tensor>>& tensors,
+                       const std::string& metadata);
+  void wait_checkpoint();
+  struct LoadedCheckpoint {
+    int step = 0;
+    std::string metadata;
+    std::vector<std::pair<std::string, Tensor>> tensors;
+  };
+  LoadedCheckpoint load_checkpoint(const std::string& path, bool header_only = false);
+  // Packed token datasets (PackedBinDataset.cs): map a shard, then device [count, seq] F32 input/target ids per batch.
+  void dataset_open(const std::string& bin_path, const std::string& dtype, int seq_len, int64_t block_count);
+  std::pair<Tensor, Tensor> dataset_batch(const std::vector<int64_t>& indices);
+  void dataset_close();
   Tensor linear_fused(const Tensor& x, const std::vector<Tensor>& weights, int mode, const Tensor& residual = nullptr,
                       const Tensor& norm_weight = nullptr, float eps = 0.0f);
   Tensor rope_append(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos_table, const Tensor& sin_table,
@@ -512,6 +529,13 @@ class Trainer {
   float step(const std::vector<std::vector<float>>& inputs, const std::vector<std::vector<float>>& targets);
   // The same step on batches already uploaded to the device ([batch, seq] id tensors from FromHost).
   float step_tensors(const std::vector<Tensor>& inputs, const std::vector<Tensor>& targets);
+  // Checkpointing.SaveModel's state (Checkpointing.cs:103-115: each parameter by name, then its AdamW moments as
+  // "opt.m::name" / "opt.v::name") written as PAICKPT2 with `step`; the file is finished by wait_checkpoint (or the
+  // next save). restore (Training.cs:156-162 with Checkpointing.ApplyWeights / ApplyOptimizer) copies the weights and
+  // moments back, sets the optimizer's step count and returns the saved step.
+  void save_checkpoint(const std::string& path, int step, const std::string& metadata = "");
+  void wait_checkpoint();
+  int restore(const std::string& path);
   LlamaModel* model;
   TrainingConfig cfg;
   std::unique_ptr<AdamW> optimizer;

@@ -293,7 +293,17 @@ void TensorImpl::backward(const Tensor& seed) {
   X(graph_end, int (*)(pai_ctx*, pai_graph**))                                                                           \
   X(graph_launch, int (*)(pai_ctx*, pai_graph*))                                                                         \
   X(graph_destroy, int (*)(pai_ctx*, pai_graph*))                                                                       \
-  X(argmax_rows, int (*)(pai_ctx*, const pai_tensor*, pai_tensor*))
+  X(argmax_rows, int (*)(pai_ctx*, const pai_tensor*, pai_tensor*))                                                     \
+  X(ckpt_save, int (*)(pai_ctx*, const char*, int32_t, const char*, int64_t, const char*, int64_t, const pai_tensor*,    \
+                       int32_t))                                                                                         \
+  X(ckpt_wait, int (*)(pai_ctx*))                                                                                        \
+  X(ckpt_load, int (*)(pai_ctx*, const char*, int32_t, int32_t*, int64_t*, int32_t*))                                    \
+  X(ckpt_meta, int (*)(pai_ctx*, char*, int64_t))                                                                        \
+  X(ckpt_tensor, int (*)(pai_ctx*, int32_t, char*, int64_t, int64_t*, pai_tensor*))                                      \
+  X(ckpt_close, int (*)(pai_ctx*))                                                                                       \
+  X(dataset_open, int (*)(pai_ctx*, const char*, int32_t, int32_t, int64_t))                                             \
+  X(dataset_batch, int (*)(pai_ctx*, const int64_t*, int32_t, pai_tensor*, pai_tensor*))                                 \
+  X(dataset_close, int (*)(pai_ctx*))
 
 template <class T>
 using Fn = T;
@@ -337,6 +347,8 @@ void NativeBackend::check(int st) const {
     case PAI_ERR_INVALID_OP: throw InvalidOperationError(msg);
     case PAI_ERR_OUT_OF_MEMORY: throw OutOfMemoryError(msg);
     case PAI_ERR_TIMEOUT: throw DeviceTimeoutError(msg);
+    case PAI_ERR_IO: throw FileIOError(msg);
+    case PAI_ERR_INVALID_DATA: throw InvalidDataError(msg);
     default: throw BackendError(msg);
   }
 }
@@ -361,6 +373,67 @@ bool NativeBackend::has_graphs() const {
 
 bool NativeBackend::has_decode_fusions() const { return fn_->linear_fused && fn_->rope_append && fn_->attn_decode_step; }
 bool NativeBackend::has_argmax_rows() const { return fn_->argmax_rows != nullptr; }
+
+// ---------------------------------------------------------------- checkpoints and packed datasets (io.cu)
+static void need_io(const void* fn, const char* what) {
+  if (!fn) throw BackendError(std::string("backend has no ") + what + " (the CUDA backend provides it)");
+}
+
+void NativeBackend::save_checkpoint(const std::string& path, int step,
+                                    const std::vector<std::pair<std::string, Tensor>>& tensors, const std::string& metadata) {
+  need_io((void*)fn_->ckpt_save, "checkpoint I/O");
+  std::string names;
+  std::vector<pai_tensor> d;
+  for (const auto& kv : tensors) {
+    names += kv.first;
+    names.push_back('\0');
+    d.push_back(kv.second->desc());
+  }
+  check(fn_->ckpt_save(ctx_, path.c_str(), step, metadata.data(), (int64_t)metadata.size(), names.data(),
+                       (int64_t)names.size(), d.data(), (int32_t)d.size()));
+}
+
+void NativeBackend::wait_checkpoint() {
+  need_io((void*)fn_->ckpt_wait, "checkpoint I/O");
+  check(fn_->ckpt_wait(ctx_));
+}
+
+NativeBackend::LoadedCheckpoint NativeBackend::load_checkpoint(const std::string& path, bool header_only) {
+  need_io((void*)fn_->ckpt_load, "checkpoint I/O");
+  LoadedCheckpoint r;
+  int32_t count = 0;
+  int64_t mlen = 0;
+  check(fn_->ckpt_load(ctx_, path.c_str(), header_only ? 1 : 0, &r.step, &mlen, &count));
+  r.metadata.resize((size_t)mlen);
+  check(fn_->ckpt_meta(ctx_, mlen ? &r.metadata[0] : nullptr, mlen));
+  for (int32_t i = 0; i < count; i++) {
+    int64_t nlen = 0;
+    check(fn_->ckpt_tensor(ctx_, i, nullptr, 0, &nlen, nullptr));
+    std::string name((size_t)nlen, '\0');
+    pai_tensor t;
+    check(fn_->ckpt_tensor(ctx_, i, nlen ? &name[0] : nullptr, nlen, nullptr, &t));
+    r.tensors.emplace_back(std::move(name), wrap(t));
+  }
+  check(fn_->ckpt_close(ctx_));
+  return r;
+}
+
+void NativeBackend::dataset_open(const std::string& bin_path, const std::string& dtype, int seq_len, int64_t block_count) {
+  need_io((void*)fn_->dataset_open, "packed datasets");
+  const int width = dtype == "u16" ? 2 : dtype == "u32" ? 4 : 0;
+  check(fn_->dataset_open(ctx_, bin_path.c_str(), width, seq_len, block_count));
+}
+
+std::pair<Tensor, Tensor> NativeBackend::dataset_batch(const std::vector<int64_t>& indices) {
+  need_io((void*)fn_->dataset_batch, "packed datasets");
+  pai_tensor in, tg;
+  check(fn_->dataset_batch(ctx_, indices.data(), (int32_t)indices.size(), &in, &tg));
+  return {wrap(in), wrap(tg)};
+}
+
+void NativeBackend::dataset_close() {
+  if (fn_->dataset_close) check(fn_->dataset_close(ctx_));
+}
 
 Tensor NativeBackend::wrap(const pai_tensor& d) {
   auto st = std::make_shared<Storage>();

@@ -407,3 +407,66 @@ GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<
 }
 
 }  // namespace paihost
+
+namespace paihost {
+
+// Checkpointing.EnumerateState (Checkpointing.cs:103-115): each parameter by name, then its AdamW moments.
+void Trainer::save_checkpoint(const std::string& path, int step, const std::string& metadata) {
+  if (optimizer->shard_world > 1)
+    throw InvalidOperationError("the optimizer state is sharded across ranks (ZeRO-1); gather it before checkpointing");
+  std::vector<std::pair<std::string, Tensor>> items;
+  for (const auto& kv : model->named_parameters()) {
+    items.push_back(kv);
+    auto it = optimizer->state.find(kv.second.get());
+    if (it != optimizer->state.end() && it->second.m && it->second.v) {
+      items.emplace_back("opt.m::" + kv.first, it->second.m);
+      items.emplace_back("opt.v::" + kv.first, it->second.v);
+    }
+  }
+  be_->save_checkpoint(path, step, items, metadata);
+}
+
+void Trainer::wait_checkpoint() { be_->wait_checkpoint(); }
+
+// Trainer.Restore (Training.cs:156-162): Checkpointing.ApplyWeights then ApplyOptimizer (Checkpointing.cs:118-142).
+int Trainer::restore(const std::string& path) {
+  be_->wait_checkpoint();  // a save of this process still writing the file finishes first
+  be_->begin_scope();
+  try {
+    auto ck = be_->load_checkpoint(path);
+    std::map<std::string, Tensor> dict(ck.tensors.begin(), ck.tensors.end());
+    const auto named = model->named_parameters();
+    for (const auto& kv : named) {
+      auto it = dict.find(kv.first);
+      if (it == dict.end()) throw InvalidDataError("checkpoint is missing parameter '" + kv.first + "'.");
+      if (it->second->shape != kv.second->shape)
+        throw InvalidDataError("checkpoint parameter '" + kv.first + "' shape " + dims_str(it->second->shape) +
+                               " != model " + dims_str(kv.second->shape) + ".");
+      be_->copy(it->second, kv.second);
+    }
+    for (const auto& kv : named) {
+      auto m = dict.find("opt.m::" + kv.first), v = dict.find("opt.v::" + kv.first);
+      if (m == dict.end() || v == dict.end()) continue;
+      AdamW::State& s = optimizer->state[kv.second.get()];
+      if (!s.m || s.m->shape != m->second->shape) {
+        s.m = be_->allocate(m->second->shape);
+        be_->keep_alive(s.m);
+      }
+      if (!s.v || s.v->shape != v->second->shape) {
+        s.v = be_->allocate(v->second->shape);
+        be_->keep_alive(s.v);
+      }
+      be_->copy(m->second, s.m);
+      be_->copy(v->second, s.v);
+      s.t = ck.step;  // every parameter is updated every step (dense LM training), as the reference assumes
+    }
+    optimizer->step_count = ck.step;
+    be_->end_scope();
+    return ck.step;
+  } catch (...) {
+    be_->end_scope();
+    throw;
+  }
+}
+
+}  // namespace paihost

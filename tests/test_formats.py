@@ -186,3 +186,72 @@ def test_dataset_open_and_id_guards(cuda, tmp_path):
     assert np.array_equal(cuda.to_host(inp)[0], ids[9:17].astype(np.float32))
     with pytest.raises(cabi.OutOfRangeError, match="exceeds the int32 range"):
         cuda.dataset_batch([2])
+
+
+@pytest.mark.gpu
+def test_trainer_checkpoint_resume_and_dataset_batches(tmp_path):
+    """The host trainer end to end: micro-batches from a packed dataset (device ids), two AdamW steps, a checkpoint
+    in the reference's state layout (each parameter, then its opt.m:: / opt.v:: moments), restored into a model
+    initialised from another seed; the restored weights and moments equal the saved ones exactly and the next step
+    matches the uninterrupted run."""
+    import projectai_b200 as pai
+    from projectai_b200 import _paihost as H
+
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", 0)
+    cfg = dict(vocab_size=256, embedding_dim=128, layer_count=2, head_count=4, kv_head_count=2, ffn_hidden=344,
+               max_sequence_length=64)
+    seq = 32
+
+    def trainer(seed):
+        m = H.LlamaModel(be, H.ModelConfig(**cfg), seed=seed)
+        tc = H.TrainingConfig(batch_size=2, sequence_length=seq, learning_rate=1e-3, weight_decay=0.1, max_steps=10,
+                              gradient_checkpointing=True, warmup_steps=0)
+        tr = H.Trainer(be, m, tc, 0.9, 0.95)
+        tr.set_constant_lr(1e-3)
+        return m, tr
+
+    ids = np.random.RandomState(11).randint(0, 256, size=12 * (seq + 1))
+    man = F.pack_dataset(ids, 256, seq, tmp_path / "ds")
+    man, shard = F.read_manifest(tmp_path / "ds")
+    be.dataset_open(str(shard), man["Dtype"], seq, man["BlockCount"])
+    picks = [[0, 5], [7, 2], [11, 3]]
+
+    def batch(i):
+        inp, tgt = be.dataset_batch(picks[i])
+        want_i, want_t = F.next_batch(man, shard, picks[i])
+        assert np.array_equal(be.to_host(inp), want_i) and np.array_equal(be.to_host(tgt), want_t)
+        return inp, tgt
+
+    m1, t1 = trainer(0)
+    for i in range(2):
+        inp, tgt = batch(i)
+        t1.step_tensors([inp], [tgt])
+    path = tmp_path / "step-2.ckpt"
+    t1.save_checkpoint(str(path), 2, '{"Config": "tiny"}')
+    t1.wait_checkpoint()
+
+    step, meta, saved = F.load_checkpoint(path)
+    names = [n for n, _ in m1.named_parameters()]
+    assert (step, meta) == (2, '{"Config": "tiny"}')
+    assert [n for n, _ in saved] == [x for n in names for x in (n, f"opt.m::{n}", f"opt.v::{n}")]
+    saved = dict(saved)
+    for n, p in m1.named_parameters():
+        assert np.array_equal(saved[n], be.to_host(p)), n
+
+    m2, t2 = trainer(1)
+    assert t2.restore(str(path)) == 2
+    for n, p in m2.named_parameters():
+        assert np.array_equal(be.to_host(p), saved[n]), n
+    inp, tgt = batch(2)
+    l1 = t1.step_tensors([inp], [tgt])
+    l2 = t2.step_tensors([inp], [tgt])
+    assert abs(l1 - l2) <= 1e-6 * abs(l1), (l1, l2)
+    w1 = dict((n, be.to_host(p)) for n, p in m1.named_parameters())
+    for n, p in m2.named_parameters():
+        np.testing.assert_allclose(be.to_host(p), w1[n], rtol=1e-5, atol=1e-7, err_msg=n)
+    be.dataset_close()
+
+    bad = tmp_path / "missing.ckpt"
+    F.save_checkpoint(bad, 1, [(n, saved[n]) for n in names[1:]])
+    with pytest.raises(H.InvalidDataError, match="is missing parameter"):
+        t2.restore(str(bad))
