@@ -352,6 +352,15 @@ PYBIND11_MODULE(_paihost, m) {
         py::gil_scoped_release nogil;
         return t.trainer->restore(path);
       })
+      // (name, tensor) pairs of the checkpointed state with full-size moments; collective under ZeRO-1
+      .def("state_items", [](PyTrainer& t) {
+        py::gil_scoped_release nogil;
+        return t.trainer->state_items();
+      })
+      .def("apply_state", [](PyTrainer& t, const std::vector<std::pair<std::string, Tensor>>& items, int step) {
+        py::gil_scoped_release nogil;
+        t.trainer->apply_state(items, step);
+      }, py::arg("items"), py::arg("step"))
       .def_property_readonly("optimizer", [](PyTrainer& t) { return t.trainer->optimizer.get(); },
                              py::return_value_policy::reference_internal)
       .def("set_constant_lr", [](PyTrainer& t, float lr) {

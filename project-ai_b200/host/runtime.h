@@ -533,9 +533,18 @@ class Trainer {
   // "opt.m::name" / "opt.v::name") written as PAICKPT2 with `step`; the file is finished by wait_checkpoint (or the
   // next save). restore (Training.cs:156-162 with Checkpointing.ApplyWeights / ApplyOptimizer) copies the weights and
   // moments back, sets the optimizer's step count and returns the saved step.
+  //
+  // Under ZeRO-1 the moments of sharded parameters live one shard per rank, so save_checkpoint is collective: every
+  // rank calls it, the shards are all-gathered into full-size moments (the file is the same as a replicated run's),
+  // and a rank that passes an empty path joins the gather without writing. restore reads the full file on each rank
+  // and keeps this rank's shard of every sharded moment.
   void save_checkpoint(const std::string& path, int step, const std::string& metadata = "");
   void wait_checkpoint();
   int restore(const std::string& path);
+  // The state save_checkpoint writes, in its order, with full-size moments (collective under ZeRO-1; the tensors
+  // belong to the caller's scope), and the part of restore that applies such a state and step count.
+  std::vector<std::pair<std::string, Tensor>> state_items();
+  void apply_state(const std::vector<std::pair<std::string, Tensor>>& items, int step);
   LlamaModel* model;
   TrainingConfig cfg;
   std::unique_ptr<AdamW> optimizer;
@@ -554,6 +563,8 @@ class Trainer {
   std::function<void(const std::vector<Tensor>&)> allgather;
 
  private:
+  // Sets the optimizer's shard rank and world from world / rank / zero1 (the backend's when unset); returns the world.
+  int configure_shards();
   NativeBackend* be_;
   std::vector<Tensor> params_;
   std::vector<std::vector<Tensor>> block_params_;

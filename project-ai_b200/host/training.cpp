@@ -135,15 +135,21 @@ float Trainer::step(const std::vector<std::vector<float>>& inputs, const std::ve
   return step_tensors(in, tg);
 }
 
+int Trainer::configure_shards() {
+  const int ranks = world > 0 ? world : be_->dp_world;
+  const int my_rank = rank >= 0 ? rank : be_->dp_rank;
+  const bool shard = ranks > 1 && zero1;
+  optimizer->shard_world = shard ? ranks : 1;
+  optimizer->shard_rank = shard ? my_rank : 0;
+  return ranks;
+}
+
 float Trainer::step_tensors(const std::vector<Tensor>& inputs, const std::vector<Tensor>& targets) {
   int micro_steps = std::max(1, (int)inputs.size());
   if ((int)targets.size() != micro_steps) throw ArgumentError("inputs and targets must hold the same number of micro-batches");
-  const int ranks = world > 0 ? world : be_->dp_world;
-  const int my_rank = rank >= 0 ? rank : be_->dp_rank;
+  const int ranks = configure_shards();
   const bool dp = ranks > 1;
   const bool shard = dp && zero1;
-  optimizer->shard_world = shard ? ranks : 1;
-  optimizer->shard_rank = shard ? my_rank : 0;
   auto exchange = [this, shard](const std::vector<Tensor>& g) {
     if (g.empty()) return;
     std::vector<Tensor> whole, split;
@@ -410,57 +416,105 @@ GenerateResult generate(NativeBackend* be, LlamaModel* model, const std::vector<
 
 namespace paihost {
 
-// Checkpointing.EnumerateState (Checkpointing.cs:103-115): each parameter by name, then its AdamW moments.
-void Trainer::save_checkpoint(const std::string& path, int step, const std::string& metadata) {
-  if (optimizer->shard_world > 1)
-    throw InvalidOperationError("the optimizer state is sharded across ranks (ZeRO-1); gather it before checkpointing");
+// Checkpointing.EnumerateState (Checkpointing.cs:103-115): each parameter by name, then its AdamW moments. Moments
+// that ZeRO-1 keeps as one shard per rank are all-gathered into full-size tensors first, so the state has the layout
+// and values of a replicated run's.
+std::vector<std::pair<std::string, Tensor>> Trainer::state_items() {
+  configure_shards();
+  const int W = optimizer->shard_world, r = optimizer->shard_rank;
   std::vector<std::pair<std::string, Tensor>> items;
+  std::vector<Tensor> gather;
   for (const auto& kv : model->named_parameters()) {
     items.push_back(kv);
     auto it = optimizer->state.find(kv.second.get());
-    if (it != optimizer->state.end() && it->second.m && it->second.v) {
-      items.emplace_back("opt.m::" + kv.first, it->second.m);
-      items.emplace_back("opt.v::" + kv.first, it->second.v);
+    if (it == optimizer->state.end() || !it->second.m || !it->second.v) continue;
+    Tensor m = it->second.m, v = it->second.v;
+    if (optimizer->sharded(kv.second) && m->numel() * W == kv.second->numel()) {
+      Tensor fm = be_->allocate(kv.second->shape), fv = be_->allocate(kv.second->shape);
+      be_->copy(m, shard_of(fm, r, W));
+      be_->copy(v, shard_of(fv, r, W));
+      gather.push_back(fm);
+      gather.push_back(fv);
+      m = fm;
+      v = fv;
     }
+    items.emplace_back("opt.m::" + kv.first, m);
+    items.emplace_back("opt.v::" + kv.first, v);
   }
-  be_->save_checkpoint(path, step, items, metadata);
+  if (!gather.empty()) {
+    // every rank holds the same sharded parameters in the same order, so the gathers pair up across ranks
+    if (allgather) allgather(gather);
+    else be_->allgather(gather);
+    if (allreduce_wait) allreduce_wait();
+    else if (!allgather) be_->allreduce_wait();
+  }
+  return items;
+}
+
+void Trainer::save_checkpoint(const std::string& path, int step, const std::string& metadata) {
+  be_->begin_scope();  // the gathered moments are released once the library has snapshotted them
+  try {
+    auto items = state_items();
+    if (!(path.empty() && optimizer->shard_world > 1)) be_->save_checkpoint(path, step, items, metadata);
+  } catch (...) {
+    be_->end_scope();
+    throw;
+  }
+  be_->end_scope();
 }
 
 void Trainer::wait_checkpoint() { be_->wait_checkpoint(); }
 
-// Trainer.Restore (Training.cs:156-162): Checkpointing.ApplyWeights then ApplyOptimizer (Checkpointing.cs:118-142).
+// Checkpointing.ApplyWeights then ApplyOptimizer (Checkpointing.cs:118-142). Under ZeRO-1 a sharded parameter's
+// saved (full-size) moments must hold as many elements as the parameter; this rank keeps its shard of them.
+void Trainer::apply_state(const std::vector<std::pair<std::string, Tensor>>& items, int step) {
+  configure_shards();
+  const int W = optimizer->shard_world, r = optimizer->shard_rank;
+  std::map<std::string, Tensor> dict(items.begin(), items.end());
+  const auto named = model->named_parameters();
+  for (const auto& kv : named) {
+    auto it = dict.find(kv.first);
+    if (it == dict.end()) throw InvalidDataError("checkpoint is missing parameter '" + kv.first + "'.");
+    if (it->second->shape != kv.second->shape)
+      throw InvalidDataError("checkpoint parameter '" + kv.first + "' shape " + dims_str(it->second->shape) +
+                             " != model " + dims_str(kv.second->shape) + ".");
+    be_->copy(it->second, kv.second);
+  }
+  for (const auto& kv : named) {
+    auto m = dict.find("opt.m::" + kv.first), v = dict.find("opt.v::" + kv.first);
+    if (m == dict.end() || v == dict.end()) continue;
+    Tensor ms = m->second, vs = v->second;
+    if (optimizer->sharded(kv.second)) {
+      if (ms->numel() != kv.second->numel() || vs->numel() != kv.second->numel())
+        throw InvalidDataError("checkpoint moments of '" + kv.first + "' hold " + std::to_string(ms->numel()) + " / " +
+                               std::to_string(vs->numel()) + " elements, the parameter " +
+                               std::to_string(kv.second->numel()) + "; a sharded optimizer needs full-size moments.");
+      ms = shard_of(ms, r, W);
+      vs = shard_of(vs, r, W);
+    }
+    AdamW::State& s = optimizer->state[kv.second.get()];
+    if (!s.m || s.m->shape != ms->shape) {
+      s.m = be_->allocate(ms->shape);
+      be_->keep_alive(s.m);
+    }
+    if (!s.v || s.v->shape != vs->shape) {
+      s.v = be_->allocate(vs->shape);
+      be_->keep_alive(s.v);
+    }
+    be_->copy(ms, s.m);
+    be_->copy(vs, s.v);
+    s.t = step;  // every parameter is updated every step (dense LM training), as the reference assumes
+  }
+  optimizer->step_count = step;
+}
+
+// Trainer.Restore (Training.cs:156-162).
 int Trainer::restore(const std::string& path) {
   be_->wait_checkpoint();  // a save of this process still writing the file finishes first
   be_->begin_scope();
   try {
     auto ck = be_->load_checkpoint(path);
-    std::map<std::string, Tensor> dict(ck.tensors.begin(), ck.tensors.end());
-    const auto named = model->named_parameters();
-    for (const auto& kv : named) {
-      auto it = dict.find(kv.first);
-      if (it == dict.end()) throw InvalidDataError("checkpoint is missing parameter '" + kv.first + "'.");
-      if (it->second->shape != kv.second->shape)
-        throw InvalidDataError("checkpoint parameter '" + kv.first + "' shape " + dims_str(it->second->shape) +
-                               " != model " + dims_str(kv.second->shape) + ".");
-      be_->copy(it->second, kv.second);
-    }
-    for (const auto& kv : named) {
-      auto m = dict.find("opt.m::" + kv.first), v = dict.find("opt.v::" + kv.first);
-      if (m == dict.end() || v == dict.end()) continue;
-      AdamW::State& s = optimizer->state[kv.second.get()];
-      if (!s.m || s.m->shape != m->second->shape) {
-        s.m = be_->allocate(m->second->shape);
-        be_->keep_alive(s.m);
-      }
-      if (!s.v || s.v->shape != v->second->shape) {
-        s.v = be_->allocate(v->second->shape);
-        be_->keep_alive(s.v);
-      }
-      be_->copy(m->second, s.m);
-      be_->copy(v->second, s.v);
-      s.t = ck.step;  // every parameter is updated every step (dense LM training), as the reference assumes
-    }
-    optimizer->step_count = ck.step;
+    apply_state(ck.tensors, ck.step);
     be_->end_scope();
     return ck.step;
   } catch (...) {

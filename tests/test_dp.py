@@ -40,8 +40,8 @@ def full_batch():
     return np.ascontiguousarray(ids[:, :32]), np.ascontiguousarray(ids[:, 1:])
 
 
-def make_trainer(H, be, world):
-    m = H.LlamaModel(be, H.ModelConfig(**TINY), seed=0)
+def make_trainer(H, be, world, seed=0):
+    m = H.LlamaModel(be, H.ModelConfig(**TINY), seed=seed)
     tc = H.TrainingConfig(batch_size=4 // world, sequence_length=32, learning_rate=1e-3, weight_decay=0.1, max_steps=10,
                           gradient_checkpointing=True, warmup_steps=0)
     tr = H.Trainer(be, m, tc, 0.9, 0.95)
@@ -174,20 +174,9 @@ def test_nccl_two_gpus_match_full_batch(tmp_path):
         np.testing.assert_array_equal(r0["p_" + n], r1["p_" + n])
 
 
-# ---------------------------------------------------------------- ZeRO-1 (sharded AdamW state)
-def _zero1_rank(rank, world, port, out_dir):
-    """Two steps of the same data-parallel training, once with replicated AdamW (all-reduce) and once with ZeRO-1
-    (reduce-scatter, AdamW on this rank's shard, all-gather), from the same initial weights."""
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    import datetime
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
-    sys.path.insert(0, str(ROOT))
-    import __graft_entry__
-    __graft_entry__.load_package()
-    from projectai_b200 import _paihost as H
-    be = H.Backend(str(ROOT / "oracle" / "build" / "liboracle.so"), "oracle_", 0)
-
+def gloo_collectives(be, rank, world):
+    """Sum-all-reduce, in-place reduce-scatter and in-place all-gather of backend tensors over the gloo group (rank
+    r's shard of a flattened tensor is elements [r·n/W, (r+1)·n/W)), standing in for the backend's NCCL exchanges."""
     def allreduce(grads):
         for t in grads:
             host = torch.from_numpy(be.to_host(t).copy())
@@ -211,6 +200,25 @@ def _zero1_rank(rank, world, port, out_dir):
             full = torch.empty(mine.numel() * world)
             dist.all_gather_into_tensor(full, mine)
             be.copy(be.from_host(full.numpy().reshape(be.to_host(p).shape)), p)
+
+    return allreduce, reduce_scatter, allgather
+
+
+# ---------------------------------------------------------------- ZeRO-1 (sharded AdamW state)
+def _zero1_rank(rank, world, port, out_dir):
+    """Two steps of the same data-parallel training, once with replicated AdamW (all-reduce) and once with ZeRO-1
+    (reduce-scatter, AdamW on this rank's shard, all-gather), from the same initial weights."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(ROOT / "oracle" / "build" / "liboracle.so"), "oracle_", 0)
+
+    allreduce, reduce_scatter, allgather = gloo_collectives(be, rank, world)
 
     x, y = full_batch()
     per = 4 // world
@@ -248,6 +256,98 @@ def test_zero1_matches_replicated_adamw_bit_for_bit(tmp_path):
     # every parameter of the tiny model splits in two: each rank holds the moments of half of them
     assert int(r0["replicated_moments"]) == 2 * int(r0["params"])
     assert int(r0["zero1_moments"]) == int(r0["params"])
+
+
+def _zero1_state_rank(rank, world, port, out_dir):
+    """The checkpointed state of a ZeRO-1 run: its sharded moments gathered into the replicated layout, then applied
+    to fresh trainers (sharded and replicated) that continue the run."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(ROOT / "oracle" / "build" / "liboracle.so"), "oracle_", 0)
+    allreduce, reduce_scatter, allgather = gloo_collectives(be, rank, world)
+    x, y = full_batch()
+    per = 4 // world
+
+    def batch(step):
+        return ([np.roll(x, step, axis=0)[rank * per:(rank + 1) * per].copy()],
+                [np.roll(y, step, axis=0)[rank * per:(rank + 1) * per].copy()])
+
+    def trainer(zero1, seed=0):
+        m, tr = make_trainer(H, be, world, seed)
+        tr.world = world
+        tr.rank = rank
+        tr.set_allreduce(allreduce)
+        if zero1:
+            tr.zero1 = True
+            tr.set_shard_exchange(reduce_scatter, allgather)
+        return m, tr
+
+    out = {}
+    m_rep, t_rep = trainer(False)
+    m_z, t_z = trainer(True)
+    for step in range(2):
+        t_rep.step(*batch(step))
+        t_z.step(*batch(step))
+    rep_items = t_rep.state_items()
+    z_items = t_z.state_items()  # collective: both ranks gather the moment shards
+    out["rep_names"] = np.array([n for n, _ in rep_items])
+    out["z_names"] = np.array([n for n, _ in z_items])
+    out.update({"rep_" + n: be.to_host(t) for n, t in rep_items})
+    out.update({"z_" + n: be.to_host(t) for n, t in z_items})
+    out["params"] = np.array(sum(be.to_host(p).size for _, p in m_z.named_parameters()))
+    out["z_moments"] = np.array(t_z.moment_elements())
+
+    # a sharded trainer from other weights takes the gathered state and continues in step with the original
+    m_zr, t_zr = trainer(True, seed=1)
+    t_zr.apply_state(z_items, 2)
+    out["zr_moments"] = np.array(t_zr.moment_elements())
+    m_rr, t_rr = trainer(False, seed=1)  # and so does a replicated one: the file is the same for both layouts
+    t_rr.apply_state(z_items, 2)
+    for tr in (t_z, t_zr, t_rr):
+        tr.step(*batch(2))
+    for tag, m in (("z3", m_z), ("zr3", m_zr), ("rr3", m_rr)):
+        out.update({f"{tag}_p_" + n: be.to_host(p) for n, p in m.named_parameters()})
+
+    if rank == 0:  # a sharded optimizer refuses moments that are not full-size (no collective on this path)
+        bad = [(n, t.reshape([t.numel()]).slice(0, 0, 2) if n.startswith("opt.") else t) for n, t in z_items]
+        try:
+            t_zr.apply_state(bad, 2)
+            out["bad"] = np.array("no error")
+        except H.InvalidDataError as e:
+            out["bad"] = np.array(str(e))
+    np.savez(out_dir / f"zero1_state_rank{rank}.npz", **out)
+    dist.destroy_process_group()
+
+
+def test_zero1_checkpoint_state_gathers_and_restores_shards(tmp_path):
+    """save_checkpoint's state under ZeRO-1 equals the replicated run's bit for bit (the moment shards are gathered
+    into full-size tensors on every rank), and restoring it into sharded or replicated trainers continues the run
+    exactly (Checkpointing.cs:103-142 layout; Optimizers.cs:81-123 update)."""
+    port = free_port()
+    mp.spawn(_zero1_state_rank, args=(2, port, tmp_path), nprocs=2, join=True)
+    r0 = np.load(tmp_path / "zero1_state_rank0.npz")
+    r1 = np.load(tmp_path / "zero1_state_rank1.npz")
+    names = list(r0["rep_names"])
+    assert list(r0["z_names"]) == names and list(r1["z_names"]) == names
+    assert sum(n.startswith("opt.m::") for n in names) == sum(not n.startswith("opt.") for n in names)
+    for n in names:
+        for r in (r0, r1):
+            np.testing.assert_array_equal(r["z_" + n].view(np.uint32), r0["rep_" + n].view(np.uint32), n)
+    params = int(r0["params"])
+    assert int(r0["z_moments"]) == params and int(r0["zr_moments"]) == params  # shards only: half of m and v each
+    for r in (r0, r1):
+        for k in r.files:
+            if k.startswith("z3_p_"):
+                n = k[len("z3_p_"):]
+                np.testing.assert_array_equal(r["zr3_p_" + n].view(np.uint32), r[k].view(np.uint32), n)
+                np.testing.assert_array_equal(r["rr3_p_" + n].view(np.uint32), r[k].view(np.uint32), n)
+    assert "a sharded optimizer needs full-size moments" in str(r0["bad"]), str(r0["bad"])
 
 
 @pytest.mark.gpu
