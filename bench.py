@@ -161,6 +161,8 @@ def ncu_traffic():
 # Tokens per step of the bounded CPU samples (batch 1): the oracle's scalar loops take ~7 GFLOP per token of the
 # ~1B model, and its composed AdamW makes ~20 passes over the 787 M parameters whatever the token count.
 CPU_SAMPLE_SEQ = {"1b": 16, "125m": 64, "tiny": 64}
+# The single-thread sample (the reference backend's loops on one core) is shorter to stay within ~10-30 s.
+CPU_SAMPLE_SEQ_1THREAD = {"1b": 4, "125m": 16, "tiny": 64}
 
 
 def flops_per_token(c, seq):
@@ -575,6 +577,7 @@ def main():
     ap.add_argument("--cpu-sample-tokens", type=int, default=None,
                     help="tokens per CPU sample step (default: 16 for 1b, 64 for 125m and tiny)")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-cpu-1thread", action="store_true", help="leave the single-thread CPU sample out")
     ap.add_argument("--skip-extra", action="store_true", help="leave the no-recompute and 125M runs out of the N=1 line")
     ap.add_argument("--op", default=None, choices=["all", "gemm", "gemm-only", "attention", "hbm", "decode", "decode-attn",
                                                    "checkpoint"],
@@ -768,6 +771,13 @@ def main():
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "cpu": cpu_model(),
                                     "sample": f"one training step of the {args.config} model (all parameters, AdamW "
                                               f"over all of them) at batch 1 x seq {seq} ({dt:.1f} s) on the CPU oracle"}
+            if not args.skip_cpu_1thread:
+                seq1 = min(CPU_SAMPLE_SEQ_1THREAD[args.config], c["seq"])
+                v1, dt1 = cpu_train_sample(args.config, seq1, 1)
+                line["cpu_baseline_1thread"] = {
+                    "value": v1, "unit": "tokens/s", "cores": 1, "kind": "port", "cpu": cpu_model(),
+                    "sample": f"one training step of the {args.config} model at batch 1 x seq {seq1} ({dt1:.1f} s) on "
+                              f"the CPU oracle with one thread (the reference backend's loops, unparallelised)"}
     else:
         del m
     if rank == 0:
