@@ -286,14 +286,11 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 // SiLU(g)·u with the element operations of the reference's Sigmoid (sign-split, CpuComputeBackend.cs:304-317), SiLU
 // (x·sigmoid(x), :385-391) and Mul, each rounded once: shared by the SwiGLU kernel and the fused decode epilogue.
+// The two branches share one exponential, expf(-|g|) (= expf(-g) for g >= 0 and expf(g) otherwise, exactly), so a
+// warp whose elements differ in sign evaluates it once per element; the quotients are the branches' own.
 __device__ __forceinline__ float silu_mul_value(float g, float u) {
-  float s;
-  if (g >= 0.0f) {
-    s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-  } else {
-    float t = expf(g);
-    s = __fdiv_rn(t, __fadd_rn(1.0f, t));
-  }
+  const float t = expf(-fabsf(g));
+  const float s = __fdiv_rn(g >= 0.0f ? 1.0f : t, __fadd_rn(1.0f, t));
   return __fmul_rn(__fmul_rn(g, s), u);
 }
 

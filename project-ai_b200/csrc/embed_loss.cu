@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace pai {
 
@@ -169,6 +170,89 @@ __global__ void k_ce_grad_reg(const float* __restrict__ logits, const int32_t* _
   }
 }
 
+// Rows of up to NT·VPT logits whose byte length is a multiple of 16 (vocab % 4 == 0): the arithmetic of k_ce_grad_reg
+// (each thread holds the same VPT values and the reductions run in the same order, so the results are bit-identical),
+// with one CTA per SM walking its rows while the next row's logits stream into shared memory as one bulk copy. The
+// HBM read of row i+gridDim.x then overlaps the exponentials and gradient stores of row i, where the register kernel
+// (one CTA per SM: its registers hold a whole row) reads, computes and writes each row in turn. A copy that has not
+// landed within the wait limit sets the device error flag (site 81) and the CTA stops.
+template <int NT, int VPT>
+__global__ void __launch_bounds__(NT, 1)
+    k_ce_grad_stream(const float* __restrict__ logits, const int32_t* __restrict__ targets, float* __restrict__ grad,
+                     double* __restrict__ row_loss, int n, int vocab, int ignore, float inv_count, float scale,
+                     int* __restrict__ error_flag) {
+  extern __shared__ __align__(128) uint8_t ce_smem[];
+  float* row = reinterpret_cast<float*>(ce_smem);
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float smf[NT / 32];
+  __shared__ double smd[NT / 32];
+  const uint32_t bytes = (uint32_t)vocab * 4u;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if ((int)blockIdx.x < n) {
+      tc::mbar_expect_tx(&bar, bytes);
+      tc::bulk_g2s(row, logits + (int64_t)blockIdx.x * vocab, bytes, &bar);
+    }
+  }
+  __syncthreads();
+  uint32_t parity = 0;
+  for (int r = blockIdx.x; r < n; r += gridDim.x, parity ^= 1u) {
+    // every thread waits on the barrier (acquiring the copy's writes); the CTA agrees on the verdict in one barrier
+    if (!__syncthreads_and(tc::mbar_wait(&bar, parity) ? 1 : 0)) {
+      if (threadIdx.x == 0) {
+        atomicExch(error_flag, 81);
+        tc::mbar_wait(&bar, parity);  // bounded: a late copy lands before the CTA's shared memory is released
+      }
+      return;
+    }
+    const int t = targets[r];
+    float x[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; k++) {
+      int v = threadIdx.x + k * NT;
+      x[k] = v < vocab ? row[v] : -INFINITY;
+    }
+    float xt = 0.0f;
+    if (threadIdx.x == 0 && t != ignore) xt = row[t];
+    __syncthreads();  // every thread has its values: the buffer takes the next row
+    if (threadIdx.x == 0 && r + (int)gridDim.x < n) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the reads above come before the copy's writes
+      tc::mbar_expect_tx(&bar, bytes);
+      tc::bulk_g2s(row, logits + (int64_t)(r + gridDim.x) * vocab, bytes, &bar);
+    }
+    float* g = grad + (int64_t)r * vocab;
+    if (t == ignore) {
+      for (int v = threadIdx.x; v < vocab; v += NT) g[v] = 0.0f;
+      if (row_loss && threadIdx.x == 0) row_loss[r] = 0.0;
+      continue;
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < VPT; k++) m = fmaxf(m, x[k]);
+    m = block_max<NT>(m, smf);
+    float sef = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; k++) {
+      int v = threadIdx.x + k * NT;
+      x[k] = v < vocab ? expf(x[k] - m) : 0.0f;
+      sef += x[k];
+    }
+    double se = block_sum_d<NT>((double)sef, smd);
+    float inv = 1.0f / (float)se;
+#pragma unroll
+    for (int k = 0; k < VPT; k++) {
+      int v = threadIdx.x + k * NT;
+      if (v < vocab) {
+        float gv = x[k] * inv * inv_count;
+        if (v == t) gv -= inv_count;
+        g[v] = gv * scale;
+      }
+    }
+    if (row_loss && threadIdx.x == 0) row_loss[r] = ((double)m + log(se)) - (double)xt;
+  }
+}
+
 // Any vocabulary size: three passes over the row.
 template <int NT>
 __global__ void k_ce_grad_loop(const float* __restrict__ logits, const int32_t* __restrict__ targets, float* __restrict__ grad,
@@ -226,8 +310,18 @@ static pai_status launch_ce_grad(pai_ctx* ctx, const float* lp, const int32_t* d
   else if (vpt <= 4) CE_REG(1024, 4);
   else if (vpt <= 8) CE_REG(1024, 8);
   else if (vpt <= 16) CE_REG(1024, 16);
-  else if (vocab <= 32768) CE_REG(512, 64);
-  else k_ce_grad_loop<1024><<<blocks, 1024, 0, ctx->stream>>>(lp, dt, grad, row_loss, n, vocab, ignore, inv_count, scale);
+  else if (vocab <= 32768) {
+    if (vocab % 4 == 0 && (reinterpret_cast<uintptr_t>(lp) & 15) == 0) {
+      // bulk copies start on 16-byte boundaries: every row does when the base does and rows are whole float4s
+      const int smem = vocab * 4;
+      PAI_CUDA(smem_limit(ctx, k_ce_grad_stream<512, 64>, smem));
+      const int grid = n < ctx->sm_count ? n : ctx->sm_count;
+      k_ce_grad_stream<512, 64><<<grid, 512, smem, ctx->stream>>>(lp, dt, grad, row_loss, n, vocab, ignore, inv_count,
+                                                                   scale, ctx->d_error_flag);
+    } else {
+      CE_REG(512, 64);
+    }
+  } else k_ce_grad_loop<1024><<<blocks, 1024, 0, ctx->stream>>>(lp, dt, grad, row_loss, n, vocab, ignore, inv_count, scale);
 #undef CE_REG
   PAI_LAUNCH_CHECK("cross_entropy_grad");
   return PAI_OK;

@@ -184,11 +184,14 @@ def test_silu_mul(cuda, oracle):
     assert_close(du_ref, cuda.to_host(du), 1e-5, 1e-6, "silu_mul dup")
 
 
-@pytest.mark.parametrize("n,vocab", [(37, 256), (64, 32000), (9, 40000)])
+# (1000, 32000) and (300, 20000): more rows than SMs, so each CTA of the streaming kernel walks several rows with the
+# next row's copy in flight; (150, 30002): a row length that is not a whole number of 16-byte units (register kernel).
+@pytest.mark.parametrize("n,vocab", [(37, 256), (64, 32000), (9, 40000), (1000, 32000), (300, 20000), (150, 30002)])
 def test_cross_entropy_fused(cuda, oracle, n, vocab):
     logits = rnd(50, n, vocab, scale=3.0)
     targets = np.random.RandomState(51).randint(0, vocab, size=n).astype(np.int32)
     targets[3] = -100
+    targets[97::149] = -100  # ignored rows between streamed ones
     exp_loss = oracle.to_host(oracle.cross_entropy(oracle.from_host(logits), targets, -100))
     exp_grad = oracle.to_host(oracle.cross_entropy_grad(oracle.from_host(logits), targets, -100))
     loss, grad = cuda.cross_entropy_fused(cuda.from_host(logits), targets, -100, 1.0)
@@ -196,6 +199,22 @@ def test_cross_entropy_fused(cuda, oracle, n, vocab):
     assert_close(exp_grad, cuda.to_host(grad), 1e-4, 1e-7, "ce grad")
     assert_close(exp_loss, cuda.to_host(cuda.cross_entropy(cuda.from_host(logits), targets, -100)), 1e-5, 1e-6, "ce")
     assert_close(exp_grad, cuda.to_host(cuda.cross_entropy_grad(cuda.from_host(logits), targets, -100)), 1e-4, 1e-7, "ce grad")
+
+
+def test_cross_entropy_streamed_rows_equal_register_rows(cuda):
+    """Logits whose rows start on 16-byte boundaries take the streaming kernel (next row copied into shared memory
+    while the current one is reduced); the same logits one float off that boundary take the register kernel. Both
+    compute each row in the same order, so loss and gradient agree bit for bit."""
+    n, vocab = 700, 32000
+    logits = rnd(52, n, vocab, scale=3.0)
+    targets = np.random.RandomState(53).randint(0, vocab, size=n).astype(np.int32)
+    targets[5::151] = -100
+    flat = np.concatenate([np.zeros(1, np.float32), logits.reshape(-1)])
+    shifted = cabi.reshape(cabi.slice_view(cuda.from_host(flat), 0, 1, n * vocab), [n, vocab])
+    loss_a, grad_a = cuda.cross_entropy_fused(cuda.from_host(logits), targets, -100, 1.0)
+    loss_b, grad_b = cuda.cross_entropy_fused(shifted, targets, -100, 1.0)
+    assert np.array_equal(cuda.to_host(loss_a).view(np.uint32), cuda.to_host(loss_b).view(np.uint32))
+    assert np.array_equal(cuda.to_host(grad_a).view(np.uint32), cuda.to_host(grad_b).view(np.uint32))
 
 
 # ---------------------------------------------------------------- bit-exact paths
