@@ -304,6 +304,40 @@ struct FileCloser {
   FILE* f;
   ~FileCloser() { if (f) fclose(f); }
 };
+
+// Reads [pos, pos + len) of the file into buf, split into up to kLoadReaders contiguous parts read concurrently (one
+// on the calling thread): a single reader copying out of the page cache holds a load to ~2 GB/s. Returns the bytes
+// read from the start of the range up to the first short part, i.e. up to the end of the file.
+constexpr int kLoadReaders = 4;
+size_t pread_parts(int fd, char* buf, size_t len, int64_t pos) {
+  const size_t min_part = size_t(4) << 20;
+  int parts = (int)std::min<size_t>((size_t)kLoadReaders, std::max<size_t>(1, (len + min_part - 1) / min_part));
+  const size_t part = (((len + parts - 1) / parts) + 4095) & ~size_t(4095);
+  size_t got[kLoadReaders] = {};
+  auto work = [&](int i) {
+    const size_t b = (size_t)i * part, e = std::min(len, b + part);
+    size_t n = 0;
+    while (b + n < e) {
+      ssize_t r = pread(fd, buf + b + n, e - b - n, (off_t)(pos + (int64_t)(b + n)));
+      if (r < 0 && errno == EINTR) continue;
+      if (r <= 0) break;
+      n += (size_t)r;
+    }
+    got[i] = n;
+  };
+  std::thread th[kLoadReaders];
+  int started = 0;
+  for (int i = 1; i < parts && (size_t)i * part < len; i++) th[started++] = std::thread(work, i);
+  work(0);
+  for (int i = 0; i < started; i++) th[i].join();
+  size_t total = 0;
+  for (int i = 0; i < parts && (size_t)i * part < len; i++) {
+    const size_t want = std::min(len, (size_t)i * part + part) - (size_t)i * part;
+    total += got[i];
+    if (got[i] < want) break;
+  }
+  return total;
+}
 }  // namespace
 
 // Reads the file's header (and, unless header_only, every tensor onto the device, allocated in the current scope);
@@ -390,11 +424,12 @@ PAI_API pai_status pai_ckpt_load(pai_ctx* ctx, const char* path, int32_t header_
     if (cudaEventRecord(io->mark, ctx->stream) != cudaSuccess || cudaStreamWaitEvent(io->stream, io->mark, 0) != cudaSuccess)
       return fail(set_error(PAI_ERR_CUDA, "checkpoint load: stream ordering failed"));
     char* dst = static_cast<char*>(t.base);
+    const int64_t pos = (int64_t)ftello(f);  // the payload's file offset (stdio's buffered position)
     for (int64_t off = 0; off < blen; off += (int64_t)kIoChunk, chunk++) {
       const size_t len = (size_t)std::min<int64_t>((int64_t)kIoChunk, blen - off);
       char* buf = io->pinned + (chunk & 1) * kIoChunk;
       cudaEventSynchronize(io->ev[chunk & 1]);  // the copy that last read this buffer is done
-      got = rd(buf, len);
+      got = pread_parts(fileno(f), buf, len, pos + off);
       if (got != len)
         return fail(set_error(PAI_ERR_INVALID_DATA, "'%s' is truncated reading tensor '%s' payload (expected %lld bytes, got %lld).",
                               path, name.c_str(), (long long)blen, (long long)(off + (int64_t)got)));
@@ -402,6 +437,8 @@ PAI_API pai_status pai_ckpt_load(pai_ctx* ctx, const char* path, int32_t header_
           cudaEventRecord(io->ev[chunk & 1], io->stream) != cudaSuccess)
         return fail(set_error(PAI_ERR_CUDA, "checkpoint load: copy to the device failed"));
     }
+    if (blen > 0 && fseeko(f, (off_t)(pos + blen), SEEK_SET) != 0)  // stdio resumes after the payload
+      return fail(set_error(PAI_ERR_IO, "could not seek in '%s': %s", path, strerror(errno)));
     io->names.push_back(std::move(name));
     io->tensors.push_back(t);
   }
