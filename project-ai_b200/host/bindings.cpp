@@ -308,16 +308,18 @@ PYBIND11_MODULE(_paihost, m) {
       });
 
   py::class_<TrainingConfig>(m, "TrainingConfig")
-      .def(py::init([](int batch, int seq, float lr, float wd, int max_steps, int accum, bool ckpt, int warmup, uint64_t seed) {
+      .def(py::init([](int batch, int seq, float lr, float wd, int max_steps, int accum, bool ckpt, int warmup, uint64_t seed,
+                       int ckpt_every, const std::string& ckpt_dir) {
              TrainingConfig c;
              c.batch_size = batch; c.sequence_length = seq; c.learning_rate = lr; c.weight_decay = wd;
              c.max_steps = max_steps; c.grad_accum = accum; c.gradient_checkpointing = ckpt; c.warmup_steps = warmup;
-             c.seed = seed;
+             c.seed = seed; c.checkpoint_every_steps = ckpt_every; c.checkpoint_directory = ckpt_dir;
              return c;
            }),
            py::arg("batch_size") = 8, py::arg("sequence_length") = 512, py::arg("learning_rate") = 3e-4f,
            py::arg("weight_decay") = 0.01f, py::arg("max_steps") = 1000, py::arg("grad_accum") = 1,
-           py::arg("gradient_checkpointing") = false, py::arg("warmup_steps") = 100, py::arg("seed") = 0);
+           py::arg("gradient_checkpointing") = false, py::arg("warmup_steps") = 100, py::arg("seed") = 0,
+           py::arg("checkpoint_every_steps") = 0, py::arg("checkpoint_directory") = "checkpoints");
 
   py::class_<PyTrainer>(m, "Trainer")
       .def(py::init([](std::shared_ptr<NativeBackend> be, std::shared_ptr<PyModel> model, const TrainingConfig& cfg,
@@ -352,6 +354,38 @@ PYBIND11_MODULE(_paihost, m) {
         py::gil_scoped_release nogil;
         return t.trainer->restore(path);
       })
+      // Trainer.Train over host sequences (lists of int ids) or, with packed_blocks > 0, the backend's open packed
+      // dataset; on_step(step, loss) is called with the GIL held. Returns the TrainingReport as a dict.
+      .def("train", [](PyTrainer& t, py::object sequences, int64_t packed_blocks, py::object on_step) {
+        std::unique_ptr<SequenceSource> src;
+        if (packed_blocks > 0) {
+          auto p = std::make_unique<PackedSequences>();
+          p->blocks = packed_blocks;
+          src = std::move(p);
+        } else {
+          auto h = std::make_unique<HostSequences>();
+          if (!sequences.is_none())
+            for (auto seq : sequences) h->seqs.push_back(seq.cast<std::vector<int32_t>>());
+          src = std::move(h);
+        }
+        std::function<void(int, float)> cb;
+        if (!on_step.is_none())
+          cb = [on_step](int step, float loss) {
+            py::gil_scoped_acquire gil;
+            on_step(step, loss);
+          };
+        TrainingReport r;
+        {
+          py::gil_scoped_release nogil;
+          r = t.trainer->train(*src, cb);
+        }
+        py::dict d;
+        d["step_losses"] = r.step_losses;
+        d["final_step"] = r.final_step;
+        d["first_loss"] = r.step_losses.empty() ? NAN : r.step_losses.front();
+        d["last_loss"] = r.step_losses.empty() ? NAN : r.step_losses.back();
+        return d;
+      }, py::arg("sequences") = py::none(), py::arg("packed_blocks") = 0, py::arg("on_step") = py::none())
       // (name, tensor) pairs of the checkpointed state with full-size moments; collective under ZeRO-1
       .def("state_items", [](PyTrainer& t) {
         py::gil_scoped_release nogil;

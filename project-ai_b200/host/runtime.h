@@ -516,6 +516,40 @@ struct TrainingConfig {
   bool gradient_checkpointing = false;
   int warmup_steps = 100;
   uint64_t seed = 0;
+  // Trainer::train writes "<checkpoint_directory>/step-<n>.ckpt" every checkpoint_every_steps steps (0: only the
+  // final one) and after the last step; an empty directory writes none (TrainingConfig, Training.cs:8-26).
+  int checkpoint_every_steps = 0;
+  std::string checkpoint_directory = "checkpoints";
+};
+
+// A source of training sequences for Trainer::train (IDataset, Training.cs:29-33): count() sequences, and NextBatch's
+// [rows, seq] input and target id tensors for the drawn row indices (inputs ids[:, :seq], targets ids[:, 1:seq+1]).
+struct SequenceSource {
+  virtual ~SequenceSource() = default;
+  virtual int64_t count() const = 0;
+  virtual std::pair<Tensor, Tensor> batch(NativeBackend* be, const std::vector<int64_t>& rows, int seq) = 0;
+};
+
+// Sequences held on the host (int token ids), uploaded per batch as NextBatch does (Training.cs:122-141), with its
+// length check.
+struct HostSequences : SequenceSource {
+  std::vector<std::vector<int32_t>> seqs;
+  int64_t count() const override { return (int64_t)seqs.size(); }
+  std::pair<Tensor, Tensor> batch(NativeBackend* be, const std::vector<int64_t>& rows, int seq) override;
+};
+
+// The packed dataset the backend has open (NativeBackend::dataset_open, PackedBinDataset.cs): blocks gathered at
+// their on-disk width and widened to F32 ids on the device.
+struct PackedSequences : SequenceSource {
+  int64_t blocks = 0;
+  int64_t count() const override { return blocks; }
+  std::pair<Tensor, Tensor> batch(NativeBackend* be, const std::vector<int64_t>& rows, int seq) override;
+};
+
+// Per-step mean losses and the final step of a run (TrainingReport, Training.cs:36-41).
+struct TrainingReport {
+  std::vector<float> step_losses;
+  int final_step = 0;
 };
 
 std::function<float(int)> warmup_cosine(const TrainingConfig& cfg);
@@ -545,6 +579,12 @@ class Trainer {
   // belong to the caller's scope), and the part of restore that applies such a state and step count.
   std::vector<std::pair<std::string, Tensor>> state_items();
   void apply_state(const std::vector<std::pair<std::string, Tensor>>& items, int step);
+  // Trainer.Train (Training.cs:59-120): max_steps steps of grad_accum micro-batches, each drawn by NextBatch's rule
+  // (row = PcgRng(seed).NextUInt32() % count per batch row), the warmup+cosine schedule, a checkpoint every
+  // checkpoint_every_steps steps and after the last one; on_step(step, loss) after each step. Returns once the last
+  // checkpoint file is complete. Under data parallelism rank r draws from PCG stream (default + r) of the same seed
+  // (rank 0: the reference's sequence), and rank 0 writes the files (every rank joins the gather under ZeRO-1).
+  TrainingReport train(SequenceSource& data, const std::function<void(int, float)>& on_step = nullptr);
   LlamaModel* model;
   TrainingConfig cfg;
   std::unique_ptr<AdamW> optimizer;

@@ -4,6 +4,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdlib>
+#include <filesystem>
 #include <memory>
 
 #include "runtime.h"
@@ -506,6 +507,73 @@ void Trainer::apply_state(const std::vector<std::pair<std::string, Tensor>>& ite
     s.t = step;  // every parameter is updated every step (dense LM training), as the reference assumes
   }
   optimizer->step_count = step;
+}
+
+// NextBatch (Training.cs:122-141) over host sequences: each drawn row's first seq + 1 ids.
+std::pair<Tensor, Tensor> HostSequences::batch(NativeBackend* be, const std::vector<int64_t>& rows, int seq) {
+  const int b = (int)rows.size();
+  std::vector<float> in((size_t)b * seq), tg((size_t)b * seq);
+  for (int r = 0; r < b; r++) {
+    const auto& s = seqs.at((size_t)rows[(size_t)r]);
+    if ((int64_t)s.size() < (int64_t)seq + 1)
+      throw InvalidOperationError("dataset sequence " + std::to_string(rows[(size_t)r]) + " has length " +
+                                  std::to_string(s.size()) + "; need " + std::to_string(seq + 1) +
+                                  " for sequence length " + std::to_string(seq) + ".");
+    for (int t = 0; t < seq; t++) {
+      in[(size_t)r * seq + t] = (float)s[(size_t)t];
+      tg[(size_t)r * seq + t] = (float)s[(size_t)t + 1];
+    }
+  }
+  return {be->from_host(in.data(), (int64_t)in.size(), {b, seq}), be->from_host(tg.data(), (int64_t)tg.size(), {b, seq})};
+}
+
+std::pair<Tensor, Tensor> PackedSequences::batch(NativeBackend* be, const std::vector<int64_t>& rows, int seq) {
+  auto b = be->dataset_batch(rows);
+  if (b.first->rank() != 2 || b.first->shape[1] != seq)
+    throw InvalidOperationError("the open dataset holds sequences of length " +
+                                std::to_string(b.first->rank() == 2 ? b.first->shape[1] : -1) +
+                                "; the training sequence length is " + std::to_string(seq) + ".");
+  return b;
+}
+
+TrainingReport Trainer::train(SequenceSource& data, const std::function<void(int, float)>& on_step) {
+  if (data.count() == 0) throw ArgumentError("dataset is empty. (Parameter 'dataset')");
+  const int ranks = configure_shards();
+  const int my_rank = rank >= 0 ? rank : be_->dp_rank;
+  const bool writer = my_rank == 0, gather = ranks > 1 && zero1;
+  const std::string& dir = cfg.checkpoint_directory;
+  if (!dir.empty() && writer) std::filesystem::create_directories(dir);
+  auto save = [&](int step) {
+    if (dir.empty()) return;
+    const std::string path = (std::filesystem::path(dir) / ("step-" + std::to_string(step) + ".ckpt")).string();
+    if (gather) save_checkpoint(writer ? path : std::string(), step);  // collective: every rank gathers its shards
+    else if (writer) save_checkpoint(path, step);
+  };
+  PcgRng rng = my_rank > 0 ? PcgRng(cfg.seed, 0xDA3E39CB94B95BDBull + (uint64_t)my_rank) : PcgRng(cfg.seed);
+  const int micro = std::max(1, cfg.grad_accum);
+  const uint32_t n = (uint32_t)data.count();
+  TrainingReport report;
+  report.step_losses.reserve((size_t)std::max(0, cfg.max_steps));
+  for (int step = 1; step <= cfg.max_steps; step++) {
+    // The reference draws each micro-batch after the previous one's backward; the draws depend on the generator
+    // alone, so drawing the step's micro-batches first gives the same rows in the same order.
+    std::vector<Tensor> in, tg;
+    for (int m = 0; m < micro; m++) {
+      std::vector<int64_t> rows((size_t)cfg.batch_size);
+      for (auto& r : rows) r = (int64_t)(rng.next_u32() % n);
+      auto b = data.batch(be_, rows, cfg.sequence_length);
+      in.push_back(b.first);
+      tg.push_back(b.second);
+    }
+    const float loss = step_tensors(in, tg);
+    report.step_losses.push_back(loss);
+    if (on_step) on_step(step, loss);
+    if (cfg.checkpoint_every_steps > 0 && step % cfg.checkpoint_every_steps == 0) save(step);
+  }
+  save(cfg.max_steps);  // the final checkpoint
+  if (!dir.empty()) wait_checkpoint();
+  report.final_step = cfg.max_steps;
+  return report;
 }
 
 // Trainer.Restore (Training.cs:156-162).

@@ -255,3 +255,52 @@ def test_trainer_checkpoint_resume_and_dataset_batches(tmp_path):
     F.save_checkpoint(bad, 1, [(n, saved[n]) for n in names[1:]])
     with pytest.raises(H.InvalidDataError, match="is missing parameter"):
         t2.restore(str(bad))
+
+
+@pytest.mark.gpu
+def test_train_loop_over_a_packed_dataset_writes_periodic_and_final_checkpoints(tmp_path):
+    """Trainer.Train end to end on the CUDA library (Training.cs:59-120): batches drawn by NextBatch's rule from the
+    open packed dataset, a checkpoint every 2 steps and a final one, named step-<n>.ckpt in the checkpoint directory.
+    The final file holds the trained weights and moments exactly, and the step-2 file restores a trainer that then
+    reproduces step 3's loss."""
+    import projectai_b200 as pai
+    from projectai_b200 import _paihost as H
+
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", 0)
+    cfg = dict(vocab_size=256, embedding_dim=128, layer_count=2, head_count=4, kv_head_count=2, ffn_hidden=344,
+               max_sequence_length=64)
+    seq = 32
+    ids = np.random.RandomState(13).randint(0, 256, size=10 * (seq + 1))
+    F.pack_dataset(ids, 256, seq, tmp_path / "ds")
+    man, shard = F.read_manifest(tmp_path / "ds")
+    be.dataset_open(str(shard), man["Dtype"], seq, man["BlockCount"])
+    ckdir = tmp_path / "ck"
+
+    def trainer(seed, steps):
+        m = H.LlamaModel(be, H.ModelConfig(**cfg), seed=seed)
+        tc = H.TrainingConfig(batch_size=2, sequence_length=seq, learning_rate=1e-3, weight_decay=0.1, max_steps=steps,
+                              grad_accum=2, gradient_checkpointing=True, warmup_steps=1, seed=9,
+                              checkpoint_every_steps=2, checkpoint_directory=str(ckdir))
+        return m, H.Trainer(be, m, tc, 0.9, 0.95)
+
+    m1, t1 = trainer(0, 3)
+    report = t1.train(packed_blocks=man["BlockCount"])
+    assert report["final_step"] == 3 and len(report["step_losses"]) == 3
+    assert sorted(p.name for p in ckdir.iterdir()) == ["step-2.ckpt", "step-3.ckpt"]
+    step, _, saved = F.load_checkpoint(ckdir / "step-3.ckpt")
+    saved = dict(saved)
+    assert step == 3
+    for n, p in m1.named_parameters():
+        assert np.array_equal(saved[n], be.to_host(p)), n
+        assert f"opt.m::{n}" in saved and f"opt.v::{n}" in saved
+
+    # resume from step 2: the rows of step 3 are the generator's draws after two steps of 2 x 2 rows
+    m2, t2 = trainer(1, 3)
+    assert t2.restore(str(ckdir / "step-2.ckpt")) == 2
+    rng = H.PcgRng(9)
+    for _ in range(2 * 2 * 2):
+        rng.next_u32()
+    batches = [be.dataset_batch([rng.next_u32() % man["BlockCount"] for _ in range(2)]) for _ in range(2)]
+    l3 = t2.step_tensors([b[0] for b in batches], [b[1] for b in batches])
+    assert abs(l3 - report["step_losses"][2]) <= 1e-6 * abs(l3), (l3, report["step_losses"][2])
+    be.dataset_close()

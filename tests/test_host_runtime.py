@@ -342,3 +342,55 @@ def test_scopes_release_intermediates(be):
     np.testing.assert_array_equal(be.to_host(y), np.full(1000, 2, np.float32))
     del y
     assert be.memory_stats()[0] == before
+
+
+# ---------------------------------------------------------------- Trainer.Train (Training.cs:59-141)
+def test_train_loop_draws_batches_like_next_batch_and_matches_manual_steps(be):
+    """Trainer.train over host sequences: every step draws grad_accum micro-batches of batch_size rows with
+    row = PcgRng(seed).NextUInt32() % count (NextBatch, Training.cs:122-141), inputs ids[:seq] and targets ids[1:seq+1],
+    under the warmup+cosine schedule. The same draws fed to Trainer.step by hand give the same losses and weights, bit
+    for bit; on_step sees each (step, loss); the report holds the per-step losses and the final step."""
+    seq, batch, accum, steps = 8, 2, 2, 3
+    data_rng = np.random.RandomState(3)
+    seqs = [list(data_rng.randint(0, 259, size=seq + 1 + (i % 3))) for i in range(7)]
+
+    def make():
+        m = H.LlamaModel(be, small_config(vocab_size=259, layer_count=2), seed=5)
+        tc = H.TrainingConfig(batch_size=batch, sequence_length=seq, learning_rate=1e-3, weight_decay=0.1, max_steps=steps,
+                              grad_accum=accum, gradient_checkpointing=True, warmup_steps=1, seed=42,
+                              checkpoint_directory="")
+        return m, H.Trainer(be, m, tc, 0.9, 0.95)
+
+    m1, t1 = make()
+    seen = []
+    report = t1.train([[int(v) for v in s] for s in seqs], on_step=lambda step, loss: seen.append((step, loss)))
+
+    m2, t2 = make()
+    rng = H.PcgRng(42)
+    manual = []
+    for _ in range(steps):
+        ins, tgs = [], []
+        for _ in range(accum):
+            rows = [rng.next_u32() % len(seqs) for _ in range(batch)]
+            ins.append(np.array([seqs[r][:seq] for r in rows], np.float32))
+            tgs.append(np.array([seqs[r][1:seq + 1] for r in rows], np.float32))
+        manual.append(t2.step(ins, tgs))
+    assert report["final_step"] == steps
+    assert np.array_equal(np.array(report["step_losses"], np.float32), np.array(manual, np.float32))
+    assert seen == [(i + 1, l) for i, l in enumerate(report["step_losses"])]
+    assert report["first_loss"] == report["step_losses"][0] and report["last_loss"] == report["step_losses"][-1]
+    w2 = dict((n, be.to_host(p)) for n, p in m2.named_parameters())
+    for n, p in m1.named_parameters():
+        assert np.array_equal(be.to_host(p).view(np.uint32), w2[n].view(np.uint32)), n
+
+
+def test_train_loop_rejects_empty_and_short_datasets(be):
+    """Training.cs:66 (empty dataset: ArgumentException) and :131-133 (a drawn sequence shorter than seq + 1:
+    InvalidOperationException with the reference's message)."""
+    m = H.LlamaModel(be, small_config(vocab_size=259, layer_count=1), seed=1)
+    tc = H.TrainingConfig(batch_size=1, sequence_length=8, max_steps=1, checkpoint_directory="")
+    tr = H.Trainer(be, m, tc)
+    with pytest.raises(H.ArgumentError, match="dataset is empty"):
+        tr.train([])
+    with pytest.raises(H.InvalidOperationError, match=r"dataset sequence 0 has length 5; need 9 for sequence length 8\."):
+        tr.train([[1, 2, 3, 4, 5]])
