@@ -231,6 +231,7 @@ PYBIND11_MODULE(_paihost, m) {
       .def_readonly("layer_count", &ModelConfig::layer_count).def_readonly("head_count", &ModelConfig::head_count)
       .def_readonly("kv_head_count", &ModelConfig::kv_head_count).def_readonly("ffn_hidden", &ModelConfig::ffn_hidden)
       .def_readonly("max_sequence_length", &ModelConfig::max_sequence_length)
+      .def_readonly("rope_theta", &ModelConfig::rope_theta).def_readonly("norm_eps", &ModelConfig::norm_eps)
       .def_property_readonly("head_dim", &ModelConfig::head_dim);
 
   py::class_<PyModel, std::shared_ptr<PyModel>>(m, "LlamaModel")
@@ -431,6 +432,12 @@ PYBIND11_MODULE(_paihost, m) {
           if (kv.second.m) n += kv.second.m->numel() + kv.second.v->numel();
         return n;
       });
+
+  m.def("apply_weights", [](std::shared_ptr<NativeBackend> be, std::shared_ptr<PyModel> model,
+                            const std::vector<std::pair<std::string, Tensor>>& items) {
+    py::gil_scoped_release nogil;
+    apply_weights(be.get(), model->model.get(), items);
+  }, py::arg("backend"), py::arg("model"), py::arg("items"));
 
   py::class_<TopKTopPSampler>(m, "TopKTopPSampler")
       .def(py::init<uint64_t, float, int, float>(), py::arg("seed"), py::arg("temperature") = 1.0f, py::arg("top_k") = 0,

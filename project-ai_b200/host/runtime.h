@@ -546,6 +546,10 @@ struct PackedSequences : SequenceSource {
   std::pair<Tensor, Tensor> batch(NativeBackend* be, const std::vector<int64_t>& rows, int seq) override;
 };
 
+// Checkpointing.ApplyWeights (Checkpointing.cs:128-137): copies each saved weight into the model parameter of the same
+// name, raising InvalidDataError for a missing parameter or a shape mismatch.
+void apply_weights(NativeBackend* be, LlamaModel* model, const std::vector<std::pair<std::string, Tensor>>& items);
+
 // Per-step mean losses and the final step of a run (TrainingReport, Training.cs:36-41).
 struct TrainingReport {
   std::vector<float> step_losses;

@@ -468,19 +468,24 @@ void Trainer::wait_checkpoint() { be_->wait_checkpoint(); }
 
 // Checkpointing.ApplyWeights then ApplyOptimizer (Checkpointing.cs:118-142). Under ZeRO-1 a sharded parameter's
 // saved (full-size) moments must hold as many elements as the parameter; this rank keeps its shard of them.
-void Trainer::apply_state(const std::vector<std::pair<std::string, Tensor>>& items, int step) {
-  configure_shards();
-  const int W = optimizer->shard_world, r = optimizer->shard_rank;
+void apply_weights(NativeBackend* be, LlamaModel* model, const std::vector<std::pair<std::string, Tensor>>& items) {
   std::map<std::string, Tensor> dict(items.begin(), items.end());
-  const auto named = model->named_parameters();
-  for (const auto& kv : named) {
+  for (const auto& kv : model->named_parameters()) {
     auto it = dict.find(kv.first);
     if (it == dict.end()) throw InvalidDataError("checkpoint is missing parameter '" + kv.first + "'.");
     if (it->second->shape != kv.second->shape)
       throw InvalidDataError("checkpoint parameter '" + kv.first + "' shape " + dims_str(it->second->shape) +
                              " != model " + dims_str(kv.second->shape) + ".");
-    be_->copy(it->second, kv.second);
+    be->copy(it->second, kv.second);
   }
+}
+
+void Trainer::apply_state(const std::vector<std::pair<std::string, Tensor>>& items, int step) {
+  configure_shards();
+  const int W = optimizer->shard_world, r = optimizer->shard_rank;
+  std::map<std::string, Tensor> dict(items.begin(), items.end());
+  const auto named = model->named_parameters();
+  apply_weights(be_, model, items);
   for (const auto& kv : named) {
     auto m = dict.find("opt.m::" + kv.first), v = dict.find("opt.v::" + kv.first);
     if (m == dict.end() || v == dict.end()) continue;

@@ -10,6 +10,7 @@ for the same tensors (views, a scalar, a payload spanning several staging chunks
 later device writes do not reach the file, a load reproduces the oracle's tensors and raises the reference's errors on
 damaged files, and a dataset batch equals Trainer.NextBatch (Training.cs:122-141) bit for bit.
 """
+import json
 import struct
 import sys
 
@@ -304,3 +305,105 @@ def test_train_loop_over_a_packed_dataset_writes_periodic_and_final_checkpoints(
     l3 = t2.step_tensors([b[0] for b in batches], [b[1] for b in batches])
     assert abs(l3 - report["step_losses"][2]) <= 1e-6 * abs(l3), (l3, report["step_losses"][2])
     be.dataset_close()
+
+
+# ---------------------------------------------------------------- self-describing model checkpoints (Checkpointing.cs)
+def _meta_json(cfg_over=None, kind="bpe", dtype=0, tokenizer='{"merges":[]}'):
+    cfg = {"VocabSize": 256, "EmbeddingDim": 128, "LayerCount": 2, "HeadCount": 4, "KvHeadCount": 2,
+           "FeedForwardHiddenDim": 344, "MaxSequenceLength": 64, "RopeTheta": 10000, "NormEpsilon": 1E-05, "HeadDim": 32}
+    cfg.update(cfg_over or {})
+    d = {"Config": cfg, "Tokenizer": tokenizer, "ComputeDType": dtype}
+    if kind is not None:
+        d["TokenizerKind"] = kind
+    return json.dumps(d)
+
+
+def test_model_metadata_round_trip_and_peek_info(tmp_path):
+    """The metadata record of Checkpointing.SaveModel (Checkpointing.cs:19, 22-36): ModelConfig under its C# property
+    names in declaration order (HeadDim, computed, last), read back by PeekInfo from the header alone."""
+    from projectai_b200 import _paihost as H
+    from projectai_b200 import checkpointing as C
+
+    cfg = H.ModelConfig(vocab_size=256, embedding_dim=128, layer_count=2, head_count=4, kv_head_count=2, ffn_hidden=344,
+                        max_sequence_length=64, rope_theta=500000.0, norm_eps=1e-6)
+    j = C.config_to_json(cfg)
+    assert list(j) == ["VocabSize", "EmbeddingDim", "LayerCount", "HeadCount", "KvHeadCount", "FeedForwardHiddenDim",
+                       "MaxSequenceLength", "RopeTheta", "NormEpsilon", "HeadDim"]
+    back = C.config_from_json(json.loads(json.dumps(j)))
+    for a in ("vocab_size", "embedding_dim", "layer_count", "head_count", "kv_head_count", "ffn_hidden",
+              "max_sequence_length", "rope_theta", "norm_eps", "head_dim"):
+        assert getattr(back, a) == getattr(cfg, a), a
+
+    p = tmp_path / "m.ckpt"
+    F.save_checkpoint(p, 12, [("w", np.ones(3, np.float32))], _meta_json(kind="hf"))
+    info = C.peek_info(p)
+    assert (info.step, info.tokenizer_kind, info.compute_dtype) == (12, "hf", "F32")
+    assert (info.config.embedding_dim, info.config.kv_head_count, info.config.head_dim) == (128, 2, 32)
+    F.save_checkpoint(p, 3, [], _meta_json(kind=None, dtype=2))  # a file from before the kind tag: BPE
+    info = C.peek_info(p)
+    assert (info.tokenizer_kind, info.compute_dtype) == ("bpe", "BF16")
+    assert C.read_metadata(p)[0] == 3
+
+
+def test_model_load_refuses_what_the_reference_refuses(tmp_path):
+    """LoadModel's checks (Checkpointing.cs:45-62) fire before any weight is read: a resume-only checkpoint (no
+    metadata), unreadable metadata, an unknown tokenizer kind, an invalid config (ModelConfig.Validate), and, here, a
+    model stored at another precision; the header checks are the reader's."""
+    from projectai_b200 import _paihost as H
+    from projectai_b200 import checkpointing as C
+
+    p = tmp_path / "r.ckpt"
+    F.save_checkpoint(p, 5, [("w", np.ones(3, np.float32))])
+    with pytest.raises(H.InvalidDataError, match="has no model metadata; it cannot be loaded for inference"):
+        C.load_model(None, p)
+    with pytest.raises(H.InvalidDataError, match="has no model metadata; it cannot be described"):
+        C.peek_info(p)
+    F.save_checkpoint(p, 5, [], "{not json")
+    with pytest.raises(H.InvalidDataError, match="unreadable model metadata"):
+        C.load_model(None, p)
+    F.save_checkpoint(p, 5, [], _meta_json(kind="sentencepiece"))
+    with pytest.raises(H.InvalidDataError, match="unknown tokenizer kind 'sentencepiece'"):
+        C.load_model(None, p)
+    F.save_checkpoint(p, 5, [], _meta_json({"HeadCount": 3}))
+    with pytest.raises(H.ArgumentError, match="must be divisible by"):
+        C.load_model(None, p)
+    F.save_checkpoint(p, 5, [], _meta_json(dtype=1))
+    with pytest.raises(H.ArgumentError, match="F16 model"):
+        C.load_model(None, p)
+    p.write_bytes(b"NOTACKPT" + bytes(8))
+    with pytest.raises(H.InvalidDataError, match=r"is not a ProjectAI checkpoint \(bad magic\)"):
+        C.read_metadata(p)
+    p.write_bytes(b"PAICKPT2" + struct.pack("<ii", 1, 40) + b"{}")
+    with pytest.raises(H.InvalidDataError, match=r"truncated reading metadata \(expected 40 bytes, got 2\)"):
+        C.read_metadata(p)
+
+
+@pytest.mark.gpu
+def test_save_model_then_load_model_rebuilds_the_trained_model(tmp_path):
+    """SaveModel with the trainer's moments, then LoadModel into a model built from the stored config: the weights
+    are the trained ones exactly and the logits match; the file carries the moments and the reference's metadata."""
+    import projectai_b200 as pai
+    from projectai_b200 import _paihost as H
+    from projectai_b200 import checkpointing as C
+
+    be = H.Backend(str(pai.CUDA_LIB_PATH), "pai_", 0)
+    cfg = H.ModelConfig(vocab_size=256, embedding_dim=128, layer_count=2, head_count=4, kv_head_count=2, ffn_hidden=344,
+                        max_sequence_length=64)
+    m = H.LlamaModel(be, cfg, seed=3)
+    tr = H.Trainer(be, m, H.TrainingConfig(batch_size=2, sequence_length=16, learning_rate=1e-3, max_steps=4,
+                                           warmup_steps=0, checkpoint_directory=""), 0.9, 0.95)
+    ids = np.random.RandomState(4).randint(0, 256, size=(2, 17)).astype(np.float32)
+    tr.step([ids[:, :16].copy()], [ids[:, 1:].copy()])
+    p = tmp_path / "model.ckpt"
+    C.save_model(be, p, m, cfg, "bpe", '{"vocab":{}}', 1, trainer=tr)
+
+    step, meta, saved = F.load_checkpoint(p)
+    assert step == 1 and json.loads(meta)["Config"]["FeedForwardHiddenDim"] == 344
+    assert any(n.startswith("opt.m::") for n, _ in saved)
+    m2, cfg2, kind, tok, step2 = C.load_model(be, p)
+    assert (kind, tok, step2, cfg2.layer_count) == ("bpe", '{"vocab":{}}', 1, 2)
+    w = dict((n, be.to_host(t)) for n, t in m.named_parameters())
+    for n, t in m2.named_parameters():
+        assert np.array_equal(be.to_host(t), w[n]), n
+    x = be.from_host(ids[:, :16].copy())
+    assert np.array_equal(be.to_host(m.forward(x)), be.to_host(m2.forward(x)))
