@@ -350,6 +350,71 @@ def test_zero1_checkpoint_state_gathers_and_restores_shards(tmp_path):
     assert "a sharded optimizer needs full-size moments" in str(r0["bad"]), str(r0["bad"])
 
 
+def _train_loop_rank(rank, world, port, out_dir):
+    """Trainer.train under data parallelism with ZeRO-1: rank r draws its rows from PCG stream (default + r) of the
+    configured seed; the same draws stepped by hand give the same losses and weights."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(ROOT / "oracle" / "build" / "liboracle.so"), "oracle_", 0)
+    allreduce, reduce_scatter, allgather = gloo_collectives(be, rank, world)
+    data = np.random.RandomState(21).randint(0, 256, size=(9, 40))
+    seqs = [[int(v) for v in row] for row in data]
+
+    def trainer():
+        m = H.LlamaModel(be, H.ModelConfig(**TINY), seed=0)
+        tc = H.TrainingConfig(batch_size=2, sequence_length=32, learning_rate=1e-3, weight_decay=0.1, max_steps=2,
+                              grad_accum=1, gradient_checkpointing=True, warmup_steps=0, seed=77,
+                              checkpoint_directory="")
+        tr = H.Trainer(be, m, tc, 0.9, 0.95)
+        tr.world = world
+        tr.rank = rank
+        tr.zero1 = True
+        tr.set_allreduce(allreduce)
+        tr.set_shard_exchange(reduce_scatter, allgather)
+        return m, tr
+
+    m1, t1 = trainer()
+    report = t1.train(seqs)
+    m2, t2 = trainer()
+    stream = 0xDA3E39CB94B95BDB + rank if rank else 0xDA3E39CB94B95BDB
+    rng = H.PcgRng(77, stream)
+    manual, rows_seen = [], []
+    for _ in range(2):
+        rows = [rng.next_u32() % len(seqs) for _ in range(2)]
+        rows_seen.append(rows)
+        x = np.array([seqs[r][:32] for r in rows], np.float32)
+        y = np.array([seqs[r][1:33] for r in rows], np.float32)
+        manual.append(t2.step([x], [y]))
+    np.savez(out_dir / f"train_rank{rank}.npz", losses=np.array(report["step_losses"], np.float32),
+             manual=np.array(manual, np.float32), rows=np.array(rows_seen),
+             **{"p_" + n: be.to_host(p) for n, p in m1.named_parameters()},
+             **{"q_" + n: be.to_host(p) for n, p in m2.named_parameters()})
+    dist.destroy_process_group()
+
+
+def test_train_loop_data_parallel_draws_per_rank_streams(tmp_path):
+    """Under data parallelism each rank's Trainer.train draws its own rows (rank 0 the reference's PcgRng(seed)
+    sequence, rank r stream default + r), the ZeRO-1 exchanges run inside the loop, and every rank ends with the
+    weights a hand-driven run of the same draws reaches."""
+    port = free_port()
+    mp.spawn(_train_loop_rank, args=(2, port, tmp_path), nprocs=2, join=True)
+    r0 = np.load(tmp_path / "train_rank0.npz")
+    r1 = np.load(tmp_path / "train_rank1.npz")
+    assert not np.array_equal(r0["rows"], r1["rows"])  # the ranks see different rows
+    for r in (r0, r1):
+        assert np.array_equal(r["losses"], r["manual"])
+        for k in r.files:
+            if k.startswith("p_"):
+                np.testing.assert_array_equal(r[k].view(np.uint32), r["q_" + k[2:]].view(np.uint32), k)
+                np.testing.assert_array_equal(r[k].view(np.uint32), r0[k].view(np.uint32), k)  # replicas agree
+
+
 @pytest.mark.gpu
 def test_nccl_zero1_two_gpus_matches_replicated(tmp_path):
     """ZeRO-1 over NCCL (in-place reduce-scatter, AdamW on the shard, in-place all-gather) gives the replicated
