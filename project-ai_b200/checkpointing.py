@@ -63,7 +63,7 @@ def read_metadata(path) -> tuple[int, str]:
         meta = f.read(mlen)
         if len(meta) != mlen:
             raise H.InvalidDataError(f"'{p}' is truncated reading metadata (expected {mlen} bytes, got {len(meta)}).")
-    return step, meta.decode("utf-8")
+    return step, meta.decode("utf-8", errors="replace")  # as Encoding.UTF8.GetString: invalid bytes become U+FFFD
 
 
 def _meta(path, what: str) -> dict:
@@ -77,6 +77,20 @@ def _meta(path, what: str) -> dict:
     if not isinstance(meta, dict):
         raise H.InvalidDataError(f"checkpoint '{path}' has unreadable model metadata.")
     return meta
+
+
+def _dtype(meta: dict, path) -> int:
+    """ComputeDType as System.Text.Json writes the enum (a number), or by name; absent means F32."""
+    v = meta.get("ComputeDType", F32)
+    if isinstance(v, str) and v in _DTYPES:
+        return _DTYPES.index(v)
+    if isinstance(v, int) and not isinstance(v, bool):
+        return v
+    raise H.InvalidDataError(f"checkpoint '{path}' has an unreadable ComputeDType ({v!r}).")
+
+
+def _dtype_name(dt: int) -> str:
+    return _DTYPES[dt] if 0 <= dt < len(_DTYPES) else str(dt)
 
 
 @dataclass
@@ -94,9 +108,7 @@ def peek_info(path) -> CheckpointInfo:
     meta = _meta(path, "described")
     step, _ = read_metadata(path)
     kind = meta.get("TokenizerKind") or "bpe"
-    dt = int(meta.get("ComputeDType", F32))
-    return CheckpointInfo(config_from_json(meta.get("Config") or {}), kind,
-                          _DTYPES[dt] if 0 <= dt < len(_DTYPES) else str(dt), step)
+    return CheckpointInfo(config_from_json(meta.get("Config") or {}), kind, _dtype_name(_dtype(meta, path)), step)
 
 
 def save_model(backend, path, model, config, tokenizer_kind: str, tokenizer_state: str, step: int, trainer=None):
@@ -120,10 +132,9 @@ def load_model(backend, path):
     allocated without the initial draws, every one overwritten from the file; a missing or misshapen parameter raises
     ``InvalidDataError``) and returns ``(model, config, tokenizer_kind, tokenizer_state, step)``."""
     meta = _meta(path, "loaded for inference")
-    dt = int(meta.get("ComputeDType", F32))
+    dt = _dtype(meta, path)
     if dt != F32:
-        name = _DTYPES[dt] if 0 <= dt < len(_DTYPES) else str(dt)
-        raise H.ArgumentError(f"checkpoint '{path}' holds a {name} model; this backend computes in F32.")
+        raise H.ArgumentError(f"checkpoint '{path}' holds a {_dtype_name(dt)} model; this backend computes in F32.")
     kind = meta.get("TokenizerKind") or "bpe"
     if kind not in ("bpe", "hf"):
         raise H.InvalidDataError(f"checkpoint '{path}' has unknown tokenizer kind '{kind}'.")

@@ -327,7 +327,14 @@ size_t pread_parts(int fd, char* buf, size_t len, int64_t pos) {
   };
   std::thread th[kLoadReaders];
   int started = 0;
-  for (int i = 1; i < parts && (size_t)i * part < len; i++) th[started++] = std::thread(work, i);
+  for (int i = 1; i < parts && (size_t)i * part < len; i++) {
+    try {
+      th[started] = std::thread(work, i);
+      started++;
+    } catch (...) {  // no thread to be had: this part is read here (entry points never throw)
+      work(i);
+    }
+  }
   work(0);
   for (int i = 0; i < started; i++) th[i].join();
   size_t total = 0;

@@ -547,7 +547,11 @@ TrainingReport Trainer::train(SequenceSource& data, const std::function<void(int
   const int my_rank = rank >= 0 ? rank : be_->dp_rank;
   const bool writer = my_rank == 0, gather = ranks > 1 && zero1;
   const std::string& dir = cfg.checkpoint_directory;
-  if (!dir.empty() && writer) std::filesystem::create_directories(dir);
+  if (!dir.empty() && writer) {
+    std::error_code ec;
+    std::filesystem::create_directories(dir, ec);
+    if (ec) throw FileIOError("could not create the checkpoint directory '" + dir + "': " + ec.message());
+  }
   auto save = [&](int step) {
     if (dir.empty()) return;
     const std::string path = (std::filesystem::path(dir) / ("step-" + std::to_string(step) + ".ckpt")).string();
