@@ -111,18 +111,24 @@ def peek_info(path) -> CheckpointInfo:
     return CheckpointInfo(config_from_json(meta.get("Config") or {}), kind, _dtype_name(_dtype(meta, path)), step)
 
 
-def save_model(backend, path, model, config, tokenizer_kind: str, tokenizer_state: str, step: int, trainer=None):
+def save_model(backend, path, model, config, tokenizer_kind: str, tokenizer_state: str, step: int, trainer=None,
+               write: bool = True):
     """``Checkpointing.SaveModel`` (Checkpointing.cs:22-36): the weights, with the trainer's AdamW moments when a
     trainer is given (``EnumerateState``), and the config / tokenizer metadata. Returns once the file is complete, as
-    the reference's synchronous save does (the library snapshots on the device and writes in the background)."""
+    the reference's synchronous save does (the library snapshots on the device and writes in the background).
+
+    Data parallelism: one rank writes. With a ZeRO-1 trainer every rank must call this (the moment shards are
+    gathered collectively) and the others pass ``write=False``; otherwise ranks with ``write=False`` return at once."""
     if tokenizer_kind not in ("bpe", "hf"):
         raise H.ArgumentError(f"can't persist tokenizer of kind '{tokenizer_kind}'.")
     metadata = json.dumps({"Config": config_to_json(config), "TokenizerKind": tokenizer_kind,
                            "Tokenizer": tokenizer_state, "ComputeDType": F32}, separators=(",", ":"))
     if trainer is not None:
-        trainer.save_checkpoint(str(path), step, metadata)
+        if not write and not trainer.zero1:
+            return
+        trainer.save_checkpoint(str(path) if write else "", step, metadata)
         trainer.wait_checkpoint()
-    else:
+    elif write:
         backend.save_checkpoint(str(path), step, model.named_parameters(), metadata)
         backend.wait_checkpoint()
 
