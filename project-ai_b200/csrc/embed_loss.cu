@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   uint32_t parity = 0;
   for (int r = blockIdx.x; r < n; r += gridDim.x, parity ^= 1u) {
-    // every thread waits on the barrier (acquiring the copy's writes); the CTA agrees on the verdict in one barrier
+    // every thread waits on the barrier (acquiring the copy's writes); the CTA agrees on the outcome in one barrier
     if (!__syncthreads_and(tc::mbar_wait(&bar, parity) ? 1 : 0)) {
       if (threadIdx.x == 0) {
         atomicExch(error_flag, 81);

@@ -64,7 +64,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
   return false;
 }
-// Lane 0 polls, the warp follows its verdict (keeps .sync.aligned instructions convergent on every path).
+// Lane 0 polls, the warp follows its result (keeps .sync.aligned instructions convergent on every path).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   int ok = 0;
   if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity) ? 1 : 0;
