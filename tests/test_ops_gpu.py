@@ -186,11 +186,12 @@ def test_silu_mul(cuda, oracle):
 
 # (1000, 32000) and (300, 20000): more rows than SMs, so each CTA of the streaming kernel walks several rows with the
 # next row's copy in flight; (150, 30002): a row length that is not a whole number of 16-byte units (register kernel).
-@pytest.mark.parametrize("n,vocab", [(37, 256), (64, 32000), (9, 40000), (1000, 32000), (300, 20000), (150, 30002)])
+@pytest.mark.parametrize("n,vocab", [(37, 256), (64, 32000), (9, 40000), (1000, 32000), (300, 20000), (150, 30002),
+                                     (1, 32768), (200, 16388)])
 def test_cross_entropy_fused(cuda, oracle, n, vocab):
     logits = rnd(50, n, vocab, scale=3.0)
     targets = np.random.RandomState(51).randint(0, vocab, size=n).astype(np.int32)
-    targets[3] = -100
+    targets[3:4] = -100
     targets[97::149] = -100  # ignored rows between streamed ones
     exp_loss = oracle.to_host(oracle.cross_entropy(oracle.from_host(logits), targets, -100))
     exp_grad = oracle.to_host(oracle.cross_entropy_grad(oracle.from_host(logits), targets, -100))
@@ -199,6 +200,18 @@ def test_cross_entropy_fused(cuda, oracle, n, vocab):
     assert_close(exp_grad, cuda.to_host(grad), 1e-4, 1e-7, "ce grad")
     assert_close(exp_loss, cuda.to_host(cuda.cross_entropy(cuda.from_host(logits), targets, -100)), 1e-5, 1e-6, "ce")
     assert_close(exp_grad, cuda.to_host(cuda.cross_entropy_grad(cuda.from_host(logits), targets, -100)), 1e-4, 1e-7, "ce grad")
+
+
+def test_cross_entropy_every_row_ignored(cuda, oracle):
+    """No counted row (CpuComputeBackend.cs:472, :480): the loss is 0 and the gradient all zeros, on the streaming
+    path (rows of whole 16-byte units, more rows than SMs) as on the others."""
+    for n, vocab in ((400, 32000), (5, 30002)):
+        logits = rnd(54, n, vocab)
+        targets = np.full(n, -100, np.int32)
+        loss, grad = cuda.cross_entropy_fused(cuda.from_host(logits), targets, -100, 1.0)
+        assert float(cuda.to_host(loss).reshape(-1)[0]) == 0.0
+        assert not np.any(cuda.to_host(grad))
+        assert float(oracle.to_host(oracle.cross_entropy(oracle.from_host(logits), targets, -100)).reshape(-1)[0]) == 0.0
 
 
 def test_cross_entropy_streamed_rows_equal_register_rows(cuda):
