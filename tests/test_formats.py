@@ -149,6 +149,28 @@ def test_load_matches_the_oracle_and_raises_its_errors(cuda, tmp_path):
 
 
 @pytest.mark.gpu
+def test_load_reads_large_payloads_in_parts_and_reports_truncation_like_the_oracle(cuda, tmp_path):
+    """Payloads of a whole 32 MB staging chunk and of a chunk and a bit load exactly (each chunk is read as up to four
+    parts at once); a file cut inside the third part of a chunk reports the bytes up to the cut, as the reference's
+    sequential reader does."""
+    big = rnd(7, 8_388_608)              # 32 MB: one full chunk
+    odd = rnd(8, 8_388_608 + 262_147)    # a full chunk, then 1 MB + 12 bytes
+    p = tmp_path / "big.ckpt"
+    F.save_checkpoint(p, 4, [("big", big), ("odd", odd)])
+    _, _, got = cuda.load_checkpoint(p)
+    assert np.array_equal(cuda.to_host(got["big"]), big) and np.array_equal(cuda.to_host(got["odd"]), odd)
+    data = p.read_bytes()
+    start = data.index(b"big") + 3 + 4 + 4 + 8  # name, rank, one dimension, payload length
+    cut = tmp_path / "cut.ckpt"
+    cut.write_bytes(data[:start + 20_000_000])
+    with pytest.raises(F.InvalidData) as want:
+        F.load_checkpoint(cut)
+    assert "got 20000000" in str(want.value)
+    with pytest.raises(cabi.InvalidDataError, match=r"expected 33554432 bytes, got 20000000\)"):
+        cuda.load_checkpoint(cut)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("vocab", [259, 100_000])
 def test_dataset_batch_equals_next_batch(cuda, tmp_path, vocab):
     seq = 64
