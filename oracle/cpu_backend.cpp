@@ -15,6 +15,7 @@
 // reduced in row order afterwards, so results are bit-identical for every thread count.
 #include "projectai_cuda.h"
 
+#include <cerrno>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -54,6 +55,10 @@ struct pai_ctx {
   std::unordered_map<void*, Block> blocks;
   std::vector<std::unordered_set<void*>> scopes;
   int64_t in_use = 0, peak = 0;
+  // the last checkpoint read by oracle_ckpt_load
+  std::string ck_meta;
+  std::vector<std::string> ck_names;
+  std::vector<pai_tensor> ck_tensors;
 };
 
 namespace {
@@ -792,5 +797,147 @@ ORC_API pai_status oracle_cat(pai_ctx* c, const pai_tensor* a, const pai_tensor*
     if (lb * inner != 0) memcpy(dst + o * lt * inner + la * inner, sb.data() + o * lb * inner, (size_t)(lb * inner) * 4);
   }
   *out = r;
+  return PAI_OK;
+}
+
+
+// ---------------------------------------------------------------- checkpoints (ProjectAI.Formats/Checkpoint.cs)
+// The same entry points as the CUDA library's, synchronous: Checkpoint.Save (Checkpoint.cs:23-57) writes the file
+// before returning (oracle_ckpt_wait has nothing to join), Checkpoint.Load (:63-110) reads every tensor into a host
+// block of the current scope with the reader's checks. They let the host trainer's checkpoint flows run on the CPU.
+
+ORC_API pai_status oracle_ckpt_save(pai_ctx* c, const char* path, int32_t step, const char* metadata, int64_t meta_len,
+                                    const char* names, int64_t names_len, const pai_tensor* tensors, int32_t n) {
+  CHECK_CTX(c);
+  if (!path || n < 0 || meta_len < 0 || (n > 0 && (!tensors || !names))) return fail(PAI_ERR_ARGUMENT, "SaveCheckpoint: bad arguments");
+  std::vector<std::string> nm;
+  for (int64_t i = 0; i < names_len && (int)nm.size() < n;) {
+    size_t len = strnlen(names + i, (size_t)(names_len - i));
+    nm.emplace_back(names + i, len);
+    i += (int64_t)len + 1;
+  }
+  if ((int)nm.size() != n) return fail(PAI_ERR_ARGUMENT, "SaveCheckpoint: %d names for %d tensors", (int)nm.size(), n);
+  for (int i = 0; i < n; i++) {
+    TRY(check_desc(c, &tensors[i], "tensor"));
+    if (numel(tensors[i]) > 2147483647LL)
+      return fail(PAI_ERR_UNSUPPORTED, "tensor '%s' has %lld elements, exceeding this format's 2^31 limit.", nm[(size_t)i].c_str(),
+                  (long long)numel(tensors[i]));
+  }
+  FILE* f = fopen(path, "wb");
+  if (!f) return fail(PAI_ERR_IO, "could not create '%s': %s", path, strerror(errno));
+  bool ok = fwrite("PAICKPT2", 1, 8, f) == 8;
+  auto w32 = [&](int32_t v) { ok = ok && fwrite(&v, 4, 1, f) == 1; };
+  w32(step);
+  w32((int32_t)meta_len);
+  if (meta_len) ok = ok && fwrite(metadata, 1, (size_t)meta_len, f) == (size_t)meta_len;
+  w32(n);
+  for (int i = 0; i < n && ok; i++) {
+    const pai_tensor& t = tensors[i];
+    const std::string& name = nm[(size_t)i];
+    w32((int32_t)name.size());
+    if (!name.empty()) ok = ok && fwrite(name.data(), 1, name.size(), f) == name.size();
+    w32(t.rank);
+    for (int d = 0; d < t.rank; d++) w32(t.dims[d]);
+    int64_t bytes = numel(t) * 4;
+    ok = ok && fwrite(&bytes, 8, 1, f) == 1;
+    auto dense = materialize(t);  // the view's logical elements in row-major order (ToHost)
+    if (dense.size()) ok = ok && fwrite(dense.data(), 4, dense.size(), f) == dense.size();
+  }
+  if (fclose(f) != 0) ok = false;
+  if (!ok) return fail(PAI_ERR_IO, "writing '%s' failed", path);
+  return PAI_OK;
+}
+
+ORC_API pai_status oracle_ckpt_wait(pai_ctx* c) { CHECK_CTX(c); return PAI_OK; }
+
+ORC_API pai_status oracle_ckpt_load(pai_ctx* c, const char* path, int32_t header_only, int32_t* step, int64_t* meta_len,
+                                    int32_t* n_tensors) {
+  CHECK_CTX(c);
+  if (!path) return fail(PAI_ERR_ARGUMENT, "LoadCheckpoint: bad arguments");
+  c->ck_meta.clear();
+  c->ck_names.clear();
+  c->ck_tensors.clear();
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(PAI_ERR_IO, "could not open '%s': %s", path, strerror(errno));
+  struct Closer { FILE* f; ~Closer() { fclose(f); } } closer{f};
+  auto exact = [&](void* dst, size_t n, const char* what) -> pai_status {
+    size_t got = n ? fread(dst, 1, n, f) : 0;
+    if (got != n)
+      return fail(PAI_ERR_INVALID_DATA, "'%s' is truncated reading %s (expected %zu bytes, got %zu).", path, what, n, got);
+    return PAI_OK;
+  };
+  char magic[8];
+  if (fread(magic, 1, 8, f) != 8 || memcmp(magic, "PAICKPT2", 8) != 0)
+    return fail(PAI_ERR_INVALID_DATA, "'%s' is not a ProjectAI checkpoint (bad magic).", path);
+  int32_t stp = 0, mlen = 0, count = 0;
+  TRY(exact(&stp, 4, "the step"));
+  TRY(exact(&mlen, 4, "the metadata length"));
+  if (mlen < 0 || mlen > (1 << 24)) return fail(PAI_ERR_INVALID_DATA, "'%s' has a bad metadata length (%d).", path, mlen);
+  std::string meta((size_t)mlen, '\0');
+  TRY(exact(mlen ? &meta[0] : nullptr, (size_t)mlen, "metadata"));
+  if (step) *step = stp;
+  if (meta_len) *meta_len = mlen;
+  if (n_tensors) *n_tensors = 0;
+  c->ck_meta = meta;
+  if (header_only) return PAI_OK;
+  TRY(exact(&count, 4, "the tensor count"));
+  if (count < 0) return fail(PAI_ERR_INVALID_DATA, "'%s' has a negative tensor count (%d).", path, count);
+  for (int32_t i = 0; i < count; i++) {
+    int32_t nlen = 0, rank = 0;
+    TRY(exact(&nlen, 4, "a tensor name length"));
+    if (nlen < 0 || nlen > (1 << 20)) return fail(PAI_ERR_INVALID_DATA, "'%s' tensor %d: bad name length %d.", path, i, nlen);
+    std::string name((size_t)nlen, '\0');
+    std::string what = "tensor " + std::to_string(i) + " name";
+    TRY(exact(nlen ? &name[0] : nullptr, (size_t)nlen, what.c_str()));
+    TRY(exact(&rank, 4, "a tensor rank"));
+    if (rank < 0 || rank > PAI_MAX_RANK) return fail(PAI_ERR_INVALID_DATA, "checkpoint tensor '%s' has invalid rank %d.", name.c_str(), rank);
+    int32_t dims[PAI_MAX_RANK] = {};
+    int64_t expected = 4;
+    for (int d = 0; d < rank; d++) {
+      TRY(exact(&dims[d], 4, "a tensor dimension"));
+      if (dims[d] < 0) return fail(PAI_ERR_INVALID_DATA, "checkpoint tensor '%s' has a negative dimension %d.", name.c_str(), dims[d]);
+      expected *= dims[d];
+    }
+    int64_t blen = 0;
+    TRY(exact(&blen, 8, "a payload length"));
+    if (blen != expected || blen > 2147483647LL)
+      return fail(PAI_ERR_INVALID_DATA, "checkpoint tensor '%s': payload length %lld != dims product × 4 (%lld).", name.c_str(),
+                  (long long)blen, (long long)expected);
+    pai_tensor t;
+    TRY(alloc(c, rank, dims, PAI_F32, &t));
+    what = "tensor '" + name + "' payload";
+    TRY(exact(t.base, (size_t)blen, what.c_str()));
+    c->ck_names.push_back(name);
+    c->ck_tensors.push_back(t);
+  }
+  if (n_tensors) *n_tensors = count;
+  return PAI_OK;
+}
+
+ORC_API pai_status oracle_ckpt_meta(pai_ctx* c, char* b, int64_t cap) {
+  CHECK_CTX(c);
+  if ((int64_t)c->ck_meta.size() > cap || (!b && !c->ck_meta.empty())) return fail(PAI_ERR_ARGUMENT, "metadata buffer too small");
+  if (!c->ck_meta.empty()) memcpy(b, c->ck_meta.data(), c->ck_meta.size());
+  return PAI_OK;
+}
+
+ORC_API pai_status oracle_ckpt_tensor(pai_ctx* c, int32_t index, char* name, int64_t name_cap, int64_t* name_len, pai_tensor* out) {
+  CHECK_CTX(c);
+  if (index < 0 || index >= (int32_t)c->ck_tensors.size())
+    return fail(PAI_ERR_OUT_OF_RANGE, "checkpoint tensor index %d out of range [0, %zu)", index, c->ck_tensors.size());
+  const std::string& n = c->ck_names[(size_t)index];
+  if (name_len) *name_len = (int64_t)n.size();
+  if (name) {
+    if (name_cap < (int64_t)n.size()) return fail(PAI_ERR_ARGUMENT, "name needs %zu bytes", n.size());
+    if (!n.empty()) memcpy(name, n.data(), n.size());
+  }
+  if (out) *out = c->ck_tensors[(size_t)index];
+  return PAI_OK;
+}
+
+ORC_API pai_status oracle_ckpt_close(pai_ctx* c) {
+  CHECK_CTX(c);
+  c->ck_names.clear();
+  c->ck_tensors.clear();
   return PAI_OK;
 }

@@ -415,6 +415,71 @@ def test_train_loop_data_parallel_draws_per_rank_streams(tmp_path):
                 np.testing.assert_array_equal(r[k].view(np.uint32), r0[k].view(np.uint32), k)  # replicas agree
 
 
+def _zero1_files_rank(rank, world, port, out_dir):
+    """Checkpoint files of a ZeRO-1 run through Trainer.train (rank 0 writes, both ranks gather), the same run
+    replicated, and a restore of the ZeRO-1 file into fresh sharded trainers that continue the run."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from projectai_b200 import _paihost as H
+    be = H.Backend(str(ROOT / "oracle" / "build" / "liboracle.so"), "oracle_", 0)
+    allreduce, reduce_scatter, allgather = gloo_collectives(be, rank, world)
+    seqs = [[int(v) for v in row] for row in np.random.RandomState(22).randint(0, 256, size=(7, 40))]
+
+    def trainer(zero1, seed, ckdir):
+        m = H.LlamaModel(be, H.ModelConfig(**TINY), seed=seed)
+        tc = H.TrainingConfig(batch_size=2, sequence_length=32, learning_rate=1e-3, weight_decay=0.1, max_steps=2,
+                              gradient_checkpointing=True, warmup_steps=0, seed=5, checkpoint_every_steps=1,
+                              checkpoint_directory=str(ckdir))
+        tr = H.Trainer(be, m, tc, 0.9, 0.95)
+        tr.world = world
+        tr.rank = rank
+        tr.set_allreduce(allreduce)
+        if zero1:
+            tr.zero1 = True
+            tr.set_shard_exchange(reduce_scatter, allgather)
+        return m, tr
+
+    m_z, t_z = trainer(True, 0, out_dir / "z")
+    t_z.train(seqs)
+    m_r, t_r = trainer(False, 0, out_dir / "r")
+    t_r.train(seqs)
+    dist.barrier()  # rank 0's files are complete (the oracle writes them before save returns)
+    m_x, t_x = trainer(True, 1, out_dir / "unused")
+    assert t_x.restore(str(out_dir / "z" / "step-2.ckpt")) == 2
+    x = np.array([seqs[rank][:32], seqs[rank + 2][:32]], np.float32)
+    y = np.array([seqs[rank][1:33], seqs[rank + 2][1:33]], np.float32)
+    t_z.step([x], [y])
+    t_x.step([x], [y])
+    np.savez(out_dir / f"files_rank{rank}.npz", moments=np.array(t_x.moment_elements()),
+             **{"z_" + n: be.to_host(p) for n, p in m_z.named_parameters()},
+             **{"x_" + n: be.to_host(p) for n, p in m_x.named_parameters()})
+    dist.destroy_process_group()
+
+
+def test_zero1_checkpoint_files_equal_the_replicated_run_and_resume(tmp_path):
+    """Trainer.train under ZeRO-1 writes step-<n>.ckpt files byte-identical to the replicated run's (the moment shards
+    gathered into the reference's layout, one writer), and sharded trainers restored from the last file continue the
+    run bit for bit with shard-sized moments."""
+    port = free_port()
+    mp.spawn(_zero1_files_rank, args=(2, port, tmp_path), nprocs=2, join=True)
+    for n in ("step-1.ckpt", "step-2.ckpt"):
+        z, r = (tmp_path / "z" / n).read_bytes(), (tmp_path / "r" / n).read_bytes()
+        assert z == r, n
+    assert not (tmp_path / "unused").exists() or not any((tmp_path / "unused").iterdir())
+    for rank in (0, 1):
+        d = np.load(tmp_path / f"files_rank{rank}.npz")
+        params = sum(d[k].size for k in d.files if k.startswith("z_"))
+        assert int(d["moments"]) == params  # each rank holds half of m and half of v
+        for k in d.files:
+            if k.startswith("z_"):
+                np.testing.assert_array_equal(d["x_" + k[2:]].view(np.uint32), d[k].view(np.uint32), k)
+
+
 @pytest.mark.gpu
 def test_nccl_zero1_two_gpus_matches_replicated(tmp_path):
     """ZeRO-1 over NCCL (in-place reduce-scatter, AdamW on the shard, in-place all-gather) gives the replicated

@@ -17,7 +17,7 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import ROOT
+from conftest import ORACLE_LIB, ROOT
 
 sys.path.insert(0, str(ROOT / "oracle"))
 import formats as F  # noqa: E402  (the oracle, test infrastructure)
@@ -71,6 +71,31 @@ def test_oracle_checkpoint_rejects_damaged_files(tmp_path):
         p.write_bytes(data)
         with pytest.raises(F.InvalidData, match=msg.replace("(", r"\(").replace(")", r"\)")):
             F.load_checkpoint(p)
+
+
+def test_oracle_library_checkpoints_match_the_format_oracle(tmp_path):
+    """The CPU oracle library's checkpoint entry points (used to run the host trainer's checkpoint flows on the CPU)
+    write the bytes of the format restatement, views in logical row-major order, and read them back with its checks."""
+    from projectai_b200 import _paihost as H
+
+    be = H.Backend(str(ORACLE_LIB), "oracle_", 0)
+    w = rnd(5, 6, 4)
+    tensors = [("w", w), ("wT", np.ascontiguousarray(w.T)), ("s", np.array(2.5, np.float32)), ("e", np.zeros((0, 3), np.float32))]
+    dev = be.from_host(w)
+    items = [("w", dev), ("wT", dev.transpose(0, 1)), ("s", be.from_host(tensors[2][1])), ("e", be.allocate([0, 3]))]
+    p = tmp_path / "o.ckpt"
+    be.save_checkpoint(str(p), 7, items, "meta ✓")
+    be.wait_checkpoint()
+    assert p.read_bytes() == F.checkpoint_bytes(7, tensors, "meta ✓")
+    step, meta, got = be.load_checkpoint(str(p))
+    assert (step, meta) == (7, "meta ✓") and [n for n, _ in got] == [n for n, _ in tensors]
+    for (n, t), (_, want) in zip(got, tensors):
+        assert np.array_equal(be.to_host(t).reshape(want.shape), want), n
+    for i, (data, msg) in enumerate(damaged_files(known_answer())):
+        q = tmp_path / f"bad{i}.ckpt"
+        q.write_bytes(data)
+        with pytest.raises(H.InvalidDataError, match=msg.replace("(", r"\(").replace(")", r"\)")):
+            be.load_checkpoint(str(q))
 
 
 def test_oracle_packed_dataset_blocks_and_guards(tmp_path):
