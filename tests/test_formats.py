@@ -454,3 +454,48 @@ def test_save_model_then_load_model_rebuilds_the_trained_model(tmp_path):
         assert np.array_equal(be.to_host(t), w[n]), n
     x = be.from_host(ids[:, :16].copy())
     assert np.array_equal(be.to_host(m.forward(x)), be.to_host(m2.forward(x)))
+
+
+def test_train_loop_checkpoints_and_model_files_on_the_oracle(tmp_path):
+    """The same flows on the CPU oracle library: Trainer.train writes step-2 and the final step-3 file, a trainer
+    restored from step 2 reproduces step 3, and save_model / load_model rebuild the trained model exactly."""
+    from projectai_b200 import _paihost as H
+    from projectai_b200 import checkpointing as C
+
+    be = H.Backend(str(ORACLE_LIB), "oracle_", 0)
+    cfg = H.ModelConfig(vocab_size=64, embedding_dim=32, layer_count=2, head_count=4, kv_head_count=2, ffn_hidden=64,
+                        max_sequence_length=16)
+    seqs = [[int(v) for v in row] for row in np.random.RandomState(8).randint(0, 64, size=(6, 12))]
+    ckdir = tmp_path / "ck"
+
+    def trainer(seed):
+        m = H.LlamaModel(be, cfg, seed=seed)
+        tc = H.TrainingConfig(batch_size=2, sequence_length=8, learning_rate=1e-3, weight_decay=0.1, max_steps=3,
+                              warmup_steps=1, seed=4, checkpoint_every_steps=2, checkpoint_directory=str(ckdir))
+        return m, H.Trainer(be, m, tc, 0.9, 0.95)
+
+    m1, t1 = trainer(0)
+    report = t1.train(seqs)
+    assert sorted(q.name for q in ckdir.iterdir()) == ["step-2.ckpt", "step-3.ckpt"]
+    m2, t2 = trainer(1)
+    assert t2.restore(str(ckdir / "step-2.ckpt")) == 2
+    rng = H.PcgRng(4)
+    for _ in range(2 * 2):
+        rng.next_u32()
+    rows = [rng.next_u32() % len(seqs) for _ in range(2)]
+    l3 = t2.step([np.array([seqs[r][:8] for r in rows], np.float32)], [np.array([seqs[r][1:9] for r in rows], np.float32)])
+    assert l3 == report["step_losses"][2]
+    w1 = dict((n, be.to_host(p)) for n, p in m1.named_parameters())
+    for n, p in m2.named_parameters():
+        assert np.array_equal(be.to_host(p), w1[n]), n
+
+    path = tmp_path / "model.ckpt"
+    C.save_model(be, path, m1, cfg, "hf", '{"model":{}}', 3, trainer=t1)
+    info = C.peek_info(path)
+    assert (info.step, info.tokenizer_kind, info.config.ffn_hidden) == (3, "hf", 64)
+    m3, cfg3, kind, tok, step = C.load_model(be, path)
+    assert (kind, tok, step, cfg3.vocab_size) == ("hf", '{"model":{}}', 3, 64)
+    for n, p in m3.named_parameters():
+        assert np.array_equal(be.to_host(p), w1[n]), n
+    with pytest.raises(H.InvalidDataError, match="has no model metadata"):
+        C.load_model(be, ckdir / "step-3.ckpt")  # a resume checkpoint carries no model metadata
