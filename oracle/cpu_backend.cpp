@@ -55,6 +55,10 @@ struct pai_ctx {
   std::unordered_map<void*, Block> blocks;
   std::vector<std::unordered_set<void*>> scopes;
   int64_t in_use = 0, peak = 0;
+  // the open packed dataset (oracle_dataset_open): its blocks' bytes, id width, sequence length, block count
+  std::vector<uint8_t> ds_bytes;
+  int ds_elem = 0, ds_seq = 0;
+  int64_t ds_blocks = 0;
   // the last checkpoint read by oracle_ckpt_load
   std::string ck_meta;
   std::vector<std::string> ck_names;
@@ -939,5 +943,83 @@ ORC_API pai_status oracle_ckpt_close(pai_ctx* c) {
   CHECK_CTX(c);
   c->ck_names.clear();
   c->ck_tensors.clear();
+  return PAI_OK;
+}
+
+
+// ---------------------------------------------------------------- packed datasets (ProjectAI.Training/PackedBinDataset.cs)
+// PackedBinDataset.Open's checks on the shard (PackedBinDataset.cs:62-83) and NextBatch (Training.cs:122-141) over
+// GetSequence (:96-117), on the host: inputs ids[:, :-1] and targets ids[:, 1:] of each drawn block as F32 ids.
+
+ORC_API pai_status oracle_dataset_open(pai_ctx* c, const char* path, int32_t elem, int32_t seq, int64_t blocks) {
+  CHECK_CTX(c);
+  if (!path) return fail(PAI_ERR_ARGUMENT, "OpenDataset: bad arguments");
+  if (elem != 2 && elem != 4) return fail(PAI_ERR_INVALID_DATA, "unsupported dataset dtype (%d-byte ids).", elem);
+  if (seq < 1) return fail(PAI_ERR_INVALID_DATA, "manifest SequenceLength must be >= 1; got %d.", seq);
+  if (blocks < 1) return fail(PAI_ERR_INVALID_DATA, "manifest BlockCount must be >= 1; got %lld.", (long long)blocks);
+  if (blocks > 2147483647LL)
+    return fail(PAI_ERR_INVALID_DATA, "manifest BlockCount %lld exceeds the dataset's int32 count.", (long long)blocks);
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(PAI_ERR_IO, "dataset shard '%s' (from manifest) not found: %s", path, strerror(errno));
+  struct Closer { FILE* f; ~Closer() { fclose(f); } } closer{f};
+  const int64_t needed = blocks * (int64_t)(seq + 1) * elem;
+  std::vector<uint8_t> bytes((size_t)needed);
+  size_t got = fread(bytes.data(), 1, (size_t)needed, f);
+  if ((int64_t)got < needed) {
+    fseek(f, 0, SEEK_END);
+    return fail(PAI_ERR_INVALID_DATA, "dataset shard '%s' is %lld bytes but the manifest needs %lld for %lld blocks of %d %s ids.",
+                path, (long long)ftell(f), (long long)needed, (long long)blocks, seq + 1, elem == 2 ? "u16" : "u32");
+  }
+  c->ds_bytes.swap(bytes);
+  c->ds_elem = elem;
+  c->ds_seq = seq;
+  c->ds_blocks = blocks;
+  return PAI_OK;
+}
+
+ORC_API pai_status oracle_dataset_batch(pai_ctx* c, const int64_t* indices, int32_t count, pai_tensor* inputs, pai_tensor* targets) {
+  CHECK_CTX(c);
+  if (c->ds_blocks == 0) return fail(PAI_ERR_INVALID_OP, "no dataset is open");
+  if (count < 1 || !indices || !inputs || !targets) return fail(PAI_ERR_ARGUMENT, "NextBatch: bad arguments");
+  const int seq = c->ds_seq, blk = seq + 1;
+  for (int32_t r = 0; r < count; r++)
+    if (indices[r] < 0 || indices[r] >= c->ds_blocks)
+      return fail(PAI_ERR_OUT_OF_RANGE, "index %lld: valid range is [0, %lld).", (long long)indices[r], (long long)c->ds_blocks);
+  std::vector<float> ids((size_t)count * blk);
+  for (int32_t r = 0; r < count; r++) {
+    const uint8_t* b = c->ds_bytes.data() + (size_t)indices[r] * blk * c->ds_elem;
+    for (int t = 0; t < blk; t++) {
+      uint32_t v;
+      if (c->ds_elem == 2) {
+        uint16_t h;
+        memcpy(&h, b + (size_t)t * 2, 2);
+        v = h;
+      } else {
+        memcpy(&v, b + (size_t)t * 4, 4);
+        if (v > 2147483647u)  // GetSequence's checked((int)id)
+          return fail(PAI_ERR_OUT_OF_RANGE, "id %u in block %lld exceeds the int32 range.", v, (long long)indices[r]);
+      }
+      ids[(size_t)r * blk + t] = (float)(int32_t)v;
+    }
+  }
+  int32_t dims[2] = {count, seq};
+  pai_tensor in, tg;
+  TRY(alloc(c, 2, dims, PAI_F32, &in));
+  TRY(alloc(c, 2, dims, PAI_F32, &tg));
+  for (int32_t r = 0; r < count; r++)
+    for (int t = 0; t < seq; t++) {
+      buf(in)[(size_t)r * seq + t] = ids[(size_t)r * blk + t];
+      buf(tg)[(size_t)r * seq + t] = ids[(size_t)r * blk + t + 1];
+    }
+  *inputs = in;
+  *targets = tg;
+  return PAI_OK;
+}
+
+ORC_API pai_status oracle_dataset_close(pai_ctx* c) {
+  CHECK_CTX(c);
+  std::vector<uint8_t>().swap(c->ds_bytes);
+  c->ds_elem = c->ds_seq = 0;
+  c->ds_blocks = 0;
   return PAI_OK;
 }

@@ -499,3 +499,46 @@ def test_train_loop_checkpoints_and_model_files_on_the_oracle(tmp_path):
         assert np.array_equal(be.to_host(p), w1[n]), n
     with pytest.raises(H.InvalidDataError, match="has no model metadata"):
         C.load_model(be, ckdir / "step-3.ckpt")  # a resume checkpoint carries no model metadata
+
+
+@pytest.mark.parametrize("vocab", [259, 100_000])
+def test_train_loop_over_a_packed_dataset_on_the_oracle(tmp_path, vocab):
+    """The oracle library's packed-dataset entry points give NextBatch's ids (u16 and u32 shards, against the numpy
+    restatement), and Trainer.train over the open dataset equals Trainer.train over the same blocks as host sequences,
+    bit for bit; a dataset whose sequence length differs from the trainer's is refused."""
+    from projectai_b200 import _paihost as H
+
+    be = H.Backend(str(ORACLE_LIB), "oracle_", 0)
+    seq = 8
+    ids = np.random.RandomState(9).randint(0, vocab, size=9 * (seq + 1) + 3)
+    F.pack_dataset(ids, vocab, seq, tmp_path / "ds")
+    man, shard = F.read_manifest(tmp_path / "ds")
+    be.dataset_open(str(shard), man["Dtype"], seq, man["BlockCount"])
+    inp, tgt = be.dataset_batch([4, 0, 8])
+    want_i, want_t = F.next_batch(man, shard, [4, 0, 8])
+    assert np.array_equal(be.to_host(inp), want_i) and np.array_equal(be.to_host(tgt), want_t)
+    with pytest.raises(H.OutOfRangeError, match=r"index 9: valid range is \[0, 9\)"):
+        be.dataset_batch([9])
+
+    cfg = H.ModelConfig(vocab_size=vocab, embedding_dim=32, layer_count=1, head_count=4, kv_head_count=2, ffn_hidden=64,
+                        max_sequence_length=16)
+
+    def trainer(s=seq):
+        m = H.LlamaModel(be, cfg, seed=2)
+        tc = H.TrainingConfig(batch_size=2, sequence_length=s, learning_rate=1e-3, max_steps=2, grad_accum=2,
+                              warmup_steps=0, seed=6, checkpoint_directory="")
+        return m, H.Trainer(be, m, tc, 0.9, 0.95)
+
+    m1, t1 = trainer()
+    r1 = t1.train(packed_blocks=man["BlockCount"])
+    blocks = [[int(v) for v in ids[b * (seq + 1):(b + 1) * (seq + 1)]] for b in range(man["BlockCount"])]
+    m2, t2 = trainer()
+    r2 = t2.train(blocks)
+    assert r1["step_losses"] == r2["step_losses"]
+    w2 = dict((n, be.to_host(p)) for n, p in m2.named_parameters())
+    for n, p in m1.named_parameters():
+        assert np.array_equal(be.to_host(p), w2[n]), n
+    _, t3 = trainer(s=4)
+    with pytest.raises(H.InvalidOperationError, match="holds sequences of length 8; the training sequence length is 4"):
+        t3.train(packed_blocks=man["BlockCount"])
+    be.dataset_close()
