@@ -350,9 +350,10 @@ def test_zero1_checkpoint_state_gathers_and_restores_shards(tmp_path):
     assert "a sharded optimizer needs full-size moments" in str(r0["bad"]), str(r0["bad"])
 
 
-def _train_loop_rank(rank, world, port, out_dir):
-    """Trainer.train under data parallelism with ZeRO-1: rank r draws its rows from PCG stream (default + r) of the
-    configured seed; the same draws stepped by hand give the same losses and weights."""
+def _train_loop_rank(rank, world, port, out_dir, accum):
+    """Trainer.train under data parallelism with ZeRO-1 and `accum` micro-batches per step: rank r draws its rows
+    from PCG stream (default + r) of the configured seed; the same draws stepped by hand give the same losses and
+    weights."""
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -369,7 +370,7 @@ def _train_loop_rank(rank, world, port, out_dir):
     def trainer():
         m = H.LlamaModel(be, H.ModelConfig(**TINY), seed=0)
         tc = H.TrainingConfig(batch_size=2, sequence_length=32, learning_rate=1e-3, weight_decay=0.1, max_steps=2,
-                              grad_accum=1, gradient_checkpointing=True, warmup_steps=0, seed=77,
+                              grad_accum=accum, gradient_checkpointing=True, warmup_steps=0, seed=77,
                               checkpoint_directory="")
         tr = H.Trainer(be, m, tc, 0.9, 0.95)
         tr.world = world
@@ -386,11 +387,13 @@ def _train_loop_rank(rank, world, port, out_dir):
     rng = H.PcgRng(77, stream)
     manual, rows_seen = [], []
     for _ in range(2):
-        rows = [rng.next_u32() % len(seqs) for _ in range(2)]
-        rows_seen.append(rows)
-        x = np.array([seqs[r][:32] for r in rows], np.float32)
-        y = np.array([seqs[r][1:33] for r in rows], np.float32)
-        manual.append(t2.step([x], [y]))
+        xs, ys = [], []
+        for _ in range(accum):
+            rows = [rng.next_u32() % len(seqs) for _ in range(2)]
+            rows_seen.append(rows)
+            xs.append(np.array([seqs[r][:32] for r in rows], np.float32))
+            ys.append(np.array([seqs[r][1:33] for r in rows], np.float32))
+        manual.append(t2.step(xs, ys))
     np.savez(out_dir / f"train_rank{rank}.npz", losses=np.array(report["step_losses"], np.float32),
              manual=np.array(manual, np.float32), rows=np.array(rows_seen),
              **{"p_" + n: be.to_host(p) for n, p in m1.named_parameters()},
@@ -398,12 +401,13 @@ def _train_loop_rank(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_train_loop_data_parallel_draws_per_rank_streams(tmp_path):
+@pytest.mark.parametrize("accum", [1, 2])
+def test_train_loop_data_parallel_draws_per_rank_streams(tmp_path, accum):
     """Under data parallelism each rank's Trainer.train draws its own rows (rank 0 the reference's PcgRng(seed)
-    sequence, rank r stream default + r), the ZeRO-1 exchanges run inside the loop, and every rank ends with the
-    weights a hand-driven run of the same draws reaches."""
+    sequence, rank r stream default + r), the ZeRO-1 exchanges run inside the loop (after the last micro-batch when a
+    step accumulates two), and every rank ends with the weights a hand-driven run of the same draws reaches."""
     port = free_port()
-    mp.spawn(_train_loop_rank, args=(2, port, tmp_path), nprocs=2, join=True)
+    mp.spawn(_train_loop_rank, args=(2, port, tmp_path, accum), nprocs=2, join=True)
     r0 = np.load(tmp_path / "train_rank0.npz")
     r1 = np.load(tmp_path / "train_rank1.npz")
     assert not np.array_equal(r0["rows"], r1["rows"])  # the ranks see different rows
